@@ -1,0 +1,289 @@
+"""Headline benchmark: DMAD training throughput (samples/s) and 4-step generation latency
+(s/clip) of the Wan2.1-T2V-1.3B-shaped DiT, on 1..8 B200s of one node.
+
+One benchmark step = one full DMAD cycle on one sample per GPU: a generator iteration
+followed by a critic iteration (the reference alternates them 1:1, student_update_freq=2).
+Both include backward simulation (1..4 student evaluations, cycling as in the reference),
+the critic forwards, backward, and the AdamW updates (plus the EMA update of the student).
+
+    python bench.py --gpus N --steps K --warmup W            # this framework
+    python bench.py --impl reference --gpus N --steps K --warmup W   # the reference build
+
+For N > 1 launch with torchrun (one rank per GPU, NCCL); throughput is the whole-job
+aggregate and every timing is the max over ranks of CUDA-event device time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+LATENT_SHAPE = (16, 21, 60, 104)   # 81 frames at 480x832, VAE stride 4x8x8
+TEXT_SHAPE = (512, 4096)           # umT5-shaped context
+SEQ_LEN = 21 * 30 * 52             # tokens after 1x2x2 patchify
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="dmad_b200", choices=["dmad_b200", "reference"])
+    ap.add_argument("--model", default="wan2.1-1.3b")
+    ap.add_argument("--layers", type=int, default=None, help="debug only: fewer blocks (invalid for the headline)")
+    ap.add_argument("--frames", type=int, default=LATENT_SHAPE[1], help="debug only: latent frames")
+    ap.add_argument("--gen-runs", type=int, default=2)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--count-launches", type=int, default=1)
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_host_batch(frames: int, seed: int):
+    g = torch.Generator().manual_seed(seed)
+    shp = (1, LATENT_SHAPE[0], frames, LATENT_SHAPE[2], LATENT_SHAPE[3])
+    b = {
+        "latents": torch.randn(shp, generator=g),            # teacher samples (Q)
+        "real_latents": torch.randn(shp, generator=g),       # caption-paired real latents (T)
+        "context": torch.randn((1,) + TEXT_SHAPE, generator=g).to(torch.bfloat16),
+    }
+    return {k: v.pin_memory() for k, v in b.items()}
+
+
+def to_device(host, device):
+    return {k: v.to(device, non_blocking=True) for k, v in host.items()}
+
+
+def flush_l2(buf):
+    buf.add_(1)
+
+
+def count_my_kernels(fn, prefixes=("dmad",)) -> int:
+    """Number of kernels from this package launched by one call of fn (torch profiler, untimed)."""
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    n = 0
+    for evt in prof.events():
+        if evt.device_type is not None and "CUDA" in str(evt.device_type) and any(p in evt.name for p in prefixes):
+            n += 1
+    return n
+
+
+def main():
+    args = parse()
+    from dmad_b200.parallel.dist import barrier, get_rank, get_world_size, init_distributed, max_over_ranks
+
+    rank, world, device = init_distributed(timeout_s=900)
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE {world}"
+    torch.backends.cuda.matmul.allow_tf32 = True
+    torch.backends.cudnn.allow_tf32 = True
+    headline_ok = args.layers is None and args.frames == LATENT_SHAPE[1]
+
+    if args.impl == "reference":
+        from baseline.reference_arm import build_reference_trainer
+        trainer = build_reference_trainer(args, device)
+        if trainer is None:
+            return
+    else:
+        from dmad_b200.distill.wan_dmad import WanDMAD, WanDMADConfig
+        from dmad_b200.models.wan import wan_config
+
+        over = {"num_layers": args.layers} if args.layers else {}
+        cfg = WanDMADConfig(net=wan_config(args.model, **over))
+        cfg.checkpoint_critic_blocks_student_phase = cfg.net.num_layers
+        trainer = WanDMAD(cfg, device=device, dtype=torch.bfloat16, seed=0)
+
+    host = make_host_batch(args.frames, seed=1234 + rank)
+    batch = to_device(host, device)
+    l2buf = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=device)
+    it = [0]
+
+    def cycle(b):
+        o1 = trainer.training_step(b, it[0])
+        o2 = trainer.training_step(b, it[0] + 1)
+        it[0] += 2
+        return o1, o2
+
+    # ------------------------------------------------------------------ warm-up
+    for _ in range(args.warmup):
+        cycle(batch)
+    torch.cuda.synchronize()
+    barrier()
+
+    # ------------------------------------------------------------------ device-timed loop
+    clocks = ClockSampler(torch.cuda.current_device())
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    per_step = []
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    for _ in range(args.steps):
+        flush_l2(l2buf)
+        start.record()
+        cycle(batch)
+        end.record()
+        end.synchronize()
+        per_step.append(start.elapsed_time(end))
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    dev_ms = max_over_ranks(sum(per_step) / len(per_step))
+
+    # ------------------------------------------------------------------ end-to-end loop (public API,
+    # pinned H2D of the step's inputs and D2H of the step's losses inside the timed region)
+    e2e = None
+    if not args.no_e2e:
+        h2d = sum(v.numel() * v.element_size() for v in host.values())
+        loss_host = torch.empty(2, dtype=torch.float32).pin_memory()
+        barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_ev.record()
+        for _ in range(args.steps):
+            b = to_device(host, device)
+            o1, o2 = cycle(b)
+            ls = torch.stack([torch.as_tensor(o1.get("dmad_g_loss", 0.0), device=device).float().reshape(()),
+                              torch.as_tensor(o2.get("dmad_d_loss", 0.0), device=device).float().reshape(())])
+            loss_host.copy_(ls, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+        e_ev.record()
+        e_ev.synchronize()
+        wall = (time.perf_counter() - t0) * 1000 / args.steps
+        e2e_ms = max_over_ranks(max(wall, s_ev.elapsed_time(e_ev) / args.steps))
+        e2e = {"value": world / (e2e_ms / 1000.0), "unit": "samples/s", "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(loss_host.numel() * 4), "ms_per_step": e2e_ms}
+
+    # ------------------------------------------------------------------ 4-step generation latency
+    gen_s = None
+    if args.gen_runs > 0:
+        ctx = batch["context"]
+        shp = (1,) + (LATENT_SHAPE[0], args.frames, LATENT_SHAPE[2], LATENT_SHAPE[3])
+        trainer.generate(ctx, shp, num_steps=4)
+        times = []
+        for _ in range(args.gen_runs):
+            barrier()
+            s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s2.record()
+            trainer.generate(ctx, shp, num_steps=4)
+            e2.record()
+            e2.synchronize()
+            times.append(s2.elapsed_time(e2) / 1000.0)
+        gen_s = max_over_ranks(min(times))
+
+    launches = None
+    if args.count_launches and args.impl == "dmad_b200":
+        try:
+            launches = count_my_kernels(lambda: cycle(batch)) * args.steps
+        except Exception as e:  # pragma: no cover
+            launches = None
+            if rank == 0:
+                print(f"# launch count failed: {e!r}", file=sys.stderr)
+
+    try:
+        from dmad_b200 import ops
+        if args.impl == "dmad_b200":
+            ops.check_device_status()
+    except Exception as e:
+        if rank == 0:
+            print(f"# device status: {e}", file=sys.stderr)
+        raise
+
+    value = world / (dev_ms / 1000.0)
+    out = {
+        "metric": "DMAD train samples/s (Wan2.1-1.3B-shaped, device-timed max over ranks)",
+        "value": value,
+        "unit": "samples/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dev_ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic N(0,1) latents/context, random-init weights",
+        "config": {"model": f"{args.model}-shaped DiT (BASELINE config 2)" if headline_ok else "DEBUG (invalid)",
+                   "global_batch": world, "seq_len": SEQ_LEN if headline_ok else None,
+                   "latents": f"16x{args.frames}x60x104", "text": "512x4096",
+                   "parallelism": f"dp{world}", "step": "1 generator + 1 critic DMAD iteration",
+                   "l2": "flushed (write of a 252 MB buffer) before every timed step; inputs > L2"},
+        "gen_latency_s_per_clip": gen_s,
+        "e2e": e2e,
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    if args.impl == "reference":
+        out["impl"] = "reference"
+        out["gpu_launches"] = None
+    if rank == 0:
+        print(json.dumps(out))
+    barrier()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,67 @@
+// Python bindings of the sm_100a kernels (module dmad_b200._C).
+#include <torch/extension.h>
+#include <vector>
+
+namespace dmad {
+void flash_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
+               double scale);
+void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+               const at::Tensor& dout, const at::Tensor& lse2, at::Tensor& dq, at::Tensor& dk, at::Tensor& dv,
+               at::Tensor& dd_scratch, double scale);
+int64_t flash_lse_pad(int64_t L);
+int64_t device_status(int64_t device, bool reset);
+void ln_mod_fwd(const at::Tensor& x, at::Tensor& y, c10::optional<at::Tensor> mean, at::Tensor& rstd,
+                c10::optional<at::Tensor> a, c10::optional<at::Tensor> c, double a_add, int64_t rows_per_group,
+                c10::optional<at::Tensor> gidx, double eps, bool rms);
+void ln_mod_bwd(const at::Tensor& dy, const at::Tensor& x, c10::optional<at::Tensor> mean, const at::Tensor& rstd,
+                c10::optional<at::Tensor> a, double a_add, int64_t rows_per_group, c10::optional<at::Tensor> gidx,
+                bool rms, at::Tensor& dx, c10::optional<at::Tensor> dres, c10::optional<at::Tensor> da,
+                c10::optional<at::Tensor> dc, c10::optional<at::Tensor> gate, c10::optional<at::Tensor> yg,
+                c10::optional<at::Tensor> dyg, c10::optional<at::Tensor> dgate);
+void gate_res_fwd(const at::Tensor& x, const at::Tensor& y, at::Tensor& out, c10::optional<at::Tensor> gate,
+                  int64_t rows_per_group, c10::optional<at::Tensor> gidx);
+void gate_res_bwd(const at::Tensor& dout, const at::Tensor& y, at::Tensor& dy, const at::Tensor& gate,
+                  at::Tensor& dgate, int64_t rows_per_group, c10::optional<at::Tensor> gidx);
+void qk_norm_rope_fwd(const at::Tensor& src, at::Tensor& dst, const at::Tensor& wq, const at::Tensor& wk,
+                      const at::Tensor& cosT, const at::Tensor& sinT, at::Tensor& rstd_q, at::Tensor& rstd_k,
+                      int64_t D, int64_t hd, double eps);
+void qk_norm_rope_bwd(const at::Tensor& gq, const at::Tensor& gk, const at::Tensor& src, at::Tensor& dx,
+                      const at::Tensor& wq, const at::Tensor& wk, const at::Tensor& cosT, const at::Tensor& sinT,
+                      const at::Tensor& rstd_q, const at::Tensor& rstd_k, at::Tensor& dwq, at::Tensor& dwk, int64_t D,
+                      int64_t hd);
+void rope_apply(const at::Tensor& x, at::Tensor& y, const at::Tensor& cosT, const at::Tensor& sinT, int64_t hd,
+                bool inverse);
+void gelu_fwd(const at::Tensor& x, at::Tensor& y);
+void gelu_bwd(const at::Tensor& g, const at::Tensor& x, at::Tensor& dx);
+void fused_adamw(std::vector<at::Tensor> master, std::vector<at::Tensor> grads, std::vector<at::Tensor> exp_avg,
+                 std::vector<at::Tensor> exp_avg_sq, std::vector<at::Tensor> lowp, std::vector<at::Tensor> ema,
+                 double lr, double beta1, double beta2, double eps, double weight_decay, int64_t step,
+                 c10::optional<at::Tensor> grad_scale, double ema_beta);
+void multi_sumsq(std::vector<at::Tensor> grads, at::Tensor& out);
+void clip_scale(const at::Tensor& sumsq, at::Tensor& scale, double max_norm);
+void sinusoid_embed(const at::Tensor& t, at::Tensor& out, int64_t dim, double max_period);
+void small_linear(const at::Tensor& x, const at::Tensor& w, c10::optional<at::Tensor> bias, at::Tensor& y,
+                  int64_t act_in);
+}  // namespace dmad
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "dmad_b200 sm_100a kernels";
+  m.def("flash_fwd", &dmad::flash_fwd);
+  m.def("flash_bwd", &dmad::flash_bwd);
+  m.def("flash_lse_pad", &dmad::flash_lse_pad);
+  m.def("device_status", &dmad::device_status);
+  m.def("ln_mod_fwd", &dmad::ln_mod_fwd);
+  m.def("ln_mod_bwd", &dmad::ln_mod_bwd);
+  m.def("gate_res_fwd", &dmad::gate_res_fwd);
+  m.def("gate_res_bwd", &dmad::gate_res_bwd);
+  m.def("qk_norm_rope_fwd", &dmad::qk_norm_rope_fwd);
+  m.def("qk_norm_rope_bwd", &dmad::qk_norm_rope_bwd);
+  m.def("rope_apply", &dmad::rope_apply);
+  m.def("gelu_fwd", &dmad::gelu_fwd);
+  m.def("gelu_bwd", &dmad::gelu_bwd);
+  m.def("fused_adamw", &dmad::fused_adamw);
+  m.def("multi_sumsq", &dmad::multi_sumsq);
+  m.def("clip_scale", &dmad::clip_scale);
+  m.def("sinusoid_embed", &dmad::sinusoid_embed);
+  m.def("small_linear", &dmad::small_linear);
+}

@@ -1,0 +1,580 @@
+// Flash-attention backward for sm_100a (bf16, head dim 128), two tcgen05 kernels.
+//
+// Functional parity target: the backward the reference pairs with its attention
+// forward (flash-attn 2 `_flash_attn_backward`, called from
+// train/wan/rcm/utils/flash_attention_jvp_triton.py:534-579, and cuDNN SDPA
+// backward through attention.py:120-167): dQ, dK, dV of O = softmax(Q K^T s) V.
+//
+// Kernel A (dK, dV): one CTA per 128-key tile, looping over 128-query tiles.
+//   S^T = K Q^T and dP^T = V dO^T go to TMEM; the row owner (thread = key)
+//   forms P^T (written back as bf16 over S^T) and dS^T = P^T (dP^T - D) s
+//   (written back as bf16 over dP^T); dV += P^T dO and dK += dS^T Q are
+//   TMEM-A MMAs.  TMEM: S^T 0..127, dP^T 128..255, dV 256..383, dK 384..511.
+// Kernel B (dQ): one CTA per 128-query tile, looping over 128-key tiles with
+//   a double-buffered S, dP, and dQ += dS K as a TMEM-A MMA.
+// Splitting dQ from dK/dV costs two extra GEMMs per tile pair but needs no
+// atomics and no fp32 scratch accumulator.
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include "sm100.cuh"
+#include "tma_host.h"
+
+namespace dmad {
+
+void check_bhld(const at::Tensor& x, const char* name);
+int* device_status_ptr(int device);
+int64_t flash_lse_pad(int64_t L);
+
+namespace {
+
+constexpr int kHalfBytes = 128 * 128;
+constexpr int kTileBytes = 2 * kHalfBytes;
+
+struct BwdParams {
+  __nv_bfloat16* out;  // dK/dV base (kernel A uses out & out2) or dQ (kernel B)
+  __nv_bfloat16* out2;
+  int64_t sb, sl, sh;     // strides of out
+  int64_t sb2, sl2, sh2;  // strides of out2
+  const float* lse2;      // [B, H, Lpad] log2-domain
+  const float* dd;        // [B, H, Lpad] rowsum(dO * O)
+  int Lq, Lk, H, Lpad;
+  float scale_log2, scale;
+  int* status;
+};
+
+__device__ __forceinline__ void store_row_bf16(__nv_bfloat16* row, uint32_t tmem_row, float mul) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t r[32];
+    tmem_ld32(tmem_row + c * 32, r);
+    tmem_wait_ld();
+    if (row != nullptr) {
+      uint4* dst = reinterpret_cast<uint4*>(row + c * 32);
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        uint4 w;
+        w.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * mul, __uint_as_float(r[8 * v + 1]) * mul);
+        w.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * mul, __uint_as_float(r[8 * v + 3]) * mul);
+        w.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * mul, __uint_as_float(r[8 * v + 5]) * mul);
+        w.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * mul, __uint_as_float(r[8 * v + 7]) * mul);
+        dst[v] = w;
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ D = rowsum(dO * O)
+__global__ void bwd_dot_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
+                               float* __restrict__ dd, int64_t osb, int64_t osl, int64_t osh, int64_t gsb,
+                               int64_t gsl, int64_t gsh, int B, int H, int Lq, int Lpad) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= (int64_t)B * H * Lpad) return;
+  const int q = row % Lpad;
+  const int h = (row / Lpad) % H;
+  const int b = row / ((int64_t)Lpad * H);
+  float acc = 0.f;
+  if (q < Lq) {
+    const uint2 ov = *reinterpret_cast<const uint2*>(o + b * osb + q * osl + h * osh + lane * 4);
+    const uint2 gv = *reinterpret_cast<const uint2*>(dout + b * gsb + q * gsl + h * gsh + lane * 4);
+    const float2 o0 = unpack_bf16x2(ov.x), o1 = unpack_bf16x2(ov.y);
+    const float2 g0 = unpack_bf16x2(gv.x), g1 = unpack_bf16x2(gv.y);
+    acc = o0.x * g0.x + o0.y * g0.y + o1.x * g1.x + o1.y * g1.y;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  }
+  if (lane == 0) dd[row] = acc;
+}
+
+// ------------------------------------------------------------------ kernel A: dK, dV
+struct DkvSmem {
+  uint8_t k[kTileBytes];
+  uint8_t v[kTileBytes];
+  uint8_t q[2][kTileBytes];
+  uint8_t g[2][kTileBytes];  // dO
+  float lse[2][128];
+  float dd[2][128];
+  uint64_t kv_full;
+  uint64_t q_full[2], q_empty[2];
+  uint64_t s_full, dp_full, p_full, ds_full, done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__global__ void __launch_bounds__(256, 1)
+flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_g,
+                      BwdParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  DkvSmem& sm = *reinterpret_cast<DkvSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  volatile int* abort_flag = &sm.abort_flag;
+  const int warp = warp_id(), lane = lane_id();
+  const int head = blockIdx.y, batch = blockIdx.z;
+  const int k0 = blockIdx.x * 128;
+  const int nq = (p.Lq + 127) / 128;
+  const int64_t bh_off = ((int64_t)batch * p.H + head) * p.Lpad;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sm.q_full[s], 1);
+      mbar_init(&sm.q_empty[s], 1);
+    }
+    mbar_init(&sm.s_full, 1);
+    mbar_init(&sm.dp_full, 1);
+    mbar_init(&sm.p_full, 128);
+    mbar_init(&sm.ds_full, 128);
+    mbar_init(&sm.done, 1);
+    sm.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(&sm.kv_full, 2 * kTileBytes);
+      for (int h = 0; h < 2; ++h) {
+        tma_load_4d(sm.k + h * kHalfBytes, &tm_k, &sm.kv_full, h * 64, head, k0, batch);
+        tma_load_4d(sm.v + h * kHalfBytes, &tm_v, &sm.kv_full, h * 64, head, k0, batch);
+      }
+      int last_s = -1;
+      uint32_t last_ph = 0;
+      for (int i = 0; i < nq; ++i) {
+        const int s = i & 1;
+        const uint32_t ph = (i >> 1) & 1;
+        if (!mbar_wait(&sm.q_empty[s], ph ^ 1, kStatusTimeoutEmpty, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(&sm.q_full[s], 2 * kTileBytes + 2 * 512);
+        for (int h = 0; h < 2; ++h) {
+          tma_load_4d(sm.q[s] + h * kHalfBytes, &tm_q, &sm.q_full[s], h * 64, head, i * 128, batch);
+          tma_load_4d(sm.g[s] + h * kHalfBytes, &tm_g, &sm.q_full[s], h * 64, head, i * 128, batch);
+        }
+        bulk_load(sm.lse[s], p.lse2 + bh_off + i * 128, 512, &sm.q_full[s]);
+        bulk_load(sm.dd[s], p.dd + bh_off + i * 128, 512, &sm.q_full[s]);
+        last_s = s;
+        last_ph = ph;
+      }
+      mbar_wait(&sm.kv_full, 0, kStatusTimeoutTmaFull, nullptr, p.status);
+      if (last_s >= 0) mbar_wait(&sm.q_full[last_s], last_ph, kStatusTimeoutTmaFull, nullptr, p.status);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_kk = idesc_bf16_f32(128, 128, false, false);
+      constexpr uint32_t idesc_mn = idesc_bf16_f32(128, 128, false, true);
+      const uint32_t ka = smem_u32(sm.k), va = smem_u32(sm.v);
+      const uint32_t t_s = tmem, t_dp = tmem + 128, t_dv = tmem + 256, t_dk = tmem + 384;
+      auto gemm_kk = [&](uint32_t d, uint32_t a, uint32_t b) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          mma_bf16_ss(d, smem_desc_sw128(a + off, 16, 1024), smem_desc_sw128(b + off, 16, 1024), idesc_kk, kk > 0);
+        }
+      };
+      auto gemm_ts = [&](uint32_t d, uint32_t a_tmem, uint32_t b, bool acc) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_bf16_ts(d, a_tmem + kk * 8, smem_desc_sw128(b + kk * 2048, kHalfBytes, 1024), idesc_mn,
+                      (acc || kk > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(&sm.kv_full, 0, kStatusTimeoutTmaFull, abort_flag, p.status);
+      if (ok) ok = mbar_wait(&sm.q_full[0], 0, kStatusTimeoutTmaFull, abort_flag, p.status);
+      if (ok) {
+        tc_fence_after();
+        gemm_kk(t_s, ka, smem_u32(sm.q[0]));
+        mma_commit(&sm.s_full);
+        gemm_kk(t_dp, va, smem_u32(sm.g[0]));
+        mma_commit(&sm.dp_full);
+      }
+      for (int i = 0; ok && i < nq; ++i) {
+        const int s = i & 1;
+        const bool has_next = i + 1 < nq;
+        const int s1 = (i + 1) & 1;
+        const uint32_t ph1 = ((i + 1) >> 1) & 1;
+        if (!(ok = mbar_wait(&sm.p_full, i & 1, kStatusTimeoutSoftmax, abort_flag, p.status))) break;
+        tc_fence_after();
+        gemm_ts(t_dv, t_s, smem_u32(sm.g[s]), i > 0);
+        if (has_next) {
+          if (!(ok = mbar_wait(&sm.q_full[s1], ph1, kStatusTimeoutTmaFull, abort_flag, p.status))) break;
+          tc_fence_after();
+          gemm_kk(t_s, ka, smem_u32(sm.q[s1]));
+          mma_commit(&sm.s_full);
+        }
+        if (!(ok = mbar_wait(&sm.ds_full, i & 1, kStatusTimeoutSoftmax, abort_flag, p.status))) break;
+        tc_fence_after();
+        gemm_ts(t_dk, t_dp, smem_u32(sm.q[s]), i > 0);
+        mma_commit(&sm.q_empty[s]);
+        if (has_next) {
+          gemm_kk(t_dp, va, smem_u32(sm.g[s1]));
+          mma_commit(&sm.dp_full);
+        }
+      }
+      mma_commit(&sm.done);
+      mbar_wait(&sm.done, 0, kStatusTimeoutMma, nullptr, p.status);
+    }
+  } else if (warp >= 4) {
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const uint32_t lb = (uint32_t)(wq * 32) << 16;
+    const uint32_t t_s = tmem + lb, t_dp = tmem + lb + 128;
+    const float scale_log2 = p.scale_log2, scale = p.scale;
+    bool ok = true;
+    for (int i = 0; i < nq; ++i) {
+      const int s = i & 1;
+      const uint32_t ph = (i >> 1) & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&sm.q_full[s], ph, kStatusTimeoutTmaFull, abort_flag, p.status));
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.s_full, i & 1, kStatusTimeoutMma, abort_flag, p.status));
+      if (!ok) break;
+      tc_fence_after();
+      float pv[128];
+      {
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(t_s + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) pv[c * 32 + e] = __uint_as_float(r[e]);
+        }
+      }
+      const float* lse = sm.lse[s];
+#pragma unroll
+      for (int e = 0; e < 128; ++e) pv[e] = ex2_approx(fmaf(pv[e], scale_log2, -lse[e]));
+      {
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = pack_bf16x2(pv[64 * c + 2 * e], pv[64 * c + 2 * e + 1]);
+          tmem_st32(t_s + c * 32, r);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&sm.p_full);
+
+      ok = __all_sync(0xffffffffu, mbar_wait(&sm.dp_full, i & 1, kStatusTimeoutMma, abort_flag, p.status));
+      if (!ok) break;
+      tc_fence_after();
+      const float* dd = sm.dd[s];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_dp + c * 32, r);
+        tmem_wait_ld();
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int q = c * 32 + 2 * e;
+          const float d0 = pv[q] * (__uint_as_float(r[2 * e]) - dd[q]) * scale;
+          const float d1 = pv[q + 1] * (__uint_as_float(r[2 * e + 1]) - dd[q + 1]) * scale;
+          w[e] = pack_bf16x2(d0, d1);
+        }
+        tmem_st16(t_dp + c * 16, w);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&sm.ds_full);
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.done, 0, kStatusTimeoutMma, abort_flag, p.status));
+    if (ok) {
+      tc_fence_after();
+      const int kr = k0 + row;
+      const bool valid = kr < p.Lk;
+      __nv_bfloat16* dv_row = valid ? p.out2 + batch * p.sb2 + (int64_t)kr * p.sl2 + head * p.sh2 : nullptr;
+      __nv_bfloat16* dk_row = valid ? p.out + batch * p.sb + (int64_t)kr * p.sl + head * p.sh : nullptr;
+      store_row_bf16(dv_row, tmem + lb + 256, 1.f);
+      store_row_bf16(dk_row, tmem + lb + 384, 1.f);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ kernel B: dQ
+struct DqSmem {
+  uint8_t q[kTileBytes];
+  uint8_t g[kTileBytes];
+  uint8_t k[2][kTileBytes];
+  uint8_t v[2][kTileBytes];
+  uint64_t q_full;
+  uint64_t kv_full[2], kv_empty[2];
+  uint64_t s_full[2], s_free[2];
+  uint64_t dp_full, ds_full, done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__global__ void __launch_bounds__(256, 1)
+flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_g,
+                    BwdParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  DqSmem& sm = *reinterpret_cast<DqSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  volatile int* abort_flag = &sm.abort_flag;
+  const int warp = warp_id(), lane = lane_id();
+  const int head = blockIdx.y, batch = blockIdx.z;
+  const int q0 = blockIdx.x * 128;
+  const int nkv = (p.Lk + 127) / 128;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sm.kv_full[s], 1);
+      mbar_init(&sm.kv_empty[s], 1);
+      mbar_init(&sm.s_full[s], 1);
+      mbar_init(&sm.s_free[s], 128);
+    }
+    mbar_init(&sm.dp_full, 1);
+    mbar_init(&sm.ds_full, 128);
+    mbar_init(&sm.done, 1);
+    sm.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(&sm.q_full, 2 * kTileBytes);
+      for (int h = 0; h < 2; ++h) {
+        tma_load_4d(sm.q + h * kHalfBytes, &tm_q, &sm.q_full, h * 64, head, q0, batch);
+        tma_load_4d(sm.g + h * kHalfBytes, &tm_g, &sm.q_full, h * 64, head, q0, batch);
+      }
+      int last_s = -1;
+      uint32_t last_ph = 0;
+      for (int j = 0; j < nkv; ++j) {
+        const int s = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&sm.kv_empty[s], ph ^ 1, kStatusTimeoutEmpty, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(&sm.kv_full[s], 2 * kTileBytes);
+        for (int h = 0; h < 2; ++h) {
+          tma_load_4d(sm.k[s] + h * kHalfBytes, &tm_k, &sm.kv_full[s], h * 64, head, j * 128, batch);
+          tma_load_4d(sm.v[s] + h * kHalfBytes, &tm_v, &sm.kv_full[s], h * 64, head, j * 128, batch);
+        }
+        last_s = s;
+        last_ph = ph;
+      }
+      mbar_wait(&sm.q_full, 0, kStatusTimeoutTmaFull, nullptr, p.status);
+      if (last_s >= 0) mbar_wait(&sm.kv_full[last_s], last_ph, kStatusTimeoutTmaFull, nullptr, p.status);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_kk = idesc_bf16_f32(128, 128, false, false);
+      constexpr uint32_t idesc_mn = idesc_bf16_f32(128, 128, false, true);
+      const uint32_t qa = smem_u32(sm.q), ga = smem_u32(sm.g);
+      const uint32_t t_dp = tmem + 256, t_dq = tmem + 384;
+      auto gemm_kk = [&](uint32_t d, uint32_t a, uint32_t b) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          mma_bf16_ss(d, smem_desc_sw128(a + off, 16, 1024), smem_desc_sw128(b + off, 16, 1024), idesc_kk, kk > 0);
+        }
+      };
+      bool ok = mbar_wait(&sm.q_full, 0, kStatusTimeoutTmaFull, abort_flag, p.status);
+      if (ok) ok = mbar_wait(&sm.kv_full[0], 0, kStatusTimeoutTmaFull, abort_flag, p.status);
+      if (ok) {
+        tc_fence_after();
+        gemm_kk(tmem, qa, smem_u32(sm.k[0]));
+        mma_commit(&sm.s_full[0]);
+        gemm_kk(t_dp, ga, smem_u32(sm.v[0]));
+        mma_commit(&sm.dp_full);
+      }
+      for (int j = 0; ok && j < nkv; ++j) {
+        const int s = j & 1;
+        const bool has_next = j + 1 < nkv;
+        const int s1 = (j + 1) & 1;
+        const uint32_t ph1 = ((j + 1) >> 1) & 1;
+        if (has_next) {
+          if (!(ok = mbar_wait(&sm.kv_full[s1], ph1, kStatusTimeoutTmaFull, abort_flag, p.status))) break;
+          if (j >= 1 && !(ok = mbar_wait(&sm.s_free[s1], ((j - 1) >> 1) & 1, kStatusTimeoutSoftmax, abort_flag, p.status)))
+            break;
+          tc_fence_after();
+          gemm_kk(tmem + s1 * 128, qa, smem_u32(sm.k[s1]));
+          mma_commit(&sm.s_full[s1]);
+        }
+        if (!(ok = mbar_wait(&sm.ds_full, j & 1, kStatusTimeoutSoftmax, abort_flag, p.status))) break;
+        tc_fence_after();
+        const uint32_t kb = smem_u32(sm.k[s]);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_bf16_ts(t_dq, t_dp + kk * 8, smem_desc_sw128(kb + kk * 2048, kHalfBytes, 1024), idesc_mn,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&sm.kv_empty[s]);
+        if (has_next) {
+          gemm_kk(t_dp, ga, smem_u32(sm.v[s1]));
+          mma_commit(&sm.dp_full);
+        }
+      }
+      mma_commit(&sm.done);
+      mbar_wait(&sm.done, 0, kStatusTimeoutMma, nullptr, p.status);
+    }
+  } else if (warp >= 4) {
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const int q_row = q0 + row;
+    const uint32_t lb = (uint32_t)(wq * 32) << 16;
+    const uint32_t t_dp = tmem + lb + 256;
+    const float scale_log2 = p.scale_log2, scale = p.scale;
+    const int64_t bh_off = ((int64_t)batch * p.H + head) * p.Lpad;
+    const float lse2 = p.lse2[bh_off + q_row];
+    const float dval = p.dd[bh_off + q_row];
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      const int s = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&sm.s_full[s], (j >> 1) & 1, kStatusTimeoutMma, abort_flag, p.status));
+      if (!ok) break;
+      tc_fence_after();
+      float pv[128];
+      {
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(tmem + lb + s * 128 + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) pv[c * 32 + e] = __uint_as_float(r[e]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&sm.s_free[s]);
+      const int kv_valid = p.Lk - j * 128;
+#pragma unroll
+      for (int e = 0; e < 128; ++e) pv[e] = e < kv_valid ? ex2_approx(fmaf(pv[e], scale_log2, -lse2)) : 0.f;
+      ok = __all_sync(0xffffffffu, mbar_wait(&sm.dp_full, j & 1, kStatusTimeoutMma, abort_flag, p.status));
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(t_dp + c * 32, r);
+        tmem_wait_ld();
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int kv = c * 32 + 2 * e;
+          w[e] = pack_bf16x2(pv[kv] * (__uint_as_float(r[2 * e]) - dval) * scale,
+                             pv[kv + 1] * (__uint_as_float(r[2 * e + 1]) - dval) * scale);
+        }
+        tmem_st16(t_dp + c * 16, w);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&sm.ds_full);
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.done, 0, kStatusTimeoutMma, abort_flag, p.status));
+    if (ok) {
+      tc_fence_after();
+      __nv_bfloat16* dq_row = q_row < p.Lq ? p.out + batch * p.sb + (int64_t)q_row * p.sl + head * p.sh : nullptr;
+      store_row_bf16(dq_row, tmem + lb + 384, 1.f);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+CUtensorMap make_map(const at::Tensor& x) {
+  const uint64_t dims[4] = {128, (uint64_t)x.size(2), (uint64_t)x.size(1), (uint64_t)x.size(0)};
+  const uint64_t strides[3] = {(uint64_t)x.stride(2) * 2, (uint64_t)x.stride(1) * 2, (uint64_t)x.stride(0) * 2};
+  const uint32_t box[4] = {64, 1, 128, 1};
+  return make_tmap_bf16(x.data_ptr(), 4, dims, strides, box);
+}
+
+}  // namespace
+
+// dq, dk, dv may be strided views (e.g. slices of one fused [B, L, 3, H, 128] buffer).
+// lse2: [B, H, Lpad] log2-domain LSE from flash_fwd; dd_scratch: [B, H, Lpad] fp32 work
+// buffer that receives rowsum(dO * O).
+void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+               const at::Tensor& dout, const at::Tensor& lse2, at::Tensor& dq, at::Tensor& dk, at::Tensor& dv,
+               at::Tensor& dd_scratch, double scale) {
+  check_bhld(q, "q");
+  check_bhld(k, "k");
+  check_bhld(v, "v");
+  check_bhld(o, "o");
+  check_bhld(dout, "dout");
+  check_bhld(dq, "dq");
+  check_bhld(dk, "dk");
+  check_bhld(dv, "dv");
+  const int B = q.size(0), Lq = q.size(1), H = q.size(2), Lk = k.size(1);
+  const int64_t Lpad = flash_lse_pad(Lq);
+  TORCH_CHECK(lse2.is_contiguous() && lse2.scalar_type() == at::kFloat && lse2.dim() == 3 && lse2.size(2) == Lpad,
+              "lse must be [B, H, round_up(Lq, 256)] fp32");
+  TORCH_CHECK(dd_scratch.is_contiguous() && dd_scratch.scalar_type() == at::kFloat &&
+                  dd_scratch.numel() >= (int64_t)B * H * Lpad,
+              "dd_scratch too small");
+  c10::cuda::CUDAGuard guard(q.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  {
+    const int64_t rows = (int64_t)B * H * Lpad;
+    const int warps = 8;
+    bwd_dot_kernel<<<(unsigned)((rows + warps - 1) / warps), warps * 32, 0, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
+        dd_scratch.data_ptr<float>(), o.stride(0), o.stride(1), o.stride(2), dout.stride(0), dout.stride(1),
+        dout.stride(2), B, H, Lq, (int)Lpad);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  CUtensorMap tq = make_map(q), tk = make_map(k), tv = make_map(v), tg = make_map(dout);
+  BwdParams p;
+  p.lse2 = lse2.data_ptr<float>();
+  p.dd = dd_scratch.data_ptr<float>();
+  p.Lq = Lq;
+  p.Lk = Lk;
+  p.H = H;
+  p.Lpad = (int)Lpad;
+  p.scale = (float)scale;
+  p.scale_log2 = (float)(scale * 1.4426950408889634);
+  p.status = device_status_ptr(q.get_device());
+  {
+    p.out = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
+    p.sb = dk.stride(0);
+    p.sl = dk.stride(1);
+    p.sh = dk.stride(2);
+    p.out2 = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+    p.sb2 = dv.stride(0);
+    p.sl2 = dv.stride(1);
+    p.sh2 = dv.stride(2);
+    const size_t smem = sizeof(DkvSmem) + 1024;
+    C10_CUDA_CHECK(
+        cudaFuncSetAttribute(flash_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    dim3 grid((Lk + 127) / 128, H, B);
+    flash_bwd_dkdv_kernel<<<grid, 256, smem, stream>>>(tq, tk, tv, tg, p);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  {
+    p.out = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr());
+    p.sb = dq.stride(0);
+    p.sl = dq.stride(1);
+    p.sh = dq.stride(2);
+    p.out2 = nullptr;
+    const size_t smem = sizeof(DqSmem) + 1024;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    dim3 grid((Lq + 127) / 128, H, B);
+    flash_bwd_dq_kernel<<<grid, 256, smem, stream>>>(tq, tk, tv, tg, p);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+}
+
+}  // namespace dmad

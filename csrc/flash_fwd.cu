@@ -1,0 +1,389 @@
+// Flash-attention forward for sm_100a (bf16 in/out, fp32 accumulate, head dim 128).
+//
+// Functional parity target: the reference's attention entry point
+// (train/wan/rcm/utils/attention.py:120-167, cuDNN SDPA on cc 100) and the
+// forward half of its Triton kernel (train/wan/rcm/utils/flash_attention_jvp_triton.py:107-232):
+// O = softmax(Q K^T * scale) V, plus the natural-log row LSE used by backward.
+//
+// Design (one CTA per pair of 128-row query tiles of one (batch, head)):
+//   warp 0      : TMA producer; Q once, then a 2-stage ring of K and V tiles
+//   warp 1      : TMEM owner and the single MMA-issuing thread
+//   warps 4..7  : softmax for query tile 0   (thread i owns TMEM lane / query row i)
+//   warps 8..11 : softmax for query tile 1
+// TMEM (512 columns): per tile, S at [t*256, +128) and O at [t*256+128, +128).
+// P is written back as bf16 over the first 64 columns of S and consumed by a
+// TMEM-A (".kind::f16 [d], [a], b") MMA, so it never touches shared memory.
+// Each tile alternates S = Q K_j^T -> softmax -> O += P V_j; the MMA thread
+// interleaves the two tiles so the tensor core works on one tile while the
+// other tile's softmax runs.  O is rescaled lazily: only when a row maximum
+// grows by more than 2^8 (values stay exact because the final normalisation
+// uses the same stale maximum as the numerator).
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include "sm100.cuh"
+#include "tma_host.h"
+
+namespace dmad {
+
+int* device_status_ptr(int device);
+
+namespace {
+
+constexpr int kHeadDim = 128;
+constexpr int kTileM = 128;   // query rows per tile
+constexpr int kTileN = 128;   // keys per KV tile
+constexpr int kStages = 2;
+constexpr int kHalfBytes = 128 * 128;            // one 128-row x 64-col bf16 swizzle panel
+constexpr int kTileBytes = 2 * kHalfBytes;       // 128 x 128 bf16
+constexpr float kRescaleThreshold = 8.0f;        // log2 units
+
+struct FwdSmem {
+  // 1024-byte aligned panels (required by the 128B swizzle atoms)
+  uint8_t q[2][kTileBytes];
+  uint8_t k[kStages][kTileBytes];
+  uint8_t v[kStages][kTileBytes];
+  uint64_t q_full;
+  uint64_t k_full[kStages], k_empty[kStages];
+  uint64_t v_full[kStages], v_empty[kStages];
+  uint64_t s_full[2], p_full[2], pv_done[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+struct FwdParams {
+  __nv_bfloat16* o;  // [B, Lq, H, 128] with strides below
+  float* lse;        // [B, H, Lpad] log2-domain LSE (+inf on padding rows)
+  int64_t o_sb, o_sl, o_sh;
+  int Lq, Lk, H, Lpad;
+  float scale_log2;
+  int* status;       // device status word (bounded-wait failures)
+};
+
+__global__ void __launch_bounds__(384, 1)
+flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                 const __grid_constant__ CUtensorMap tm_v, FwdParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  FwdSmem& sm = *reinterpret_cast<FwdSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  volatile int* abort_flag = &sm.abort_flag;
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int head = blockIdx.y;
+  const int batch = blockIdx.z;
+  const int q0 = blockIdx.x * (2 * kTileM);
+  const int nkv = (p.Lk + kTileN - 1) / kTileN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.k_full[s], 1);
+      mbar_init(&sm.k_empty[s], 1);
+      mbar_init(&sm.v_full[s], 1);
+      mbar_init(&sm.v_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&sm.s_full[t], 1);
+      mbar_init(&sm.p_full[t], 128);
+      mbar_init(&sm.pv_done[t], 1);
+    }
+    mbar_init(&sm.drain, 1);
+    sm.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, 512);
+    tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      mbar_arrive_expect_tx(&sm.q_full, 2 * kTileBytes);
+      for (int t = 0; t < 2; ++t)
+        for (int h = 0; h < 2; ++h)
+          tma_load_4d(sm.q[t] + h * kHalfBytes, &tm_q, &sm.q_full, h * 64, head, q0 + t * kTileM, batch);
+      int last_s = -1, last_ph = 0;
+      for (int j = 0; j < nkv; ++j) {
+        const int s = j % kStages;
+        const uint32_t ph = (j / kStages) & 1;
+        if (!mbar_wait(&sm.k_empty[s], ph ^ 1, kStatusTimeoutEmpty, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(&sm.k_full[s], kTileBytes);
+        for (int h = 0; h < 2; ++h)
+          tma_load_4d(sm.k[s] + h * kHalfBytes, &tm_k, &sm.k_full[s], h * 64, head, j * kTileN, batch);
+        if (!mbar_wait(&sm.v_empty[s], ph ^ 1, kStatusTimeoutEmpty, abort_flag, p.status)) {
+          // K load of this stage is in flight: wait for it before leaving
+          mbar_wait(&sm.k_full[s], ph, kStatusTimeoutTmaFull, nullptr, p.status);
+          break;
+        }
+        mbar_arrive_expect_tx(&sm.v_full[s], kTileBytes);
+        for (int h = 0; h < 2; ++h)
+          tma_load_4d(sm.v[s] + h * kHalfBytes, &tm_v, &sm.v_full[s], h * 64, head, j * kTileN, batch);
+        last_s = s;
+        last_ph = ph;
+      }
+      // never leave while our own copies may still be landing
+      mbar_wait(&sm.q_full, 0, kStatusTimeoutTmaFull, nullptr, p.status);
+      if (last_s >= 0) {
+        mbar_wait(&sm.k_full[last_s], last_ph, kStatusTimeoutTmaFull, nullptr, p.status);
+        mbar_wait(&sm.v_full[last_s], last_ph, kStatusTimeoutTmaFull, nullptr, p.status);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idesc_qk = idesc_bf16_f32(128, 128, false, false);
+      constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 128, false, true);
+      const uint32_t q_addr0 = smem_u32(sm.q[0]);
+      const uint32_t q_addr1 = smem_u32(sm.q[1]);
+      bool ok = mbar_wait(&sm.q_full, 0, kStatusTimeoutTmaFull, abort_flag, p.status);
+
+      auto issue_qk = [&](int t, int s) {
+        const uint32_t qa = t == 0 ? q_addr0 : q_addr1;
+        const uint32_t ka = smem_u32(sm.k[s]);
+        const uint32_t d_tmem = tmem + t * 256;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          mma_bf16_ss(d_tmem, smem_desc_sw128(qa + off, 16, 1024), smem_desc_sw128(ka + off, 16, 1024), idesc_qk,
+                      kk > 0);
+        }
+      };
+      auto issue_pv = [&](int t, int s, bool acc) {
+        const uint32_t va = smem_u32(sm.v[s]);
+        const uint32_t p_tmem = tmem + t * 256;        // bf16 P over S columns [0,64)
+        const uint32_t o_tmem = tmem + t * 256 + 128;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          mma_bf16_ts(o_tmem, p_tmem + kk * 8, smem_desc_sw128(va + kk * 2048, kHalfBytes, 1024), idesc_pv,
+                      (acc || kk > 0) ? 1u : 0u);
+        }
+      };
+
+      if (ok) ok = mbar_wait(&sm.k_full[0], 0, kStatusTimeoutTmaFull, abort_flag, p.status);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(0, 0);
+        mma_commit(&sm.s_full[0]);
+        issue_qk(1, 0);
+        mma_commit(&sm.s_full[1]);
+        mma_commit(&sm.k_empty[0]);
+      }
+      for (int j = 0; ok && j < nkv; ++j) {
+        const int s = j % kStages;
+        const uint32_t ph = (j / kStages) & 1;
+        const int s1 = (j + 1) % kStages;
+        const uint32_t ph1 = ((j + 1) / kStages) & 1;
+        const bool has_next = j + 1 < nkv;
+        if (!(ok = mbar_wait(&sm.v_full[s], ph, kStatusTimeoutTmaFull, abort_flag, p.status))) break;
+        for (int t = 0; t < 2; ++t) {
+          if (!(ok = mbar_wait(&sm.p_full[t], j & 1, kStatusTimeoutSoftmax, abort_flag, p.status))) break;
+          tc_fence_after();
+          issue_pv(t, s, j > 0);
+          mma_commit(&sm.pv_done[t]);
+          if (has_next) {
+            if (t == 0 && !(ok = mbar_wait(&sm.k_full[s1], ph1, kStatusTimeoutTmaFull, abort_flag, p.status))) break;
+            tc_fence_after();
+            issue_qk(t, s1);
+            mma_commit(&sm.s_full[t]);
+          }
+        }
+        if (!ok) break;
+        mma_commit(&sm.v_empty[s]);
+        if (has_next) mma_commit(&sm.k_empty[s1]);
+      }
+      // drain: every MMA issued by this thread has completed before TMEM is freed
+      mma_commit(&sm.drain);
+      mbar_wait(&sm.drain, 0, kStatusTimeoutMma, nullptr, p.status);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax / epilogue
+    const int t = (warp - 4) >> 2;           // query tile
+    const int wq = warp & 3;                 // TMEM lane quarter
+    const int row = wq * 32 + lane;          // row within the tile
+    const int q_row = q0 + t * kTileM + row;
+    const uint32_t lane_base = (uint32_t)(wq * 32) << 16;
+    const uint32_t s_tmem = tmem + lane_base + t * 256;
+    const uint32_t o_tmem = s_tmem + 128;
+    const float scale_log2 = p.scale_log2;
+    float m_used = -INFINITY;
+    float l_sum = 0.f;
+    bool ok = true;
+
+    for (int j = 0; j < nkv; ++j) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&sm.s_full[t], j & 1, kStatusTimeoutMma, abort_flag, p.status));
+      if (!ok) break;
+      tc_fence_after();
+      // pass 1: row maximum over the tile (32 columns at a time, low register pressure)
+      const int kv_valid = p.Lk - j * kTileN;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(s_tmem + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (c * 32 + i < kv_valid) mx = fmaxf(mx, __uint_as_float(r[i]));
+      }
+      const float m_blk = mx * scale_log2;
+      float alpha = 1.f;
+      bool rescale = false;
+      if (j == 0) {
+        m_used = m_blk;
+      } else if (m_blk > m_used + kRescaleThreshold) {
+        alpha = ex2_approx(m_used - m_blk);
+        m_used = m_blk;
+        rescale = true;
+      }
+      // O holds the sum over tiles < j (PV(j-1) finished before S(j) completed).
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(o_tmem + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st32(o_tmem + c * 32, r);
+        }
+      }
+      // pass 2: P = exp2(S * scale - m), row sum, bf16 P written over S columns [0, 64).
+      // Chunk c reads S columns [32c, 32c+32) and writes P columns [16c, 16c+16),
+      // which only overlap S columns already consumed.
+      const float neg_m = -m_used;
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(s_tmem + c * 32, r);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int col = c * 32 + 2 * i;
+          const float p0 = col < kv_valid ? ex2_approx(fmaf(__uint_as_float(r[2 * i]), scale_log2, neg_m)) : 0.f;
+          const float p1 = col + 1 < kv_valid ? ex2_approx(fmaf(__uint_as_float(r[2 * i + 1]), scale_log2, neg_m)) : 0.f;
+          rs += p0 + p1;
+          pk[i] = pack_bf16x2(p0, p1);
+        }
+        tmem_st16(s_tmem + c * 16, pk);
+      }
+      l_sum = l_sum * alpha + rs;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&sm.p_full[t]);
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.pv_done[t], (nkv - 1) & 1, kStatusTimeoutMma, abort_flag, p.status));
+    if (ok) {
+      tc_fence_after();
+      const float inv_l = 1.f / l_sum;
+      const bool valid = q_row < p.Lq;
+      __nv_bfloat16* orow = p.o + batch * p.o_sb + (int64_t)q_row * p.o_sl + head * p.o_sh;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(o_tmem + c * 32, r);
+        tmem_wait_ld();
+        if (valid) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * inv_l, __uint_as_float(r[8 * v + 1]) * inv_l);
+            w.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv_l, __uint_as_float(r[8 * v + 3]) * inv_l);
+            w.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
+            w.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
+            dst[v] = w;
+          }
+        }
+      }
+      if (p.lse != nullptr && q_row < p.Lpad)
+        p.lse[((int64_t)batch * p.H + head) * p.Lpad + q_row] = valid ? (m_used + __log2f(l_sum)) : INFINITY;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// q/k/v: [B, L, H, 128] bf16 views (last dim contiguous, any row / head / batch stride
+// that is a multiple of 8 elements).
+CUtensorMap make_qkv_map(const at::Tensor& x) {
+  const uint64_t dims[4] = {128, (uint64_t)x.size(2), (uint64_t)x.size(1), (uint64_t)x.size(0)};
+  const uint64_t strides[3] = {(uint64_t)x.stride(2) * 2, (uint64_t)x.stride(1) * 2, (uint64_t)x.stride(0) * 2};
+  const uint32_t box[4] = {64, 1, 128, 1};
+  return make_tmap_bf16(x.data_ptr(), 4, dims, strides, box);
+}
+
+}  // namespace
+
+void check_bhld(const at::Tensor& x, const char* name) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16, name, " must be a CUDA bf16 tensor");
+  TORCH_CHECK(x.dim() == 4 && x.size(3) == kHeadDim, name, " must be [B, L, H, 128]");
+  TORCH_CHECK(x.stride(3) == 1, name, " last dim must be contiguous");
+  TORCH_CHECK(x.stride(2) % 8 == 0 && x.stride(1) % 8 == 0 && x.stride(0) % 8 == 0, name,
+              " strides must be multiples of 8 elements");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0, name, " must be 16-byte aligned");
+}
+
+size_t flash_fwd_smem_bytes() { return sizeof(FwdSmem) + 1024; }
+
+int64_t flash_lse_pad(int64_t L) { return (L + 255) / 256 * 256; }
+
+// Writes O (same layout rules as q) and the log2-domain LSE [B, H, Lpad] (fp32),
+// Lpad = Lq rounded up to a multiple of 256 (padding rows hold +inf).
+void flash_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
+               double scale) {
+  check_bhld(q, "q");
+  check_bhld(k, "k");
+  check_bhld(v, "v");
+  check_bhld(o, "o");
+  TORCH_CHECK(k.sizes() == v.sizes(), "k and v shapes differ");
+  TORCH_CHECK(q.size(0) == k.size(0) && q.size(2) == k.size(2), "q/k batch or head mismatch");
+  TORCH_CHECK(o.sizes() == q.sizes(), "o shape mismatch");
+  const int B = q.size(0), Lq = q.size(1), H = q.size(2), Lk = k.size(1);
+  TORCH_CHECK(Lk > 0 && Lq > 0, "empty attention");
+  bool has_lse = lse.defined() && lse.numel() > 0;
+  if (has_lse) {
+    TORCH_CHECK(lse.is_cuda() && lse.scalar_type() == at::kFloat && lse.is_contiguous(), "lse must be fp32 contiguous");
+    TORCH_CHECK(lse.dim() == 3 && lse.size(0) == B && lse.size(1) == H && lse.size(2) == flash_lse_pad(Lq),
+                "lse must be [B, H, round_up(Lq, 256)]");
+  }
+  c10::cuda::CUDAGuard guard(q.device());
+  CUtensorMap tq = make_qkv_map(q), tk = make_qkv_map(k), tv = make_qkv_map(v);
+  FwdParams p;
+  p.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  p.lse = has_lse ? lse.data_ptr<float>() : nullptr;
+  p.o_sb = o.stride(0);
+  p.o_sl = o.stride(1);
+  p.o_sh = o.stride(2);
+  p.Lq = Lq;
+  p.Lk = Lk;
+  p.H = H;
+  p.Lpad = has_lse ? (int)lse.size(2) : 0;
+  p.scale_log2 = (float)(scale * 1.4426950408889634);
+  p.status = device_status_ptr(q.get_device());
+  const size_t smem = flash_fwd_smem_bytes();
+  C10_CUDA_CHECK(cudaFuncSetAttribute(flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  dim3 grid((Lq + 2 * kTileM - 1) / (2 * kTileM), H, B);
+  flash_fwd_kernel<<<grid, 384, smem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace dmad

@@ -1,0 +1,717 @@
+// Row-wise memory-bound kernels of the DiT blocks (sm_100a, bf16 activations,
+// fp32 math):
+//   * ln_mod_fwd / ln_mod_bwd : LayerNorm or RMSNorm followed by a per-group
+//     affine y = n * A + C.  Covers the adaLN "norm(x) * (1 + scale) + shift" of
+//     the Wan and H3 blocks (train/wan/rcm/networks/wan2pt1.py:419-436,
+//     dmad_h3/lowmem.py:436-458), the affine cross-attention LayerNorm and the
+//     non-affine RMSNorm of the H3 critic heads.  The group of a row is
+//     row / rows_per_group, or an explicit int32 index per row (H3 packed rows).
+//     The backward optionally fuses a residual-gradient addend and the backward
+//     of the gated residual that produced its input.
+//   * gate_res_fwd : out = x + y * gate[g]  (gated residual, wan2pt1.py:426-436)
+//   * qk_norm_rope_fwd / _bwd : RMSNorm over the full hidden size of q and k
+//     (wan2pt1.py:193-211) followed by interleaved rotary embedding per head
+//     (rcm/utils/rope.py:36-70) from cos/sin tables.
+//   * gelu_tanh_fwd / _bwd.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include "common.cuh"
+
+namespace dmad {
+namespace {
+
+
+// Row kernels are instantiated for the number of 8-element vectors each thread
+// holds (VEC) and the block size (TH); rows of up to 8192 columns are covered.
+#define DMAD_ROW_DISPATCH(nvec, ...)                                        \
+  [&] {                                                                     \
+    if ((nvec) <= 128) { constexpr int VEC = 1, TH = 128; __VA_ARGS__(); }  \
+    else if ((nvec) <= 256) { constexpr int VEC = 2, TH = 128; __VA_ARGS__(); } \
+    else if ((nvec) <= 512) { constexpr int VEC = 2, TH = 256; __VA_ARGS__(); } \
+    else if ((nvec) <= 768) { constexpr int VEC = 3, TH = 256; __VA_ARGS__(); } \
+    else { constexpr int VEC = 4, TH = 256; __VA_ARGS__(); }                \
+  }()
+
+struct ModSpec {
+  const float* a;   // [G, D] fp32 (row stride a_sg; 0 = shared row) or nullptr
+  const float* c;   // [G, D] fp32 or nullptr
+  int64_t a_sg, c_sg;
+  float a_add;      // A = a_add + a[g]
+  int rows_per_group;
+  const int* gidx;  // optional explicit group per row
+};
+
+__device__ __forceinline__ int row_group(const ModSpec& m, int64_t r) {
+  return m.gidx != nullptr ? m.gidx[r] : (int)(r / m.rows_per_group);
+}
+
+template <int kMaxVec, int kTh>
+__global__ void __launch_bounds__(kTh)
+ln_mod_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx, __nv_bfloat16* __restrict__ y, int64_t sy,
+                  float* __restrict__ mean_out, float* __restrict__ rstd_out, ModSpec m, int64_t R, int D, float eps,
+                  bool rms) {
+  __shared__ float red[32];
+  const int64_t r = blockIdx.x;
+  if (r >= R) return;
+  const int nvec = D >> 3;
+  const bf16x8* xr = reinterpret_cast<const bf16x8*>(x + r * sx);
+  float v[kMaxVec][8];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = threadIdx.x + i * kTh;
+    if (c < nvec) {
+      bf16x8_to_float(xr[c], v[i]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s += v[i][e];
+    }
+  }
+  const float mu = rms ? 0.f : block_sum(s, red) / D;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = threadIdx.x + i * kTh;
+    if (c < nvec) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float d = v[i][e] - mu;
+        ss += d * d;
+      }
+    }
+  }
+  const float rstd = rsqrtf(block_sum(ss, red) / D + eps);
+  const int g = row_group(m, r);
+  const float* ar = m.a != nullptr ? m.a + (int64_t)g * m.a_sg : nullptr;
+  const float* cr = m.c != nullptr ? m.c + (int64_t)g * m.c_sg : nullptr;
+  bf16x8* yr = reinterpret_cast<bf16x8*>(y + r * sy);
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = threadIdx.x + i * kTh;
+    if (c < nvec) {
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int col = c * 8 + e;
+        const float A = m.a_add + (ar != nullptr ? ar[col] : 0.f);
+        const float C = cr != nullptr ? cr[col] : 0.f;
+        o[e] = (v[i][e] - mu) * rstd * A + C;
+      }
+      yr[c] = float_to_bf16x8(o);
+    }
+  }
+  if (threadIdx.x == 0) {
+    if (mean_out != nullptr) mean_out[r] = mu;
+    rstd_out[r] = rstd;
+  }
+}
+
+// Backward.  Each block walks `rows_per_block` consecutive rows, keeps the
+// per-column partial sums of dy*n (-> da) and dy (-> dc) in registers and
+// flushes them with atomics whenever the group changes.
+// Optional fusions:
+//   dres   : dx_total = LN_bwd(dy) + dres
+//   gate/yg: the input of the norm was out = xg + yg * gate[g]; additionally
+//            write dyg = dx_total * gate and accumulate dgate += dx_total * yg.
+struct LnBwdArgs {
+  const __nv_bfloat16* dy;
+  int64_t sdy;
+  const __nv_bfloat16* x;
+  int64_t sx;
+  const float* mean;
+  const float* rstd;
+  __nv_bfloat16* dx;
+  int64_t sdx;
+  const __nv_bfloat16* dres;
+  int64_t sdres;
+  float* da;  // [G, D] accum (row stride D) or nullptr
+  float* dc;
+  // gated-residual fusion
+  const float* gate;
+  int64_t gate_sg;
+  const __nv_bfloat16* yg;
+  int64_t syg;
+  __nv_bfloat16* dyg;
+  int64_t sdyg;
+  float* dgate;  // [G, D] accum
+  int64_t R;
+  int D;
+  bool rms;
+  int rows_per_block;
+};
+
+template <int kMaxVec, int kTh>
+__global__ void __launch_bounds__(kTh)
+ln_mod_bwd_kernel(LnBwdArgs p, ModSpec m) {
+  __shared__ float red[32];
+  const int nvec = p.D >> 3;
+  const int64_t r0 = (int64_t)blockIdx.x * p.rows_per_block;
+  const int64_t r1 = min(p.R, r0 + p.rows_per_block);
+  float acc_a[kMaxVec][8], acc_c[kMaxVec][8], acc_g[kMaxVec][8];
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc_a[i][e] = acc_c[i][e] = acc_g[i][e] = 0.f;
+  int cur_g = -1;
+  auto flush = [&](int g) {
+    if (g < 0) return;
+#pragma unroll
+    for (int i = 0; i < kMaxVec; ++i) {
+      const int c = threadIdx.x + i * kTh;
+      if (c < nvec) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int col = c * 8 + e;
+          if (p.da != nullptr) atomicAdd(p.da + (int64_t)g * p.D + col, acc_a[i][e]);
+          if (p.dc != nullptr) atomicAdd(p.dc + (int64_t)g * p.D + col, acc_c[i][e]);
+          if (p.dgate != nullptr) atomicAdd(p.dgate + (int64_t)g * p.D + col, acc_g[i][e]);
+          acc_a[i][e] = acc_c[i][e] = acc_g[i][e] = 0.f;
+        }
+      }
+    }
+  };
+  for (int64_t r = r0; r < r1; ++r) {
+    const int g = row_group(m, r);
+    if (g != cur_g) {
+      flush(cur_g);
+      cur_g = g;
+    }
+    const float mu = p.rms ? 0.f : p.mean[r];
+    const float rstd = p.rstd[r];
+    const float* ar = m.a != nullptr ? m.a + (int64_t)g * m.a_sg : nullptr;
+    const bf16x8* xr = reinterpret_cast<const bf16x8*>(p.x + r * p.sx);
+    const bf16x8* dyr = reinterpret_cast<const bf16x8*>(p.dy + r * p.sdy);
+    float n[kMaxVec][8], dn[kMaxVec][8];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxVec; ++i) {
+      const int c = threadIdx.x + i * kTh;
+      if (c < nvec) {
+        float xv[8], gv[8];
+        bf16x8_to_float(xr[c], xv);
+        bf16x8_to_float(dyr[c], gv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int col = c * 8 + e;
+          n[i][e] = (xv[e] - mu) * rstd;
+          const float A = m.a_add + (ar != nullptr ? ar[col] : 0.f);
+          dn[i][e] = gv[e] * A;
+          acc_a[i][e] += gv[e] * n[i][e];
+          acc_c[i][e] += gv[e];
+          s1 += dn[i][e];
+          s2 += dn[i][e] * n[i][e];
+        }
+      }
+    }
+    const float mdn = p.rms ? 0.f : block_sum(s1, red) / p.D;
+    const float mdnn = block_sum(s2, red) / p.D;
+    bf16x8* dxr = reinterpret_cast<bf16x8*>(p.dx + r * p.sdx);
+    const bf16x8* dresr = p.dres != nullptr ? reinterpret_cast<const bf16x8*>(p.dres + r * p.sdres) : nullptr;
+    const float* gr = p.gate != nullptr ? p.gate + (int64_t)g * p.gate_sg : nullptr;
+    const bf16x8* ygr = p.yg != nullptr ? reinterpret_cast<const bf16x8*>(p.yg + r * p.syg) : nullptr;
+    bf16x8* dygr = p.dyg != nullptr ? reinterpret_cast<bf16x8*>(p.dyg + r * p.sdyg) : nullptr;
+#pragma unroll
+    for (int i = 0; i < kMaxVec; ++i) {
+      const int c = threadIdx.x + i * kTh;
+      if (c < nvec) {
+        float o[8];
+        float rv[8];
+        if (dresr != nullptr) bf16x8_to_float(dresr[c], rv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          o[e] = rstd * (dn[i][e] - mdn - n[i][e] * mdnn) + (dresr != nullptr ? rv[e] : 0.f);
+        }
+        dxr[c] = float_to_bf16x8(o);
+        if (gr != nullptr) {
+          float yv[8], d[8];
+          bf16x8_to_float(ygr[c], yv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int col = c * 8 + e;
+            d[e] = o[e] * gr[col];
+            acc_g[i][e] += o[e] * yv[e];
+          }
+          dygr[c] = float_to_bf16x8(d);
+        }
+      }
+    }
+  }
+  flush(cur_g);
+}
+
+__global__ void gate_res_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx, const __nv_bfloat16* __restrict__ y,
+                                    int64_t sy, __nv_bfloat16* __restrict__ out, int64_t so, ModSpec m, int64_t R,
+                                    int D) {
+  const int nvec = D >> 3;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= R * nvec) return;
+  const int64_t r = idx / nvec;
+  const int c = idx % nvec;
+  const int g = row_group(m, r);
+  float xv[8], yv[8], o[8];
+  bf16x8_to_float(reinterpret_cast<const bf16x8*>(x + r * sx)[c], xv);
+  bf16x8_to_float(reinterpret_cast<const bf16x8*>(y + r * sy)[c], yv);
+  const float* ar = m.a != nullptr ? m.a + (int64_t)g * m.a_sg : nullptr;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) o[e] = xv[e] + yv[e] * (m.a_add + (ar != nullptr ? ar[c * 8 + e] : 0.f));
+  reinterpret_cast<bf16x8*>(out + r * so)[c] = float_to_bf16x8(o);
+}
+
+// Gated-residual backward: dy = dout * gate[g], dgate[g] += sum_rows dout * y.
+template <int kMaxVec, int kTh>
+__global__ void __launch_bounds__(kTh)
+gate_res_bwd_kernel(const __nv_bfloat16* __restrict__ dout, int64_t sdo, const __nv_bfloat16* __restrict__ y, int64_t sy,
+                    __nv_bfloat16* __restrict__ dy, int64_t sdy, float* __restrict__ dgate, ModSpec m, int64_t R, int D,
+                    int rows_per_block) {
+  const int nvec = D >> 3;
+  const int64_t r0 = (int64_t)blockIdx.x * rows_per_block, r1 = min(R, r0 + rows_per_block);
+  float acc[kMaxVec][8];
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
+  int cur_g = -1;
+  auto flush = [&](int g) {
+    if (g < 0 || dgate == nullptr) return;
+#pragma unroll
+    for (int i = 0; i < kMaxVec; ++i) {
+      const int c = threadIdx.x + i * kTh;
+      if (c < nvec)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          atomicAdd(dgate + (int64_t)g * D + c * 8 + e, acc[i][e]);
+          acc[i][e] = 0.f;
+        }
+    }
+  };
+  for (int64_t r = r0; r < r1; ++r) {
+    const int g = row_group(m, r);
+    if (g != cur_g) {
+      flush(cur_g);
+      cur_g = g;
+    }
+    const float* ar = m.a + (int64_t)g * m.a_sg;
+#pragma unroll
+    for (int i = 0; i < kMaxVec; ++i) {
+      const int c = threadIdx.x + i * kTh;
+      if (c < nvec) {
+        float gv[8], yv[8], o[8];
+        bf16x8_to_float(reinterpret_cast<const bf16x8*>(dout + r * sdo)[c], gv);
+        bf16x8_to_float(reinterpret_cast<const bf16x8*>(y + r * sy)[c], yv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          o[e] = gv[e] * ar[c * 8 + e];
+          acc[i][e] += gv[e] * yv[e];
+        }
+        reinterpret_cast<bf16x8*>(dy + r * sdy)[c] = float_to_bf16x8(o);
+      }
+    }
+  }
+  flush(cur_g);
+}
+
+// ------------------------------------------------------------------ q/k RMSNorm + RoPE
+// src: q at column 0, k at column D of each row (row stride ss); writes q/k
+// into dst (row stride sd, q at 0, k at D).  cos/sin: [Lrope, hd/2] fp32,
+// row r uses table row (r % Lrope).  hd = head dim (128), heads = D / hd.
+template <int kMaxVec, int kTh>
+__global__ void __launch_bounds__(kTh)
+qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ src, int64_t ss, __nv_bfloat16* __restrict__ dst, int64_t sd,
+                        const float* __restrict__ wq, const float* __restrict__ wk, const float* __restrict__ cosT,
+                        const float* __restrict__ sinT, float* __restrict__ rstd_q, float* __restrict__ rstd_k,
+                        int64_t R, int D, int hd, int Lrope, float eps) {
+  __shared__ float red[32];
+  const int64_t r = blockIdx.x;
+  const int which = blockIdx.y;  // 0 = q, 1 = k
+  const int nvec = D >> 3;
+  const bf16x8* xr = reinterpret_cast<const bf16x8*>(src + r * ss + which * D);
+  const float* w = which == 0 ? wq : wk;
+  float v[kMaxVec][8];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = threadIdx.x + i * kTh;
+    if (c < nvec) {
+      bf16x8_to_float(xr[c], v[i]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s += v[i][e] * v[i][e];
+    }
+  }
+  const float rstd = rsqrtf(block_sum(s, red) / D + eps);
+  const int64_t tr = (r % Lrope) * (hd >> 1);
+  bf16x8* yr = reinterpret_cast<bf16x8*>(dst + r * sd + which * D);
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = threadIdx.x + i * kTh;
+    if (c < nvec) {
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const int col = c * 8 + e;
+        const float a0 = v[i][e] * rstd * w[col];
+        const float a1 = v[i][e + 1] * rstd * w[col + 1];
+        const int pi = (col % hd) >> 1;
+        const float cs = cosT[tr + pi], sn = sinT[tr + pi];
+        o[e] = a0 * cs - a1 * sn;
+        o[e + 1] = a1 * cs + a0 * sn;
+      }
+      yr[c] = float_to_bf16x8(o);
+    }
+  }
+  if (threadIdx.x == 0) (which == 0 ? rstd_q : rstd_k)[r] = rstd;
+}
+
+// Backward: g (grad of the rotated output, q at col 0 / k at col D, row stride sg)
+// -> dx (grad of the pre-norm input, row stride sdx); dw accumulates (fp32 [D]).
+template <int kMaxVec, int kTh>
+__global__ void __launch_bounds__(kTh)
+qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ gq, int64_t sgq, const __nv_bfloat16* __restrict__ gk,
+                        int64_t sgk, const __nv_bfloat16* __restrict__ src, int64_t ss, __nv_bfloat16* __restrict__ dx,
+                        int64_t sdx, const float* __restrict__ wq, const float* __restrict__ wk,
+                        const float* __restrict__ cosT, const float* __restrict__ sinT, const float* __restrict__ rstd_q,
+                        const float* __restrict__ rstd_k, float* __restrict__ dwq, float* __restrict__ dwk, int64_t R,
+                        int D, int hd, int Lrope, int rows_per_block) {
+  __shared__ float red[32];
+  const int which = blockIdx.y;
+  const int nvec = D >> 3;
+  const float* w = which == 0 ? wq : wk;
+  float* dw = which == 0 ? dwq : dwk;
+  const __nv_bfloat16* g = which == 0 ? gq : gk;
+  const int64_t sg = which == 0 ? sgq : sgk;
+  float accw[kMaxVec][8];
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) accw[i][e] = 0.f;
+  const int64_t r0 = (int64_t)blockIdx.x * rows_per_block, r1 = min(R, r0 + rows_per_block);
+  for (int64_t r = r0; r < r1; ++r) {
+    const float rstd = (which == 0 ? rstd_q : rstd_k)[r];
+    const int64_t tr = (r % Lrope) * (hd >> 1);
+    const bf16x8* xr = reinterpret_cast<const bf16x8*>(src + r * ss + which * D);
+    const bf16x8* gr = reinterpret_cast<const bf16x8*>(g + r * sg);
+    float n[kMaxVec][8], dn[kMaxVec][8];
+    float s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxVec; ++i) {
+      const int c = threadIdx.x + i * kTh;
+      if (c < nvec) {
+        float xv[8], gv[8];
+        bf16x8_to_float(xr[c], xv);
+        bf16x8_to_float(gr[c], gv);
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          const int col = c * 8 + e;
+          const int pi = (col % hd) >> 1;
+          const float cs = cosT[tr + pi], sn = sinT[tr + pi];
+          // inverse rotation of the output gradient
+          const float da0 = gv[e] * cs + gv[e + 1] * sn;
+          const float da1 = -gv[e] * sn + gv[e + 1] * cs;
+          n[i][e] = xv[e] * rstd;
+          n[i][e + 1] = xv[e + 1] * rstd;
+          accw[i][e] += da0 * n[i][e];
+          accw[i][e + 1] += da1 * n[i][e + 1];
+          dn[i][e] = da0 * w[col];
+          dn[i][e + 1] = da1 * w[col + 1];
+          s2 += dn[i][e] * n[i][e] + dn[i][e + 1] * n[i][e + 1];
+        }
+      }
+    }
+    const float mdnn = block_sum(s2, red) / D;
+    bf16x8* dxr = reinterpret_cast<bf16x8*>(dx + r * sdx + which * D);
+#pragma unroll
+    for (int i = 0; i < kMaxVec; ++i) {
+      const int c = threadIdx.x + i * kTh;
+      if (c < nvec) {
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = rstd * (dn[i][e] - n[i][e] * mdnn);
+        dxr[c] = float_to_bf16x8(o);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kMaxVec; ++i) {
+    const int c = threadIdx.x + i * kTh;
+    if (c < nvec)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) atomicAdd(dw + c * 8 + e, accw[i][e]);
+  }
+}
+
+// Standalone interleaved RoPE on [R, H, hd] rows (forward sign +1, backward -1).
+__global__ void rope_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx, __nv_bfloat16* __restrict__ y, int64_t sy,
+                            const float* __restrict__ cosT, const float* __restrict__ sinT, int64_t R, int D, int hd,
+                            int Lrope, float sign) {
+  const int nvec = D >> 3;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= R * nvec) return;
+  const int64_t r = idx / nvec;
+  const int c = idx % nvec;
+  const int64_t tr = (r % Lrope) * (hd >> 1);
+  float v[8], o[8];
+  bf16x8_to_float(reinterpret_cast<const bf16x8*>(x + r * sx)[c], v);
+#pragma unroll
+  for (int e = 0; e < 8; e += 2) {
+    const int pi = ((c * 8 + e) % hd) >> 1;
+    const float cs = cosT[tr + pi], sn = sign * sinT[tr + pi];
+    o[e] = v[e] * cs - v[e + 1] * sn;
+    o[e + 1] = v[e + 1] * cs + v[e] * sn;
+  }
+  reinterpret_cast<bf16x8*>(y + r * sy)[c] = float_to_bf16x8(o);
+}
+
+__global__ void gelu_fwd_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y, int64_t nvec) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nvec) return;
+  float v[8];
+  bf16x8_to_float(reinterpret_cast<const bf16x8*>(x)[i], v);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = gelu_tanh(v[e]);
+  reinterpret_cast<bf16x8*>(y)[i] = float_to_bf16x8(v);
+}
+
+__global__ void gelu_bwd_kernel(const __nv_bfloat16* __restrict__ g, const __nv_bfloat16* __restrict__ x,
+                                __nv_bfloat16* __restrict__ dx, int64_t nvec) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= nvec) return;
+  float gv[8], xv[8];
+  bf16x8_to_float(reinterpret_cast<const bf16x8*>(g)[i], gv);
+  bf16x8_to_float(reinterpret_cast<const bf16x8*>(x)[i], xv);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) gv[e] *= gelu_tanh_grad(xv[e]);
+  reinterpret_cast<bf16x8*>(dx)[i] = float_to_bf16x8(gv);
+}
+
+void check_rows(const at::Tensor& t, const char* name, int64_t D) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16, name, " must be CUDA bf16");
+  TORCH_CHECK(t.dim() == 2 && t.size(1) == D && t.stride(1) == 1, name, " must be [R, D] with contiguous rows");
+  TORCH_CHECK(t.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0, name,
+              " rows must be 16-byte aligned");
+}
+
+ModSpec make_mod(const c10::optional<at::Tensor>& a, const c10::optional<at::Tensor>& c, double a_add,
+                 int64_t rows_per_group, const c10::optional<at::Tensor>& gidx, int64_t D) {
+  ModSpec m;
+  m.a = nullptr;
+  m.c = nullptr;
+  m.a_sg = m.c_sg = 0;
+  if (a.has_value() && a->defined()) {
+    TORCH_CHECK(a->scalar_type() == at::kFloat && a->dim() == 2 && a->size(1) == D && a->stride(1) == 1,
+                "modulation A must be fp32 [G, D]");
+    m.a = a->data_ptr<float>();
+    m.a_sg = a->size(0) == 1 ? 0 : a->stride(0);
+  }
+  if (c.has_value() && c->defined()) {
+    TORCH_CHECK(c->scalar_type() == at::kFloat && c->dim() == 2 && c->size(1) == D && c->stride(1) == 1,
+                "modulation C must be fp32 [G, D]");
+    m.c = c->data_ptr<float>();
+    m.c_sg = c->size(0) == 1 ? 0 : c->stride(0);
+  }
+  m.a_add = (float)a_add;
+  m.rows_per_group = (int)std::max<int64_t>(1, rows_per_group);
+  m.gidx = nullptr;
+  if (gidx.has_value() && gidx->defined()) {
+    TORCH_CHECK(gidx->scalar_type() == at::kInt && gidx->is_contiguous(), "group index must be int32");
+    m.gidx = gidx->data_ptr<int>();
+  }
+  return m;
+}
+
+}  // namespace
+
+void ln_mod_fwd(const at::Tensor& x, at::Tensor& y, c10::optional<at::Tensor> mean, at::Tensor& rstd,
+                c10::optional<at::Tensor> a, c10::optional<at::Tensor> c, double a_add, int64_t rows_per_group,
+                c10::optional<at::Tensor> gidx, double eps, bool rms) {
+  const int64_t D = x.size(1), R = x.size(0);
+  TORCH_CHECK(D % 8 == 0 && D <= 8192, "ln_mod: D must be a multiple of 8 and <= 8192");
+  check_rows(x, "x", D);
+  check_rows(y, "y", D);
+  c10::cuda::CUDAGuard guard(x.device());
+  ModSpec m = make_mod(a, c, a_add, rows_per_group, gidx, D);
+  float* mp = (mean.has_value() && mean->defined()) ? mean->data_ptr<float>() : nullptr;
+  TORCH_CHECK(rms || mp != nullptr, "LayerNorm needs a mean buffer");
+  if (R == 0) return;
+  DMAD_ROW_DISPATCH(D / 8, [&] {
+    ln_mod_fwd_kernel<VEC, TH><<<(unsigned)R, TH, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+        reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), y.stride(0), mp, rstd.data_ptr<float>(), m, R, (int)D,
+        (float)eps, rms);
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void ln_mod_bwd(const at::Tensor& dy, const at::Tensor& x, c10::optional<at::Tensor> mean, const at::Tensor& rstd,
+                c10::optional<at::Tensor> a, double a_add, int64_t rows_per_group, c10::optional<at::Tensor> gidx,
+                bool rms, at::Tensor& dx, c10::optional<at::Tensor> dres, c10::optional<at::Tensor> da,
+                c10::optional<at::Tensor> dc, c10::optional<at::Tensor> gate, c10::optional<at::Tensor> yg,
+                c10::optional<at::Tensor> dyg, c10::optional<at::Tensor> dgate) {
+  const int64_t D = x.size(1), R = x.size(0);
+  check_rows(dy, "dy", D);
+  check_rows(x, "x", D);
+  check_rows(dx, "dx", D);
+  c10::cuda::CUDAGuard guard(x.device());
+  ModSpec m = make_mod(a, c10::nullopt, a_add, rows_per_group, gidx, D);
+  LnBwdArgs p{};
+  p.dy = reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr());
+  p.sdy = dy.stride(0);
+  p.x = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  p.sx = x.stride(0);
+  p.mean = (mean.has_value() && mean->defined()) ? mean->data_ptr<float>() : nullptr;
+  p.rstd = rstd.data_ptr<float>();
+  p.dx = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr());
+  p.sdx = dx.stride(0);
+  if (dres.has_value() && dres->defined()) {
+    check_rows(*dres, "dres", D);
+    p.dres = reinterpret_cast<const __nv_bfloat16*>(dres->data_ptr());
+    p.sdres = dres->stride(0);
+  }
+  auto acc_ptr = [&](const c10::optional<at::Tensor>& t) -> float* {
+    if (!(t.has_value() && t->defined())) return nullptr;
+    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->size(-1) == D, "accumulator must be fp32 [G, D]");
+    return t->data_ptr<float>();
+  };
+  p.da = acc_ptr(da);
+  p.dc = acc_ptr(dc);
+  if (gate.has_value() && gate->defined()) {
+    TORCH_CHECK(gate->scalar_type() == at::kFloat && gate->stride(1) == 1, "gate must be fp32 [G, D]");
+    p.gate = gate->data_ptr<float>();
+    p.gate_sg = gate->size(0) == 1 ? 0 : gate->stride(0);
+    TORCH_CHECK(yg.has_value() && dyg.has_value() && dgate.has_value(), "gate fusion needs yg, dyg, dgate");
+    check_rows(*yg, "yg", D);
+    check_rows(*dyg, "dyg", D);
+    p.yg = reinterpret_cast<const __nv_bfloat16*>(yg->data_ptr());
+    p.syg = yg->stride(0);
+    p.dyg = reinterpret_cast<__nv_bfloat16*>(dyg->data_ptr());
+    p.sdyg = dyg->stride(0);
+    p.dgate = acc_ptr(dgate);
+  }
+  p.R = R;
+  p.D = (int)D;
+  p.rms = rms;
+  p.rows_per_block = 32;
+  if (R == 0) return;
+  const unsigned blocks = (unsigned)((R + p.rows_per_block - 1) / p.rows_per_block);
+  DMAD_ROW_DISPATCH(D / 8, [&] { ln_mod_bwd_kernel<VEC, TH><<<blocks, TH, 0, at::cuda::getCurrentCUDAStream()>>>(p, m); });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gate_res_fwd(const at::Tensor& x, const at::Tensor& y, at::Tensor& out, c10::optional<at::Tensor> gate,
+                  int64_t rows_per_group, c10::optional<at::Tensor> gidx) {
+  const int64_t D = x.size(1), R = x.size(0);
+  check_rows(x, "x", D);
+  check_rows(y, "y", D);
+  check_rows(out, "out", D);
+  c10::cuda::CUDAGuard guard(x.device());
+  const bool has_gate = gate.has_value() && gate->defined();
+  ModSpec m = make_mod(gate, c10::nullopt, has_gate ? 0.0 : 1.0, rows_per_group, gidx, D);
+  const int64_t n = R * (D / 8);
+  if (n == 0) return;
+  gate_res_fwd_kernel<<<(unsigned)((n + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+      reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), y.stride(0),
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), m, R, (int)D);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gate_res_bwd(const at::Tensor& dout, const at::Tensor& y, at::Tensor& dy, const at::Tensor& gate,
+                  at::Tensor& dgate, int64_t rows_per_group, c10::optional<at::Tensor> gidx) {
+  const int64_t D = y.size(1), R = y.size(0);
+  check_rows(dout, "dout", D);
+  check_rows(y, "y", D);
+  check_rows(dy, "dy", D);
+  TORCH_CHECK(dgate.scalar_type() == at::kFloat && dgate.is_contiguous() && dgate.size(-1) == D, "dgate fp32 [G, D]");
+  c10::cuda::CUDAGuard guard(y.device());
+  ModSpec m = make_mod(gate, c10::nullopt, 0.0, rows_per_group, gidx, D);
+  if (R == 0) return;
+  const int rpb = 32;
+  const unsigned blocks = (unsigned)((R + rpb - 1) / rpb);
+  DMAD_ROW_DISPATCH(D / 8, [&] {
+    gate_res_bwd_kernel<VEC, TH><<<blocks, TH, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0),
+        reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), y.stride(0),
+        reinterpret_cast<__nv_bfloat16*>(dy.data_ptr()), dy.stride(0), dgate.data_ptr<float>(), m, R, (int)D, rpb);
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void qk_norm_rope_fwd(const at::Tensor& src, at::Tensor& dst, const at::Tensor& wq, const at::Tensor& wk,
+                      const at::Tensor& cosT, const at::Tensor& sinT, at::Tensor& rstd_q, at::Tensor& rstd_k,
+                      int64_t D, int64_t hd, double eps) {
+  TORCH_CHECK(src.dim() == 2 && src.size(1) >= 2 * D && src.stride(1) == 1, "src must be [R, >=2D]");
+  TORCH_CHECK(dst.dim() == 2 && dst.size(1) >= 2 * D && dst.stride(1) == 1, "dst must be [R, >=2D]");
+  TORCH_CHECK(src.stride(0) % 8 == 0 && dst.stride(0) % 8 == 0 && D % 8 == 0 && D <= 8192 && D % hd == 0, "bad layout");
+  TORCH_CHECK(wq.scalar_type() == at::kFloat && wk.scalar_type() == at::kFloat, "norm weights must be fp32");
+  TORCH_CHECK(cosT.is_contiguous() && sinT.is_contiguous() && cosT.size(1) == hd / 2, "rope tables must be [L, hd/2]");
+  const int64_t R = src.size(0);
+  if (R == 0) return;
+  c10::cuda::CUDAGuard guard(src.device());
+  dim3 grid((unsigned)R, 2);
+  DMAD_ROW_DISPATCH(D / 8, [&] {
+    qk_norm_rope_fwd_kernel<VEC, TH><<<grid, TH, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), src.stride(0),
+        reinterpret_cast<__nv_bfloat16*>(dst.data_ptr()), dst.stride(0), wq.data_ptr<float>(), wk.data_ptr<float>(),
+        cosT.data_ptr<float>(), sinT.data_ptr<float>(), rstd_q.data_ptr<float>(), rstd_k.data_ptr<float>(), R,
+        (int)D, (int)hd, (int)cosT.size(0), (float)eps);
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void qk_norm_rope_bwd(const at::Tensor& gq, const at::Tensor& gk, const at::Tensor& src, at::Tensor& dx,
+                      const at::Tensor& wq, const at::Tensor& wk, const at::Tensor& cosT, const at::Tensor& sinT,
+                      const at::Tensor& rstd_q, const at::Tensor& rstd_k, at::Tensor& dwq, at::Tensor& dwk, int64_t D,
+                      int64_t hd) {
+  TORCH_CHECK(gq.stride(-1) == 1 && gk.stride(-1) == 1 && dx.stride(1) == 1, "contiguous rows required");
+  const int64_t R = src.size(0);
+  if (R == 0) return;
+  c10::cuda::CUDAGuard guard(src.device());
+  const int rpb = 32;
+  dim3 grid((unsigned)((R + rpb - 1) / rpb), 2);
+  DMAD_ROW_DISPATCH(D / 8, [&] {
+    qk_norm_rope_bwd_kernel<VEC, TH><<<grid, TH, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const __nv_bfloat16*>(gq.data_ptr()), gq.stride(0),
+        reinterpret_cast<const __nv_bfloat16*>(gk.data_ptr()), gk.stride(0),
+        reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), src.stride(0),
+        reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), dx.stride(0), wq.data_ptr<float>(), wk.data_ptr<float>(),
+        cosT.data_ptr<float>(), sinT.data_ptr<float>(), rstd_q.data_ptr<float>(), rstd_k.data_ptr<float>(),
+        dwq.data_ptr<float>(), dwk.data_ptr<float>(), R, (int)D, (int)hd, (int)cosT.size(0), rpb);
+  });
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void rope_apply(const at::Tensor& x, at::Tensor& y, const at::Tensor& cosT, const at::Tensor& sinT, int64_t hd,
+                bool inverse) {
+  const int64_t R = x.size(0), D = x.size(1);
+  check_rows(x, "x", D);
+  check_rows(y, "y", D);
+  const int64_t n = R * (D / 8);
+  if (n == 0) return;
+  c10::cuda::CUDAGuard guard(x.device());
+  rope_kernel<<<(unsigned)((n + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()),
+      y.stride(0), cosT.data_ptr<float>(), sinT.data_ptr<float>(), R, (int)D, (int)hd, (int)cosT.size(0),
+      inverse ? -1.f : 1.f);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gelu_fwd(const at::Tensor& x, at::Tensor& y) {
+  TORCH_CHECK(x.is_contiguous() && y.is_contiguous() && x.numel() % 8 == 0, "gelu: contiguous, numel % 8 == 0");
+  const int64_t n = x.numel() / 8;
+  if (n == 0) return;
+  c10::cuda::CUDAGuard guard(x.device());
+  gelu_fwd_kernel<<<(unsigned)((n + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), n);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gelu_bwd(const at::Tensor& g, const at::Tensor& x, at::Tensor& dx) {
+  TORCH_CHECK(g.is_contiguous() && x.is_contiguous() && dx.is_contiguous() && x.numel() % 8 == 0, "gelu_bwd layout");
+  const int64_t n = x.numel() / 8;
+  if (n == 0) return;
+  c10::cuda::CUDAGuard guard(x.device());
+  gelu_bwd_kernel<<<(unsigned)((n + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+      reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), n);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace dmad

@@ -1,0 +1,314 @@
+"""DMAD distillation of a Wan2.1-shaped DiT (rCM's distillation model with the DMD term
+replaced by the two-head critic; no sCM loss).
+
+Parity with train/wan/rcm/models/t2v_model_distill_dmad.py and the rCM base class
+(train/wan/rcm/models/t2v_model_distill_rcm.py):
+* nets: student ``net`` (few-step generator), critic backbone ``net_fake_score`` (a copy of the
+  teacher) with ``CriticHeads`` on the token output of its last block, fp32 power-EMA of the student;
+* G / Q / T share one TrigFlow time drawn from p_D per sample, with independent noise
+  (``_noise_with_D_time``, dmad :344-352);
+* student step: backward simulation with 1..4 student evaluations (only the last carries grad,
+  rcm :514-542), critic frozen, loss ``-d_real(G) - w_gap d_teacher(G)`` (dmad :399-426);
+* critic step: no-grad backward simulation, three critic forwards, softplus BCE, all-reduced gap
+  EMA over CDF-decile bands of p_D (dmad :437-469, :356-395);
+* generator and critic alternate 1:1 (``student_update_freq=2``, rcm :297-311);
+* frozen-gain spectral norm on every critic block Linear and head, and on the first half of the
+  generator's blocks (dmad :488-517);
+* few-step sampler ``x <- cos(t') x0 + sin(t') eps`` from t = atan(sigma_max) (rcm :830-895).
+
+The critic's three forwards are run forward+backward one at a time (the gradient of the summed
+BCE is identical), so activations of only one forward are alive at once.
+"""
+from __future__ import annotations
+
+import copy
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn as nn
+
+from ..algorithms import (CriticHeads, GapRouter, TrigFlowScaling, UniformShift, LogNormal, critic_bce_loss,
+                          ema_exp_coefficient, generator_linear_loss, rf_to_trig_time, trig_to_rf_time)
+from ..algorithms.dmad import band_of_cdf, critic_accuracies
+from ..models.wan import WanConfig, WanModel, WAN_1P3B
+from ..ops.optim import FusedAdamW, clip_grad_scale
+from ..parallel.dist import broadcast_module
+from ..parallel.dp import GradSync
+
+
+@dataclass
+class WanDMADConfig:
+    net: WanConfig = field(default_factory=lambda: WanConfig(**WAN_1P3B.__dict__))
+    sigma_max: float = 80.0
+    p_D_shift: float = 5.0          # p_D = UniformShift(5) (rcm 1.3B experiment)
+    p_D_lognormal: tuple | None = None  # (mean, std) to use LogNormal instead
+    max_simulation_steps_fake: int = 4
+    student_update_freq: int = 2
+    backward_timesteps: tuple = (1.5, 1.4, 1.0)
+    dmd_fix_timesteps: bool = False
+    loss_scale_dmd: float = 1.0
+    critic_spectral_norm: bool = True
+    generator_spectral_norm: bool = True
+    sn_generator_frac: float = 0.5
+    sn_power_iters: int = 30
+    gap_route: bool = True
+    gap_tau: float = 2.0
+    gap_ema_beta: float = 0.99
+    lr: float = 2e-6
+    critic_lr: float = 2e-6
+    betas: tuple = (0.0, 0.99)
+    weight_decay: float = 0.01
+    eps: float = 1e-8
+    ema_enabled: bool = True
+    ema_rate: float = 0.1
+    grad_clip: float | None = None
+    student_lora_rank: int = 0
+    checkpoint_student_blocks: int = 0
+    checkpoint_critic_blocks: int = 0
+    checkpoint_critic_blocks_student_phase: int | None = None
+    rectified_flow_t_scaling_factor: float = 1000.0
+
+
+class WanDMAD(nn.Module):
+    def __init__(self, cfg: WanDMADConfig, device=None, dtype=torch.bfloat16, seed: int = 0):
+        super().__init__()
+        self.cfg = cfg
+        self.dtype = dtype
+        device = torch.device(device) if device is not None else torch.device("cpu")
+        torch.manual_seed(seed)
+        teacher = WanModel(cfg.net)
+        # student and critic backbone both start from the teacher weights (rcm :247-251)
+        self.net = teacher
+        self.net_fake_score = copy.deepcopy(teacher)
+        self.critic_heads = CriticHeads(cfg.net.dim)
+        if cfg.critic_spectral_norm:
+            self.net_fake_score.enable_spectral_norm(range(cfg.net.num_layers), cfg.sn_power_iters)
+            for head in (self.critic_heads.real, self.critic_heads.teacher):
+                for i, m in enumerate(head):
+                    if isinstance(m, nn.Linear):
+                        _sn_wrap_torch_linear(m, cfg.sn_power_iters)
+        if cfg.generator_spectral_norm:
+            nb = math.ceil(cfg.net.num_layers * cfg.sn_generator_frac)
+            self.net.enable_spectral_norm(range(nb), cfg.sn_power_iters)
+        if cfg.student_lora_rank:
+            self.net.enable_lora(cfg.student_lora_rank)
+        self.net.to(device=device, dtype=dtype)
+        self.net_fake_score.to(device=device, dtype=dtype)
+        self.critic_heads.to(device=device, dtype=torch.float32)
+        self.net.checkpoint_blocks = cfg.checkpoint_student_blocks
+        self.net_fake_score.checkpoint_blocks = cfg.checkpoint_critic_blocks
+        broadcast_module(self.net)
+        broadcast_module(self.net_fake_score)
+        broadcast_module(self.critic_heads)
+        self.gap = GapRouter("allreduce", tau=cfg.gap_tau, beta=cfg.gap_ema_beta, enabled=cfg.gap_route).to(device)
+        self.scaling = TrigFlowScaling(1.0, cfg.rectified_flow_t_scaling_factor)
+        self.p_D = LogNormal(*cfg.p_D_lognormal) if cfg.p_D_lognormal else UniformShift(cfg.p_D_shift)
+        self.device = device
+        # optimisers; the student's optimiser also advances the fp32 EMA copy in the same kernel pass
+        s_params = [p for p in self.net.parameters() if p.requires_grad]
+        self.ema_params = [p.detach().float().clone() for p in s_params] if cfg.ema_enabled else None
+        self.ema_coef = ema_exp_coefficient(cfg.ema_rate)
+        self.opt_student = FusedAdamW(s_params, lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
+                                      weight_decay=cfg.weight_decay, ema=self.ema_params)
+        c_params = [p for p in self.net_fake_score.parameters() if p.requires_grad] + list(self.critic_heads.parameters())
+        self.opt_critic = FusedAdamW(c_params, lr=cfg.critic_lr, betas=cfg.betas, eps=cfg.eps,
+                                     weight_decay=cfg.weight_decay)
+        self.sync_student = GradSync(s_params)
+        self.sync_critic = GradSync(c_params)
+
+    # ------------------------------------------------------------------ schedule (rcm :297-311)
+    def is_student_phase(self, it: int) -> bool:
+        return it % self.cfg.student_update_freq == 0
+
+    def effective_iteration(self, it: int) -> int:
+        return it // self.cfg.student_update_freq
+
+    def effective_iteration_fake(self, it: int) -> int:
+        return it - self.effective_iteration(it) - 1
+
+    def ema_beta(self, it: int) -> float:
+        if it < 1:
+            return 0.0
+        return (1 - 1 / (it + 1)) ** (self.ema_coef + 1)
+
+    # ------------------------------------------------------------------ time draws
+    def draw_time_D(self, n: int):
+        rf = self.p_D((n, 1), device=self.device, dtype=torch.float64).clamp(0.0, 1.0)
+        return rf_to_trig_time(rf)
+
+    def gap_band(self, t_trig):
+        return band_of_cdf(self.p_D.cdf_rf(trig_to_rf_time(t_trig.reshape(-1).to(torch.float64))))
+
+    # ------------------------------------------------------------------ denoiser
+    def _net_timesteps(self, c_noise):
+        # the reference hands the network bf16 timesteps (rcm :438-441)
+        return c_noise.to(self.dtype).float()
+
+    def denoise(self, net, xt, t_B_1, context):
+        """x0 prediction of ``net`` at TrigFlow time t (uniform per sample)."""
+        t5 = t_B_1.reshape(-1, 1, 1, 1, 1).to(torch.float64)
+        c_skip, c_out, c_in, c_noise = self.scaling(t5)
+        out = net((xt * c_in).to(self.dtype), self._net_timesteps(c_noise.reshape(-1, 1)), context).float()
+        return (c_skip * xt + c_out * out).float()
+
+    def critic_forward(self, xt, t_B_1, context, need_x0=False):
+        """(x0 or None, d_real [B], d_teacher [B]) from the critic backbone's last-block tokens."""
+        net = self.net_fake_score
+        t5 = t_B_1.reshape(-1, 1, 1, 1, 1).to(torch.float64)
+        c_skip, c_out, c_in, c_noise = self.scaling(t5)
+        xin = (xt * c_in).to(self.dtype)
+        ts = self._net_timesteps(c_noise.reshape(-1, 1))
+        if need_x0:
+            out, feats = net(xin, ts, context, feature_hook_block=-1)
+            x0 = (c_skip * xt + c_out * out.float()).float()
+        else:
+            feats = net(xin, ts, context, stop_after_block=len(net.blocks) - 1)
+            x0 = None
+        d_real, d_teacher = self.critic_heads.pooled(feats)
+        return x0, d_real, d_teacher
+
+    # ------------------------------------------------------------------ backward simulation (rcm :514-542)
+    def backward_simulation(self, context, shape, n_steps: int, with_grad: bool):
+        B = shape[0]
+        t = torch.full((B, 1), math.pi / 2, device=self.device, dtype=torch.float64)
+        x = torch.randn(shape, device=self.device)
+        traj = [t]
+        for i in range(n_steps - 1):
+            if self.cfg.dmd_fix_timesteps:
+                t = torch.full((B, 1), self.cfg.backward_timesteps[i], device=self.device, dtype=torch.float64)
+            else:
+                t = torch.minimum(self.draw_time_D(B), t)
+            traj.append(t)
+        traj.append(torch.zeros_like(t))
+        for step, (tc, tn) in enumerate(zip(traj[:-1], traj[1:])):
+            grad_on = with_grad and step == n_steps - 1
+            with torch.set_grad_enabled(grad_on):
+                x = self.denoise(self.net, x, tc, context)
+            if step < n_steps - 1:
+                tn5 = tn.reshape(-1, 1, 1, 1, 1)
+                x = torch.cos(tn5) * x + torch.sin(tn5) * torch.randn_like(x)
+                x = x.float()
+        return x
+
+    def _noise(self, x0, t_B_1):
+        eps = torch.randn(x0.shape, device=self.device)
+        t5 = t_B_1.reshape(-1, 1, 1, 1, 1)
+        return (torch.cos(t5) * x0 + torch.sin(t5) * eps).float()
+
+    # ------------------------------------------------------------------ steps
+    def _set_critic_grad(self, on: bool):
+        for p in self.opt_critic.params:
+            p.requires_grad_(on)
+
+    def student_step(self, batch, it: int) -> dict:
+        cfg = self.cfg
+        ctx = batch["context"]
+        shape = batch["latents"].shape
+        n_sim = self.effective_iteration(it) % cfg.max_simulation_steps_fake + 1
+        self.net.train()
+        ckpt_stu_phase = cfg.checkpoint_critic_blocks_student_phase
+        saved = self.net_fake_score.checkpoint_blocks
+        if ckpt_stu_phase is not None:
+            self.net_fake_score.checkpoint_blocks = ckpt_stu_phase
+        G_x0 = self.backward_simulation(ctx, shape, n_sim, with_grad=True)
+        D_time = self.draw_time_D(shape[0])
+        xt_G = self._noise(G_x0, D_time)
+        self._set_critic_grad(False)
+        try:
+            _, d_real_G, d_teacher_G = self.critic_forward(xt_G, D_time, ctx)
+            w, E_w = self.gap.weights(self.gap_band(D_time))
+            loss = cfg.loss_scale_dmd * generator_linear_loss(d_real_G, d_teacher_G, w, E_w)
+            loss.sum().backward()
+        finally:
+            self._set_critic_grad(True)
+            self.net_fake_score.checkpoint_blocks = saved
+        self.sync_student.sync()
+        scale = clip_grad_scale(self.opt_student.params, cfg.grad_clip) if cfg.grad_clip else None
+        beta = self.ema_beta(self.effective_iteration(it)) if cfg.ema_enabled else None
+        self.opt_student.step(grad_scale=scale, ema_beta=beta)
+        self.opt_student.zero_grad()
+        out = {"dmad_g_loss": loss.detach().mean(), "dmad_g_d_real": d_real_G.detach().mean(),
+               "dmad_g_d_teacher": d_teacher_G.detach().mean(), "n_sim": n_sim}
+        if w is not None:
+            out["dmad_gap_w_mean"] = w.mean()
+            out["dmad_gap_w_norm"] = E_w
+        return out
+
+    def critic_step(self, batch, it: int) -> dict:
+        cfg = self.cfg
+        ctx = batch["context"]
+        x0_Q = batch["latents"]
+        x0_T = batch["real_latents"]
+        shape = x0_Q.shape
+        n_sim = self.effective_iteration_fake(it) % cfg.max_simulation_steps_fake + 1
+        self.net_fake_score.train()
+        with torch.no_grad():
+            G_x0 = self.backward_simulation(ctx, shape, n_sim, with_grad=False)
+        D_time = self.draw_time_D(shape[0])
+        xt_G = self._noise(G_x0, D_time)
+        _, d_real_G, d_teacher_G = self.critic_forward(xt_G, D_time, ctx)
+        (torch.nn.functional.softplus(d_teacher_G) + torch.nn.functional.softplus(d_real_G)).sum().backward()
+        xt_Q = self._noise(x0_Q, D_time)
+        _, d_real_Q, d_teacher_Q = self.critic_forward(xt_Q, D_time, ctx)
+        torch.nn.functional.softplus(-d_teacher_Q).sum().backward()
+        xt_T = self._noise(x0_T, D_time)
+        _, d_real_T, _ = self.critic_forward(xt_T, D_time, ctx)
+        torch.nn.functional.softplus(-d_real_T).sum().backward()
+        bce = critic_bce_loss(d_real_T.detach(), d_real_G.detach(), d_teacher_Q.detach(), d_teacher_G.detach())
+        self.gap.update(d_real_T.detach(), d_real_Q.detach(), self.gap_band(D_time), self.gap_band(D_time))
+        self.sync_critic.sync()
+        scale = clip_grad_scale(self.opt_critic.params, cfg.grad_clip) if cfg.grad_clip else None
+        self.opt_critic.step(grad_scale=scale)
+        self.opt_critic.zero_grad()
+        out = {"dmad_d_loss": bce.mean(), "n_sim": n_sim}
+        out.update(critic_accuracies(d_real_T, d_real_G, d_teacher_Q, d_teacher_G))
+        return out
+
+    def training_step(self, batch, it: int) -> dict:
+        return self.student_step(batch, it) if self.is_student_phase(it) else self.critic_step(batch, it)
+
+    # ------------------------------------------------------------------ sampling (rcm :830-895)
+    @torch.no_grad()
+    def generate(self, context, shape, num_steps: int = 4, mid_t=None, generator=None, use_ema=False):
+        cfg = self.cfg
+        mid_t = list(mid_t) if mid_t is not None else list(cfg.backward_timesteps[: num_steps - 1])
+        t_steps = [math.atan(cfg.sigma_max)] + mid_t + [0.0]
+        was = self.net.training
+        self.net.eval()
+        x = torch.randn(shape, device=self.device, generator=generator, dtype=torch.float32)
+        B = shape[0]
+        for tc, tn in zip(t_steps[:-1], t_steps[1:]):
+            x0 = self.denoise(self.net, x, torch.full((B, 1), tc, device=self.device, dtype=torch.float64), context)
+            x = math.cos(tn) * x0 + math.sin(tn) * torch.randn(shape, device=self.device, generator=generator)
+        self.net.train(was)
+        return torch.nan_to_num(x.float())
+
+
+def _sn_wrap_torch_linear(lin: nn.Linear, power_iters: int):
+    """Frozen-gain spectral norm on a plain nn.Linear (the critic heads), via torch parametrizations
+    exactly as the reference registers it (t2v_model_distill_dmad.py:488-507)."""
+    from torch.nn.utils import parametrize
+    from torch.nn.utils.parametrizations import spectral_norm
+
+    w = lin.weight
+    if float(torch.linalg.matrix_norm(w.detach().float(), ord=2)) < 1e-8:
+        return 0
+    w_orig = w.detach().clone()
+    spectral_norm(lin, name="weight", n_power_iterations=1)
+    with torch.no_grad():
+        for _ in range(power_iters):
+            _ = lin.weight
+        wn = lin.weight.detach()
+        gain = (w_orig.flatten().float() @ wn.flatten().float()) / (wn.flatten().float() @ wn.flatten().float())
+
+    class _Gain(nn.Module):
+        def __init__(self, g):
+            super().__init__()
+            self.register_buffer("gain", g)
+
+        def forward(self, x):
+            return x * self.gain
+
+    parametrize.register_parametrization(lin, "weight", _Gain(gain.to(w_orig.dtype)))
+    return 1

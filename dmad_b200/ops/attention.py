@@ -1,0 +1,65 @@
+"""Flash attention (forward + backward) on the sm_100a tcgen05 kernels.
+
+Parity: ``attention(q, k, v)`` of the reference (train/wan/rcm/utils/attention.py:120-167),
+layout ``[B, L, H, D]`` in and out, softmax scale ``1/sqrt(D)`` by default.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import ext
+
+
+def attention_reference(q, k, v, scale=None):
+    """fp32 math of softmax(q k^T * scale) v on [B, L, H, D] tensors (oracle / CPU path)."""
+    scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    qf, kf, vf = (t.float().transpose(1, 2) for t in (q, k, v))
+    s = torch.matmul(qf, kf.transpose(-1, -2)) * scale
+    p = torch.softmax(s, dim=-1)
+    return torch.matmul(p, vf).transpose(1, 2).to(q.dtype)
+
+
+def _lse_pad(L: int) -> int:
+    return (L + 255) // 256 * 256
+
+
+class _FlashAttn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, scale):
+        B, Lq, H, D = q.shape
+        o = torch.empty((B, Lq, H, D), dtype=q.dtype, device=q.device)
+        lse = torch.empty((B, H, _lse_pad(Lq)), dtype=torch.float32, device=q.device)
+        ext().flash_fwd(q, k, v, o, lse, float(scale))
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.scale = scale
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse = ctx.saved_tensors
+        do = do.contiguous() if do.stride(-1) != 1 or do.stride(1) % 8 else do
+        dq = torch.empty_like(q, memory_format=torch.contiguous_format)
+        dk = torch.empty(k.shape, dtype=k.dtype, device=k.device)
+        dv = torch.empty(v.shape, dtype=v.dtype, device=v.device)
+        dd = torch.empty_like(lse)
+        ext().flash_bwd(q, k, v, o, do, lse, dq, dk, dv, dd, float(ctx.scale))
+        return dq, dk, dv, None
+
+
+def _supported(q, k, v) -> bool:
+    return q.is_cuda and q.shape[-1] == 128 and q.dtype == torch.bfloat16 and k.dtype == q.dtype and v.dtype == q.dtype
+
+
+def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float | None = None) -> torch.Tensor:
+    """softmax(q k^T * scale) v for [B, L, H, 128] bf16 tensors (strided views allowed).
+
+    CUDA: sm_100a tcgen05 forward/backward kernels.  CPU: fp32 PyTorch math.
+    """
+    scale = float(scale) if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    if not q.is_cuda:
+        return attention_reference(q, k, v, scale)
+    if not _supported(q, k, v):
+        raise ValueError(f"flash_attention: need CUDA bf16 [B, L, H, 128], got {tuple(q.shape)} {q.dtype}")
+    return _FlashAttn.apply(q, k, v, scale)
