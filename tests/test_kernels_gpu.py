@@ -108,7 +108,8 @@ def test_gate_residual():
     out = gate_residual(x, y, gt, rows_per_group=R // G)
     g = torch.arange(R, device=dev) // (R // G)
     ref = x.float() + y.float() * gt[g]
-    assert (out.float() - ref).abs().max().item() < 3e-2
+    # one bf16 rounding of the output: relative error <= 2^-8
+    assert ((out.float() - ref).abs() / ref.abs().clamp_min(1.0)).max().item() < 8e-3
     go = torch.randn_like(out)
     out.backward(go)
     assert torch.allclose(x.grad.float(), go.float())
