@@ -1,0 +1,94 @@
+"""Kernel microbenchmarks: the sm_100a flash-attention forward/backward against PyTorch's
+cuDNN SDPA (the reference's attention backend on cc 10.0) at Wan shapes.
+
+    python -m benchmarks.bench_kernels --L 32760 --H 12 --B 1          # timing (CUDA events)
+    python -m benchmarks.bench_kernels --L 4096 --H 4 --iters 1 --warmup 1 --only fwd   # small case for ncu
+
+Prints one JSON line per op: ms, achieved TFLOP/s and the fraction of the measured
+cuBLAS bf16 peak (MEASURED_PEAKS.json when present).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+
+
+def peak_tflops():
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    try:
+        return float(json.load(open(p))["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def timeit(fn, iters, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    e.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--B", type=int, default=1)
+    ap.add_argument("--L", type=int, default=32760)
+    ap.add_argument("--Lk", type=int, default=None)
+    ap.add_argument("--H", type=int, default=12)
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--only", default="all", choices=["all", "fwd", "bwd", "sdpa"])
+    a = ap.parse_args()
+    from dmad_b200 import ops
+
+    e = ops.ext()
+    B, L, H = a.B, a.L, a.H
+    Lk = a.Lk or L
+    torch.manual_seed(0)
+    q = torch.randn(B, L, H, 128, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(B, Lk, H, 128, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(B, Lk, H, 128, device="cuda", dtype=torch.bfloat16)
+    do = torch.randn_like(q)
+    o = torch.empty_like(q)
+    lse = torch.empty(B, H, e.flash_lse_pad(L), device="cuda")
+    scale = 1 / math.sqrt(128)
+    fl_fwd = 4.0 * B * H * L * Lk * 128
+    peak, src = peak_tflops()
+    res = []
+    if a.only in ("all", "fwd"):
+        ms = timeit(lambda: e.flash_fwd(q, k, v, o, lse, scale), a.iters, a.warmup)
+        res.append(("flash_fwd_sm100", ms, fl_fwd))
+    if a.only in ("all", "bwd"):
+        e.flash_fwd(q, k, v, o, lse, scale)
+        dq, dk, dv, dd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(lse)
+        ms = timeit(lambda: e.flash_bwd(q, k, v, o, do, lse, dq, dk, dv, dd, scale), a.iters, a.warmup)
+        res.append(("flash_bwd_sm100", ms, 2.5 * fl_fwd))
+    if a.only in ("all", "sdpa"):
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+
+        qt, kt, vt = (t.transpose(1, 2) for t in (q, k, v))
+        with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+            ms = timeit(lambda: torch.nn.functional.scaled_dot_product_attention(qt, kt, vt), a.iters, a.warmup)
+            res.append(("cudnn_sdpa_fwd", ms, fl_fwd))
+            qg, kg, vg = (t.detach().requires_grad_(True) for t in (qt, kt, vt))
+            out = torch.nn.functional.scaled_dot_product_attention(qg, kg, vg)
+            gt = do.transpose(1, 2)
+            ms = timeit(lambda: torch.autograd.grad(out, (qg, kg, vg), gt, retain_graph=True), a.iters, a.warmup)
+            res.append(("cudnn_sdpa_bwd", ms, 2.5 * fl_fwd))
+    for name, ms, fl in res:
+        tf = fl / (ms * 1e-3) / 1e12
+        print(json.dumps({"op": name, "B": B, "L": L, "Lk": Lk, "H": H, "ms": round(ms, 4), "tflops": round(tf, 1),
+                          f"frac_of_{src}_bf16_peak": round(tf / peak, 3)}))
+
+
+if __name__ == "__main__":
+    main()

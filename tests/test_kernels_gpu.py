@@ -113,7 +113,8 @@ def test_gate_residual():
     go = torch.randn_like(out)
     out.backward(go)
     assert torch.allclose(x.grad.float(), go.float())
-    assert (y.grad.float() - go.float() * gt[g].detach()).abs().max().item() < 3e-2
+    dy_ref = go.float() * gt[g].detach()
+    assert ((y.grad.float() - dy_ref).abs() / dy_ref.abs().clamp_min(1.0)).max().item() < 8e-3
     ref_dg = torch.zeros(G, D, device=dev).index_add_(0, g, go.float() * y.detach().float())
     assert ((gt.grad - ref_dg).norm() / ref_dg.norm()).item() < 1e-3
 
