@@ -578,3 +578,150 @@ void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, co
 }
 
 }  // namespace dmad
+
+// ============================================================================
+// Allocation-free entry point (declaration, rules of use and the reason it
+// exists: flash_bwd_noalloc.h).  No counterpart in the reference.
+// ============================================================================
+#include "flash_bwd_noalloc.h"
+#include <cstdio>
+#include <mutex>
+
+namespace dmad {
+namespace {
+
+// rowsum(dO * O) work rows and the bounded-wait status word of the entry point
+static __device__ __align__(256) float g_noalloc_rows[DMAD_NOALLOC_MAX_ROWS];
+static __device__ __align__(256) int g_noalloc_status;
+
+struct NoallocSymbols {
+  float* rows = nullptr;
+  int* status = nullptr;
+};
+
+// Device addresses of the static arrays, looked up once per device with that device current.
+bool noalloc_symbols(NoallocSymbols& out) {
+  static std::mutex mu;
+  static NoallocSymbols table[64];
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  NoallocSymbols& s = table[dev];
+  if (s.rows == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_rows) != cudaSuccess || p == nullptr) return false;
+    void* st = nullptr;
+    if (cudaGetSymbolAddress(&st, g_noalloc_status) != cudaSuccess || st == nullptr) return false;
+    s.rows = static_cast<float*>(p);
+    s.status = static_cast<int*>(st);
+  }
+  out = s;
+  return true;
+}
+
+CUtensorMap map_raw(const void* base, int B, int L, int H, const int64_t* st) {
+  const uint64_t dims[4] = {128, (uint64_t)H, (uint64_t)L, (uint64_t)B};
+  const uint64_t strides[3] = {(uint64_t)st[2] * 2, (uint64_t)st[1] * 2, (uint64_t)st[0] * 2};
+  const uint32_t box[4] = {64, 1, 128, 1};
+  return make_tmap_bf16(base, 4, dims, strides, box);
+}
+
+}  // namespace
+}  // namespace dmad
+
+extern "C" int dmad_flash_attn_bwd_noalloc(const void* q, const void* k, const void* v, const void* o,
+                                           const void* dout, const float* lse2, void* dq, void* dk, void* dv, int B,
+                                           int Lq, int Lk, int H, const int64_t* strides, float scale,
+                                           void* stream) {
+  using namespace dmad;
+  const void* ptrs[10] = {q, k, v, o, dout, lse2, dq, dk, dv, strides};
+  for (const void* p : ptrs)
+    if (p == nullptr) {
+      fprintf(stderr, "dmad_flash_attn_bwd_noalloc: null pointer argument\n");
+      return DMAD_NOALLOC_ERR_ARGS;
+    }
+  if (B <= 0 || Lq <= 0 || Lk <= 0 || H <= 0) {
+    fprintf(stderr, "dmad_flash_attn_bwd_noalloc: sizes must be positive\n");
+    return DMAD_NOALLOC_ERR_ARGS;
+  }
+  for (int i = 0; i < 24; ++i)
+    if (strides[i] <= 0 || strides[i] % 8 != 0) {
+      fprintf(stderr, "dmad_flash_attn_bwd_noalloc: stride %d must be a positive multiple of 8 elements\n", i);
+      return DMAD_NOALLOC_ERR_ARGS;
+    }
+  const int64_t Lpad = flash_lse_pad(Lq);
+  const int64_t rows = (int64_t)B * H * Lpad;
+  if (rows > DMAD_NOALLOC_MAX_ROWS) {
+    fprintf(stderr,
+            "dmad_flash_attn_bwd_noalloc: B*H*round_up(Lq,256) = %lld exceeds the static work array of %d rows; "
+            "use the regular entry point for this size\n",
+            (long long)rows, DMAD_NOALLOC_MAX_ROWS);
+    return DMAD_NOALLOC_ERR_TOO_LARGE;
+  }
+  NoallocSymbols sym;
+  if (!noalloc_symbols(sym)) {
+    fprintf(stderr, "dmad_flash_attn_bwd_noalloc: cudaGetSymbolAddress failed\n");
+    return DMAD_NOALLOC_ERR_CUDA;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t* sq = strides + 0;
+  const int64_t* sk = strides + 3;
+  const int64_t* sv = strides + 6;
+  const int64_t* so = strides + 9;
+  const int64_t* sg = strides + 12;
+  const int64_t* sdq = strides + 15;
+  const int64_t* sdk = strides + 18;
+  const int64_t* sdv = strides + 21;
+  CUtensorMap tq, tk, tv, tg;
+  try {
+    tq = map_raw(q, B, Lq, H, sq);
+    tk = map_raw(k, B, Lk, H, sk);
+    tv = map_raw(v, B, Lk, H, sv);
+    tg = map_raw(dout, B, Lq, H, sg);
+  } catch (const std::exception& e) {
+    fprintf(stderr, "dmad_flash_attn_bwd_noalloc: %s\n", e.what());
+    return DMAD_NOALLOC_ERR_ARGS;
+  }
+  if (cudaMemsetAsync(sym.status, 0, sizeof(int), s) != cudaSuccess) return DMAD_NOALLOC_ERR_CUDA;
+  {
+    const int warps = 8;
+    bwd_dot_kernel<<<(unsigned)((rows + warps - 1) / warps), warps * 32, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(o), static_cast<const __nv_bfloat16*>(dout), sym.rows, so[0], so[1], so[2],
+        sg[0], sg[1], sg[2], B, H, Lq, (int)Lpad);
+  }
+  BwdParams p;
+  p.lse2 = lse2;
+  p.dd = sym.rows;
+  p.Lq = Lq;
+  p.Lk = Lk;
+  p.H = H;
+  p.Lpad = (int)Lpad;
+  p.scale = scale;
+  p.scale_log2 = (float)((double)scale * 1.4426950408889634);
+  p.status = sym.status;
+  p.out = static_cast<__nv_bfloat16*>(dk);
+  p.sb = sdk[0];
+  p.sl = sdk[1];
+  p.sh = sdk[2];
+  p.out2 = static_cast<__nv_bfloat16*>(dv);
+  p.sb2 = sdv[0];
+  p.sl2 = sdv[1];
+  p.sh2 = sdv[2];
+  const size_t smem_a = sizeof(DkvSmem) + 1024;
+  if (cudaFuncSetAttribute(flash_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_a) !=
+      cudaSuccess)
+    return DMAD_NOALLOC_ERR_CUDA;
+  flash_bwd_dkdv_kernel<<<dim3((Lk + 127) / 128, H, B), 256, smem_a, s>>>(tq, tk, tv, tg, p);
+  p.out = static_cast<__nv_bfloat16*>(dq);
+  p.sb = sdq[0];
+  p.sl = sdq[1];
+  p.sh = sdq[2];
+  p.out2 = nullptr;
+  const size_t smem_b = sizeof(DqSmem) + 1024;
+  if (cudaFuncSetAttribute(flash_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_b) !=
+      cudaSuccess)
+    return DMAD_NOALLOC_ERR_CUDA;
+  flash_bwd_dq_kernel<<<dim3((Lq + 127) / 128, H, B), 256, smem_b, s>>>(tq, tk, tv, tg, p);
+  if (cudaGetLastError() != cudaSuccess) return DMAD_NOALLOC_ERR_CUDA;
+  return DMAD_NOALLOC_OK;
+}
