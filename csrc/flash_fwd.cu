@@ -19,6 +19,7 @@
 // grows by more than 2^8 (values stay exact because the final normalisation
 // uses the same stale maximum as the numerator).
 #include <cuda_runtime.h>
+#include <type_traits>
 #include <cuda_bf16.h>
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -226,61 +227,94 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       ok = __all_sync(0xffffffffu, mbar_wait(&sm.s_full[t], j & 1, kStatusTimeoutMma, abort_flag, p.status));
       if (!ok) break;
       tc_fence_after();
-      // pass 1: row maximum over the tile (32 columns at a time, low register pressure)
       const int kv_valid = p.Lk - j * kTileN;
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(s_tmem + c * 32, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (c * 32 + i < kv_valid) mx = fmaxf(mx, __uint_as_float(r[i]));
-      }
-      const float m_blk = mx * scale_log2;
+      const bool masked = kv_valid < kTileN;  // only the last key tile (warp-uniform)
       float alpha = 1.f;
-      bool rescale = false;
-      if (j == 0) {
-        m_used = m_blk;
-      } else if (m_blk > m_used + kRescaleThreshold) {
-        alpha = ex2_approx(m_used - m_blk);
-        m_used = m_blk;
-        rescale = true;
-      }
-      // O holds the sum over tiles < j (PV(j-1) finished before S(j) completed).
-      if (__any_sync(0xffffffffu, rescale)) {
+      float rsum[4] = {0.f, 0.f, 0.f, 0.f};
+      // The softmax body is instantiated twice: unmasked (every key tile but the last) and
+      // masked (keys >= Lk read as -inf).
+      auto body = [&](auto masked_t) {
+        constexpr bool kMasked = decltype(masked_t)::value;
+        // pass 1: the whole S row in one TMEM read (four loads, one wait); row maximum with
+        // eight independent 3-input-max chains
+        float m_blk;
+        {
+          uint32_t sr[4][32];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) tmem_ld32(s_tmem + c * 32, sr[c]);
+          tmem_wait_ld();
+          auto sv = [&](int c, int i) -> float {
+            const float v = __uint_as_float(sr[c][i]);
+            return (kMasked && c * 32 + i >= kv_valid) ? -INFINITY : v;
+          };
+          float mc[4];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float a = sv(c, 0), b = sv(c, 1);
+#pragma unroll
+            for (int i = 2; i < 30; i += 4) {
+              a = fmax3(a, sv(c, i), sv(c, i + 1));
+              b = fmax3(b, sv(c, i + 2), sv(c, i + 3));
+            }
+            mc[c] = fmax3(a, b, fmaxf(sv(c, 30), sv(c, 31)));
+          }
+          m_blk = fmaxf(fmaxf(mc[0], mc[1]), fmaxf(mc[2], mc[3])) * scale_log2;
+        }
+        bool rescale = false;
+        if (j == 0) {
+          m_used = m_blk;
+        } else if (m_blk > m_used + kRescaleThreshold) {
+          alpha = ex2_approx(m_used - m_blk);
+          m_used = m_blk;
+          rescale = true;
+        }
+        // O holds the sum over tiles < j (PV(j-1) finished before S(j) completed).
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld32(o_tmem + c * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32(o_tmem + c * 32, r);
+          }
+        }
+        // pass 2: P = exp2(S * scale - m) and the row sum, 32 columns at a time with the next
+        // chunk's TMEM read in flight.  Chunk c writes bf16 P columns [16c, 16c+16), which
+        // only overlap S columns already read.  On full tiles one exponential in four runs on
+        // the FMA pipe (ex2_poly); masked columns of the last tile give exactly 0 via MUFU.
+        const float neg_m = -m_used;
+        uint32_t buf[2][32];
+        tmem_ld32(s_tmem, buf[0]);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tmem_ld32(o_tmem + c * 32, r);
           tmem_wait_ld();
+          if (c + 1 < 4) tmem_ld32(s_tmem + (c + 1) * 32, buf[(c + 1) & 1]);
+          const uint32_t(&r)[32] = buf[c & 1];
+          uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st32(o_tmem + c * 32, r);
+          for (int i = 0; i < 16; ++i) {
+            const int col = c * 32 + 2 * i;
+            float x0 = fmaf(__uint_as_float(r[2 * i]), scale_log2, neg_m);
+            float x1 = fmaf(__uint_as_float(r[2 * i + 1]), scale_log2, neg_m);
+            if (kMasked) {
+              x0 = col < kv_valid ? x0 : -INFINITY;
+              x1 = col + 1 < kv_valid ? x1 : -INFINITY;
+            }
+            const float p0 = ex2_approx(x0);
+            const float p1 = (!kMasked && (i & 1)) ? ex2_poly(x1) : ex2_approx(x1);
+            rsum[c] += p0 + p1;
+            pk[i] = pack_bf16x2(p0, p1);
+          }
+          tmem_st16(s_tmem + c * 16, pk);
         }
-      }
-      // pass 2: P = exp2(S * scale - m), row sum, bf16 P written over S columns [0, 64).
-      // Chunk c reads S columns [32c, 32c+32) and writes P columns [16c, 16c+16),
-      // which only overlap S columns already consumed.
-      const float neg_m = -m_used;
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(s_tmem + c * 32, r);
-        tmem_wait_ld();
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int col = c * 32 + 2 * i;
-          const float p0 = col < kv_valid ? ex2_approx(fmaf(__uint_as_float(r[2 * i]), scale_log2, neg_m)) : 0.f;
-          const float p1 = col + 1 < kv_valid ? ex2_approx(fmaf(__uint_as_float(r[2 * i + 1]), scale_log2, neg_m)) : 0.f;
-          rs += p0 + p1;
-          pk[i] = pack_bf16x2(p0, p1);
-        }
-        tmem_st16(s_tmem + c * 16, pk);
-      }
+      };
+      if (masked)
+        body(std::true_type{});
+      else
+        body(std::false_type{});
+      const float rs = (rsum[0] + rsum[1]) + (rsum[2] + rsum[3]);
       l_sum = l_sum * alpha + rs;
       tmem_wait_st();
       tc_fence_before();

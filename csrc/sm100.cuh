@@ -283,11 +283,44 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                : "memory");
 }
 
+// ---------------------------------------------------------------- register reallocation
+// Warpgroup-wide; the per-thread counts of all warpgroups must fit in the registers
+// the block was launched with (threads x registers per thread at launch).
+template <uint32_t N>
+__device__ __forceinline__ void regs_increase() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_decrease() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ---------------------------------------------------------------- math helpers
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 3-input maximum (sm_100 PTX form of max.f32).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x on the FMA/ALU pipes, used for a fraction of the softmax exponentials so the
+// MUFU pipe is not the only exp2 unit.  Method: Cody-Waite range reduction
+// x = n + f (n = floor(x) obtained by a round-down add of 1.5 * 2^23, f in [0, 1)),
+// 2^f from a degree-3 polynomial fitted here by error-equalising least squares on
+// [0, 1] (max relative error 7.5e-5, below bf16's 3.9e-3), and 2^n added to the
+// exponent field with integer ops.  Inputs below -126 are clamped (result ~1e-38).
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -126.f);
+  const float t = __fadd_rd(x, 12582912.f);
+  const float f = x - (t - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.07802403f, f, 0.22606707f), f, 0.69583398f), f, 0.99992514f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 // Packs two floats into one bf16x2 word: `lo` in bits [0,16), `hi` in [16,32).
