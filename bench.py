@@ -46,6 +46,7 @@ def parse():
     ap.add_argument("--gen-runs", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--count-launches", type=int, default=1)
+    ap.add_argument("--profile", default=None, help="write a per-kernel time table of one cycle to this path")
     return ap.parse_args()
 
 
@@ -232,6 +233,16 @@ def main():
             e2.synchronize()
             times.append(s2.elapsed_time(e2) / 1000.0)
         gen_s = max_over_ranks(min(times))
+
+    if args.profile and rank == 0:
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA, ProfilerActivity.CPU]) as prof:
+            cycle(batch)
+            torch.cuda.synchronize()
+        with open(args.profile, "w") as f:
+            f.write(prof.key_averages().table(sort_by="cuda_time_total", row_limit=60, max_name_column_width=90))
+        print(f"# peak memory {torch.cuda.max_memory_allocated() / 2**30:.1f} GiB", file=sys.stderr)
 
     launches = None
     if args.count_launches and args.impl == "dmad_b200":
