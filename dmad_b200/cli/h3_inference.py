@@ -1,0 +1,136 @@
+"""Few-step text-to-audio-video inference with an H3-shaped DMAD student.
+
+Flag-compatible with the reference's ``inference.py`` (inference.py:50-98): --steps, --video-shift,
+--audio-shift, --euler, --height/--width/--num-frames, --low-vram [auto|8|12|16|24], --weights-in-ram,
+--weights-int8, --lora, --lora-alpha, --seed, --prompt/--prompt-file, --output-dir.
+
+Without real checkpoints (``--model-dir`` absent or ``--random-init``), the network is randomly
+initialised with the H3-shaped configuration (``--config 33b`` or ``tiny``) and prompts are replaced by
+N(0,1) embeddings of ``--text-tokens`` rows; latents are written instead of decoded video when no VAE
+is available.  Per-stage peak GPU memory is logged as the reference does.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import time
+
+import torch
+
+from ..inference.h3 import (H3Geometry, build_packed_sequence, build_row_timesteps, latent_shape_of, rollout,
+                            sigma_grid)
+from ..models.h3 import H3Config, H3Model
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--model-dir", default=None)
+    p.add_argument("--random-init", action="store_true")
+    p.add_argument("--config", default="33b", choices=["33b", "tiny"])
+    p.add_argument("--lora", default=None)
+    p.add_argument("--lora-alpha", type=float, default=None)
+    p.add_argument("--prompt", action="append", default=[])
+    p.add_argument("--prompt-file", default=None)
+    p.add_argument("--text-tokens", type=int, default=256)
+    p.add_argument("--output-dir", required=True)
+    p.add_argument("--seed", type=int, default=42)
+    p.add_argument("--steps", type=int, default=4)
+    p.add_argument("--video-shift", type=float, default=12.0)
+    p.add_argument("--audio-shift", type=float, default=2.0)
+    p.add_argument("--euler", action="store_true")
+    p.add_argument("--height", type=int, default=768)
+    p.add_argument("--width", type=int, default=1344)
+    p.add_argument("--num-frames", type=int, default=124)
+    p.add_argument("--low-vram", nargs="?", const="auto", choices=["auto", "8", "12", "16", "24"], default=None)
+    p.add_argument("--weights-in-ram", action="store_true")
+    p.add_argument("--weights-int8", action="store_true")
+    return p.parse_args(argv)
+
+
+def read_prompts(path):
+    out = []
+    for line in open(path, encoding="utf-8"):
+        line = line.strip()
+        if not line:
+            continue
+        out.append(json.loads(line)["prompt"] if path.endswith(".jsonl") else line)
+    return out
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    prompts = list(args.prompt) + (read_prompts(args.prompt_file) if args.prompt_file else [])
+    if not prompts:
+        prompts = ["synthetic prompt"]
+    os.makedirs(args.output_dir, exist_ok=True)
+    device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
+    t0 = time.time()
+
+    def log(msg):
+        print(f"[{time.time() - t0:6.0f}s] {msg}", flush=True)
+
+    def peak(stage):
+        if device.type == "cuda":
+            log(f"{stage}: peak GPU memory {torch.cuda.max_memory_allocated() / 2**30:.1f} GiB")
+            torch.cuda.reset_peak_memory_stats()
+
+    cfg = H3Config() if args.config == "33b" else H3Config(dim=512, num_heads=4, ffn_dim=1024, num_layers=4,
+                                                            text_dim=512, time_embed_dim=256)
+    geometry = H3Geometry.from_model_dir(args.model_dir) if (args.model_dir and not args.random_init) else H3Geometry()
+    shape = latent_shape_of(args.height, args.width, args.num_frames, geometry)
+    vsig, asig = sigma_grid(args.steps, args.video_shift), sigma_grid(args.steps, args.audio_shift)
+    g = torch.Generator().manual_seed(args.seed)
+    conds = [{"prompt_embeds": torch.randn(1, args.text_tokens, cfg.text_dim, generator=g).to(torch.bfloat16),
+              "text_token_tags": torch.ones(args.text_tokens, dtype=torch.long)} for _ in prompts]
+    layouts = [build_packed_sequence(c["text_token_tags"], shape["latent_frames"], shape["latent_height"],
+                                     shape["latent_width"], shape["audio_latents"], geometry.patch_size) for c in conds]
+    torch.manual_seed(args.seed)
+    model = H3Model(cfg).to(torch.bfloat16)
+    if args.lora:
+        from ..lora import attach_lora, lora_rank_alpha, read_lora_file
+
+        pairs, meta = read_lora_file(args.lora)
+        rank, alpha = lora_rank_alpha(pairs, meta, args.lora_alpha)
+        attach_lora(model, pairs, rank, alpha)
+        model.to(torch.bfloat16)
+        log(f"LoRA attached: {len(pairs)} modules, rank {rank}, alpha {alpha:g}")
+    model.eval().requires_grad_(False)
+    streamed = None
+    text_feats = [None] * len(conds)
+    tables = None
+    if args.low_vram:
+        from ..inference.lowmem import LowMemH3
+
+        ts = [build_row_timesteps(layouts[0], vsig[s], asig[s])[0] for s in range(args.steps)]
+        streamed = LowMemH3(model, device, ts, codec="int8" if args.weights_int8 else None)
+        streamed.precompute_text([c["prompt_embeds"] for c in conds])
+        text_feats = [streamed.text_features(c["prompt_embeds"]) for c in conds]
+        tables = streamed.tables
+        log(f"streaming {streamed.streamer.bytes_per_pass / 2**30:.1f} GiB of weights per model evaluation")
+    else:
+        model.to(device)
+    outs = []
+    for i, (c, lay) in enumerate(zip(conds, layouts)):
+        t1 = time.time()
+        v, a = rollout(model, c["prompt_embeds"].to(device), lay, shape, geometry, vsig, asig, args.seed, device,
+                       renoise=not args.euler, text_features=text_feats[i], adaln_tables_per_step=tables)
+        if device.type == "cuda":
+            torch.cuda.synchronize()
+        log(f"sampled {i + 1}/{len(prompts)} in {time.time() - t1:.1f}s")
+        outs.append((v.to(torch.bfloat16), a.to(torch.bfloat16)))
+    if streamed is not None:
+        streamed.close()
+    peak("sampling")
+    for i, ((v, a), prompt) in enumerate(zip(outs, prompts)):
+        torch.save({"video_rows": v, "audio_rows": a, "shape": shape}, os.path.join(args.output_dir, f"{i:04d}.pt"))
+        with open(os.path.join(args.output_dir, f"{i:04d}.txt"), "w", encoding="utf-8") as f:
+            f.write(prompt)
+    with open(os.path.join(args.output_dir, "settings.json"), "w") as f:
+        json.dump({k: v for k, v in vars(args).items() if k != "prompt"}, f, indent=2)
+    log("done")
+    return outs
+
+
+if __name__ == "__main__":
+    main()

@@ -60,7 +60,7 @@ def check_device_status(device: int | None = None) -> None:
 
 
 from .attention import flash_attention, attention_reference  # noqa: E402
-from .norm import ln_mod, gate_residual, qk_norm_rope, rope_apply, rms_norm, layer_norm_affine  # noqa: E402
+from .norm import ln_mod, gate_residual, qk_norm_rope, rope, rope_apply, rms_norm, layer_norm_affine  # noqa: E402
 from .activation import gelu_tanh  # noqa: E402
 from .temb import sinusoidal_embedding, small_linear  # noqa: E402
 
@@ -74,6 +74,7 @@ __all__ = [
     "ln_mod",
     "gate_residual",
     "qk_norm_rope",
+    "rope",
     "rope_apply",
     "rms_norm",
     "layer_norm_affine",

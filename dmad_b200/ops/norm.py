@@ -187,3 +187,30 @@ def qk_norm_rope(src, wq, wk, cos, sin, D, hd=128, eps=1e-6):
     rk = torch.empty(R, dtype=torch.float32, device=src.device)
     ext().qk_norm_rope_fwd(src, out, wq, wk, cos, sin, rq, rk, int(D), int(hd), float(eps))
     return out, rq, rk
+
+
+class _Rope(torch.autograd.Function):
+    """Differentiable interleaved RoPE: the backward is the inverse rotation."""
+
+    @staticmethod
+    def forward(ctx, x, cos, sin, hd):
+        ctx.save_for_backward(cos, sin)
+        ctx.hd = hd
+        y = torch.empty_like(x, memory_format=torch.contiguous_format)
+        ext().rope_apply(x, y, cos, sin, int(hd), False)
+        return y
+
+    @staticmethod
+    def backward(ctx, g):
+        cos, sin = ctx.saved_tensors
+        g = g.contiguous()
+        dx = torch.empty_like(g)
+        ext().rope_apply(g, dx, cos, sin, int(ctx.hd), True)
+        return dx, None, None, None
+
+
+def rope(x, cos, sin, hd=128):
+    """Differentiable interleaved RoPE of [R, H*hd] rows (row r uses table row r % len(cos))."""
+    if not x.is_cuda:
+        return rope_reference(x, cos, sin, hd)
+    return _Rope.apply(x, cos.float().contiguous(), sin.float().contiguous(), hd)
