@@ -65,3 +65,20 @@ def test_lora_roundtrip_and_comfyui():
         out = convert(p2, 4, 4.0)
         verify(p2, out)
         assert out["diffusion_model.blocks.0.attn.qkv_proj.lora_A.weight"].shape[0] == 12
+
+
+def test_h3_dmad_iterations_cpu():
+    from dmad_b200.distill.h3_dmad import H3DMAD, H3DMADConfig
+    from dmad_b200.models.h3 import H3Config
+    cfg = H3DMADConfig(model=H3Config(dim=64, num_heads=1, ffn_dim=96, num_layers=2, refiner_layers=1, text_dim=16,
+                                      time_embed_dim=32), height=64, width=64, num_frames=22, student_lora_rank=4,
+                       text_tokens=4)
+    m = H3DMAD(cfg, "cpu", dtype=torch.float32)
+    before = [p.detach().clone() for p in m.s_params]
+    for _ in range(2):
+        out = m.train_iteration()
+        assert all(torch.isfinite(torch.tensor(v)) for v in out["student"].values())
+    assert any(not torch.equal(a, b) for a, b in zip(before, m.s_params))
+    sd = m.critic_state()
+    m.load_critic_state(sd)
+    assert m.student_steps == 2 and m.ema_banks[0].t == 2
