@@ -1,0 +1,237 @@
+"""DMAD for the SDXL-shaped U-Net.
+
+Parity with train/image/main/sd_guidance.py and sd_unified_model.py:
+* generator: epsilon-prediction U-Net; 4-step ``denoising_step_list`` (999, 749, 499, 249); backward
+  simulation runs the generator's own sampler for a random number of steps (shared across ranks) and
+  re-noises to the selected step; the pure-noise step starts from noise; x0 = (x_t - sqrt(1-a) eps)/sqrt(a);
+* critic: a copy of the U-Net with the decoder removed (bottleneck [N, 1280, H/4, W/4]), two conv heads
+  (three stride-2 convs, a 4x4/stride-4 conv, a 1x1 conv), frozen-gain spectral norm on every trainable
+  conv (200 power iterations at set-up); DDPM noising at t ~ U[0, critic_max_timestep), one t per sample
+  index shared by T / G / Q; gap bands t // 100, all-reduced;
+* one iteration = generator update then critic update on the same generated batch.
+"""
+from __future__ import annotations
+
+import copy
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+import torch.nn.functional as F
+from torch.nn.utils import parametrize
+
+from ..algorithms.dmad import NUM_GAP_BANDS
+from ..models.sdxl import SDXLUNet, ddpm_alphas_cumprod
+
+
+class ScaledSN(nn.Module):
+    """weight -> gain * W / sigma_max(W), one power iteration per forward, gain frozen at set-up."""
+
+    def __init__(self, weight, iters=200):
+        super().__init__()
+        w2 = weight.detach().float().reshape(weight.shape[0], -1)
+        u = torch.randn(w2.shape[0], device=weight.device)
+        v = torch.randn(w2.shape[1], device=weight.device)
+        for _ in range(iters):
+            v = F.normalize(w2.t() @ u, dim=0)
+            u = F.normalize(w2 @ v, dim=0)
+        self.register_buffer("u", u.clone())
+        self.register_buffer("v", v.clone())
+        v1 = F.normalize(w2.t() @ u, dim=0)
+        u1 = F.normalize(w2 @ v1, dim=0)
+        self.register_buffer("gain", torch.sum(u1 * (w2 @ v1)).clone())
+
+    def forward(self, w):
+        w2 = w.reshape(w.shape[0], -1).float()
+        with torch.no_grad():
+            self.v.copy_(F.normalize(w2.t() @ self.u, dim=0))
+            self.u.copy_(F.normalize(w2 @ self.v, dim=0))
+        u, v = self.u.clone(), self.v.clone()
+        sigma = torch.sum(u * (w2 @ v)).clamp(min=1e-12)
+        return w * (self.gain / sigma).to(w.dtype)
+
+
+def apply_scaled_spectral_norm(module, iters=200):
+    n = 0
+    for m in module.modules():
+        if isinstance(m, nn.Conv2d) and m.weight.requires_grad and m.weight.detach().abs().max() >= 1e-8:
+            parametrize.register_parametrization(m, "weight", ScaledSN(m.weight, iters))
+            n += 1
+    return n
+
+
+def make_head(ch=1280, spatial=32):
+    """Stride-2 convs down to 4x4, a 4x4/stride-4 conv, a 1x1 conv (three stride-2 convs for the
+    32x32 bottleneck of 1024-pixel images, as the reference head)."""
+    layers, s = [], spatial
+    while s > 4:
+        layers += [nn.Conv2d(ch, ch, 4, 2, 1), nn.GroupNorm(32, ch), nn.SiLU()]
+        s //= 2
+    layers += [nn.Conv2d(ch, ch, 4, 4, 0), nn.GroupNorm(32, ch), nn.SiLU(), nn.Conv2d(ch, 1, 1)]
+    return nn.Sequential(*layers)
+
+
+@dataclass
+class SDXLDMADConfig:
+    resolution: int = 1024
+    latent: int = 128
+    num_denoising_step: int = 4
+    denoising_timestep: int = 1000
+    critic_max_timestep: int = 1000
+    teacher_gap_route: bool = True
+    gap_tau: float = 2.0
+    critic_spectral_norm: bool = True
+    sn_iters: int = 200
+    generator_lr: float = 5e-7
+    guidance_lr: float = 5e-7
+    betas: tuple = (0.0, 0.999)
+    teacher_loss_weight: float = 1.0
+    real_loss_weight: float = 1.0
+    backward_simulation: bool = True
+    gradient_checkpointing: bool = True
+    unet_kwargs: dict | None = None
+
+
+class SDXLDMAD:
+    def __init__(self, cfg: SDXLDMADConfig = SDXLDMADConfig(), device="cuda", dtype=torch.bfloat16, seed=0):
+        self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
+        torch.manual_seed(seed)
+        teacher = SDXLUNet(**(cfg.unet_kwargs or {}))
+        self.generator = teacher
+        self.critic = copy.deepcopy(teacher)
+        self.critic.up_blocks = nn.ModuleList()
+        self.critic.conv_norm_out = self.critic.conv_out = None
+        ch = teacher.channels[-1]
+        spatial = cfg.latent >> (len(teacher.channels) - 1)
+        self.head_real, self.head_teacher = make_head(ch, spatial), make_head(ch, spatial)
+        for m in self.head_teacher.modules():
+            if isinstance(m, nn.Conv2d):
+                nn.init.kaiming_normal_(m.weight, nonlinearity="relu")
+                nn.init.zeros_(m.bias)
+        if cfg.critic_spectral_norm:
+            for mod in (self.critic.down_blocks, self.critic.mid_block, self.head_real, self.head_teacher):
+                apply_scaled_spectral_norm(mod, cfg.sn_iters)
+        for m in (self.generator, self.critic):
+            m.gradient_checkpointing = cfg.gradient_checkpointing
+            m.to(self.device, dtype)
+        self.head_real.to(self.device)
+        self.head_teacher.to(self.device)
+        self.ac = ddpm_alphas_cumprod().to(self.device)
+        step = cfg.denoising_timestep // cfg.num_denoising_step
+        self.step_list = torch.arange(cfg.denoising_timestep - 1, 0, -step, device=self.device)
+        self.interval = step
+        self.gap_ema = torch.zeros(NUM_GAP_BANDS, device=self.device)
+        self.gap_ready = torch.zeros(NUM_GAP_BANDS, device=self.device)
+        cp = list(self.critic.parameters()) + list(self.head_real.parameters()) + list(self.head_teacher.parameters())
+        self.opt_g = torch.optim.AdamW(self.generator.parameters(), lr=cfg.generator_lr, betas=cfg.betas, foreach=True)
+        self.opt_c = torch.optim.AdamW([p for p in cp if p.requires_grad], lr=cfg.guidance_lr, betas=cfg.betas,
+                                       foreach=True)
+        self.time_ids = torch.tensor([[cfg.resolution, cfg.resolution, 0, 0, cfg.resolution, cfg.resolution]],
+                                     device=self.device, dtype=torch.float32)
+
+    # ------------------------------------------------------------------ DDPM helpers
+    def add_noise(self, x, eps, t):
+        a = self.ac[t].reshape(-1, 1, 1, 1)
+        return (a.sqrt() * x.double() + (1 - a).sqrt() * eps.double()).float()
+
+    def x0_from_eps(self, xt, eps, t):
+        a = self.ac[t].reshape(-1, 1, 1, 1)
+        return ((xt.double() - (1 - a).sqrt() * eps.double()) / a.sqrt()).float()
+
+    def unet(self, net, x, t, ctx, pooled, bottleneck=False):
+        ids = self.time_ids.repeat(x.shape[0], 1)
+        return net(x.to(self.dtype), t, ctx.to(self.dtype), ids, pooled.to(self.dtype), return_bottleneck=bottleneck)
+
+    def _synced_int(self, hi):
+        s = torch.randint(0, hi, (1,), device=self.device)
+        if dist.is_available() and dist.is_initialized():
+            dist.broadcast(s, 0)
+        return int(s.item())
+
+    @torch.no_grad()
+    def sample_backward(self, noise, ctx, pooled):
+        B = noise.shape[0]
+        sel = self._synced_int(self.cfg.num_denoising_step)
+        x, img = noise, noise
+        for c in self.step_list[:sel]:
+            t = torch.full((B,), int(c), device=self.device, dtype=torch.long)
+            eps = self.unet(self.generator, x, t, ctx, pooled).float()
+            img = self.x0_from_eps(x, eps, t)
+            x = self.add_noise(img, torch.randn_like(img), t - self.interval)
+        return img, torch.full((B,), int(self.step_list[sel]), device=self.device, dtype=torch.long)
+
+    # ------------------------------------------------------------------ critic
+    def critic_logits(self, x, t, ctx, pooled):
+        xt = self.add_noise(x, torch.randn_like(x), t)
+        rep = self.unet(self.critic, xt, t, ctx, pooled, bottleneck=True).float()
+        return self.head_real(rep).reshape(-1), self.head_teacher(rep).reshape(-1)
+
+    def gap_weight(self, t):
+        if not self.cfg.teacher_gap_route:
+            return None
+        n_reach = min(NUM_GAP_BANDS, max(1, self.cfg.critic_max_timestep // 100 + 1))
+        if float(self.gap_ready.sum()) < max(2, (n_reach + 1) // 2):
+            return None
+        center = float(self.gap_ema[self.gap_ready > 0].median())
+        return torch.sigmoid((center - self.gap_ema[(t // 100).clamp(0, 9)]) / self.cfg.gap_tau)
+
+    @torch.no_grad()
+    def update_gap(self, dT, dQ, t):
+        b = (t // 100).clamp(0, 9)
+        s = torch.zeros(4, NUM_GAP_BANDS, device=self.device)
+        s[0].scatter_add_(0, b, dT.float())
+        s[1].scatter_add_(0, b, torch.ones_like(dT, dtype=torch.float32))
+        s[2].scatter_add_(0, b, dQ.float())
+        s[3].scatter_add_(0, b, torch.ones_like(dQ, dtype=torch.float32))
+        if dist.is_available() and dist.is_initialized():
+            dist.all_reduce(s)
+        valid = (s[1] > 0) & (s[3] > 0)
+        now = s[0] / s[1].clamp(min=1) - s[2] / s[3].clamp(min=1)
+        upd = torch.where(valid & (self.gap_ready > 0), 0.99 * self.gap_ema + 0.01 * now, now)
+        self.gap_ema.copy_(torch.where(valid, upd, self.gap_ema))
+        self.gap_ready.copy_(torch.where(valid, torch.ones_like(self.gap_ready), self.gap_ready))
+
+    def _critic_params(self):
+        return list(self.critic.parameters()) + list(self.head_real.parameters()) + list(self.head_teacher.parameters())
+
+    # ------------------------------------------------------------------ iteration
+    def train_step(self, batch):
+        """batch: noise / real / teacher latents [B, 4, 128, 128], ctx [B, 77, 2048], pooled [B, 1280]."""
+        cfg = self.cfg
+        noise, ctx, pooled = batch["noise"], batch["ctx"], batch["pooled"]
+        B = noise.shape[0]
+        with torch.no_grad():
+            if cfg.backward_simulation:
+                clean, t = self.sample_backward(torch.randn_like(noise), ctx, pooled)
+            else:
+                t = self.step_list[torch.randint(0, cfg.num_denoising_step, (B,), device=self.device)]
+                clean = batch["teacher"]
+            noisy = self.add_noise(clean, noise, t)
+            pure = t == cfg.denoising_timestep - 1
+            noisy[pure] = noise[pure]
+        self.generator.train()
+        eps = self.unet(self.generator, noisy, t, ctx, pooled).float()
+        G = self.x0_from_eps(noisy, eps, t)
+        for p in self._critic_params():
+            p.requires_grad_(False)
+        tc = torch.randint(0, cfg.critic_max_timestep, (B,), device=self.device)
+        dr, dt = self.critic_logits(G, tc, ctx, pooled)
+        w = self.gap_weight(tc)
+        tl = (-dt).mean() if w is None else (-dt * w).sum() / w.sum().clamp(min=1.0) + (-dt).sum() * 0.0
+        loss_g = cfg.teacher_loss_weight * tl + cfg.real_loss_weight * (-dr).mean()
+        loss_g.backward()
+        self.opt_g.step()
+        self.opt_g.zero_grad(set_to_none=True)
+        for p in self._critic_params():
+            p.requires_grad_(True)
+        tc = torch.randint(0, cfg.critic_max_timestep, (B,), device=self.device)
+        dR_T, _ = self.critic_logits(batch["real"], tc, ctx, pooled)
+        dR_G, dQ_G = self.critic_logits(G.detach(), tc, ctx, pooled)
+        dR_Q, dQ_Q = self.critic_logits(batch["teacher"], tc, ctx, pooled)
+        loss_c = F.softplus(-dR_T).mean() + F.softplus(dR_G).mean() + F.softplus(-dQ_Q).mean() + F.softplus(dQ_G).mean()
+        self.update_gap(dR_T.detach(), dR_Q.detach(), tc)
+        loss_c.backward()
+        self.opt_c.step()
+        self.opt_c.zero_grad(set_to_none=True)
+        return {"generator_loss": loss_g.detach(), "critic_loss": loss_c.detach()}
