@@ -68,6 +68,21 @@ class WanDMADConfig:
     checkpoint_critic_blocks: int = 0
     checkpoint_critic_blocks_student_phase: int | None = None
     rectified_flow_t_scaling_factor: float = 1000.0
+    # rCM consistency term (0 = pure DMAD, as the reference's DMAD experiments; > 0 adds the sCM /
+    # dCM loss of the rCM recipe in the student phase, which needs the teacher network)
+    loss_scale: float = 0.0
+    cm_type: str = "scm"            # "scm" | "dcm"
+    use_rf_scm: bool = False
+    teacher_guidance: float = 5.0
+    tangent_warmup: int = 0
+    p_G_lognormal: tuple = (0.7, 1.6)
+    fd_type: int = 0
+    fd_size: float = 1e-4
+    dcm_total_steps: int = 48
+    dcm_skipping_interval_steps: int = 1
+    dcm_timestep_shift: float = 5.0
+    # "dmad": two-head GAN critic (this model); "dmd": rCM's DMD with a denoising fake score
+    critic_mode: str = "dmad"
 
 
 class WanDMAD(nn.Module):
@@ -81,6 +96,8 @@ class WanDMAD(nn.Module):
         # student and critic backbone both start from the teacher weights (rcm :247-251)
         self.net = teacher
         self.net_fake_score = copy.deepcopy(teacher)
+        need_teacher = cfg.loss_scale > 0 or cfg.critic_mode == "dmd"
+        self.net_teacher = copy.deepcopy(teacher).requires_grad_(False) if need_teacher else None
         self.critic_heads = CriticHeads(cfg.net.dim)
         if cfg.critic_spectral_norm:
             self.net_fake_score.enable_spectral_norm(range(cfg.net.num_layers), cfg.sn_power_iters)
@@ -95,6 +112,9 @@ class WanDMAD(nn.Module):
             self.net.enable_lora(cfg.student_lora_rank)
         self.net.to(device=device, dtype=dtype)
         self.net_fake_score.to(device=device, dtype=dtype)
+        if self.net_teacher is not None:
+            self.net_teacher.to(device=device, dtype=dtype).eval()
+            broadcast_module(self.net_teacher)
         self.critic_heads.to(device=device, dtype=torch.float32)
         self.net.checkpoint_blocks = cfg.checkpoint_student_blocks
         self.net_fake_score.checkpoint_blocks = cfg.checkpoint_critic_blocks
@@ -119,10 +139,12 @@ class WanDMAD(nn.Module):
 
     # ------------------------------------------------------------------ schedule (rcm :297-311)
     def is_student_phase(self, it: int) -> bool:
-        return it % self.cfg.student_update_freq == 0
+        w = self.cfg.tangent_warmup
+        return it < w or (it - w) % self.cfg.student_update_freq == 0
 
     def effective_iteration(self, it: int) -> int:
-        return it // self.cfg.student_update_freq
+        w = self.cfg.tangent_warmup
+        return it if it < w else w + (it - w) // self.cfg.student_update_freq
 
     def effective_iteration_fake(self, it: int) -> int:
         return it - self.effective_iteration(it) - 1
@@ -266,7 +288,14 @@ class WanDMAD(nn.Module):
         return out
 
     def training_step(self, batch, it: int) -> dict:
-        return self.student_step(batch, it) if self.is_student_phase(it) else self.critic_step(batch, it)
+        from . import rcm
+
+        cfg = self.cfg
+        if not self.is_student_phase(it):
+            return self.critic_step(batch, it) if cfg.critic_mode == "dmad" else rcm.critic_denoise_step(self, batch, it)
+        if cfg.loss_scale > 0:
+            return rcm.student_step_with_cm(self, batch, it)
+        return self.student_step(batch, it) if cfg.critic_mode == "dmad" else rcm.student_dmd_step(self, batch, it, True)
 
     # ------------------------------------------------------------------ sampling (rcm :830-895)
     @torch.no_grad()

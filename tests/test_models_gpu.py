@@ -50,3 +50,21 @@ def test_wan_dmad_iterations():
     ops.check_device_status()
     x = m.generate(batch["context"], shp)
     assert torch.isfinite(x).all()
+
+
+def test_wan_forward_jvp_gpu_matches_cpu():
+    from dmad_b200.models.wan import WanConfig, WanModel
+    from dmad_b200.models.wan_jvp import wan_forward_jvp
+    torch.manual_seed(0)
+    cfg = WanConfig(dim=256, ffn_dim=512, num_heads=2, num_layers=2, text_dim=128)
+    m = WanModel(cfg)
+    for p in m.parameters():
+        p.data.normal_(0, 0.05)
+    x, tx = torch.randn(1, 16, 3, 8, 12), torch.randn(1, 16, 3, 8, 12)
+    t, tt = torch.tensor([[600.0]]), torch.tensor([[25.0]])
+    c = torch.randn(1, 40, 128)
+    ref, tref = wan_forward_jvp(m, x, tx, t, tt, c)
+    mg = m.to("cuda", torch.bfloat16)
+    out, tout = wan_forward_jvp(mg, x.cuda(), tx.cuda(), t.cuda(), tt.cuda(), c.cuda().bfloat16())
+    assert ((out.cpu() - ref).norm() / ref.norm()).item() < 5e-2
+    assert ((tout.cpu() - tref).norm() / tref.norm()).item() < 5e-2
