@@ -100,6 +100,8 @@ class BlockStreamer:
         if len(self.blocks) < 2:
             raise ValueError("need at least two streamed blocks")
         self.device = torch.device(device)
+        if self.device.type == "cuda" and self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
         for b in self.blocks:  # buffers (LoRA masks, norm statistics) stay resident
             for m in b.modules():
                 for k, buf in list(m._buffers.items()):
@@ -192,6 +194,8 @@ class LowMemH3:
     def __init__(self, model, device, timesteps_per_step, codec=None):
         self.model = model.eval().requires_grad_(False)
         self.device = torch.device(device)
+        if self.device.type == "cuda" and self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
         blocks = list(model.transformer_blocks)
         # resident pieces
         for name in ("proj_in", "audio_proj_in", "context_embedder", "time_embedder", "token_refiner", "norm_out",
