@@ -1,5 +1,8 @@
 """Kernel microbenchmarks: the sm_100a flash-attention forward/backward against PyTorch's
-cuDNN SDPA (the reference's attention backend on cc 10.0) at Wan shapes.
+cuDNN SDPA (the reference's attention backend on cc 10.0), and the flash-attention JVP forward
+against the reference's own Triton kernel (`_attention` in
+train/wan/rcm/utils/flash_attention_jvp_triton.py, run from the installed copy under
+baseline/_ref), at Wan shapes.
 
     python -m benchmarks.bench_kernels --L 32760 --H 12 --B 1          # timing (CUDA events)
     python -m benchmarks.bench_kernels --L 4096 --H 4 --iters 1 --warmup 1 --only fwd   # small case for ncu
@@ -25,6 +28,20 @@ def peak_tflops():
         return 1590.0, "fallback"
 
 
+def _reference_jvp():
+    """The reference's Triton JVP attention (`_attention.apply`) from baseline/_ref, or None."""
+    import sys
+
+    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(root, "rcm")):
+        return None
+    if root not in sys.path:
+        sys.path.insert(0, root)
+    from rcm.utils.flash_attention_jvp_triton import attention
+
+    return attention
+
+
 def timeit(fn, iters, warmup):
     for _ in range(warmup):
         fn()
@@ -46,7 +63,7 @@ def main():
     ap.add_argument("--H", type=int, default=12)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--only", default="all", choices=["all", "fwd", "bwd", "sdpa"])
+    ap.add_argument("--only", default="all", choices=["all", "fwd", "bwd", "sdpa", "jvp", "ref_jvp"])
     a = ap.parse_args()
     from dmad_b200 import ops
 
@@ -84,6 +101,21 @@ def main():
             gt = do.transpose(1, 2)
             ms = timeit(lambda: torch.autograd.grad(out, (qg, kg, vg), gt, retain_graph=True), a.iters, a.warmup)
             res.append(("cudnn_sdpa_bwd", ms, 2.5 * fl_fwd))
+    if a.only in ("all", "jvp", "ref_jvp"):
+        tq, tk, tv = (torch.randn_like(t) * 0.5 for t in (q, k, v))
+        to = torch.empty_like(q)
+        fl_jvp = 3.0 * fl_fwd  # S, tq k^T, q tk^T, P V, P tV, (P * tS) V
+        if a.only in ("all", "jvp"):
+            ms = timeit(lambda: e.flash_jvp_fwd(q, k, v, tq, tk, tv, o, to, lse, scale), a.iters, a.warmup)
+            res.append(("flash_jvp_fwd_sm100", ms, fl_jvp))
+        if a.only in ("all", "ref_jvp"):
+            ref = _reference_jvp()
+            if ref is None:
+                print(json.dumps({"op": "reference_triton_jvp_fwd", "unavailable": "baseline/_ref not installed"}))
+            else:
+                qt, kt, vt, tqt, tkt, tvt = (t.transpose(1, 2).contiguous() for t in (q, k, v, tq, tk, tv))
+                ms = timeit(lambda: ref(qt, kt, vt, tqt, tkt, tvt, scale), a.iters, a.warmup)
+                res.append(("reference_triton_jvp_fwd", ms, fl_jvp))
     for name, ms, fl in res:
         tf = fl / (ms * 1e-3) / 1e12
         print(json.dumps({"op": name, "B": B, "L": L, "Lk": Lk, "H": H, "ms": round(ms, 4), "tflops": round(tf, 1),

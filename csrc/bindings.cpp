@@ -42,6 +42,26 @@ void clip_scale(const at::Tensor& sumsq, at::Tensor& scale, double max_norm);
 void sinusoid_embed(const at::Tensor& t, at::Tensor& out, int64_t dim, double max_period);
 void small_linear(const at::Tensor& x, const at::Tensor& w, c10::optional<at::Tensor> bias, at::Tensor& y,
                   int64_t act_in);
+void flash_jvp_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& tq,
+                   c10::optional<at::Tensor> tk, c10::optional<at::Tensor> tv, at::Tensor& o, at::Tensor& to,
+                   at::Tensor& lse, double scale);
+void flash_fwd_scatter(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
+                       double scale, std::vector<int64_t> scatter, int64_t ld, int64_t col);
+void cp_qkv_push(const at::Tensor& src, std::vector<int64_t> dst, const at::Tensor& wq, const at::Tensor& wk,
+                 const at::Tensor& cosT, const at::Tensor& sinT, at::Tensor& rstd_q, at::Tensor& rstd_k, int64_t B,
+                 int64_t D, int64_t hd, int64_t rank, double eps);
+void cp_seq_to_head(const at::Tensor& src, std::vector<int64_t> dst, int64_t B, int64_t D, int64_t n, int64_t hd,
+                    int64_t rank);
+void cp_head_to_seq(std::vector<at::Tensor> srcs, std::vector<int64_t> dst, int64_t ld, int64_t D, int64_t rank);
+void symm_barrier(const at::Tensor& buf_ptrs, int64_t rank, int64_t epoch, c10::optional<at::Tensor> payload,
+                  double timeout_s);
+void dp_sumsq(std::vector<int64_t> grad_ptrs, std::vector<int64_t> param_ptrs, int64_t mc_grads, int64_t mc_params,
+              int64_t elem_size, int64_t off, int64_t len, at::Tensor& acc);
+void dp_adamw(std::vector<int64_t> grad_ptrs, std::vector<int64_t> param_ptrs, int64_t mc_grads, int64_t mc_params,
+              int64_t elem_size, at::Tensor& master, at::Tensor& exp_avg, at::Tensor& exp_avg_sq,
+              c10::optional<at::Tensor> ema, int64_t off, int64_t len, double lr, double beta1, double beta2,
+              double eps, double weight_decay, int64_t step, double ema_beta, c10::optional<at::Tensor> slots,
+              double max_norm);
 }  // namespace dmad
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -64,4 +84,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("clip_scale", &dmad::clip_scale);
   m.def("sinusoid_embed", &dmad::sinusoid_embed);
   m.def("small_linear", &dmad::small_linear);
+  m.def("flash_jvp_fwd", &dmad::flash_jvp_fwd);
+  m.def("flash_fwd_scatter", &dmad::flash_fwd_scatter);
+  m.def("cp_qkv_push", &dmad::cp_qkv_push);
+  m.def("cp_seq_to_head", &dmad::cp_seq_to_head);
+  m.def("cp_head_to_seq", &dmad::cp_head_to_seq);
+  m.def("symm_barrier", &dmad::symm_barrier);
+  m.def("dp_sumsq", &dmad::dp_sumsq);
+  m.def("dp_adamw", &dmad::dp_adamw);
 }

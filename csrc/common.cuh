@@ -4,6 +4,16 @@
 #include <cuda_bf16.h>
 #include <cstdint>
 
+// Row kernels: vector count per row -> (vectors per thread VEC, threads per block TH).
+#define DMAD_ROW_DISPATCH(nvec, ...)                                        \
+  [&] {                                                                     \
+    if ((nvec) <= 128) { constexpr int VEC = 1, TH = 128; __VA_ARGS__(); }  \
+    else if ((nvec) <= 256) { constexpr int VEC = 2, TH = 128; __VA_ARGS__(); } \
+    else if ((nvec) <= 512) { constexpr int VEC = 2, TH = 256; __VA_ARGS__(); } \
+    else if ((nvec) <= 768) { constexpr int VEC = 3, TH = 256; __VA_ARGS__(); } \
+    else { constexpr int VEC = 4, TH = 256; __VA_ARGS__(); }                \
+  }()
+
 namespace dmad {
 
 struct alignas(16) bf16x8 {

@@ -62,6 +62,12 @@ struct FwdParams {
   int Lq, Lk, H, Lpad;
   float scale_log2;
   int* status;       // device status word (bounded-wait failures)
+  // optional second copy of every output row, scattered to the rank that owns the row
+  // (context-parallel head->sequence exchange): row g of sample b goes to
+  // scat[g / scat_ll] + (b * scat_ll + g % scat_ll) * scat_ld + scat_col + head * 128
+  int64_t scat[16];
+  int scat_n, scat_ll, scat_col;
+  int64_t scat_ld;
 };
 
 __global__ void __launch_bounds__(384, 1)
@@ -341,6 +347,12 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             w.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv_l, __uint_as_float(r[8 * v + 5]) * inv_l);
             w.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv_l, __uint_as_float(r[8 * v + 7]) * inv_l);
             dst[v] = w;
+            if (p.scat_n > 0) {
+              const int peer = q_row / p.scat_ll, lr = q_row - peer * p.scat_ll;
+              __nv_bfloat16* srow = reinterpret_cast<__nv_bfloat16*>(p.scat[peer]) +
+                                    ((int64_t)batch * p.scat_ll + lr) * p.scat_ld + p.scat_col + head * 128;
+              reinterpret_cast<uint4*>(srow + c * 32)[v] = w;
+            }
           }
         }
       }
@@ -380,10 +392,10 @@ size_t flash_fwd_smem_bytes() { return sizeof(FwdSmem) + 1024; }
 
 int64_t flash_lse_pad(int64_t L) { return (L + 255) / 256 * 256; }
 
-// Writes O (same layout rules as q) and the log2-domain LSE [B, H, Lpad] (fp32),
-// Lpad = Lq rounded up to a multiple of 256 (padding rows hold +inf).
-void flash_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
-               double scale) {
+// Launches the forward; `scat` (optional) adds the owner-rank copy of every output row.
+static void flash_fwd_launch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
+                             at::Tensor& lse, double scale, const std::vector<int64_t>& scat, int64_t scat_ld,
+                             int64_t scat_col) {
   check_bhld(q, "q");
   check_bhld(k, "k");
   check_bhld(v, "v");
@@ -413,11 +425,38 @@ void flash_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at
   p.Lpad = has_lse ? (int)lse.size(2) : 0;
   p.scale_log2 = (float)(scale * 1.4426950408889634);
   p.status = device_status_ptr(q.get_device());
+  p.scat_n = (int)scat.size();
+  TORCH_CHECK(p.scat_n <= 16, "at most 16 scatter targets");
+  for (int i = 0; i < 16; ++i) p.scat[i] = i < p.scat_n ? scat[i] : 0;
+  p.scat_ll = p.scat_n > 0 ? Lq / p.scat_n : 1;
+  p.scat_ld = scat_ld;
+  p.scat_col = (int)scat_col;
+  if (p.scat_n > 0) {
+    TORCH_CHECK(Lq % p.scat_n == 0, "Lq must divide over the scatter targets");
+    TORCH_CHECK(scat_ld % 8 == 0 && scat_col % 8 == 0, "scatter row stride / column must be multiples of 8");
+    for (int i = 0; i < p.scat_n; ++i) TORCH_CHECK(scat[i] % 16 == 0, "scatter targets must be 16-byte aligned");
+  }
   const size_t smem = flash_fwd_smem_bytes();
   C10_CUDA_CHECK(cudaFuncSetAttribute(flash_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((Lq + 2 * kTileM - 1) / (2 * kTileM), H, B);
   flash_fwd_kernel<<<grid, 384, smem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Writes O (same layout rules as q) and the log2-domain LSE [B, H, Lpad] (fp32),
+// Lpad = Lq rounded up to a multiple of 256 (padding rows hold +inf).
+void flash_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
+               double scale) {
+  flash_fwd_launch(q, k, v, o, lse, scale, {}, 0, 0);
+}
+
+// flash_fwd that also stores every output row into the [B*Ll, ld] row buffer of the rank that
+// owns the row (scatter[r] = that rank's buffer address, Ll = Lq / #ranks), at columns
+// col + head * 128 -- the reverse all-to-all of context parallelism fused into the epilogue.
+void flash_fwd_scatter(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
+                       double scale, std::vector<int64_t> scatter, int64_t ld, int64_t col) {
+  TORCH_CHECK(!scatter.empty(), "scatter targets required");
+  flash_fwd_launch(q, k, v, o, lse, scale, scatter, ld, col);
 }
 
 }  // namespace dmad

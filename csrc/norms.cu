@@ -24,14 +24,6 @@ namespace {
 
 // Row kernels are instantiated for the number of 8-element vectors each thread
 // holds (VEC) and the block size (TH); rows of up to 8192 columns are covered.
-#define DMAD_ROW_DISPATCH(nvec, ...)                                        \
-  [&] {                                                                     \
-    if ((nvec) <= 128) { constexpr int VEC = 1, TH = 128; __VA_ARGS__(); }  \
-    else if ((nvec) <= 256) { constexpr int VEC = 2, TH = 128; __VA_ARGS__(); } \
-    else if ((nvec) <= 512) { constexpr int VEC = 2, TH = 256; __VA_ARGS__(); } \
-    else if ((nvec) <= 768) { constexpr int VEC = 3, TH = 256; __VA_ARGS__(); } \
-    else { constexpr int VEC = 4, TH = 256; __VA_ARGS__(); }                \
-  }()
 
 struct ModSpec {
   const float* a;   // [G, D] fp32 (row stride a_sg; 0 = shared row) or nullptr

@@ -32,9 +32,10 @@ from ..algorithms import (CriticHeads, GapRouter, TrigFlowScaling, UniformShift,
                           ema_exp_coefficient, generator_linear_loss, rf_to_trig_time, trig_to_rf_time)
 from ..algorithms.dmad import band_of_cdf, critic_accuracies
 from ..models.wan import WanConfig, WanModel, WAN_1P3B
-from ..ops.optim import FusedAdamW, clip_grad_scale
+from ..ops.optim import FusedAdamW
 from ..parallel.dist import broadcast_module
 from ..parallel.dp import GradSync
+from ..parallel.zero import ShardedAdamW
 
 
 @dataclass
@@ -83,6 +84,12 @@ class WanDMADConfig:
     dcm_timestep_shift: float = 5.0
     # "dmad": two-head GAN critic (this model); "dmd": rCM's DMD with a denoising fake score
     critic_mode: str = "dmad"
+    # "sharded": flat symmetric buffers + one fused reduce-scatter / AdamW / all-gather kernel per
+    # step (fp32 optimiser state sharded over the ranks); "replicated": NCCL all-reduce of the
+    # gradients, then the same multi-tensor AdamW on every rank
+    dp_optimizer: str = "sharded"
+    dp_multicast: bool = True
+    dp_sync_timeout_s: float = 120.0
 
 
 class WanDMAD(nn.Module):
@@ -127,15 +134,32 @@ class WanDMAD(nn.Module):
         self.device = device
         # optimisers; the student's optimiser also advances the fp32 EMA copy in the same kernel pass
         s_params = [p for p in self.net.parameters() if p.requires_grad]
-        self.ema_params = [p.detach().float().clone() for p in s_params] if cfg.ema_enabled else None
-        self.ema_coef = ema_exp_coefficient(cfg.ema_rate)
-        self.opt_student = FusedAdamW(s_params, lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
-                                      weight_decay=cfg.weight_decay, ema=self.ema_params)
         c_params = [p for p in self.net_fake_score.parameters() if p.requires_grad] + list(self.critic_heads.parameters())
-        self.opt_critic = FusedAdamW(c_params, lr=cfg.critic_lr, betas=cfg.betas, eps=cfg.eps,
-                                     weight_decay=cfg.weight_decay)
-        self.sync_student = GradSync(s_params)
-        self.sync_critic = GradSync(c_params)
+        self.ema_coef = ema_exp_coefficient(cfg.ema_rate)
+        if cfg.dp_optimizer == "sharded":
+            kw = dict(betas=cfg.betas, eps=cfg.eps, weight_decay=cfg.weight_decay, use_multicast=cfg.dp_multicast,
+                      sync_timeout_s=cfg.dp_sync_timeout_s)
+            self.opt_student = ShardedAdamW(s_params, lr=cfg.lr, ema=cfg.ema_enabled, **kw)
+            self.opt_critic = ShardedAdamW(c_params, lr=cfg.critic_lr, **kw)
+            self.ema_params = None
+            self.sync_student = GradSync(s_params, enabled=False)
+            self.sync_critic = GradSync(c_params, enabled=False)
+        elif cfg.dp_optimizer == "replicated":
+            self.ema_params = [p.detach().float().clone() for p in s_params] if cfg.ema_enabled else None
+            self.opt_student = FusedAdamW(s_params, lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
+                                          weight_decay=cfg.weight_decay, ema=self.ema_params)
+            self.opt_critic = FusedAdamW(c_params, lr=cfg.critic_lr, betas=cfg.betas, eps=cfg.eps,
+                                         weight_decay=cfg.weight_decay)
+            self.sync_student = GradSync(s_params)
+            self.sync_critic = GradSync(c_params)
+        else:
+            raise ValueError(f"unknown dp_optimizer {cfg.dp_optimizer!r}")
+
+    def ema_weights(self) -> list[torch.Tensor] | None:
+        """Full fp32 EMA of the student's trainable parameters (collective when sharded)."""
+        if isinstance(self.opt_student, ShardedAdamW):
+            return self.opt_student.full_ema()
+        return self.ema_params
 
     # ------------------------------------------------------------------ schedule (rcm :297-311)
     def is_student_phase(self, it: int) -> bool:
@@ -188,6 +212,11 @@ class WanDMAD(nn.Module):
             feats = net(xin, ts, context, stop_after_block=len(net.blocks) - 1)
             x0 = None
         d_real, d_teacher = self.critic_heads.pooled(feats)
+        cp = net.cp
+        if cp is not None and cp.world > 1:
+            # mean over this rank's tokens, summed over the CP group / cp (dmad :338-339)
+            d_real = cp.all_reduce_sum(d_real) / cp.world
+            d_teacher = cp.all_reduce_sum(d_teacher) / cp.world
         return x0, d_real, d_teacher
 
     # ------------------------------------------------------------------ backward simulation (rcm :514-542)
@@ -246,9 +275,8 @@ class WanDMAD(nn.Module):
             self._set_critic_grad(True)
             self.net_fake_score.checkpoint_blocks = saved
         self.sync_student.sync()
-        scale = clip_grad_scale(self.opt_student.params, cfg.grad_clip) if cfg.grad_clip else None
         beta = self.ema_beta(self.effective_iteration(it)) if cfg.ema_enabled else None
-        self.opt_student.step(grad_scale=scale, ema_beta=beta)
+        self.opt_student.step(ema_beta=beta, max_grad_norm=cfg.grad_clip)
         self.opt_student.zero_grad()
         out = {"dmad_g_loss": loss.detach().mean(), "dmad_g_d_real": d_real_G.detach().mean(),
                "dmad_g_d_teacher": d_teacher_G.detach().mean(), "n_sim": n_sim}
@@ -280,8 +308,7 @@ class WanDMAD(nn.Module):
         bce = critic_bce_loss(d_real_T.detach(), d_real_G.detach(), d_teacher_Q.detach(), d_teacher_G.detach())
         self.gap.update(d_real_T.detach(), d_real_Q.detach(), self.gap_band(D_time), self.gap_band(D_time))
         self.sync_critic.sync()
-        scale = clip_grad_scale(self.opt_critic.params, cfg.grad_clip) if cfg.grad_clip else None
-        self.opt_critic.step(grad_scale=scale)
+        self.opt_critic.step(max_grad_norm=cfg.grad_clip)
         self.opt_critic.zero_grad()
         out = {"dmad_d_loss": bce.mean(), "n_sim": n_sim}
         out.update(critic_accuracies(d_real_T, d_real_G, d_teacher_Q, d_teacher_G))

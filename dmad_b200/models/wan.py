@@ -131,28 +131,35 @@ class WanBlock(nn.Module):
         return [self.self_attn.qkv, self.self_attn.o, self.cross_attn.q, self.cross_attn.kv, self.cross_attn.o,
                 getattr(self.ffn, "0"), getattr(self.ffn, "2")]
 
-    def forward(self, x, e0, context, cos, sin, B, L, rpg):
-        """x: [B*L, D] bf16; e0: [G, 6, D] fp32; context: [B*Lc, D] bf16."""
+    def forward(self, x, e0, context, cos, sin, B, L, rpg, cp=None):
+        """x: [B*L, D] bf16 (L = this rank's tokens under context parallelism); e0: [G, 6, D] fp32;
+        context: [B*Lc, D] bf16; rpg: rows per modulation group (int) or an int32 group index per row."""
         cfg = self.cfg
         D, H = cfg.dim, cfg.num_heads
         Lc = context.shape[0] // B
+        grp = {"gidx": rpg} if torch.is_tensor(rpg) else {"rows_per_group": rpg}
         e = self.modulation.float()[0] + e0  # [G, 6, D]
-        h = ops.ln_mod(x, e[:, 1], e[:, 0], a_add=1.0, rows_per_group=rpg, eps=cfg.eps)
+        h = ops.ln_mod(x, e[:, 1], e[:, 0], a_add=1.0, eps=cfg.eps, **grp)
         qkv = self.self_attn.qkv(h)
-        a = self_attention_core(qkv, self.self_attn.norm_q.weight, self.self_attn.norm_k.weight, cos, sin, B, L, H,
-                                cfg.eps)
+        if cp is not None and cp.world > 1:
+            from ..parallel.cp import self_attention_cp
+            a = self_attention_cp(qkv, self.self_attn.norm_q.weight, self.self_attn.norm_k.weight, cos, sin, B, H,
+                                  cfg.eps, cp)
+        else:
+            a = self_attention_core(qkv, self.self_attn.norm_q.weight, self.self_attn.norm_k.weight, cos, sin, B, L,
+                                    H, cfg.eps)
         y = self.self_attn.o(a)
-        x = ops.gate_residual(x, y, e[:, 2], rows_per_group=rpg)
+        x = ops.gate_residual(x, y, e[:, 2], **grp)
         h3 = ops.layer_norm_affine(x, self.norm3.weight, self.norm3.bias, cfg.eps) if self.norm3 is not None else x
         cq = self.cross_attn.q(h3)
         ckv = self.cross_attn.kv(context)
         c = cross_attention_core(cq, ckv, self.cross_attn.norm_q.weight, self.cross_attn.norm_k.weight, B, L, Lc, H,
                                  cfg.eps)
         x = x + self.cross_attn.o(c)
-        h2 = ops.ln_mod(x, e[:, 4], e[:, 3], a_add=1.0, rows_per_group=rpg, eps=cfg.eps)
+        h2 = ops.ln_mod(x, e[:, 4], e[:, 3], a_add=1.0, eps=cfg.eps, **grp)
         f = ops.gelu_tanh(getattr(self.ffn, "0")(h2))
         y2 = getattr(self.ffn, "2")(f)
-        return ops.gate_residual(x, y2, e[:, 5], rows_per_group=rpg)
+        return ops.gate_residual(x, y2, e[:, 5], **grp)
 
 
 class _Head(nn.Module):
@@ -171,7 +178,8 @@ class _Head(nn.Module):
         m = self.modulation.float()[0]  # [2, D]
         shift = m[0][None] + e
         scale = m[1][None] + e
-        h = ops.ln_mod(x, scale, shift, a_add=1.0, rows_per_group=rpg, eps=self.cfg.eps)
+        grp = {"gidx": rpg} if torch.is_tensor(rpg) else {"rows_per_group": rpg}
+        h = ops.ln_mod(x, scale, shift, a_add=1.0, eps=self.cfg.eps, **grp)
         # the reference runs the head under fp32 autocast
         return F.linear(h.float(), self.head.weight.float(), self.head.bias.float())
 
@@ -192,6 +200,7 @@ class WanModel(nn.Module):
         self.head = _Head(cfg)
         self.checkpoint_blocks = 0  # activation-checkpoint the first N blocks
         self._rope_cache: dict = {}
+        self.cp = None  # ContextParallel (sequence sharding) or None
         self.init_weights()
 
     # --------------------------------------------------------------- init (wan2pt1.py:839-880)
@@ -266,6 +275,12 @@ class WanModel(nn.Module):
         where features is the token output of that block (the critic's feature tap).  With
         ``stop_after_block`` the forward stops after that block and returns only its features."""
         cfg = self.cfg
+        cp = self.cp if (self.cp is not None and self.cp.world > 1) else None
+        if cp is not None and cp.broadcast_inputs:
+            # every rank of the CP group works on rank 0's sample (wan2pt1.py:723-733)
+            x_B_C_T_H_W = cp.broadcast(x_B_C_T_H_W)
+            timesteps_B_T = cp.broadcast(timesteps_B_T)
+            crossattn_emb = cp.broadcast(crossattn_emb)
         B = x_B_C_T_H_W.shape[0]
         wdt = self.patch_embedding.weight.dtype
         x, (T, H, W) = self.patchify(x_B_C_T_H_W.to(wdt))
@@ -274,28 +289,48 @@ class WanModel(nn.Module):
             timesteps_B_T = timesteps_B_T[:, None]
         uniform = timesteps_B_T.shape[1] == 1
         assert uniform or timesteps_B_T.shape[1] == T, "timesteps must be [B, 1] or [B, T]"
-        rpg = L if uniform else H * W
+        cos, sin = self.rope_tables(T, H, W, x.device)
+        Ll, r0 = L, 0
+        if cp is not None:
+            assert L % cp.world == 0, f"L = T*H*W = {L} must be divisible by cp = {cp.world}"
+            Ll = L // cp.world
+            r0 = cp.rank * Ll
+            x = x.view(B, L, -1)[:, r0:r0 + Ll].reshape(B * Ll, -1)
+            cos, sin = cos[r0:r0 + Ll].contiguous(), sin[r0:r0 + Ll].contiguous()
+        if uniform:
+            rpg = Ll
+        elif cp is None:
+            rpg = H * W
+        else:  # per-frame modulation rows: group = b * T + global_row // (H*W)
+            gr = torch.arange(r0, r0 + Ll, device=x.device) // (H * W)
+            rpg = (torch.arange(B, device=x.device)[:, None] * T + gr[None]).reshape(-1).int()
         x = F.linear(x, self.patch_embedding.weight, self.patch_embedding.bias)
         e, e0 = self.time_embed(timesteps_B_T.reshape(-1))
         context = self.text_embed(crossattn_emb)
-        cos, sin = self.rope_tables(T, H, W, x.device)
         feats = None
         nblocks = len(self.blocks) if stop_after_block is None else stop_after_block + 1
         for i in range(nblocks):
             blk = self.blocks[i]
             if self.training and torch.is_grad_enabled() and i < self.checkpoint_blocks:
-                x = checkpoint(blk, x, e0, context, cos, sin, B, L, rpg, use_reentrant=False)
+                x = checkpoint(blk, x, e0, context, cos, sin, B, Ll, rpg, cp, use_reentrant=False)
             else:
-                x = blk(x, e0, context, cos, sin, B, L, rpg)
+                x = blk(x, e0, context, cos, sin, B, Ll, rpg, cp)
             if feature_hook_block is not None and i == (feature_hook_block % len(self.blocks)):
                 feats = x
         if stop_after_block is not None:
-            return x.view(B, L, cfg.dim)
+            return x.view(B, Ll, cfg.dim)
         out = self.head(x, e, rpg)
+        if cp is not None:
+            out = cp.gather(out.view(B, Ll, -1), dim=1).reshape(B * L, -1)
         out = self.unpatchify(out, B, (T, H, W))
         if feature_hook_block is not None:
-            return out, feats.view(B, L, cfg.dim)
+            return out, feats.view(B, Ll, cfg.dim)
         return out
+
+    def enable_context_parallel(self, cp):
+        """Shard the token sequence over ``cp`` (a ``parallel.cp.ContextParallel``); None disables.
+        Features returned for the critic are this rank's token slice (pool with ``cp.all_reduce_sum``)."""
+        self.cp = cp
 
     # --------------------------------------------------------------- utilities
     def seg_linears(self):

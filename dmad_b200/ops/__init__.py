@@ -59,7 +59,7 @@ def check_device_status(device: int | None = None) -> None:
         raise RuntimeError(f"dmad kernel reported a bounded-wait failure: {names.get(code, code)} (code {code})")
 
 
-from .attention import flash_attention, attention_reference  # noqa: E402
+from .attention import flash_attention, attention_reference, flash_attention_jvp, attention_jvp_reference  # noqa: E402
 from .norm import ln_mod, gate_residual, qk_norm_rope, rope, rope_apply, rms_norm, layer_norm_affine  # noqa: E402
 from .activation import gelu_tanh  # noqa: E402
 from .temb import sinusoidal_embedding, small_linear  # noqa: E402
@@ -70,6 +70,8 @@ __all__ = [
     "device_status",
     "check_device_status",
     "flash_attention",
+    "flash_attention_jvp",
+    "attention_jvp_reference",
     "attention_reference",
     "ln_mod",
     "gate_residual",

@@ -63,3 +63,71 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: fl
     if not _supported(q, k, v):
         raise ValueError(f"flash_attention: need CUDA bf16 [B, L, H, 128], got {tuple(q.shape)} {q.dtype}")
     return _FlashAttn.apply(q, k, v, scale)
+
+
+def _bhld_ok(t):
+    return t.stride(-1) == 1 and all(s % 8 == 0 for s in t.stride()[:-1]) and t.data_ptr() % 16 == 0
+
+
+class _FlashAttnJvp(torch.autograd.Function):
+    """(O, tO) in one tcgen05 pass; the gradient flows through O only (tangents are detached), by
+    the plain flash backward on the LSE the JVP kernel writes."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, tq, tk, tv, scale):
+        B, Lq, H, D = q.shape
+        o = torch.empty((B, Lq, H, D), dtype=q.dtype, device=q.device)
+        to = torch.empty_like(o)
+        lse = torch.empty((B, H, _lse_pad(Lq)), dtype=torch.float32, device=q.device)
+        fix = lambda t: t if t is None or _bhld_ok(t) else t.contiguous()  # noqa: E731
+        tq, tk, tv = fix(tq.detach()), fix(tk.detach() if tk is not None else None), fix(
+            tv.detach() if tv is not None else None)
+        ext().flash_jvp_fwd(q, k, v, tq, tk, tv, o, to, lse, float(scale))
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.scale = scale
+        ctx.mark_non_differentiable(to)
+        return o, to
+
+    @staticmethod
+    def backward(ctx, do, _dto):
+        q, k, v, o, lse = ctx.saved_tensors
+        do = do.contiguous() if do.stride(-1) != 1 or do.stride(1) % 8 else do
+        dq = torch.empty_like(q, memory_format=torch.contiguous_format)
+        dk = torch.empty(k.shape, dtype=k.dtype, device=k.device)
+        dv = torch.empty(v.shape, dtype=v.dtype, device=v.device)
+        dd = torch.empty_like(lse)
+        ext().flash_bwd(q, k, v, o, do, lse, dq, dk, dv, dd, float(ctx.scale))
+        return dq, dk, dv, None, None, None, None
+
+
+def attention_jvp_reference(q, k, v, tq, tk=None, tv=None, scale=None):
+    """fp32 (O, tO) of softmax attention and its forward-mode tangent ([B, L, H, D]; oracle / CPU)."""
+    scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    tr = lambda t: t.float().transpose(1, 2)  # noqa: E731
+    qf, kf, vf, tqf = tr(q), tr(k), tr(v), tr(tq)
+    s = qf @ kf.transpose(-1, -2) * scale
+    ts = tqf @ kf.transpose(-1, -2)
+    if tk is not None:
+        ts = ts + qf @ tr(tk).transpose(-1, -2)
+    ts = ts * scale
+    p = torch.softmax(s, dim=-1)
+    o = p @ vf
+    pts = p * ts
+    to = pts @ vf - pts.sum(-1, keepdim=True) * o
+    if tv is not None:
+        to = to + p @ tr(tv)
+    return o.transpose(1, 2).to(q.dtype), to.transpose(1, 2).to(q.dtype)
+
+
+def flash_attention_jvp(q, k, v, tq, tk=None, tv=None, scale: float | None = None):
+    """(softmax(q k^T s) v, its tangent along (tq, tk, tv)) for [B, L, H, 128] bf16 tensors.
+
+    CUDA: one sm_100a tcgen05 kernel (S, tS, O, A+B accumulators in TMEM); differentiable in O.
+    CPU: fp32 PyTorch math.  ``tk`` / ``tv`` = None means a zero tangent (no GEMM is spent on it).
+    """
+    scale = float(scale) if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    if not q.is_cuda:
+        return attention_jvp_reference(q, k, v, tq, tk, tv, scale)
+    if not _supported(q, k, v) or tq.dtype != q.dtype:
+        raise ValueError(f"flash_attention_jvp: need CUDA bf16 [B, L, H, 128], got {tuple(q.shape)} {q.dtype}")
+    return _FlashAttnJvp.apply(q, k, v, tq, tk, tv, scale)

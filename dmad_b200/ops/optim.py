@@ -43,14 +43,18 @@ class FusedAdamW:
         return idx
 
     @torch.no_grad()
-    def step(self, grad_scale: torch.Tensor | None = None, ema_beta: float | None = None):
-        """One AdamW step.  ``grad_scale``: optional device scalar multiplied into the grads
-        (clipping).  ``ema_beta``: when given (and an EMA list was attached), the EMA copies
-        are advanced in the same kernel pass."""
+    def step(self, grad_scale: torch.Tensor | None = None, ema_beta: float | None = None,
+             max_grad_norm: float | None = None):
+        """One AdamW step.  ``grad_scale``: optional device scalar multiplied into the grads;
+        ``max_grad_norm``: clip by the global gradient norm (computes ``grad_scale``).
+        ``ema_beta``: when given (and an EMA list was attached), the EMA copies are advanced in
+        the same kernel pass."""
         self.step_count += 1
         idx = self._lists()
         if not idx:
             return
+        if grad_scale is None and max_grad_norm:
+            grad_scale = clip_grad_scale([self.params[i] for i in idx], max_grad_norm)
         b1, b2 = self.betas
         on_cuda = self.params[idx[0]].is_cuda
         if not on_cuda:

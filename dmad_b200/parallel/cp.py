@@ -1,0 +1,300 @@
+"""Ulysses context parallelism (sequence sharding with a head all-to-all around attention).
+
+Every rank of a context-parallel (CP) group holds the contiguous token slice
+``[r*Ll, (r+1)*Ll)`` of every sample (``Ll = L / cp``).  Everything but self-attention is
+row-local.  Self-attention exchanges sequence shards for head shards (each rank then attends
+over the full sequence with ``H / cp`` heads) and back.  Parity: the reference's
+``DistributedAttention`` / ``_SeqAllToAllQKV`` / ``_SeqAllToAll``
+(train/wan/rcm/utils/a2a_cp.py:43-258), ``split_inputs_cp`` / ``cat_outputs_cp(_with_grad)``
+(train/wan/rcm/utils/context_parallel.py:25-210) and the CP handling of ``WanModel.forward``
+(train/wan/rcm/networks/wan2pt1.py:723-823).
+
+Two implementations of the exchange, selected by ``impl``:
+
+* ``"fused"`` -- this framework's kernels over NVLink peer memory.  The q/k RMSNorm + RoPE
+  kernel stores q, k and v straight into the head-sharded receive slot of the rank that owns
+  each head; the flash-attention epilogue stores each output row into its owner's row buffer
+  as well as locally; the backward uses plain peer-copy kernels.  Each exchange ends with the
+  bounded-wait ``PeerSync`` barrier.  Receive slots come from one symmetric arena with two
+  slots used alternately by successive exchanges: a rank pushes into slot s again only after
+  the barrier of the exchange in between, which every peer enters after the kernels that read
+  slot s (stream order), so no push overwrites data that is still being read.
+* ``"nccl"`` -- ``all_to_all_single`` on permuted copies, as the reference does (the baseline).
+
+On CPU (gloo ranks, tests) only ``"nccl"`` is available and attention runs in fp32 PyTorch.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+
+from .dist import is_distributed
+from .symm import PeerSync, SymmBuffer
+
+
+class ContextParallel:
+    def __init__(self, group=None, impl: str = "fused", device=None, timeout_s: float = 120.0,
+                 broadcast_inputs: bool = True):
+        if impl not in ("fused", "nccl"):
+            raise ValueError(f"unknown context-parallel impl {impl!r}")
+        self.group = group if group is not None else (dist.group.WORLD if is_distributed() else None)
+        self.world = dist.get_world_size(self.group) if self.group is not None else 1
+        self.rank = dist.get_rank(self.group) if self.group is not None else 0
+        self.device = torch.device(device) if device is not None else (
+            torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu"))
+        if self.device.type != "cuda":
+            impl = "nccl"
+        self.impl = impl
+        self.timeout_s = timeout_s
+        self.broadcast_inputs = broadcast_inputs
+        self._arena: SymmBuffer | None = None
+        self._slot_elems = 0
+        self._op = 0
+        self.sync = PeerSync(self.device, self.group, timeout_s) if impl == "fused" else None
+
+    # ------------------------------------------------------------------ symmetric receive slots
+    def reserve(self, elems: int):
+        """Make both slots hold at least ``elems`` bf16 elements (collective; same value on all ranks)."""
+        elems = -(-elems // 64) * 64
+        if elems <= self._slot_elems:
+            return
+        if self._arena is not None:
+            torch.cuda.synchronize(self.device)
+        self._arena = SymmBuffer(2 * elems, torch.bfloat16, self.device, self.group, zero=False)
+        self._slot_elems = elems
+
+    def slot(self, elems: int):
+        """(local view [elems], peer addresses) of the next slot."""
+        self.reserve(elems)
+        s = self._op & 1
+        self._op += 1
+        base = s * self._slot_elems
+        view = self._arena.tensor[base:base + elems]
+        ptrs = [p + base * 2 for p in self._arena.ptrs]
+        return view, ptrs
+
+    # ------------------------------------------------------------------ token sharding (cold path)
+    def split(self, x: torch.Tensor, dim: int = 1) -> torch.Tensor:
+        n = x.shape[dim]
+        assert n % self.world == 0, f"sequence length {n} must be divisible by cp={self.world}"
+        ll = n // self.world
+        return x.narrow(dim, self.rank * ll, ll).contiguous()
+
+    def gather(self, x: torch.Tensor, dim: int = 1) -> torch.Tensor:
+        """all_gather along ``dim``; differentiable (each rank keeps the gradient of its own slice)."""
+        if self.world == 1:
+            return x
+        return _GatherSeq.apply(x, dim, self)
+
+    def all_reduce_sum(self, t: torch.Tensor) -> torch.Tensor:
+        """Sum over the CP group; the gradient passes through unchanged (each rank's local term)."""
+        if self.world == 1:
+            return t
+        return _AllReduceSum.apply(t, self)
+
+    def broadcast(self, t: torch.Tensor, src_rank_in_group: int = 0) -> torch.Tensor:
+        """Values of the group's rank ``src_rank_in_group``; the gradient flows to the local input
+        unchanged (context_parallel.py:167-190 ``item + (bcast - item.detach())``)."""
+        if self.world == 1:
+            return t
+        return _Broadcast.apply(t, src_rank_in_group, self)
+
+    # ------------------------------------------------------------------ NCCL all-to-all (baseline)
+    def a2a_seq_to_head(self, x: torch.Tensor, B: int, n: int, H: int, hd: int) -> torch.Tensor:
+        """[B*Ll, n*H*hd] rows -> [B, L, n, Hl, hd] (NCCL)."""
+        cp, Hl = self.world, H // self.world
+        Ll = x.shape[0] // B
+        send = x.reshape(B, Ll, n, cp, Hl, hd).permute(3, 0, 1, 2, 4, 5).contiguous()
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=self.group)
+        return recv.permute(1, 0, 2, 3, 4, 5).reshape(B, cp * Ll, n, Hl, hd)
+
+    def a2a_head_to_seq(self, y: torch.Tensor, B: int, n: int) -> torch.Tensor:
+        """[B, L, n, Hl, hd] -> [B*Ll, n*H*hd] rows (NCCL)."""
+        cp = self.world
+        _, L, _, Hl, hd = y.shape
+        Ll = L // cp
+        send = y.reshape(B, cp, Ll, n, Hl, hd).permute(1, 0, 2, 3, 4, 5).contiguous()
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=self.group)
+        # recv[src] = rows of my slice, heads of rank src
+        return recv.permute(1, 2, 3, 0, 4, 5).reshape(B * Ll, n * cp * Hl * hd)
+
+
+class _GatherSeq(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, dim, cp):
+        ctx.dim, ctx.cp = dim, cp
+        parts = [torch.empty_like(x) for _ in range(cp.world)]
+        dist.all_gather(parts, x.contiguous(), group=cp.group)
+        return torch.cat(parts, dim=dim)
+
+    @staticmethod
+    def backward(ctx, g):
+        cp = ctx.cp
+        ll = g.shape[ctx.dim] // cp.world
+        return g.narrow(ctx.dim, cp.rank * ll, ll).contiguous(), None, None
+
+
+class _Broadcast(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, t, src_in_group, cp):
+        out = t.detach().clone().contiguous()
+        src = dist.get_global_rank(cp.group, src_in_group) if cp.group is not dist.group.WORLD else src_in_group
+        dist.broadcast(out, src=src, group=cp.group)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        return g, None, None
+
+
+class _AllReduceSum(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, t, cp):
+        t = t.clone()
+        dist.all_reduce(t, group=cp.group)
+        return t
+
+    @staticmethod
+    def backward(ctx, g):
+        return g, None
+
+
+# ---------------------------------------------------------------------- self-attention under CP
+class _SelfAttnCP(torch.autograd.Function):
+    """qkv [B*Ll, 3D] (pre-norm, local rows) -> attention output [B*Ll, D] over the full sequence.
+
+    cos / sin: RoPE tables of this rank's Ll rows."""
+
+    @staticmethod
+    def forward(ctx, qkv, wq, wk, cos, sin, B, H, eps, cp):
+        from .. import ops
+        from ..ops import attention as attn_ops
+        from ..ops import norm as norm_ops
+
+        e = ops.ext()
+        R, D3 = qkv.shape
+        D = D3 // 3
+        hd = D // H
+        Hl = H // cp.world
+        Ll = R // B
+        L = Ll * cp.world
+        scale = 1.0 / math.sqrt(hd)
+        if cp.impl == "fused":
+            slot, ptrs = cp.slot(B * L * 3 * Hl * hd)
+            rq = torch.empty(R, dtype=torch.float32, device=qkv.device)
+            rk = torch.empty_like(rq)
+            e.cp_qkv_push(qkv, ptrs, wq, wk, cos, sin, rq, rk, B, D, hd, cp.rank, eps)
+            cp.sync()
+            qkv_g = slot.view(B, L, 3, Hl, hd)
+            if any(ctx.needs_input_grad):
+                qkv_g = qkv_g.clone()  # kept for backward; the slot is reused two exchanges later
+        else:
+            qk, rq, rk = norm_ops.qk_norm_rope(qkv, wq, wk, cos, sin, D, hd, eps)
+            rows = torch.cat([qk, qkv[:, 2 * D:]], dim=1)
+            qkv_g = cp.a2a_seq_to_head(rows, B, 3, H, hd)
+        q_g, k_g, v_g = qkv_g[:, :, 0], qkv_g[:, :, 1], qkv_g[:, :, 2]
+        o_g = torch.empty((B, L, Hl, hd), dtype=qkv.dtype, device=qkv.device)
+        lse = torch.empty((B, Hl, attn_ops._lse_pad(L)), dtype=torch.float32, device=qkv.device)
+        if cp.impl == "fused":
+            oslot, optrs = cp.slot(R * D)
+            e.flash_fwd_scatter(q_g, k_g, v_g, o_g, lse, scale, optrs, D, cp.rank * Hl * hd)
+            cp.sync()
+            out = oslot.view(R, D).clone()
+        else:
+            e.flash_fwd(q_g, k_g, v_g, o_g, lse, scale)
+            out = cp.a2a_head_to_seq(o_g.view(B, L, 1, Hl, hd), B, 1)
+        ctx.save_for_backward(qkv, wq, wk, cos, sin, rq, rk, qkv_g, o_g, lse)
+        ctx.cfg = (B, H, eps, scale, cp)
+        return out
+
+    @staticmethod
+    def backward(ctx, do):
+        from .. import ops
+
+        qkv, wq, wk, cos, sin, rq, rk, qkv_g, o_g, lse = ctx.saved_tensors
+        B, H, eps, scale, cp = ctx.cfg
+        e = ops.ext()
+        R, D3 = qkv.shape
+        D = D3 // 3
+        hd = D // H
+        Hl = H // cp.world
+        Ll = R // B
+        L = Ll * cp.world
+        do = do.contiguous()
+        if cp.impl == "fused":
+            dslot, dptrs = cp.slot(B * L * Hl * hd)
+            e.cp_seq_to_head(do, dptrs, B, D, 1, hd, cp.rank)
+            cp.sync()
+            do_g = dslot.view(B, L, Hl, hd)
+        else:
+            do_g = cp.a2a_seq_to_head(do, B, 1, H, hd)[:, :, 0]
+        dqkv_g = torch.empty((B, L, 3, Hl, hd), dtype=qkv.dtype, device=qkv.device)
+        dd = torch.empty_like(lse)
+        e.flash_bwd(qkv_g[:, :, 0], qkv_g[:, :, 1], qkv_g[:, :, 2], o_g, do_g, lse, dqkv_g[:, :, 0],
+                    dqkv_g[:, :, 1], dqkv_g[:, :, 2], dd, scale)
+        if cp.impl == "fused":
+            gslot, gptrs = cp.slot(R * 3 * D)
+            e.cp_head_to_seq([dqkv_g[:, :, 0], dqkv_g[:, :, 1], dqkv_g[:, :, 2]], gptrs, 3 * D, D, cp.rank)
+            cp.sync()
+            g_rows = gslot.view(R, 3 * D)
+        else:
+            g_rows = cp.a2a_head_to_seq(dqkv_g, B, 3)
+        dqkv = torch.empty_like(qkv)
+        dqkv[:, 2 * D:].copy_(g_rows[:, 2 * D:])
+        dwq = torch.zeros(D, dtype=torch.float32, device=qkv.device)
+        dwk = torch.zeros(D, dtype=torch.float32, device=qkv.device)
+        e.qk_norm_rope_bwd(g_rows[:, :D], g_rows[:, D:2 * D], qkv, dqkv, wq, wk, cos, sin, rq, rk, dwq, dwk, D, hd)
+        return dqkv, dwq, dwk, None, None, None, None, None, None
+
+
+def self_attention_cp(qkv, wq, wk, cos, sin, B, H, eps, cp: ContextParallel):
+    """Self-attention of the local rows ``qkv`` [B*Ll, 3D] against the whole CP-sharded sequence."""
+    if not qkv.is_cuda:
+        return _self_attention_cp_cpu(qkv, wq, wk, cos, sin, B, H, eps, cp)
+    return _SelfAttnCP.apply(qkv, wq.float().contiguous(), wk.float().contiguous(), cos, sin, B, H, eps, cp)
+
+
+def _self_attention_cp_cpu(qkv, wq, wk, cos, sin, B, H, eps, cp):
+    """fp32 PyTorch path (gloo ranks): the same exchange through differentiable all-to-alls."""
+    from ..ops import attention as attn_ops
+    from ..ops import norm as norm_ops
+
+    R, D3 = qkv.shape
+    D = D3 // 3
+    hd = D // H
+    q = norm_ops.ln_mod_reference(qkv[:, :D], wq.reshape(1, -1), None, 0.0, None, None, eps, True)
+    k = norm_ops.ln_mod_reference(qkv[:, D:2 * D], wk.reshape(1, -1), None, 0.0, None, None, eps, True)
+    q = norm_ops.rope_reference(q, cos, sin, hd)
+    k = norm_ops.rope_reference(k, cos, sin, hd)
+    rows = torch.cat([q, k, qkv[:, 2 * D:]], dim=1)
+    g = _A2ASeqToHead.apply(rows, B, 3, H, hd, cp)
+    o = attn_ops.attention_reference(g[:, :, 0], g[:, :, 1], g[:, :, 2])
+    return _A2AHeadToSeq.apply(o.unsqueeze(2), B, 1, H, cp)
+
+
+class _A2ASeqToHead(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, rows, B, n, H, hd, cp):
+        ctx.cfg = (B, n, H, cp)
+        return cp.a2a_seq_to_head(rows, B, n, H, hd)
+
+    @staticmethod
+    def backward(ctx, g):
+        B, n, H, cp = ctx.cfg
+        return cp.a2a_head_to_seq(g.contiguous(), B, n), None, None, None, None, None
+
+
+class _A2AHeadToSeq(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, y, B, n, H, cp):
+        ctx.cfg = (B, n, H, y.shape[-1], cp)
+        return cp.a2a_head_to_seq(y.contiguous(), B, n)
+
+    @staticmethod
+    def backward(ctx, g):
+        B, n, H, hd, cp = ctx.cfg
+        return cp.a2a_seq_to_head(g.contiguous(), B, n, H, hd), None, None, None, None

@@ -13,14 +13,15 @@ from .dist import get_world_size, is_distributed
 
 
 class GradSync:
-    def __init__(self, params, bucket_bytes: int = 256 << 20, group=None):
+    def __init__(self, params, bucket_bytes: int = 256 << 20, group=None, enabled: bool = True):
+        self.enabled = enabled
         self.params = [p for p in params if p.requires_grad]
         self.bucket_bytes = bucket_bytes
         self.group = group
 
     @torch.no_grad()
     def sync(self):
-        if not is_distributed() or get_world_size(self.group) == 1:
+        if not self.enabled or not is_distributed() or get_world_size(self.group) == 1:
             return
         world = get_world_size(self.group)
         by_dtype: dict = {}
