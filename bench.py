@@ -47,6 +47,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--count-launches", type=int, default=1)
     ap.add_argument("--profile", default=None, help="write a per-kernel time table of one cycle to this path")
+    ap.add_argument("--dp-optimizer", default="sharded", choices=["sharded", "replicated"],
+                    help="sharded: fused reduce-scatter/AdamW/all-gather kernel; replicated: NCCL all-reduce baseline")
     return ap.parse_args()
 
 
@@ -132,6 +134,16 @@ def count_my_kernels(fn, prefixes=("dmad",)) -> int:
     return n
 
 
+def _dp_desc(trainer, args):
+    if args.impl == "reference":
+        return "reference: NCCL gradient all-reduce + master-weight AdamW"
+    opt = getattr(trainer, "opt_student", None)
+    if args.dp_optimizer == "sharded" and opt is not None and hasattr(opt, "multicast"):
+        return "sharded fp32 state; fused reduce-scatter+AdamW+all-gather kernel (" + \
+            ("NVLS multimem" if opt.multicast else "P2P peer loads/stores") + ")"
+    return "replicated: NCCL all-reduce + multi-tensor AdamW"
+
+
 def main():
     args = parse()
     from dmad_b200.parallel.dist import barrier, get_rank, get_world_size, init_distributed, max_over_ranks
@@ -152,7 +164,7 @@ def main():
         from dmad_b200.models.wan import wan_config
 
         over = {"num_layers": args.layers} if args.layers else {}
-        cfg = WanDMADConfig(net=wan_config(args.model, **over))
+        cfg = WanDMADConfig(net=wan_config(args.model, **over), dp_optimizer=args.dp_optimizer)
         cfg.checkpoint_critic_blocks_student_phase = cfg.net.num_layers
         trainer = WanDMAD(cfg, device=device, dtype=torch.bfloat16, seed=0)
 
@@ -280,6 +292,7 @@ def main():
                    "global_batch": world, "seq_len": SEQ_LEN if headline_ok else None,
                    "latents": f"16x{args.frames}x60x104", "text": "512x4096",
                    "parallelism": f"dp{world}", "step": "1 generator + 1 critic DMAD iteration",
+                   "dp_optimizer": _dp_desc(trainer, args),
                    "l2": "flushed (write of a 252 MB buffer) before every timed step; inputs > L2"},
         "gen_latency_s_per_clip": gen_s,
         "e2e": e2e,

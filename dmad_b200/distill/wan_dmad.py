@@ -155,6 +155,45 @@ class WanDMAD(nn.Module):
         else:
             raise ValueError(f"unknown dp_optimizer {cfg.dp_optimizer!r}")
 
+    # ------------------------------------------------------------------ trainer interface
+    def phase_of(self, it: int) -> str:
+        return "student" if self.is_student_phase(it) else "critic"
+
+    def optimizers(self) -> dict:
+        return {"student": self.opt_student, "critic": self.opt_critic}
+
+    def context_parallel_nets(self) -> list:
+        return [n for n in (self.net, self.net_fake_score, self.net_teacher) if n is not None]
+
+    # ------------------------------------------------------------------ checkpoint state
+    def state_dicts(self) -> tuple[dict, dict | None]:
+        """(state every rank holds identically, this rank's optimiser shards or None)."""
+        shared = {"net": self.net.state_dict(), "net_fake_score": self.net_fake_score.state_dict(),
+                  "critic_heads": self.critic_heads.state_dict(), "gap": self.gap.state_dict()}
+        if isinstance(self.opt_student, ShardedAdamW):
+            return shared, {"opt_student": self.opt_student.state_dict(), "opt_critic": self.opt_critic.state_dict()}
+        shared["opt_student"] = self.opt_student.state_dict()
+        shared["opt_critic"] = self.opt_critic.state_dict()
+        shared["ema"] = self.ema_params
+        return shared, None
+
+    def load_state_dicts(self, shared: dict, per_rank: dict | None):
+        self.net.load_state_dict(shared["net"])
+        self.net_fake_score.load_state_dict(shared["net_fake_score"])
+        self.critic_heads.load_state_dict(shared["critic_heads"])
+        self.gap.load_state_dict(shared["gap"])
+        if isinstance(self.opt_student, ShardedAdamW):
+            if not per_rank or "opt_student" not in per_rank:
+                raise RuntimeError("checkpoint has no per-rank optimiser shards (saved with a replicated optimiser)")
+            self.opt_student.load_state_dict(per_rank["opt_student"])
+            self.opt_critic.load_state_dict(per_rank["opt_critic"])
+        else:
+            self.opt_student.load_state_dict(shared["opt_student"])
+            self.opt_critic.load_state_dict(shared["opt_critic"])
+            if self.ema_params is not None and shared.get("ema") is not None:
+                for d, s_ in zip(self.ema_params, shared["ema"]):
+                    d.copy_(s_)
+
     def ema_weights(self) -> list[torch.Tensor] | None:
         """Full fp32 EMA of the student's trainable parameters (collective when sharded)."""
         if isinstance(self.opt_student, ShardedAdamW):
