@@ -171,6 +171,8 @@ class WanDMAD(nn.Module):
         shared = {"net": self.net.state_dict(), "net_fake_score": self.net_fake_score.state_dict(),
                   "critic_heads": self.critic_heads.state_dict(), "gap": self.gap.state_dict()}
         if isinstance(self.opt_student, ShardedAdamW):
+            names = {id(p): n for n, p in self.net.named_parameters()}
+            shared["student_layout"] = self.opt_student.layout(names)
             return shared, {"opt_student": self.opt_student.state_dict(), "opt_critic": self.opt_critic.state_dict()}
         shared["opt_student"] = self.opt_student.state_dict()
         shared["opt_critic"] = self.opt_critic.state_dict()

@@ -132,13 +132,21 @@ class SegLinear(nn.Module):
 
     @torch.no_grad()
     def folded_weight(self):
-        """Weight with the spectral norm folded in (one power iteration from the stored u),
+        """Weight with the frozen-gain spectral norm folded in: per segment one power iteration
+        from the stored u (v = W^T u / |.|, u' = W v / |.|, sigma = u'^T W v), W * gain / sigma,
         as the release converter does (train/wan/scripts/dcp_to_pth_dmad.py:180-209)."""
-        was = self.training
-        self.train(False)
-        w = self.effective_weight().detach().clone()
-        self.train(was)
-        return w
+        if not self.sn_enabled:
+            return self.weight.detach().clone()
+        w = self.weight.detach().float().clone()
+        for i, (name, sl) in enumerate(self.seg_slices()):
+            if not bool(self.sn_mask[i]):
+                continue
+            ws = w[sl]
+            v = _l2n(ws.t() @ self.sn_u[sl].float())
+            u = _l2n(ws @ v)
+            sigma = torch.dot(u, ws @ v)
+            w[sl] = ws * (self.sn_gain[i].float() / sigma)
+        return w.to(self.weight.dtype)
 
     # ------------------------------------------------------------------ LoRA
     def enable_lora(self, rank: int, alpha: float | None = None, segments: Sequence[str] | None = None):

@@ -221,6 +221,16 @@ class ShardedAdamW:
             return None
         return self._gather(lambda g: g.ema)
 
+    def layout(self, names: dict | None = None) -> list[dict]:
+        """Flat-buffer layout of every group: shard length, world and (name, offset, shape) per parameter
+        (``names``: id(param) -> name), so full tensors can be rebuilt from the per-rank shards offline."""
+        out = []
+        for g in self.groups:
+            out.append({"dtype": str(g.dtype), "len": g.len, "world": self.world,
+                        "params": [((names or {}).get(id(p), str(i)), o, tuple(p.shape))
+                                   for i, (p, o) in enumerate(zip(g.params, g.offsets))]})
+        return out
+
     def state_dict(self):
         """This rank's shard state (save one file per rank, or gather with ``full_*``)."""
         return {"step": self.step_count, "lr": self.lr, "world": self.world, "rank": self.rank,
@@ -245,3 +255,20 @@ class ShardedAdamW:
                 g.pbuf.tensor.copy_(torch.cat(parts))
             else:
                 g.pbuf.tensor[g.off:g.off + g.len].copy_(new)
+
+
+def tensors_from_shards(layout: list[dict], rank_states: list[dict], key: str = "ema") -> dict:
+    """Rebuild full fp32 tensors (name -> tensor) from every rank's ``state_dict()`` shards
+    (``key``: "master", "ema", "exp_avg" or "exp_avg_sq"), e.g. to export the EMA offline."""
+    out = {}
+    for gi, g in enumerate(layout):
+        parts = [rs["shards"][gi][key] for rs in sorted(rank_states, key=lambda r: r["rank"])]
+        if any(p is None for p in parts):
+            raise KeyError(f"shard state {key!r} missing")
+        full = torch.cat([p.float().cpu() for p in parts])
+        for name, off, shape in g["params"]:
+            n = 1
+            for d in shape:
+                n *= d
+            out[name] = full[off:off + n].view(shape).clone()
+    return out

@@ -224,3 +224,39 @@ def test_train_cli_resume_matches_uninterrupted(tmp_path):
     assert lines[-1]["iteration"] == 6 and "dmad_g_loss" in lines[0]
     for (ra, wa, _), (rb, wb, _) in zip(res_a, res_b):
         assert torch.equal(torch.from_numpy(wa), torch.from_numpy(wb)), "resumed run diverged"
+
+
+def test_export_release_folds_sn_and_uses_ema(tmp_path):
+    """Train 4 tiny iterations in-process, export the EMA student with SN folded, and check the
+    plain (no SN, no LoRA) network reproduces the student's EMA forward."""
+    from dmad_b200.models.wan import WanConfig, WanModel
+    from dmad_b200.runtime.config import load_config
+    from dmad_b200.tools.export_release import build_student, export
+    from dmad_b200.train.trainer import DistillTrainer
+
+    cfg_path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "configs",
+                            "wan_1p3b_dmad.yaml")
+    cfg = load_config(cfg_path, _TINY + [f"training.output_dir={tmp_path}", "training.max_iters=4",
+                                         "training.save_every=4", "model.distill.ema_rate=0.5"])
+    tr = DistillTrainer(cfg)
+    tr.train()
+    ck = os.path.join(str(tmp_path), "checkpoint-000000004")
+    sd = export(ck, str(tmp_path / "release.pth"), use_ema=True, dtype=torch.float32)
+    assert all(k.startswith("net.") for k in sd) and not any("sn_" in k for k in sd)
+    plain = WanModel(WanConfig(dim=128, ffn_dim=256, num_heads=1, num_layers=2, text_dim=32, freq_dim=64))
+    plain.load_state_dict({k[4:]: v for k, v in sd.items()})
+    # reference: the trained student with its EMA weights, SN applied from the stored vectors
+    stud = build_student(cfg)
+    stud.load_state_dict(tr.model.net.state_dict())
+    ema = dict(zip([n for n, p in tr.model.net.named_parameters() if p.requires_grad], tr.model.ema_weights()))
+    with torch.no_grad():
+        for n, p in stud.named_parameters():
+            p.copy_(ema[n])
+    stud.eval()
+    plain.eval()
+    g = torch.Generator().manual_seed(0)
+    x, t, ctx = torch.randn(1, 16, 2, 4, 4, generator=g), torch.rand(1, 1, generator=g), torch.randn(1, 8, 32, generator=g)
+    with torch.no_grad():
+        a, b = stud(x, t, ctx), plain(x, t, ctx)
+    assert (a - b).abs().max().item() < 1e-3 * max(1.0, a.abs().max().item())
+    assert not torch.equal(ema[next(iter(ema))], tr.model.net.state_dict()[next(iter(ema))])
