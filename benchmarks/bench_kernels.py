@@ -37,6 +37,23 @@ def _reference_jvp():
         return None
     if root not in sys.path:
         sys.path.insert(0, root)
+    try:
+        import matplotlib.pyplot  # noqa: F401
+    except ImportError:
+        # the reference's mask module imports pyplot for a debug plot only; matplotlib is not in this
+        # image, so an empty stand-in module lets the (unmodified) kernel module import
+        import types
+
+        class _Stub(types.ModuleType):
+            def __getattr__(self, name):  # any attribute used only in annotations / plotting code
+                if name.startswith("__"):
+                    raise AttributeError(name)
+                return type(name, (), {})
+
+        for name in ("matplotlib", "matplotlib.pyplot", "matplotlib.patches"):
+            sys.modules.setdefault(name, _Stub(name))
+        sys.modules["matplotlib"].pyplot = sys.modules["matplotlib.pyplot"]
+        sys.modules["matplotlib"].patches = sys.modules["matplotlib.patches"]
     from rcm.utils.flash_attention_jvp_triton import attention
 
     return attention
@@ -63,7 +80,9 @@ def main():
     ap.add_argument("--H", type=int, default=12)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--only", default="all", choices=["all", "fwd", "bwd", "sdpa", "jvp", "ref_jvp"])
+    ap.add_argument("--only", default="all", choices=["all", "fwd", "bwd", "sdpa", "jvp", "ref_jvp", "gemm"])
+    ap.add_argument("--gemm", default="32760,8960,1536", help="M,N,K of the GEMM benchmark")
+    ap.add_argument("--rank", type=int, default=128, help="LoRA rank of the GEMM benchmark")
     a = ap.parse_args()
     from dmad_b200 import ops
 
@@ -116,6 +135,32 @@ def main():
                 qt, kt, vt, tqt, tkt, tvt = (t.transpose(1, 2).contiguous() for t in (q, k, v, tq, tk, tv))
                 ms = timeit(lambda: ref(qt, kt, vt, tqt, tkt, tvt, scale), a.iters, a.warmup)
                 res.append(("reference_triton_jvp_fwd", ms, fl_jvp))
+    if a.only == "gemm":
+        M, N, K = (int(v) for v in a.gemm.split(","))
+        r = a.rank
+        x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+        w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * K ** -0.5
+        la = torch.randn(r, K, device="cuda", dtype=torch.bfloat16) * K ** -0.5
+        lb = torch.randn(N, r, device="cuda", dtype=torch.bfloat16) * 0.01
+        y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        xa = torch.empty(M, r, device="cuda", dtype=torch.bfloat16)
+        fl = 2.0 * M * N * K
+        ms = timeit(lambda: e.gemm_bf16(x, w, None, None, None, y, 1.0, 0), a.iters, a.warmup)
+        res.append(("gemm_sm100", ms, fl))
+        ms = timeit(lambda: torch.matmul(x, w.t(), out=y), a.iters, a.warmup)
+        res.append(("cublas_gemm", ms, fl))
+
+        def ours_lora():
+            e.gemm_bf16(x, la, None, None, None, xa, 0.5, 0)
+            e.gemm_bf16(x, w, xa, lb, None, y, 1.0, 0)
+
+        def peft_lora():
+            torch.matmul(x, w.t(), out=y)
+            y.add_(torch.matmul(torch.matmul(x, la.t()), lb.t()), alpha=0.5)
+
+        fl_lora = fl + 2.0 * M * r * (K + N)
+        res.append(("lora_linear_sm100", timeit(ours_lora, a.iters, a.warmup), fl_lora))
+        res.append(("cublas_linear_plus_lora", timeit(peft_lora, a.iters, a.warmup), fl_lora))
     for name, ms, fl in res:
         tf = fl / (ms * 1e-3) / 1e12
         print(json.dumps({"op": name, "B": B, "L": L, "Lk": Lk, "H": H, "ms": round(ms, 4), "tflops": round(tf, 1),

@@ -417,8 +417,12 @@ flash_jvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           }
         }
       }
-      if (g == 0 && p.lse != nullptr && q_row < p.Lpad)
-        p.lse[((int64_t)batch * p.H + head) * p.Lpad + q_row] = valid ? (m_used + __log2f(l_tot)) : INFINITY;
+      if (g == 0 && p.lse != nullptr) {
+        float* lrow = p.lse + ((int64_t)batch * p.H + head) * p.Lpad;
+        if (q_row < p.Lpad) lrow[q_row] = valid ? (m_used + __log2f(l_tot)) : INFINITY;
+        // Lpad (a multiple of 256) can exceed the last tile by 128 rows: the last CTA pads them
+        if (blockIdx.x == gridDim.x - 1 && q_row + kTileM < p.Lpad) lrow[q_row + kTileM] = INFINITY;
+      }
     }
   }
   tc_fence_before();

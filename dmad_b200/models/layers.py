@@ -178,10 +178,13 @@ class SegLinear(nn.Module):
         b = self.bias
         if x.dtype != w.dtype:
             x = x.to(w.dtype)
-        y = F.linear(x, w, b)
         if self.lora_rank:
-            y = y + self.lora_scale * F.linear(F.linear(x, self.lora_A), self.lora_B * self.lora_mask)
-        return y
+            if x.is_cuda:  # one tcgen05 GEMM over [x | s x A^T] [W | B o mask]^T
+                from ..ops.linear import lora_linear
+                return lora_linear(x, w, b, self.lora_A, self.lora_B * self.lora_mask, self.lora_scale)
+            y = F.linear(x, w, b)
+            return y + self.lora_scale * F.linear(F.linear(x, self.lora_A), self.lora_B * self.lora_mask)
+        return F.linear(x, w, b)
 
     # ------------------------------------------------------------------ state dict (per-segment keys)
     def _split_prefix(self, prefix):
