@@ -83,13 +83,19 @@ def _norm_tangent(n, rstd, tx, rms):
 
 
 def _rows(g, rpg, R):
+    if torch.is_tensor(rpg):  # explicit group index per row (context-parallel slices)
+        return g[rpg.long()]
     return g.repeat_interleave(rpg, dim=0)[:R] if g.shape[0] > 1 else g.expand(R, -1)
+
+
+def _grp(rpg):
+    return {"gidx": rpg} if torch.is_tensor(rpg) else {"rows_per_group": rpg}
 
 
 def ln_mod_jvp(x, tx, a, ta, c, tc, rpg, eps, a_add=1.0):
     """y = LN(x) (a_add + a) + c with tangent (a / c per group of ``rpg`` rows; ta / tc may be None)."""
     R = x.shape[0]
-    y = ops.ln_mod(x, a, c, a_add=a_add, rows_per_group=rpg, eps=eps)
+    y = ops.ln_mod(x, a, c, a_add=a_add, eps=eps, **_grp(rpg))
     n, rstd = _norm_stats(x, False, eps)
     tn = _norm_tangent(n, rstd, tx, False)
     A = a_add + (_rows(a.float(), rpg, R) if a is not None else 0.0)
@@ -116,7 +122,7 @@ def _lin(lin, x, tx):
 def _gate(x, tx, y, ty, g, tg, rpg):
     R = x.shape[0]
     G = _rows(g.float(), rpg, R)
-    out = ops.gate_residual(x, y, g, rows_per_group=rpg)
+    out = ops.gate_residual(x, y, g, **_grp(rpg))
     t = tx.float() + ty.float() * G + y.float() * _rows(tg.float(), rpg, R)
     return out, t.to(x.dtype)
 
@@ -129,7 +135,7 @@ def _gelu_grad(x):
     return 0.5 * (1 + th) + 0.5 * x * (1 - th * th) * k0 * (1 + 3 * 0.044715 * x2)
 
 
-def block_jvp(blk, x, tx, e0, te0, context, cos, sin, B, L, rpg):
+def block_jvp(blk, x, tx, e0, te0, context, cos, sin, B, L, rpg, cp=None):
     cfg = blk.cfg
     D, H = cfg.dim, cfg.num_heads
     hd = D // H
@@ -142,8 +148,16 @@ def block_jvp(blk, x, tx, e0, te0, context, cos, sin, B, L, rpg):
     q, tq = ops.rope_apply(q, cos, sin, hd), ops.rope_apply(tq, cos, sin, hd)
     k, tk = ops.rope_apply(k, cos, sin, hd), ops.rope_apply(tk, cos, sin, hd)
     v, tv = qkv[:, 2 * D:], tqkv[:, 2 * D:]
-    a, ta = _attn_jvp(q.reshape(B, L, H, hd), k.reshape(B, L, H, hd), v.reshape(B, L, H, hd),
-                      tq.reshape(B, L, H, hd), tk.reshape(B, L, H, hd), tv.reshape(B, L, H, hd))
+    if cp is not None and cp.world > 1:
+        # the six primal / tangent tensors in one head exchange, the two outputs in one back
+        # (the reference's _SeqAllToAllQKVWithT / _SeqAllToAllOutputWithT, jvp_helper.py:69-205)
+        g = cp.seq_to_head(torch.cat([q, k, v, tq, tk, tv], dim=1), B, 6, H, hd)
+        a, ta = _attn_jvp(g[:, :, 0], g[:, :, 1], g[:, :, 2], g[:, :, 3], g[:, :, 4], g[:, :, 5])
+        back = cp.head_to_seq(torch.stack([a, ta], dim=2), B)
+        a, ta = back[:, :D], back[:, D:]
+    else:
+        a, ta = _attn_jvp(q.reshape(B, L, H, hd), k.reshape(B, L, H, hd), v.reshape(B, L, H, hd),
+                          tq.reshape(B, L, H, hd), tk.reshape(B, L, H, hd), tv.reshape(B, L, H, hd))
     y, ty = _lin(blk.self_attn.o, a.reshape(B * L, D), ta.reshape(B * L, D))
     x, tx = _gate(x, tx, y, ty, e[:, 2], te0[:, 2], rpg)
     if blk.norm3 is not None:
@@ -197,6 +211,10 @@ def time_embed_jvp(model, t, tt):
 def wan_forward_jvp(model, x, tx, timesteps, t_timesteps, crossattn_emb):
     """(out, t_out) [B, 16, T, H, W] fp32 of ``model`` at (x, timesteps) along (tx, t_timesteps)."""
     cfg = model.cfg
+    cp0 = model.cp if (model.cp is not None and model.cp.world > 1) else None
+    if cp0 is not None and cp0.broadcast_inputs:  # rank 0's sample for the whole CP group
+        x, tx, crossattn_emb = cp0.broadcast(x), cp0.broadcast(tx), cp0.broadcast(crossattn_emb)
+        timesteps, t_timesteps = cp0.broadcast(timesteps), cp0.broadcast(t_timesteps)
     B = x.shape[0]
     wdt = model.patch_embedding.weight.dtype
     xr, (T, H, W) = model.patchify(x.to(wdt))
@@ -205,17 +223,33 @@ def wan_forward_jvp(model, x, tx, timesteps, t_timesteps, crossattn_emb):
     if timesteps.ndim == 1:
         timesteps, t_timesteps = timesteps[:, None], t_timesteps[:, None]
     uniform = timesteps.shape[1] == 1
-    rpg = L if uniform else H * W
+    cos, sin = model.rope_tables(T, H, W, xr.device)
+    cp = model.cp if (model.cp is not None and model.cp.world > 1) else None
+    Ll, r0 = L, 0
+    if cp is not None:
+        Ll, r0 = L // cp.world, cp.rank * (L // cp.world)
+        xr = xr.view(B, L, -1)[:, r0:r0 + Ll].reshape(B * Ll, -1)
+        txr = txr.view(B, L, -1)[:, r0:r0 + Ll].reshape(B * Ll, -1)
+        cos, sin = cos[r0:r0 + Ll].contiguous(), sin[r0:r0 + Ll].contiguous()
+    if uniform:
+        rpg = Ll
+    elif cp is None:
+        rpg = H * W
+    else:
+        gr = torch.arange(r0, r0 + Ll, device=xr.device) // (H * W)
+        rpg = (torch.arange(B, device=xr.device)[:, None] * T + gr[None]).reshape(-1).int()
     h = F.linear(xr, model.patch_embedding.weight, model.patch_embedding.bias)
     th = F.linear(txr, model.patch_embedding.weight)
     e, e0, te, te0 = time_embed_jvp(model, timesteps.reshape(-1).float(), t_timesteps.reshape(-1).float())
     context = model.text_embed(crossattn_emb)
-    cos, sin = model.rope_tables(T, H, W, h.device)
     for blk in model.blocks:
-        h, th = block_jvp(blk, h, th, e0, te0, context, cos, sin, B, L, rpg)
+        h, th = block_jvp(blk, h, th, e0, te0, context, cos, sin, B, Ll, rpg, cp)
     m = model.head.modulation.float()[0]
     ho, tho = ln_mod_jvp(h, th, m[1][None] + e, te, m[0][None] + e, te, rpg, cfg.eps)
     hw = model.head.head
     out = F.linear(ho.float(), hw.weight.float(), hw.bias.float())
     tout = F.linear(tho.float(), hw.weight.float())
+    if cp is not None:
+        both = cp.gather(torch.cat([out, tout], dim=1).view(B, Ll, -1), dim=1).reshape(B * L, -1)
+        out, tout = both[:, :out.shape[1]], both[:, out.shape[1]:]
     return model.unpatchify(out, B, (T, H, W)), model.unpatchify(tout, B, (T, H, W))

@@ -101,6 +101,36 @@ class ContextParallel:
             return t
         return _Broadcast.apply(t, src_rank_in_group, self)
 
+    # ------------------------------------------------------------------ exchanges (either implementation)
+    def seq_to_head(self, rows: torch.Tensor, B: int, n: int, H: int, hd: int) -> torch.Tensor:
+        """[B*Ll, n*H*hd] local rows -> [B, L, n, Hl, hd] head shard of the full sequence.  The fused
+        result is a view of a receive slot: consume it before two more exchanges (or clone it)."""
+        if self.impl != "fused" or not rows.is_cuda:
+            return self.a2a_seq_to_head(rows, B, n, H, hd)
+        from .. import ops
+
+        Hl = H // self.world
+        L = rows.shape[0] // B * self.world
+        slot, ptrs = self.slot(B * L * n * Hl * hd)
+        rows = rows if (rows.stride(-1) == 1 and rows.stride(0) % 8 == 0) else rows.contiguous()
+        ops.ext().cp_seq_to_head(rows, ptrs, B, H * hd, n, hd, self.rank)
+        self.sync()
+        return slot.view(B, L, n, Hl, hd)
+
+    def head_to_seq(self, y: torch.Tensor, B: int) -> torch.Tensor:
+        """[B, L, n, Hl, hd] -> [B*Ll, n*H*hd] local rows (a slot view when fused)."""
+        if self.impl != "fused" or not y.is_cuda:
+            return self.a2a_head_to_seq(y.contiguous(), B, y.shape[2])
+        from .. import ops
+
+        _, L, n, Hl, hd = y.shape
+        D = Hl * self.world * hd
+        R = B * (L // self.world)
+        slot, ptrs = self.slot(R * n * D)
+        ops.ext().cp_head_to_seq([y[:, :, i] for i in range(n)], ptrs, n * D, D, self.rank)
+        self.sync()
+        return slot.view(R, n * D)
+
     # ------------------------------------------------------------------ NCCL all-to-all (baseline)
     def a2a_seq_to_head(self, x: torch.Tensor, B: int, n: int, H: int, hd: int) -> torch.Tensor:
         """[B*Ll, n*H*hd] rows -> [B, L, n, Hl, hd] (NCCL)."""

@@ -53,11 +53,17 @@ def _worker(rank, world, port, per_frame, q):
         grads = torch.cat([p.grad.reshape(-1) for p in m.parameters()])
         dist.all_reduce(grads)  # parameter gradients summed over the CP group
         pooled = m.cp.all_reduce_sum(feats.mean(dim=1)) / m.cp.world
-        q.put((rank, out.detach().numpy(), grads.numpy(), pooled.detach().numpy(), None))
+        from dmad_b200.models.wan_jvp import wan_forward_jvp
+        g = torch.Generator().manual_seed(11)
+        tx = torch.randn(x.shape, generator=g)
+        tt = torch.rand(t.shape, generator=g)
+        jo, jt = wan_forward_jvp(m, x, tx, t, tt, ctx)
+        q.put((rank, out.detach().numpy(), grads.numpy(), pooled.detach().numpy(),
+               (jo.numpy(), jt.numpy()), None))
         dist.destroy_process_group()
     except Exception as e:  # pragma: no cover
         import traceback
-        q.put((rank, None, None, None, traceback.format_exc()))
+        q.put((rank, None, None, None, None, traceback.format_exc()))
 
 
 @pytest.mark.parametrize("per_frame", [False, True])
@@ -77,9 +83,16 @@ def test_cp_matches_unsharded(per_frame):
     out, feats = m(x, t, ctx, feature_hook_block=-1)
     (out.square().sum() + feats.sum()).backward()
     ref_grads = torch.cat([p.grad.reshape(-1) for p in m.parameters()])
-    for rank, o, g, pooled, err in res:
+    from dmad_b200.models.wan_jvp import wan_forward_jvp
+    gj = torch.Generator().manual_seed(11)
+    tx = torch.randn(x.shape, generator=gj)
+    tt = torch.rand(t.shape, generator=gj)
+    rjo, rjt = wan_forward_jvp(m, x, tx, t, tt, ctx)
+    for rank, o, g, pooled, jvp, err in res:
         assert err is None, err
         o, g, pooled = torch.from_numpy(o), torch.from_numpy(g), torch.from_numpy(pooled)
+        torch.testing.assert_close(torch.from_numpy(jvp[0]), rjo, rtol=1e-4, atol=1e-5)
+        torch.testing.assert_close(torch.from_numpy(jvp[1]), rjt, rtol=1e-3, atol=1e-5)
         torch.testing.assert_close(o, out.detach(), rtol=1e-4, atol=1e-5)
         torch.testing.assert_close(g, ref_grads, rtol=1e-3, atol=1e-5)
         torch.testing.assert_close(pooled, feats.detach().mean(dim=1), rtol=1e-4, atol=1e-5)

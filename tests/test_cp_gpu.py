@@ -38,11 +38,17 @@ def _inputs(dev, per_frame):
 
 
 def _run(m, dev, per_frame):
+    from dmad_b200.models.wan_jvp import wan_forward_jvp
+
     x, t, ctx = _inputs(dev, per_frame)
     out, feats = m(x, t, ctx, feature_hook_block=-1)
     (out.float().square().mean() + feats.float().mean()).backward()
     grads = torch.cat([p.grad.float().reshape(-1) for p in m.parameters()])
-    return out.detach().float(), feats.detach().float(), grads
+    g = torch.Generator().manual_seed(3)
+    tx = torch.randn(x.shape, generator=g).to(dev)
+    tt = torch.rand(t.shape, generator=g).to(dev)
+    _, jt = wan_forward_jvp(m, x, tx, t * 1000, tt * 1000, ctx)
+    return out.detach().float(), feats.detach().float(), torch.cat([grads, jt.float().reshape(-1)])
 
 
 def _worker(rank, world, port, impl, per_frame, q):
@@ -60,7 +66,10 @@ def _worker(rank, world, port, impl, per_frame, q):
         out, feats, grads = _run(m, dev, per_frame)
         torch.cuda.synchronize()
         check_device_status()
-        dist.all_reduce(grads)
+        n = sum(p.numel() for p in m.parameters())
+        gpart = grads[:n].clone()
+        dist.all_reduce(gpart)  # parameter gradients summed over the CP group; the JVP tail is full
+        grads = torch.cat([gpart, grads[n:]])
         fl = [torch.empty_like(feats) for _ in range(world)]
         dist.all_gather(fl, feats.contiguous())
         feats_full = torch.cat(fl, dim=1)
