@@ -91,6 +91,7 @@ class SDXLDMADConfig:
     backward_simulation: bool = True
     gradient_checkpointing: bool = True
     unet_kwargs: dict | None = None
+    batch_size: int = 4  # per GPU (config 4)
 
 
 class SDXLDMAD:

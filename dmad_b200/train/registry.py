@@ -54,3 +54,113 @@ def _build_wan_dmad(cfg: dict, device, seed: int):
         dcfg.dp_optimizer = par["dp_optimizer"]
     dtype = torch.bfloat16 if device.type == "cuda" else torch.float32
     return WanDMAD(dcfg, device=device, dtype=dtype, seed=seed)
+
+
+class _IterationAdapter:
+    """Trainer interface for models whose step is one whole DMAD iteration with their own optimisers
+    and their own (synthetic or pooled) data: H3, EDM, SDXL."""
+
+    def __init__(self, model, step_fn, modules: dict, optims: dict):
+        self.model, self.step_fn = model, step_fn
+        self.modules, self.optims = modules, optims
+
+    def training_step(self, batch, it: int) -> dict:
+        out = self.step_fn(batch, it)
+        flat = {}
+        for k, v in out.items():
+            if isinstance(v, dict):
+                flat.update({f"{k}/{kk}": vv for kk, vv in v.items()})
+            else:
+                flat[k] = v
+        return flat
+
+    def phase_of(self, it: int) -> str:
+        return "all"
+
+    def optimizers(self) -> dict:
+        return {}
+
+    def context_parallel_nets(self) -> list:
+        return []
+
+    def state_dicts(self):
+        shared = {f"module/{k}": m.state_dict() for k, m in self.modules.items()}
+        shared.update({f"optim/{k}": o.state_dict() for k, o in self.optims.items()})
+        extra = getattr(self.model, "critic_state", None)
+        if extra is not None:
+            shared["critic_state"] = extra()
+        return shared, None
+
+    def load_state_dicts(self, shared, per_rank):
+        for k, m in self.modules.items():
+            m.load_state_dict(shared[f"module/{k}"])
+        for k, o in self.optims.items():
+            o.load_state_dict(shared[f"optim/{k}"])
+        if "critic_state" in shared and hasattr(self.model, "load_critic_state"):
+            self.model.load_critic_state(shared["critic_state"])
+
+
+def _dtype(device):
+    return torch.bfloat16 if device.type == "cuda" else torch.float32
+
+
+@register_model("h3_dmad")
+def _build_h3(cfg: dict, device, seed: int):
+    from ..distill.h3_dmad import H3DMAD, H3DMADConfig
+    from ..models.h3 import H3Config
+    from ..runtime.config import to_dataclass
+
+    m = cfg.get("model", {})
+    d = dict(m.get("distill") or {})
+    net = m.get("net")
+    hc = to_dataclass(H3DMADConfig, d)
+    if isinstance(net, dict):
+        hc.model = to_dataclass(H3Config, net)
+    model = H3DMAD(hc, device=device, dtype=_dtype(device), seed=seed)
+    return _IterationAdapter(model, lambda batch, it: model.train_iteration(),
+                             {"student": model.student, "fake": model.fake, "heads": model.heads},
+                             {"student": model.opt_s, "fake": model.opt_f})
+
+
+@register_model("edm_dmad")
+def _build_edm(cfg: dict, device, seed: int):
+    from ..distill.edm_dmad import EDMDMAD, EDMDMADConfig
+    from ..runtime.config import to_dataclass
+
+    m = cfg.get("model", {})
+    ec = to_dataclass(EDMDMADConfig, dict(m.get("distill") or {}))
+    torch.manual_seed(seed)
+    model = EDMDMAD(ec, device=device)
+    gen = torch.Generator().manual_seed(seed + 17)
+
+    def step(batch, it):
+        return model.train_step(batch if batch is not None else model.synthetic_batch(gen))
+    return _IterationAdapter(model, step, {"generator": model.generator, "critic": model.critic},
+                             {"generator": model.opt_g, "critic": model.opt_c})
+
+
+@register_model("sdxl_dmad")
+def _build_sdxl(cfg: dict, device, seed: int):
+    from ..distill.sdxl_dmad import SDXLDMAD, SDXLDMADConfig
+    from ..runtime.config import to_dataclass
+
+    m = cfg.get("model", {})
+    sc = to_dataclass(SDXLDMADConfig, dict(m.get("distill") or {}))
+    model = SDXLDMAD(sc, device=device, dtype=_dtype(device), seed=seed)
+    gen = torch.Generator().manual_seed(seed + 19)
+    ucfg = sc.unet_kwargs or {}
+    ctx_dim, pooled_dim = ucfg.get("ctx_dim", 2048), ucfg.get("pooled_dim", 1280)
+
+    def step(batch, it):
+        if batch is None:  # synthetic config-4 inputs: N(0,1) latents / text, uniform timesteps inside
+            B, r = sc.batch_size, sc.latent
+            dt = _dtype(device)
+            batch = {"noise": torch.randn(B, 4, r, r, generator=gen).to(device),
+                     "real": torch.randn(B, 4, r, r, generator=gen).to(device),
+                     "teacher": torch.randn(B, 4, r, r, generator=gen).to(device),
+                     "ctx": torch.randn(B, 77, ctx_dim, generator=gen).to(device, dt),
+                     "pooled": torch.randn(B, pooled_dim, generator=gen).to(device, dt)}
+        return model.train_step(batch)
+    return _IterationAdapter(model, step, {"generator": model.generator, "critic": model.critic,
+                                           "head_real": model.head_real, "head_teacher": model.head_teacher},
+                             {"generator": model.opt_g, "critic": model.opt_c})

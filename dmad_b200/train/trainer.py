@@ -101,6 +101,9 @@ class DistillTrainer:
 
         kind = d.get("kind", "synthetic")
         bs = int(d.get("batch_size", 1))
+        if kind == "internal":  # the model draws its own batches (H3 latent pool, EDM / SDXL synthetic inputs)
+            import itertools
+            return itertools.repeat(None)
         if kind == "synthetic":
             src = SyntheticWanData(tuple(d.get("latent_shape", (16, 21, 60, 104))),
                                    tuple(d.get("text_shape", (512, 4096))), bs, self.dp_rank,

@@ -260,3 +260,20 @@ def test_export_release_folds_sn_and_uses_ema(tmp_path):
         a, b = stud(x, t, ctx), plain(x, t, ctx)
     assert (a - b).abs().max().item() < 1e-3 * max(1.0, a.abs().max().item())
     assert not torch.equal(ema[next(iter(ema))], tr.model.net.state_dict()[next(iter(ema))])
+
+
+def test_train_cli_edm_family(tmp_path):
+    """The CLI trains the EDM config-1 family (own synthetic batches) and resumes it."""
+    from dmad_b200.cli.train import main
+
+    cfg = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "configs",
+                       "edm_imagenet64_dmad.yaml")
+    out = str(tmp_path / "edm")
+    main(["--config", cfg, f"training.output_dir={out}", "training.max_iters=2", "training.save_every=1",
+          "training.log_every=1"])
+    assert "checkpoint-000000002" in os.listdir(out)
+    main(["--config", cfg, f"training.output_dir={out}", "training.max_iters=3", "training.save_every=1",
+          "training.log_every=1"])
+    assert "checkpoint-000000003" in os.listdir(out)
+    lines = [json.loads(x) for x in open(os.path.join(out, "metrics.jsonl"))]
+    assert lines[-1]["iteration"] == 3 and "generator_loss" in lines[-1]
