@@ -86,8 +86,11 @@ class _H3Attention(nn.Module):
         self.norm_k.weight = nn.Parameter(torch.ones(self.head_dim))
         install_segment_key_remap(self)
 
-    def forward(self, x, cos, sin, L):
-        """x [L, D] (batch 1) -> [L, D]."""
+    def forward(self, x, cos, sin, L, cp=None, L_valid=None):
+        """x [L, D] (batch 1; this rank's rows under context parallelism) -> [L, D].
+
+        With ``cp`` the rows are one slice of a sequence padded at its end; ``L_valid`` is the
+        true global length, so the padded keys are left out of every softmax."""
         H, hd = self.heads, self.head_dim
         D = H * hd
         qkv = self.qkv(x)
@@ -97,6 +100,12 @@ class _H3Attention(nn.Module):
             q = ops.rope(q, cos, sin, hd)
             k = ops.rope(k, cos, sin, hd)
         v = qkv[:, 2 * D:]
+        if cp is not None and cp.world > 1:
+            # per-head q/k norms and RoPE are row-local, so they run before the head exchange
+            g = cp.seq_to_head(torch.cat([q, k, v], dim=1), 1, 3, H, hd)       # [1, Lp, 3, H/cp, hd]
+            lv = L_valid if L_valid is not None else g.shape[1]
+            o = ops.flash_attention(g[:, :, 0], g[:, :lv, 1], g[:, :lv, 2])
+            return getattr(self.to_out, "0")(cp.head_to_seq(o.unsqueeze(2), 1))
         o = ops.flash_attention(q.view(1, L, H, hd), k.view(1, L, H, hd), v.reshape(1, L, H, hd))
         return getattr(self.to_out, "0")(o.reshape(L, D))
 
@@ -137,12 +146,12 @@ class H3Block(nn.Module):
         return m.view(T, 6, self.cfg.num_tags, self.cfg.dim).permute(1, 0, 2, 3).reshape(6, T * self.cfg.num_tags,
                                                                                           self.cfg.dim)
 
-    def forward(self, h, tables, adaln_idx, cos, sin):
+    def forward(self, h, tables, adaln_idx, cos, sin, cp=None, L_valid=None):
         L = h.shape[0]
         if self.modulated:
             sh1, sc1, g1, sh2, sc2, g2 = tables
             x = ops.ln_mod(h, sc1, sh1, a_add=1.0, gidx=adaln_idx, eps=self.cfg.eps)
-            h = ops.gate_residual(h, self.attn(x, cos, sin, L), g1, gidx=adaln_idx)
+            h = ops.gate_residual(h, self.attn(x, cos, sin, L, cp, L_valid), g1, gidx=adaln_idx)
             x = ops.ln_mod(h, sc2, sh2, a_add=1.0, gidx=adaln_idx, eps=self.cfg.eps)
             return ops.gate_residual(h, self.ff(x), g2, gidx=adaln_idx)
         x = ops.layer_norm_affine(h, self.norm1.weight, self.norm1.bias, self.cfg.eps)
@@ -172,6 +181,7 @@ class H3Model(nn.Module):
         self.audio_proj_out = nn.Linear(D, cfg.audio_in_channels)
         self.checkpoint_blocks = 0
         self._rope_cache = {}
+        self.cp = None  # parallel.cp.ContextParallel: shard the packed sequence over a CP group
         self.init_weights()
 
     @torch.no_grad()
@@ -227,14 +237,32 @@ class H3Model(nn.Module):
         adaln_idx = (timestep_indices.long() * cfg.num_tags + token_tags.long()).int()
         temb = self.temb(timestep) if adaln_tables is None else None
         cos, sin = self.rope_tables(position_ids)
+        cp = self.cp if (getattr(self, "cp", None) is not None and self.cp.world > 1) else None
+        full_idx = adaln_idx
+        if cp is not None:
+            # pad the packed [text | audio | video] sequence at its end to a multiple of cp and keep
+            # this rank's contiguous slice; padded keys are excluded inside attention
+            Lp = -(-L // cp.world) * cp.world
+            pad = Lp - L
+            if pad:
+                h = torch.cat([h, h.new_zeros(pad, h.shape[1])])
+                adaln_idx = torch.cat([adaln_idx, adaln_idx.new_zeros(pad)])
+                cos = torch.cat([cos, cos.new_ones(pad, cos.shape[1])])
+                sin = torch.cat([sin, sin.new_zeros(pad, sin.shape[1])])
+            Ll = Lp // cp.world
+            sl = slice(cp.rank * Ll, (cp.rank + 1) * Ll)
+            h, adaln_idx, cos, sin = h[sl], adaln_idx[sl].contiguous(), cos[sl].contiguous(), sin[sl].contiguous()
         n = len(self.transformer_blocks) if stop_after_block is None else stop_after_block + 1
         for i in range(n):
             blk = self.transformer_blocks[i]
             tables = adaln_tables[i] if adaln_tables is not None else blk.adaln_tables(temb)
             if self.training and torch.is_grad_enabled() and i < self.checkpoint_blocks:
-                h = checkpoint(blk, h, tables, adaln_idx, cos, sin, use_reentrant=False)
+                h = checkpoint(blk, h, tables, adaln_idx, cos, sin, cp, L, use_reentrant=False)
             else:
-                h = blk(h, tables, adaln_idx, cos, sin)
+                h = blk(h, tables, adaln_idx, cos, sin, cp, L)
+        if cp is not None:
+            h = cp.gather(h[None], dim=1)[0, :L]
+            adaln_idx = full_idx
         if stop_after_block is not None:
             return h.view(1, L, cfg.dim)
         if temb is None:
@@ -249,6 +277,10 @@ class H3Model(nn.Module):
         return v_out[None], a_out[None]
 
     # ------------------------------------------------------------------ adapters
+    def enable_context_parallel(self, cp):
+        """Shard the packed sequence over ``cp`` (a ``parallel.cp.ContextParallel``); None disables."""
+        self.cp = cp
+
     def lora_linears(self, targets=("to_q", "to_k", "to_v", "to_out.0", "ff.net.0.proj", "ff.net.2")):
         out = []
         for b in self.transformer_blocks:
