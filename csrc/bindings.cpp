@@ -55,6 +55,7 @@ void cp_seq_to_head(const at::Tensor& src, std::vector<int64_t> dst, int64_t B, 
 void cp_head_to_seq(std::vector<at::Tensor> srcs, std::vector<int64_t> dst, int64_t ld, int64_t D, int64_t rank);
 void gemm_bf16(const at::Tensor& a, const at::Tensor& b, c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2,
                c10::optional<at::Tensor> bias, at::Tensor& d, double alpha, int64_t act);
+void fsdp_gather(std::vector<int64_t> shard_ptrs, at::Tensor& dst, int64_t len, int64_t numel);
 void symm_barrier(const at::Tensor& buf_ptrs, int64_t rank, int64_t epoch, c10::optional<at::Tensor> payload,
                   double timeout_s);
 void dp_sumsq(std::vector<int64_t> grad_ptrs, std::vector<int64_t> param_ptrs, int64_t mc_grads, int64_t mc_params,
@@ -92,6 +93,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cp_seq_to_head", &dmad::cp_seq_to_head);
   m.def("cp_head_to_seq", &dmad::cp_head_to_seq);
   m.def("gemm_bf16", &dmad::gemm_bf16);
+  m.def("fsdp_gather", &dmad::fsdp_gather);
   m.def("symm_barrier", &dmad::symm_barrier);
   m.def("dp_sumsq", &dmad::dp_sumsq);
   m.def("dp_adamw", &dmad::dp_adamw);

@@ -87,6 +87,9 @@ class WanDMADConfig:
     # "sharded": flat symmetric buffers + one fused reduce-scatter / AdamW / all-gather kernel per
     # step (fp32 optimiser state sharded over the ranks); "replicated": NCCL all-reduce of the
     # gradients, then the same multi-tensor AdamW on every rank
+    # shard the frozen block weights (LoRA student base, teacher) over the ranks and gather them one
+    # block ahead (needs the student blocks activation-checkpointed)
+    shard_frozen: bool = False
     dp_optimizer: str = "sharded"
     dp_multicast: bool = True
     dp_sync_timeout_s: float = 120.0
@@ -128,6 +131,15 @@ class WanDMAD(nn.Module):
         broadcast_module(self.net)
         broadcast_module(self.net_fake_score)
         broadcast_module(self.critic_heads)
+        self.sharded = []
+        if cfg.shard_frozen:
+            from ..parallel.fsdp import ShardedFrozenBlocks
+            if cfg.student_lora_rank:
+                sh = ShardedFrozenBlocks(self.net.blocks)
+                sh.check_checkpointing(cfg.checkpoint_student_blocks)
+                self.sharded.append(sh)
+            if self.net_teacher is not None:
+                self.sharded.append(ShardedFrozenBlocks(self.net_teacher.blocks))
         self.gap = GapRouter("allreduce", tau=cfg.gap_tau, beta=cfg.gap_ema_beta, enabled=cfg.gap_route).to(device)
         self.scaling = TrigFlowScaling(1.0, cfg.rectified_flow_t_scaling_factor)
         self.p_D = LogNormal(*cfg.p_D_lognormal) if cfg.p_D_lognormal else UniformShift(cfg.p_D_shift)
@@ -168,7 +180,9 @@ class WanDMAD(nn.Module):
     # ------------------------------------------------------------------ checkpoint state
     def state_dicts(self) -> tuple[dict, dict | None]:
         """(state every rank holds identically, this rank's optimiser shards or None)."""
-        shared = {"net": self.net.state_dict(), "net_fake_score": self.net_fake_score.state_dict(),
+        # sharded frozen weights are never saved (they do not change; they come from the teacher checkpoint)
+        net_sd = {k: v for k, v in self.net.state_dict().items() if v.numel() > 0 or not self.sharded}
+        shared = {"net": net_sd, "net_fake_score": self.net_fake_score.state_dict(),
                   "critic_heads": self.critic_heads.state_dict(), "gap": self.gap.state_dict()}
         if isinstance(self.opt_student, ShardedAdamW):
             names = {id(p): n for n, p in self.net.named_parameters()}
@@ -180,7 +194,7 @@ class WanDMAD(nn.Module):
         return shared, None
 
     def load_state_dicts(self, shared: dict, per_rank: dict | None):
-        self.net.load_state_dict(shared["net"])
+        self.net.load_state_dict(shared["net"], strict=not self.sharded)
         self.net_fake_score.load_state_dict(shared["net_fake_score"])
         self.critic_heads.load_state_dict(shared["critic_heads"])
         self.gap.load_state_dict(shared["gap"])
