@@ -56,6 +56,11 @@ void cp_head_to_seq(std::vector<at::Tensor> srcs, std::vector<int64_t> dst, int6
 void gemm_bf16(const at::Tensor& a, const at::Tensor& b, c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2,
                c10::optional<at::Tensor> bias, at::Tensor& d, double alpha, int64_t act);
 void fsdp_gather(std::vector<int64_t> shard_ptrs, at::Tensor& dst, int64_t len, int64_t numel);
+void flash_fwd_accumulate(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
+                          at::Tensor& lse, at::Tensor& acc_o, at::Tensor& acc_lse, bool read, bool final_,
+                          double scale);
+void peer_copy(at::Tensor& dst, int64_t src_ptr, int64_t nbytes);
+void peer_copy_to(int64_t dst_ptr, const at::Tensor& src, int64_t nbytes);
 void symm_barrier(const at::Tensor& buf_ptrs, int64_t rank, int64_t epoch, c10::optional<at::Tensor> payload,
                   double timeout_s);
 void dp_sumsq(std::vector<int64_t> grad_ptrs, std::vector<int64_t> param_ptrs, int64_t mc_grads, int64_t mc_params,
@@ -94,6 +99,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cp_head_to_seq", &dmad::cp_head_to_seq);
   m.def("gemm_bf16", &dmad::gemm_bf16);
   m.def("fsdp_gather", &dmad::fsdp_gather);
+  m.def("flash_fwd_accumulate", &dmad::flash_fwd_accumulate);
+  m.def("peer_copy", &dmad::peer_copy);
+  m.def("peer_copy_to", &dmad::peer_copy_to);
   m.def("symm_barrier", &dmad::symm_barrier);
   m.def("dp_sumsq", &dmad::dp_sumsq);
   m.def("dp_adamw", &dmad::dp_adamw);

@@ -68,6 +68,12 @@ struct FwdParams {
   int64_t scat[16];
   int scat_n, scat_ll, scat_col;
   int64_t scat_ld;
+  // optional running merge over successive key blocks (ring context parallelism):
+  // acc_o fp32 [B, Lq, H, 128] and acc_lse (log2) [B, H, Lpad] hold the softmax-weighted output
+  // of the blocks seen so far; acc_read merges into them, acc_final also writes the bf16 o
+  float* acc_o;
+  float* acc_lse;
+  int acc_read, acc_final;
 };
 
 __global__ void __launch_bounds__(384, 1)
@@ -327,7 +333,50 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       mbar_arrive(&sm.p_full[t]);
     }
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.pv_done[t], (nkv - 1) & 1, kStatusTimeoutMma, abort_flag, p.status));
-    if (ok) {
+    if (ok && p.acc_o != nullptr) {
+      // merge this key block into the running result: weights 2^(lse_prev - lse_new) and
+      // 2^(m - lse_new) on the previous output and on this block's unnormalised O
+      tc_fence_after();
+      const bool valid = q_row < p.Lq;
+      const float lse_j = m_used + __log2f(l_sum);
+      float* lrow = p.acc_lse + ((int64_t)batch * p.H + head) * p.Lpad + q_row;
+      const float lp = (p.acc_read && valid) ? *lrow : -INFINITY;
+      const float mx = fmaxf(lp, lse_j);
+      const float nl = mx + __log2f(exp2f(lp - mx) + exp2f(lse_j - mx));
+      const float wa = p.acc_read ? exp2f(lp - nl) : 0.f;
+      const float wb = exp2f(m_used - nl);
+      float* arow = p.acc_o + (((int64_t)batch * p.Lq + q_row) * p.H + head) * 128;
+      __nv_bfloat16* orow = p.o + batch * p.o_sb + (int64_t)q_row * p.o_sl + head * p.o_sh;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(o_tmem + c * 32, r);
+        tmem_wait_ld();
+        if (valid) {
+          float4* a4 = reinterpret_cast<float4*>(arow + c * 32);
+#pragma unroll
+          for (int v = 0; v < 8; ++v) {
+            float4 prev = p.acc_read ? a4[v] : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 nw;
+            nw.x = prev.x * wa + __uint_as_float(r[4 * v + 0]) * wb;
+            nw.y = prev.y * wa + __uint_as_float(r[4 * v + 1]) * wb;
+            nw.z = prev.z * wa + __uint_as_float(r[4 * v + 2]) * wb;
+            nw.w = prev.w * wa + __uint_as_float(r[4 * v + 3]) * wb;
+            a4[v] = nw;
+            if (p.acc_final) {
+              uint2 w2;
+              w2.x = pack_bf16x2(nw.x, nw.y);
+              w2.y = pack_bf16x2(nw.z, nw.w);
+              reinterpret_cast<uint2*>(orow + c * 32)[v] = w2;
+            }
+          }
+        }
+      }
+      if (q_row < p.Lpad) {
+        *lrow = valid ? nl : INFINITY;
+        if (p.lse != nullptr) p.lse[((int64_t)batch * p.H + head) * p.Lpad + q_row] = valid ? nl : INFINITY;
+      }
+    } else if (ok) {
       tc_fence_after();
       const float inv_l = 1.f / l_sum;
       const bool valid = q_row < p.Lq;
@@ -395,7 +444,8 @@ int64_t flash_lse_pad(int64_t L) { return (L + 255) / 256 * 256; }
 // Launches the forward; `scat` (optional) adds the owner-rank copy of every output row.
 static void flash_fwd_launch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
                              at::Tensor& lse, double scale, const std::vector<int64_t>& scat, int64_t scat_ld,
-                             int64_t scat_col) {
+                             int64_t scat_col, float* acc_o = nullptr, float* acc_lse = nullptr, int acc_read = 0,
+                             int acc_final = 0) {
   check_bhld(q, "q");
   check_bhld(k, "k");
   check_bhld(v, "v");
@@ -431,6 +481,10 @@ static void flash_fwd_launch(const at::Tensor& q, const at::Tensor& k, const at:
   p.scat_ll = p.scat_n > 0 ? Lq / p.scat_n : 1;
   p.scat_ld = scat_ld;
   p.scat_col = (int)scat_col;
+  p.acc_o = acc_o;
+  p.acc_lse = acc_lse;
+  p.acc_read = acc_read;
+  p.acc_final = acc_final;
   if (p.scat_n > 0) {
     TORCH_CHECK(Lq % p.scat_n == 0, "Lq must divide over the scatter targets");
     TORCH_CHECK(scat_ld % 8 == 0 && scat_col % 8 == 0, "scatter row stride / column must be multiples of 8");
@@ -448,6 +502,23 @@ static void flash_fwd_launch(const at::Tensor& q, const at::Tensor& k, const at:
 void flash_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
                double scale) {
   flash_fwd_launch(q, k, v, o, lse, scale, {}, 0, 0);
+}
+
+// One key block of ring attention: merges softmax(q k^T) v over this block into the fp32 running
+// output acc_o [B, Lq, H, 128] (contiguous) and its log2 LSE acc_lse [B, H, round_up(Lq, 256)];
+// read = merge with the previous blocks, final = also write the bf16 result to o (and lse if given).
+void flash_fwd_accumulate(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
+                          at::Tensor& lse, at::Tensor& acc_o, at::Tensor& acc_lse, bool read, bool final_,
+                          double scale) {
+  TORCH_CHECK(acc_o.is_cuda() && acc_o.scalar_type() == at::kFloat && acc_o.is_contiguous() && acc_o.dim() == 4 &&
+                  acc_o.size(0) == q.size(0) && acc_o.size(1) == q.size(1) && acc_o.size(2) == q.size(2) &&
+                  acc_o.size(3) == 128,
+              "acc_o must be contiguous fp32 [B, Lq, H, 128]");
+  TORCH_CHECK(acc_lse.is_cuda() && acc_lse.scalar_type() == at::kFloat && acc_lse.is_contiguous() &&
+                  acc_lse.dim() == 3 && acc_lse.size(2) == flash_lse_pad(q.size(1)),
+              "acc_lse must be fp32 [B, H, round_up(Lq, 256)]");
+  flash_fwd_launch(q, k, v, o, lse, scale, {}, 0, 0, acc_o.data_ptr<float>(), acc_lse.data_ptr<float>(), read ? 1 : 0,
+                   final_ ? 1 : 0);
 }
 
 // flash_fwd that also stores every output row into the [B*Ll, ld] row buffer of the rank that

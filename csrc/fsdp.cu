@@ -57,4 +57,25 @@ void fsdp_gather(std::vector<int64_t> shard_ptrs, at::Tensor& dst, int64_t len, 
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Copy engine transfer of nbytes from an address of another GPU's (mapped) memory into dst on the
+// current stream: the ring-attention key/value blocks move without occupying SMs.
+void peer_copy(at::Tensor& dst, int64_t src_ptr, int64_t nbytes) {
+  TORCH_CHECK(dst.is_cuda() && dst.is_contiguous() && (int64_t)(dst.numel() * dst.element_size()) >= nbytes,
+              "dst must be a contiguous CUDA tensor of at least nbytes");
+  if (nbytes == 0) return;
+  c10::cuda::CUDAGuard guard(dst.device());
+  C10_CUDA_CHECK(cudaMemcpyAsync(dst.data_ptr(), reinterpret_cast<const void*>(src_ptr), (size_t)nbytes,
+                                 cudaMemcpyDeviceToDevice, at::cuda::getCurrentCUDAStream()));
+}
+
+// Copy engine transfer of src into an address of another GPU's (mapped) memory.
+void peer_copy_to(int64_t dst_ptr, const at::Tensor& src, int64_t nbytes) {
+  TORCH_CHECK(src.is_cuda() && src.is_contiguous() && (int64_t)(src.numel() * src.element_size()) >= nbytes,
+              "src must be a contiguous CUDA tensor of at least nbytes");
+  if (nbytes == 0) return;
+  c10::cuda::CUDAGuard guard(src.device());
+  C10_CUDA_CHECK(cudaMemcpyAsync(reinterpret_cast<void*>(dst_ptr), src.data_ptr(), (size_t)nbytes,
+                                 cudaMemcpyDeviceToDevice, at::cuda::getCurrentCUDAStream()));
+}
+
 }  // namespace dmad

@@ -142,9 +142,9 @@ class WanBlock(nn.Module):
         h = ops.ln_mod(x, e[:, 1], e[:, 0], a_add=1.0, eps=cfg.eps, **grp)
         qkv = self.self_attn.qkv(h)
         if cp is not None and cp.world > 1:
-            from ..parallel.cp import self_attention_cp
-            a = self_attention_cp(qkv, self.self_attn.norm_q.weight, self.self_attn.norm_k.weight, cos, sin, B, H,
-                                  cfg.eps, cp)
+            from ..parallel.cp import ring_self_attention, self_attention_cp
+            attn = ring_self_attention if cp.impl == "ring" else self_attention_cp
+            a = attn(qkv, self.self_attn.norm_q.weight, self.self_attn.norm_k.weight, cos, sin, B, H, cfg.eps, cp)
         else:
             a = self_attention_core(qkv, self.self_attn.norm_q.weight, self.self_attn.norm_k.weight, cos, sin, B, L,
                                     H, cfg.eps)

@@ -37,14 +37,14 @@ from .symm import PeerSync, SymmBuffer
 class ContextParallel:
     def __init__(self, group=None, impl: str = "fused", device=None, timeout_s: float = 120.0,
                  broadcast_inputs: bool = True):
-        if impl not in ("fused", "nccl"):
+        if impl not in ("fused", "nccl", "ring"):
             raise ValueError(f"unknown context-parallel impl {impl!r}")
         self.group = group if group is not None else (dist.group.WORLD if is_distributed() else None)
         self.world = dist.get_world_size(self.group) if self.group is not None else 1
         self.rank = dist.get_rank(self.group) if self.group is not None else 0
         self.device = torch.device(device) if device is not None else (
             torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu"))
-        if self.device.type != "cuda":
+        if self.device.type != "cuda" and impl == "fused":
             impl = "nccl"
         self.impl = impl
         self.timeout_s = timeout_s
@@ -52,7 +52,11 @@ class ContextParallel:
         self._arena: SymmBuffer | None = None
         self._slot_elems = 0
         self._op = 0
-        self.sync = PeerSync(self.device, self.group, timeout_s) if impl == "fused" else None
+        self.sync = PeerSync(self.device, self.group, timeout_s) if impl in ("fused", "ring") and \
+            self.device.type == "cuda" else None
+        self.ring_stream = torch.cuda.Stream(device=self.device) if impl == "ring" and self.device.type == "cuda" \
+            else None
+        self._ring_bufs = None
 
     # ------------------------------------------------------------------ symmetric receive slots
     def reserve(self, elems: int):
@@ -74,6 +78,12 @@ class ContextParallel:
         view = self._arena.tensor[base:base + elems]
         ptrs = [p + base * 2 for p in self._arena.ptrs]
         return view, ptrs
+
+    def ring_buffers(self, elems: int):
+        """Two local bf16 buffers for the key/value blocks copied from peers (ring attention)."""
+        if self._ring_bufs is None or self._ring_bufs[0].numel() < elems:
+            self._ring_bufs = [torch.empty(elems, dtype=torch.bfloat16, device=self.device) for _ in range(2)]
+        return self._ring_bufs
 
     # ------------------------------------------------------------------ token sharding (cold path)
     def split(self, x: torch.Tensor, dim: int = 1) -> torch.Tensor:
@@ -105,7 +115,7 @@ class ContextParallel:
     def seq_to_head(self, rows: torch.Tensor, B: int, n: int, H: int, hd: int) -> torch.Tensor:
         """[B*Ll, n*H*hd] local rows -> [B, L, n, Hl, hd] head shard of the full sequence.  The fused
         result is a view of a receive slot: consume it before two more exchanges (or clone it)."""
-        if self.impl != "fused" or not rows.is_cuda:
+        if self.impl == "nccl" or not rows.is_cuda:
             return self.a2a_seq_to_head(rows, B, n, H, hd)
         from .. import ops
 
@@ -119,7 +129,7 @@ class ContextParallel:
 
     def head_to_seq(self, y: torch.Tensor, B: int) -> torch.Tensor:
         """[B, L, n, Hl, hd] -> [B*Ll, n*H*hd] local rows (a slot view when fused)."""
-        if self.impl != "fused" or not y.is_cuda:
+        if self.impl == "nccl" or not y.is_cuda:
             return self.a2a_head_to_seq(y.contiguous(), B, y.shape[2])
         from .. import ops
 
@@ -328,3 +338,174 @@ class _A2AHeadToSeq(torch.autograd.Function):
     def backward(ctx, g):
         B, n, H, hd, cp = ctx.cfg
         return cp.a2a_seq_to_head(g.contiguous(), B, n, H, hd), None, None, None, None
+
+
+# ---------------------------------------------------------------------- ring attention
+# impl="ring": every rank keeps the queries of its own tokens (all heads) and visits the key / value
+# block of every rank.  Each rank's normalised k and v sit in a symmetric slot; the block of the next
+# rank is copied into a local double buffer by the copy engine on a side stream while the flash kernel
+# works on the current block, and the kernel's epilogue merges the block into an fp32 running output
+# with its log-sum-exp (flash_fwd_accumulate).  The backward visits the blocks again with the final
+# LSE: dQ accumulates locally, the dK / dV partials of a block are pushed into per-source slots of
+# its owner and summed there.  Parity: there is no ring attention in the reference (Ulysses only,
+# train/wan/rcm/utils/a2a_cp.py); this is the ring variant of the same context parallelism.
+
+def _ring_blocks(cp, slot_ptrs, R, D, stream, bufs, visit):
+    """Call ``visit(j, src, kv)`` for the key/value block of every rank ``src = rank + j`` (``kv`` None
+    for this rank's own block).  The block of step j + 1 is copied into ``bufs[(j + 1) % 2]`` on
+    ``stream`` while step j computes; a copy starts only after the work that last read its buffer."""
+    from .. import ops
+
+    e = ops.ext()
+    nbytes = 2 * R * D * 2
+    cur = torch.cuda.current_stream()
+    ready = {}
+
+    def prefetch(j):
+        src = (cp.rank + j) % cp.world
+        ev = torch.cuda.Event()
+        ev.record(cur)
+        with torch.cuda.stream(stream):
+            stream.wait_event(ev)
+            e.peer_copy(bufs[j & 1], slot_ptrs[src], nbytes)
+            done = torch.cuda.Event()
+            done.record(stream)
+        ready[j] = done
+
+    if cp.world > 1:
+        prefetch(1)
+    for j in range(cp.world):
+        if 1 <= j < cp.world - 1:
+            prefetch(j + 1)  # its buffer was last read by step j - 1, already issued
+        kv = None
+        if j > 0:
+            cur.wait_event(ready[j])
+            kv = bufs[j & 1]
+        visit(j, (cp.rank + j) % cp.world, kv)
+    cur.wait_stream(stream)
+
+
+class _RingSelfAttn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, wq, wk, cos, sin, B, H, eps, cp):
+        from .. import ops
+        from ..ops import attention as attn_ops
+        from ..ops import norm as norm_ops
+
+        e = ops.ext()
+        R, D3 = qkv.shape
+        D = D3 // 3
+        hd = D // H
+        Ll = R // B
+        scale = 1.0 / math.sqrt(hd)
+        qk, rq, rk = norm_ops.qk_norm_rope(qkv, wq, wk, cos, sin, D, hd, eps)
+        q = qk[:, :D].view(B, Ll, H, hd)
+        slot, ptrs = cp.slot(2 * R * D)
+        own = slot.view(2, R, D)
+        own[0].copy_(qk[:, D:])
+        own[1].copy_(qkv[:, 2 * D:])
+        cp.sync()  # every rank's block is in place
+        o = torch.empty((B, Ll, H, hd), dtype=qkv.dtype, device=qkv.device)
+        lse = torch.empty((B, H, attn_ops._lse_pad(Ll)), dtype=torch.float32, device=qkv.device)
+        acc_o = torch.empty((B, Ll, H, hd), dtype=torch.float32, device=qkv.device)
+        acc_lse = torch.empty_like(lse)
+        bufs = cp.ring_buffers(2 * R * D)
+
+        def visit(j, src, kv):
+            blk = own if kv is None else kv.view(2, R, D)
+            e.flash_fwd_accumulate(q, blk[0].view(B, Ll, H, hd), blk[1].view(B, Ll, H, hd), o, lse, acc_o, acc_lse,
+                                   j > 0, j == cp.world - 1, scale)
+
+        _ring_blocks(cp, ptrs, R, D, cp.ring_stream, bufs, visit)
+        cp.sync()  # the peers have copied this rank's block before the slot is reused
+        ctx.save_for_backward(qkv, wq, wk, cos, sin, rq, rk, o, lse)
+        ctx.cfg = (B, H, eps, scale, cp)
+        return o.view(R, D)
+
+    @staticmethod
+    def backward(ctx, do):
+        from .. import ops
+        from ..ops import norm as norm_ops
+
+        qkv, wq, wk, cos, sin, rq, rk, o, lse = ctx.saved_tensors
+        B, H, eps, scale, cp = ctx.cfg
+        e = ops.ext()
+        R, D3 = qkv.shape
+        D = D3 // 3
+        hd = D // H
+        Ll = R // B
+        qk, _, _ = norm_ops.qk_norm_rope(qkv, wq, wk, cos, sin, D, hd, eps)
+        q = qk[:, :D].view(B, Ll, H, hd)
+        slot, ptrs = cp.slot(2 * R * D)
+        own = slot.view(2, R, D)
+        own[0].copy_(qk[:, D:])
+        own[1].copy_(qkv[:, 2 * D:])
+        part, pptrs = cp.slot(cp.world * 2 * R * D)  # [source rank, dK | dV, R, D] of this rank's block
+        cp.sync()
+        do = do.contiguous().view(B, Ll, H, hd)
+        dq_acc = torch.zeros((R, D), dtype=torch.float32, device=qkv.device)
+        dq = torch.empty((B, Ll, H, hd), dtype=qkv.dtype, device=qkv.device)
+        dkv = torch.empty((2, R, D), dtype=qkv.dtype, device=qkv.device)
+        dd = torch.empty_like(lse)
+        bufs = cp.ring_buffers(2 * R * D)
+        part_v = part.view(cp.world, 2, R, D)
+
+        def visit(j, src, kv):
+            blk = own if kv is None else kv.view(2, R, D)
+            e.flash_bwd(q, blk[0].view(B, Ll, H, hd), blk[1].view(B, Ll, H, hd), o, do, lse, dq,
+                        dkv[0].view(B, Ll, H, hd), dkv[1].view(B, Ll, H, hd), dd, scale)
+            dq_acc.add_(dq.view(R, D).float())
+            if src == cp.rank:
+                part_v[cp.rank].copy_(dkv)
+            else:  # into the owner's slot for this source rank (copy engine)
+                e.peer_copy_to(pptrs[src] + cp.rank * 2 * R * D * 2, dkv, 2 * R * D * 2)
+            # dkv is reused by the next block: wait for the copy (same stream, ordered)
+
+        _ring_blocks(cp, ptrs, R, D, cp.ring_stream, bufs, visit)
+        cp.sync()  # every partial has landed
+        g = part_v.float().sum(0)
+        dqk = torch.cat([dq_acc, g[0]], dim=1).to(qkv.dtype)
+        dqkv = torch.empty_like(qkv)
+        dqkv[:, 2 * D:].copy_(g[1].to(qkv.dtype))
+        dwq = torch.zeros(D, dtype=torch.float32, device=qkv.device)
+        dwk = torch.zeros(D, dtype=torch.float32, device=qkv.device)
+        e.qk_norm_rope_bwd(dqk[:, :D], dqk[:, D:], qkv, dqkv, wq, wk, cos, sin, rq, rk, dwq, dwk, D, hd)
+        return dqkv, dwq, dwk, None, None, None, None, None, None
+
+
+def _ring_cpu(qkv, wq, wk, cos, sin, B, H, eps, cp):
+    """fp32 restatement of ring attention (gloo ranks): all-gather the blocks, merge per block by LSE."""
+    from ..ops import norm as norm_ops
+
+    R, D3 = qkv.shape
+    D = D3 // 3
+    hd = D // H
+    Ll = R // B
+    q = norm_ops.rope_reference(norm_ops.ln_mod_reference(qkv[:, :D], wq.reshape(1, -1), None, 0.0, None, None, eps,
+                                                          True), cos, sin, hd)
+    k = norm_ops.rope_reference(norm_ops.ln_mod_reference(qkv[:, D:2 * D], wk.reshape(1, -1), None, 0.0, None, None,
+                                                          eps, True), cos, sin, hd)
+    kv = torch.cat([k, qkv[:, 2 * D:]], dim=1)
+    blocks = _GatherSeq.apply(kv.view(1, R, 2 * D), 1, cp).view(cp.world, R, 2 * D)
+    qf = q.float().view(B, Ll, H, hd).transpose(1, 2)
+    acc, lse = None, None
+    for j in range(cp.world):
+        src = (cp.rank + j) % cp.world
+        kj = blocks[src, :, :D].float().view(B, Ll, H, hd).transpose(1, 2)
+        vj = blocks[src, :, D:].float().view(B, Ll, H, hd).transpose(1, 2)
+        s = qf @ kj.transpose(-1, -2) / math.sqrt(hd)
+        l_j = torch.logsumexp(s, -1, keepdim=True)
+        o_j = torch.softmax(s, -1) @ vj
+        if acc is None:
+            acc, lse = o_j, l_j
+        else:
+            nl = torch.logaddexp(lse, l_j)
+            acc = acc * torch.exp(lse - nl) + o_j * torch.exp(l_j - nl)
+            lse = nl
+    return acc.transpose(1, 2).reshape(R, D).to(qkv.dtype)
+
+
+def ring_self_attention(qkv, wq, wk, cos, sin, B, H, eps, cp: ContextParallel):
+    if not qkv.is_cuda:
+        return _ring_cpu(qkv, wq, wk, cos, sin, B, H, eps, cp)
+    return _RingSelfAttn.apply(qkv, wq.float().contiguous(), wk.float().contiguous(), cos, sin, B, H, eps, cp)

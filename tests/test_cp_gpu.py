@@ -83,7 +83,7 @@ def _worker(rank, world, port, impl, per_frame, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("impl,per_frame", [("fused", False), ("nccl", False), ("fused", True)])
+@pytest.mark.parametrize("impl,per_frame", [("fused", False), ("nccl", False), ("fused", True), ("ring", False)])
 def test_cp_two_gpus_matches_unsharded(impl, per_frame):
     world = 2
     ctx_mp = mp.get_context("spawn")

@@ -1,0 +1,85 @@
+"""Sharded frozen block weights on 2 GPUs (skipped with fewer): peer-pull gathers one block ahead on a
+side stream reproduce the unsharded LoRA-student forward and LoRA gradients exactly."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _model(dev):
+    from dmad_b200.models.wan import WanConfig, WanModel
+
+    torch.manual_seed(0)
+    m = WanModel(WanConfig(dim=256, ffn_dim=512, num_heads=2, num_layers=4, text_dim=64, freq_dim=64))
+    torch.nn.init.normal_(m.head.head.weight, std=0.05)
+    m.enable_lora(16)
+    for b in m.blocks:
+        for lin in b.linears():
+            torch.nn.init.normal_(lin.lora_B, std=0.02)
+    m = m.to(dev, torch.bfloat16)
+    m.checkpoint_blocks = 4
+    return m.train()
+
+
+def _run(m, dev):
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(1, 16, 4, 16, 16, generator=g).to(dev)
+    t, ctx = torch.rand(1, 1, generator=g).to(dev), torch.randn(1, 24, 64, generator=g).to(dev)
+    out = m(x, t, ctx)
+    out.float().square().mean().backward()
+    grads = torch.cat([p.grad.float().reshape(-1) for p in m.parameters() if p.grad is not None])
+    return out.detach().float(), grads
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    try:
+        import torch.distributed as dist
+        from dmad_b200.ops import check_device_status
+        from dmad_b200.parallel.dist import init_distributed
+        from dmad_b200.parallel.fsdp import ShardedFrozenBlocks
+
+        _, _, dev = init_distributed(timeout_s=60)
+        m = _model(dev)
+        ShardedFrozenBlocks(m.blocks)
+        out, grads = _run(m, dev)
+        torch.cuda.synchronize()
+        check_device_status()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, out.cpu().numpy(), grads.cpu().numpy(), None))
+    except Exception:  # pragma: no cover
+        import traceback
+        q.put((rank, None, None, traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_sharded_frozen_blocks_two_gpus():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    dev = torch.device("cuda", 0)
+    out, grads = _run(_model(dev), dev)
+    for rank, o, g, err in res:
+        assert err is None, err
+        assert torch.equal(torch.from_numpy(o).to(dev), out)
+        assert torch.equal(torch.from_numpy(g).to(dev), grads)

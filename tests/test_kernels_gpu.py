@@ -203,3 +203,47 @@ def test_temb_kernels():
     y = small_linear(x, w, b, act_in="silu")
     yr = torch.nn.functional.linear(torch.nn.functional.silu(x), w.float(), b)
     assert (y - yr).abs().max().item() < 1e-3
+
+
+def test_flash_fwd_accumulate_merges_key_blocks():
+    """Attention over keys split into three blocks, merged by the accumulate epilogue, equals the
+    attention over all keys (output and log2 LSE)."""
+    e = _ext()
+    torch.manual_seed(4)
+    B, Lq, H = 1, 300, 2
+    q = torch.randn(B, Lq, H, 128, device=dev, dtype=torch.bfloat16)
+    ks = [torch.randn(B, n, H, 128, device=dev, dtype=torch.bfloat16) for n in (256, 100, 384)]
+    vs = [torch.randn_like(k) for k in ks]
+    scale = 1 / math.sqrt(128)
+    o = torch.empty_like(q)
+    lse = torch.empty(B, H, e.flash_lse_pad(Lq), device=dev)
+    acc = torch.empty(B, Lq, H, 128, device=dev)
+    acc_lse = torch.empty_like(lse)
+    for j, (k, v) in enumerate(zip(ks, vs)):
+        e.flash_fwd_accumulate(q, k, v, o, lse, acc, acc_lse, j > 0, j == 2, scale)
+    torch.cuda.synchronize()
+    from dmad_b200 import ops
+    ops.check_device_status()
+    ref, ref_lse = _attn_ref(q, torch.cat(ks, 1), torch.cat(vs, 1), scale)
+    assert (o.float() - ref).abs().max().item() < 2e-2
+    assert (lse[:, :, :Lq] / math.log2(math.e) - ref_lse).abs().max().item() < 2e-3
+
+
+def test_peer_copy_local():
+    e = _ext()
+    src = torch.randn(1000, device=dev)
+    dst = torch.empty_like(src)
+    e.peer_copy(dst, src.data_ptr(), src.numel() * 4)
+    dst2 = torch.empty_like(src)
+    e.peer_copy_to(dst2.data_ptr(), src, src.numel() * 4)
+    torch.cuda.synchronize()
+    assert torch.equal(dst, src) and torch.equal(dst2, src)
+
+
+def test_fsdp_gather_single_rank():
+    e = _ext()
+    shard = torch.randn(1024, device=dev).to(torch.bfloat16)
+    dst = torch.empty(1024, device=dev, dtype=torch.bfloat16)
+    e.fsdp_gather([shard.data_ptr()], dst, 1024, 1000)
+    torch.cuda.synchronize()
+    assert torch.equal(dst[:1000], shard[:1000])
