@@ -14,6 +14,9 @@
 //   a double-buffered S, dP, and dQ += dS K as a TMEM-A MMA.
 // Splitting dQ from dK/dV costs two extra GEMMs per tile pair but needs no
 // atomics and no fp32 scratch accumulator.
+// In both kernels two 128-thread groups (warps 4..7 and 8..11) share the elementwise work of a
+// tile by columns: group g handles columns [64g, 64g + 64) and writes its bf16 P / dS packed over
+// the first half of its own columns; the TMEM-A MMAs take the halves from [0, 32) and [64, 96).
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <torch/extension.h>
@@ -45,9 +48,13 @@ struct BwdParams {
   int* status;
 };
 
-__device__ __forceinline__ void store_row_bf16(__nv_bfloat16* row, uint32_t tmem_row, float mul) {
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
+// Columns [c_begin, c_begin + 32 * n_chunks) of one TMEM row as bf16.
+__device__ __forceinline__ void store_row_bf16(__nv_bfloat16* row, uint32_t tmem_row, float mul, int c_begin = 0,
+                                               int n_chunks = 4) {
+  if (row != nullptr) row += c_begin;
+  tmem_row += c_begin;
+#pragma unroll 1
+  for (int c = 0; c < n_chunks; ++c) {
     uint32_t r[32];
     tmem_ld32(tmem_row + c * 32, r);
     tmem_wait_ld();
@@ -65,6 +72,10 @@ __device__ __forceinline__ void store_row_bf16(__nv_bfloat16* row, uint32_t tmem
     }
   }
 }
+
+// TMEM column of the bf16 A operand for K step kk (16 elements = 8 columns): the two column groups'
+// packed halves live at [0, 32) and [64, 96) of the region.
+__device__ __forceinline__ uint32_t split_a_col(int kk) { return kk < 4 ? kk * 8 : 64 + (kk - 4) * 8; }
 
 // ------------------------------------------------------------------ D = rowsum(dO * O)
 __global__ void bwd_dot_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
@@ -104,7 +115,7 @@ struct DkvSmem {
   int abort_flag;
 };
 
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(384, 1)
 flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_g,
                       BwdParams p) {
@@ -125,8 +136,8 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
     }
     mbar_init(&sm.s_full, 1);
     mbar_init(&sm.dp_full, 1);
-    mbar_init(&sm.p_full, 128);
-    mbar_init(&sm.ds_full, 128);
+    mbar_init(&sm.p_full, 256);
+    mbar_init(&sm.ds_full, 256);
     mbar_init(&sm.done, 1);
     sm.abort_flag = 0;
     fence_barrier_init();
@@ -182,7 +193,7 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       auto gemm_ts = [&](uint32_t d, uint32_t a_tmem, uint32_t b, bool acc) {
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_bf16_ts(d, a_tmem + kk * 8, smem_desc_sw128(b + kk * 2048, kHalfBytes, 1024), idesc_mn,
+          mma_bf16_ts(d, a_tmem + split_a_col(kk), smem_desc_sw128(b + kk * 2048, kHalfBytes, 1024), idesc_mn,
                       (acc || kk > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(&sm.kv_full, 0, kStatusTimeoutTmaFull, abort_flag, p.status);
@@ -221,10 +232,12 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       mbar_wait(&sm.done, 0, kStatusTimeoutMma, nullptr, p.status);
     }
   } else if (warp >= 4) {
+    const int g = (warp - 4) >> 2;  // column group: query columns [64g, 64g + 64)
+    const int c0 = 64 * g;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
     const uint32_t lb = (uint32_t)(wq * 32) << 16;
-    const uint32_t t_s = tmem + lb, t_dp = tmem + lb + 128;
+    const uint32_t t_s = tmem + lb + c0, t_dp = tmem + lb + 128 + c0;
     const float scale_log2 = p.scale_log2, scale = p.scale;
     bool ok = true;
     for (int i = 0; i < nq; ++i) {
@@ -234,28 +247,24 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.s_full, i & 1, kStatusTimeoutMma, abort_flag, p.status));
       if (!ok) break;
       tc_fence_after();
-      float pv[128];
+      float pv[64];
       {
-        uint32_t r[32];
+        uint32_t r[2][32];
+        tmem_ld32(t_s, r[0]);
+        tmem_ld32(t_s + 32, r[1]);
+        tmem_wait_ld();
+        const float* lse = sm.lse[s] + c0;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(t_s + c * 32, r);
-          tmem_wait_ld();
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) pv[c * 32 + e] = __uint_as_float(r[e]);
-        }
+          for (int e = 0; e < 32; ++e)
+            pv[c * 32 + e] = ex2_approx(fmaf(__uint_as_float(r[c][e]), scale_log2, -lse[c * 32 + e]));
       }
-      const float* lse = sm.lse[s];
-#pragma unroll
-      for (int e = 0; e < 128; ++e) pv[e] = ex2_approx(fmaf(pv[e], scale_log2, -lse[e]));
       {
-        uint32_t r[32];
+        uint32_t w[32];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) r[e] = pack_bf16x2(pv[64 * c + 2 * e], pv[64 * c + 2 * e + 1]);
-          tmem_st32(t_s + c * 32, r);
-        }
+        for (int e = 0; e < 32; ++e) w[e] = pack_bf16x2(pv[2 * e], pv[2 * e + 1]);
+        tmem_st32(t_s, w);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -264,21 +273,23 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       ok = __all_sync(0xffffffffu, mbar_wait(&sm.dp_full, i & 1, kStatusTimeoutMma, abort_flag, p.status));
       if (!ok) break;
       tc_fence_after();
-      const float* dd = sm.dd[s];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(t_dp + c * 32, r);
+      {
+        uint32_t r[2][32];
+        tmem_ld32(t_dp, r[0]);
+        tmem_ld32(t_dp + 32, r[1]);
         tmem_wait_ld();
-        uint32_t w[16];
+        const float* dd = sm.dd[s] + c0;
+        uint32_t w[32];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int q = c * 32 + 2 * e;
-          const float d0 = pv[q] * (__uint_as_float(r[2 * e]) - dd[q]) * scale;
-          const float d1 = pv[q + 1] * (__uint_as_float(r[2 * e + 1]) - dd[q + 1]) * scale;
-          w[e] = pack_bf16x2(d0, d1);
-        }
-        tmem_st16(t_dp + c * 16, w);
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int q = c * 32 + 2 * e;
+            const float d0 = pv[q] * (__uint_as_float(r[c][2 * e]) - dd[q]) * scale;
+            const float d1 = pv[q + 1] * (__uint_as_float(r[c][2 * e + 1]) - dd[q + 1]) * scale;
+            w[c * 16 + e] = pack_bf16x2(d0, d1);
+          }
+        tmem_st32(t_dp, w);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -291,8 +302,8 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       const bool valid = kr < p.Lk;
       __nv_bfloat16* dv_row = valid ? p.out2 + batch * p.sb2 + (int64_t)kr * p.sl2 + head * p.sh2 : nullptr;
       __nv_bfloat16* dk_row = valid ? p.out + batch * p.sb + (int64_t)kr * p.sl + head * p.sh : nullptr;
-      store_row_bf16(dv_row, tmem + lb + 256, 1.f);
-      store_row_bf16(dk_row, tmem + lb + 384, 1.f);
+      store_row_bf16(dv_row, tmem + lb + 256, 1.f, c0, 2);
+      store_row_bf16(dk_row, tmem + lb + 384, 1.f, c0, 2);
     }
   }
   tc_fence_before();
@@ -317,7 +328,7 @@ struct DqSmem {
   int abort_flag;
 };
 
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(384, 1)
 flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_g,
                     BwdParams p) {
@@ -335,10 +346,10 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       mbar_init(&sm.kv_full[s], 1);
       mbar_init(&sm.kv_empty[s], 1);
       mbar_init(&sm.s_full[s], 1);
-      mbar_init(&sm.s_free[s], 128);
+      mbar_init(&sm.s_free[s], 256);
     }
     mbar_init(&sm.dp_full, 1);
-    mbar_init(&sm.ds_full, 128);
+    mbar_init(&sm.ds_full, 256);
     mbar_init(&sm.done, 1);
     sm.abort_flag = 0;
     fence_barrier_init();
@@ -416,7 +427,7 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         const uint32_t kb = smem_u32(sm.k[s]);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_bf16_ts(t_dq, t_dp + kk * 8, smem_desc_sw128(kb + kk * 2048, kHalfBytes, 1024), idesc_mn,
+          mma_bf16_ts(t_dq, t_dp + split_a_col(kk), smem_desc_sw128(kb + kk * 2048, kHalfBytes, 1024), idesc_mn,
                       (j > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&sm.kv_empty[s]);
         if (has_next) {
@@ -428,11 +439,13 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       mbar_wait(&sm.done, 0, kStatusTimeoutMma, nullptr, p.status);
     }
   } else if (warp >= 4) {
+    const int g = (warp - 4) >> 2;  // column group: key columns [64g, 64g + 64)
+    const int c0 = 64 * g;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
     const int q_row = q0 + row;
     const uint32_t lb = (uint32_t)(wq * 32) << 16;
-    const uint32_t t_dp = tmem + lb + 256;
+    const uint32_t t_dp = tmem + lb + 256 + c0;
     const float scale_log2 = p.scale_log2, scale = p.scale;
     const int64_t bh_off = ((int64_t)batch * p.H + head) * p.Lpad;
     const float lse2 = p.lse2[bh_off + q_row];
@@ -443,38 +456,40 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       ok = __all_sync(0xffffffffu, mbar_wait(&sm.s_full[s], (j >> 1) & 1, kStatusTimeoutMma, abort_flag, p.status));
       if (!ok) break;
       tc_fence_after();
-      float pv[128];
+      float pv[64];
+      const int kv_valid = p.Lk - j * 128 - c0;
       {
-        uint32_t r[32];
+        uint32_t r[2][32];
+        tmem_ld32(tmem + lb + s * 128 + c0, r[0]);
+        tmem_ld32(tmem + lb + s * 128 + c0 + 32, r[1]);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&sm.s_free[s]);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(tmem + lb + s * 128 + c * 32, r);
-          tmem_wait_ld();
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) pv[c * 32 + e] = __uint_as_float(r[e]);
-        }
+          for (int e = 0; e < 32; ++e)
+            pv[c * 32 + e] = (c * 32 + e < kv_valid) ? ex2_approx(fmaf(__uint_as_float(r[c][e]), scale_log2, -lse2))
+                                                     : 0.f;
       }
-      tc_fence_before();
-      mbar_arrive(&sm.s_free[s]);
-      const int kv_valid = p.Lk - j * 128;
-#pragma unroll
-      for (int e = 0; e < 128; ++e) pv[e] = e < kv_valid ? ex2_approx(fmaf(pv[e], scale_log2, -lse2)) : 0.f;
       ok = __all_sync(0xffffffffu, mbar_wait(&sm.dp_full, j & 1, kStatusTimeoutMma, abort_flag, p.status));
       if (!ok) break;
       tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(t_dp + c * 32, r);
+      {
+        uint32_t r[2][32];
+        tmem_ld32(t_dp, r[0]);
+        tmem_ld32(t_dp + 32, r[1]);
         tmem_wait_ld();
-        uint32_t w[16];
+        uint32_t w[32];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int kv = c * 32 + 2 * e;
-          w[e] = pack_bf16x2(pv[kv] * (__uint_as_float(r[2 * e]) - dval) * scale,
-                             pv[kv + 1] * (__uint_as_float(r[2 * e + 1]) - dval) * scale);
-        }
-        tmem_st16(t_dp + c * 16, w);
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int kv = c * 32 + 2 * e;
+            w[c * 16 + e] = pack_bf16x2(pv[kv] * (__uint_as_float(r[c][2 * e]) - dval) * scale,
+                                        pv[kv + 1] * (__uint_as_float(r[c][2 * e + 1]) - dval) * scale);
+          }
+        tmem_st32(t_dp, w);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -484,7 +499,7 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     if (ok) {
       tc_fence_after();
       __nv_bfloat16* dq_row = q_row < p.Lq ? p.out + batch * p.sb + (int64_t)q_row * p.sl + head * p.sh : nullptr;
-      store_row_bf16(dq_row, tmem + lb + 384, 1.f);
+      store_row_bf16(dq_row, tmem + lb + 384, 1.f, c0, 2);
     }
   }
   tc_fence_before();
@@ -560,7 +575,7 @@ void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, co
     C10_CUDA_CHECK(
         cudaFuncSetAttribute(flash_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid((Lk + 127) / 128, H, B);
-    flash_bwd_dkdv_kernel<<<grid, 256, smem, stream>>>(tq, tk, tv, tg, p);
+    flash_bwd_dkdv_kernel<<<grid, 384, smem, stream>>>(tq, tk, tv, tg, p);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
   {
@@ -572,7 +587,7 @@ void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, co
     const size_t smem = sizeof(DqSmem) + 1024;
     C10_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid((Lq + 127) / 128, H, B);
-    flash_bwd_dq_kernel<<<grid, 256, smem, stream>>>(tq, tk, tv, tg, p);
+    flash_bwd_dq_kernel<<<grid, 384, smem, stream>>>(tq, tk, tv, tg, p);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }
@@ -711,7 +726,7 @@ extern "C" int dmad_flash_attn_bwd_noalloc(const void* q, const void* k, const v
   if (cudaFuncSetAttribute(flash_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_a) !=
       cudaSuccess)
     return DMAD_NOALLOC_ERR_CUDA;
-  flash_bwd_dkdv_kernel<<<dim3((Lk + 127) / 128, H, B), 256, smem_a, s>>>(tq, tk, tv, tg, p);
+  flash_bwd_dkdv_kernel<<<dim3((Lk + 127) / 128, H, B), 384, smem_a, s>>>(tq, tk, tv, tg, p);
   p.out = static_cast<__nv_bfloat16*>(dq);
   p.sb = sdq[0];
   p.sl = sdq[1];
@@ -721,7 +736,7 @@ extern "C" int dmad_flash_attn_bwd_noalloc(const void* q, const void* k, const v
   if (cudaFuncSetAttribute(flash_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_b) !=
       cudaSuccess)
     return DMAD_NOALLOC_ERR_CUDA;
-  flash_bwd_dq_kernel<<<dim3((Lq + 127) / 128, H, B), 256, smem_b, s>>>(tq, tk, tv, tg, p);
+  flash_bwd_dq_kernel<<<dim3((Lq + 127) / 128, H, B), 384, smem_b, s>>>(tq, tk, tv, tg, p);
   if (cudaGetLastError() != cudaSuccess) return DMAD_NOALLOC_ERR_CUDA;
   return DMAD_NOALLOC_OK;
 }

@@ -18,3 +18,20 @@ def test_wan_sample_cli_tiny(tmp_path):
         assert os.path.exists(tmp_path / "out" / r["path"])
     g = t_grid(parse(["--distilled", "--num_steps", "4"]))
     assert len(g) == 5 and g[-1] == 0.0 and abs(g[0] - 1600 / 1601) < 1e-9
+
+
+def test_build_wan_dataset_tiny(tmp_path):
+    """Teacher shards from the dataset builder load through the tar-shard dataset."""
+    import torch
+    from dmad_b200.data import TarShardDataset
+    from dmad_b200.tools.build_wan_dataset import main
+
+    (tmp_path / "p.txt").write_text("a cat\na dog\na bird\n")
+    paths = main(["--tiny", "--prompts", str(tmp_path / "p.txt"), "--out", str(tmp_path / "shards"),
+                  "--num-frames", "5", "--height", "32", "--width", "32", "--steps", "3",
+                  "--samples-per-shard", "2"])
+    assert len(paths) == 2
+    batches = list(TarShardDataset(str(tmp_path / "shards" / "*.tar"), batch_size=1, shuffle_buffer=1, epochs=1))
+    assert len(batches) == 3
+    assert batches[0]["latents"].shape == (1, 16, 2, 4, 4) and batches[0]["t5_text_embeddings"].shape == (1, 16, 64)
+    assert torch.isfinite(batches[0]["latents"].float()).all()
