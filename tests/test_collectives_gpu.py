@@ -130,9 +130,10 @@ def _worker(rank, world, port, multicast, clip, q):
             opt.step(ema_beta=0.9, max_grad_norm=clip)
         torch.cuda.synchronize()
         check_device_status()
-        out = [p.detach().float().cpu() for p in params]
-        ema = [e.cpu() for e in opt.full_ema()]
-        master = [m_.cpu() for m_ in opt.full_master()]
+        # numpy arrays: tensors sent through the queue would need the worker alive to be received
+        out = [p.detach().float().cpu().numpy() for p in params]
+        ema = [e.cpu().numpy() for e in opt.full_ema()]
+        master = [m_.cpu().numpy() for m_ in opt.full_master()]
         del opt
         dist.barrier()
         dist.destroy_process_group()
@@ -172,6 +173,7 @@ def test_sharded_adamw_two_gpus(multicast, clip):
                                                   scale, ema[i], 0.9)
     for rank, out, e_out, master, used_mc, err in res:
         assert err is None, err
+        out, e_out, master = ([torch.from_numpy(a) for a in xs] for xs in (out, e_out, master))
         tol = 2e-2 if used_mc else 1e-4  # the switch returns bf16 sums
         for a, b in zip(master, w):
             torch.testing.assert_close(a, b, rtol=tol, atol=tol)
