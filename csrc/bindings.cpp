@@ -64,12 +64,12 @@ void peer_copy_to(int64_t dst_ptr, const at::Tensor& src, int64_t nbytes);
 void symm_barrier(const at::Tensor& buf_ptrs, int64_t rank, int64_t epoch, c10::optional<at::Tensor> payload,
                   double timeout_s);
 void dp_sumsq(std::vector<int64_t> grad_ptrs, std::vector<int64_t> param_ptrs, int64_t mc_grads, int64_t mc_params,
-              int64_t elem_size, int64_t off, int64_t len, at::Tensor& acc);
+              int64_t elem_size, int64_t off, int64_t len, at::Tensor& acc, bool force_finite);
 void dp_adamw(std::vector<int64_t> grad_ptrs, std::vector<int64_t> param_ptrs, int64_t mc_grads, int64_t mc_params,
               int64_t elem_size, at::Tensor& master, at::Tensor& exp_avg, at::Tensor& exp_avg_sq,
               c10::optional<at::Tensor> ema, int64_t off, int64_t len, double lr, double beta1, double beta2,
               double eps, double weight_decay, int64_t step, double ema_beta, c10::optional<at::Tensor> slots,
-              double max_norm);
+              double max_norm, bool force_finite);
 }  // namespace dmad
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {

@@ -138,6 +138,7 @@ struct DpArgs {
   const int* status;
   int64_t off, len;  // shard in elements (multiples of 8)
   int world;
+  int force_finite;  // replace non-finite averaged gradients by 0 (GradClip(force_finite))
   float inv_world, lr, b1, b2, eps, wd, step_size, inv_sqrt_bc2, ema_beta, max_norm;
 };
 
@@ -159,7 +160,10 @@ __device__ __forceinline__ void gather_avg(const DpArgs& a, int64_t e, float (&g
     }
   }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) g[i] *= a.inv_world;
+  for (int i = 0; i < 8; ++i) {
+    g[i] *= a.inv_world;
+    if (a.force_finite && !isfinite(g[i])) g[i] = 0.f;
+  }
 }
 
 template <typename T>
@@ -230,7 +234,7 @@ __global__ void __launch_bounds__(256) dp_adamw_kernel(DpArgs a) {
 }
 
 DpArgs make_args(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_t>& param_ptrs, int64_t mc_grads,
-                 int64_t mc_params, int64_t elem_size, int64_t off, int64_t len, int device) {
+                 int64_t mc_params, int64_t elem_size, int64_t off, int64_t len, int device, bool force_finite) {
   const int world = (int)grad_ptrs.size();
   TORCH_CHECK(world >= 1 && world <= kMaxWorld && (int)param_ptrs.size() == world, "bad world size ", world);
   TORCH_CHECK(off % 8 == 0 && len % 8 == 0 && len > 0, "shard offset / length must be positive multiples of 8");
@@ -250,6 +254,7 @@ DpArgs make_args(const std::vector<int64_t>& grad_ptrs, const std::vector<int64_
   a.world = world;
   a.inv_world = 1.f / world;
   a.status = device_status_ptr(device);
+  a.force_finite = force_finite ? 1 : 0;
   (void)elem_size;
   return a;
 }
@@ -281,10 +286,10 @@ void symm_barrier(const at::Tensor& buf_ptrs, int64_t rank, int64_t epoch, c10::
 
 // acc: one-float CUDA tensor (zeroed by the caller) that receives this rank's partial sum of squares.
 void dp_sumsq(std::vector<int64_t> grad_ptrs, std::vector<int64_t> param_ptrs, int64_t mc_grads, int64_t mc_params,
-              int64_t elem_size, int64_t off, int64_t len, at::Tensor& acc) {
+              int64_t elem_size, int64_t off, int64_t len, at::Tensor& acc, bool force_finite) {
   TORCH_CHECK(acc.is_cuda() && acc.scalar_type() == at::kFloat, "acc must be a float CUDA tensor");
   c10::cuda::CUDAGuard guard(acc.device());
-  DpArgs a = make_args(grad_ptrs, param_ptrs, mc_grads, mc_params, elem_size, off, len, acc.get_device());
+  DpArgs a = make_args(grad_ptrs, param_ptrs, mc_grads, mc_params, elem_size, off, len, acc.get_device(), force_finite);
   auto stream = at::cuda::getCurrentCUDAStream();
   if (elem_size == 2)
     dp_sumsq_kernel<__nv_bfloat16><<<grid_for(len), 256, 0, stream>>>(a, acc.data_ptr<float>());
@@ -301,14 +306,15 @@ void dp_adamw(std::vector<int64_t> grad_ptrs, std::vector<int64_t> param_ptrs, i
               int64_t elem_size, at::Tensor& master, at::Tensor& exp_avg, at::Tensor& exp_avg_sq,
               c10::optional<at::Tensor> ema, int64_t off, int64_t len, double lr, double beta1, double beta2,
               double eps, double weight_decay, int64_t step, double ema_beta, c10::optional<at::Tensor> slots,
-              double max_norm) {
+              double max_norm, bool force_finite) {
   for (const at::Tensor* t : {&master, &exp_avg, &exp_avg_sq}) {
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() >= len,
                 "shard state must be contiguous fp32 CUDA tensors of at least len elements");
     TORCH_CHECK(reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0, "shard state must be 16-byte aligned");
   }
   c10::cuda::CUDAGuard guard(master.device());
-  DpArgs a = make_args(grad_ptrs, param_ptrs, mc_grads, mc_params, elem_size, off, len, master.get_device());
+  DpArgs a = make_args(grad_ptrs, param_ptrs, mc_grads, mc_params, elem_size, off, len, master.get_device(),
+                       force_finite);
   a.master = master.data_ptr<float>();
   a.m = exp_avg.data_ptr<float>();
   a.v = exp_avg_sq.data_ptr<float>();

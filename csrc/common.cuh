@@ -14,6 +14,17 @@
     else { constexpr int VEC = 4, TH = 256; __VA_ARGS__(); }                \
   }()
 
+// Optional index guards (build with DMAD_BOUNDS_CHECK=1): a guarded access whose index is out of
+// range records status code 6 (bounds) in the device status word and is skipped instead of faulting.
+#ifdef DMAD_BOUNDS_CHECK
+#define DMAD_GUARD(cond, status)                          \
+  if (!(cond)) {                                         \
+    if ((status) != nullptr) atomicCAS((status), 0, 6);  \
+  } else
+#else
+#define DMAD_GUARD(cond, status)
+#endif
+
 namespace dmad {
 
 struct alignas(16) bf16x8 {

@@ -24,6 +24,8 @@
 
 namespace dmad {
 
+int* device_status_ptr(int device);
+
 namespace {
 
 constexpr int kMaxCp = 16;
@@ -38,7 +40,7 @@ __global__ void __launch_bounds__(kTh)
 cp_qkv_push_kernel(const __nv_bfloat16* __restrict__ src, int64_t ss, PeerTable dst, const float* __restrict__ wq,
                    const float* __restrict__ wk, const float* __restrict__ cosT, const float* __restrict__ sinT,
                    float* __restrict__ rstd_q, float* __restrict__ rstd_k, int Ll, int L, int D, int hd, int Hl,
-                   int rank, float eps) {
+                   int rank, float eps, int cp, int* status) {
   __shared__ float red[32];
   const int64_t r = blockIdx.x;
   const int which = blockIdx.y;
@@ -92,6 +94,7 @@ cp_qkv_push_kernel(const __nv_bfloat16* __restrict__ src, int64_t ss, PeerTable 
       }
       __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(dst.p[peer]) +
                          ((grow * 3 + which) * Hl + hl) * (int64_t)hd + (col % hd);
+      DMAD_GUARD(peer < cp && grow < (int64_t)(r / Ll + 1) * L, status)
       *reinterpret_cast<bf16x8*>(d) = float_to_bf16x8(o);
     }
   }
@@ -100,7 +103,7 @@ cp_qkv_push_kernel(const __nv_bfloat16* __restrict__ src, int64_t ss, PeerTable 
 
 // one thread per 8 elements of the local [B*Ll, n*D] source
 __global__ void cp_seq_to_head_kernel(const __nv_bfloat16* __restrict__ src, int64_t ss, PeerTable dst, int64_t R,
-                                      int Ll, int L, int D, int n, int hd, int Hl, int rank) {
+                                      int Ll, int L, int D, int n, int hd, int Hl, int rank, int cp, int* status) {
   const int per_row = n * D / 8;
   const int64_t total = R * per_row;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -113,6 +116,7 @@ __global__ void cp_seq_to_head_kernel(const __nv_bfloat16* __restrict__ src, int
     const bf16x8 x = *reinterpret_cast<const bf16x8*>(src + r * ss + cc);
     __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(dst.p[peer]) +
                        ((grow * n + which) * Hl + hl) * (int64_t)hd + (col % hd);
+    DMAD_GUARD(peer < cp, status)
     *reinterpret_cast<bf16x8*>(d) = x;
   }
 }
@@ -126,7 +130,7 @@ struct HeadSrc {
 };
 
 __global__ void cp_head_to_seq_kernel(HeadSrc src, PeerTable dst, int64_t ld, int B, int Ll, int L, int D, int n,
-                                      int hd, int Hl, int rank) {
+                                      int hd, int Hl, int rank, int cp, int* status) {
   const int per_row = n * Hl * hd / 8;
   const int64_t total = (int64_t)B * L * per_row;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -141,6 +145,7 @@ __global__ void cp_head_to_seq_kernel(HeadSrc src, PeerTable dst, int64_t ld, in
     const bf16x8 x = *reinterpret_cast<const bf16x8*>(s);
     __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(dst.p[peer]) + ((int64_t)b * Ll + lr) * ld + which * D +
                        (int64_t)(rank * Hl + hl) * hd + e;
+    DMAD_GUARD(peer < cp && which < n, status)
     *reinterpret_cast<bf16x8*>(d) = x;
   }
 }
@@ -182,7 +187,8 @@ void cp_qkv_push(const at::Tensor& src, std::vector<int64_t> dst, const at::Tens
     cp_qkv_push_kernel<VEC, TH><<<grid, TH, 0, at::cuda::getCurrentCUDAStream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), src.stride(0), t, wq.data_ptr<float>(),
         wk.data_ptr<float>(), cosT.data_ptr<float>(), sinT.data_ptr<float>(), rstd_q.data_ptr<float>(),
-        rstd_k.data_ptr<float>(), Ll, Ll * cp, (int)D, (int)hd, (int)(D / hd / cp), (int)rank, (float)eps);
+        rstd_k.data_ptr<float>(), Ll, Ll * cp, (int)D, (int)hd, (int)(D / hd / cp), (int)rank, (float)eps, cp,
+        device_status_ptr(src.get_device()));
   });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -201,7 +207,7 @@ void cp_seq_to_head(const at::Tensor& src, std::vector<int64_t> dst, int64_t B, 
   const int Ll = (int)(R / B);
   cp_seq_to_head_kernel<<<grid_1d(R * n * D / 8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), src.stride(0), make_table(dst), R, Ll, Ll * cp,
-      (int)D, (int)n, (int)hd, (int)(D / hd / cp), (int)rank);
+      (int)D, (int)n, (int)hd, (int)(D / hd / cp), (int)rank, cp, device_status_ptr(src.get_device()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -229,7 +235,7 @@ void cp_head_to_seq(std::vector<at::Tensor> srcs, std::vector<int64_t> dst, int6
   const int64_t total = (int64_t)B * L * n * Hl * hd / 8;
   if (total == 0) return;
   cp_head_to_seq_kernel<<<grid_1d(total), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      hs, make_table(dst), ld, B, L / cp, L, (int)D, n, hd, Hl, (int)rank);
+      hs, make_table(dst), ld, B, L / cp, L, (int)D, n, hd, Hl, (int)rank, cp, device_status_ptr(s0.get_device()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -12,6 +12,9 @@
 #include "common.cuh"
 
 namespace dmad {
+
+int* device_status_ptr(int device);
+
 namespace {
 
 constexpr int kMaxRanks = 16;
@@ -21,7 +24,7 @@ struct Shards {
 };
 
 __global__ void fsdp_gather_kernel(Shards src, uint4* __restrict__ dst, int world, int64_t len_vec,
-                                   int64_t n_vec) {
+                                   int64_t n_vec, int* status) {
   const int64_t total = len_vec * world;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     // visit the ranks in an order that starts at a different peer for every CTA
@@ -29,6 +32,7 @@ __global__ void fsdp_gather_kernel(Shards src, uint4* __restrict__ dst, int worl
     const int r = (int)((chunk + blockIdx.x) % world);
     const int64_t j = i % len_vec;
     const int64_t g = (int64_t)r * len_vec + j;  // element-vector index in the gathered buffer
+    DMAD_GUARD(r < world && j < len_vec, status)
     if (g < n_vec) dst[g] = reinterpret_cast<const uint4*>(src.p[r])[j];
   }
 }
@@ -53,7 +57,7 @@ void fsdp_gather(std::vector<int64_t> shard_ptrs, at::Tensor& dst, int64_t len, 
   const int64_t len_vec = len / 8, total = len_vec * world;
   const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
   fsdp_gather_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      s, reinterpret_cast<uint4*>(dst.data_ptr()), world, len_vec, numel / 8);
+      s, reinterpret_cast<uint4*>(dst.data_ptr()), world, len_vec, numel / 8, device_status_ptr(dst.get_device()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

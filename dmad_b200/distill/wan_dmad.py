@@ -63,7 +63,8 @@ class WanDMADConfig:
     eps: float = 1e-8
     ema_enabled: bool = True
     ema_rate: float = 0.1
-    grad_clip: float | None = None
+    grad_clip: float | None = None  # rcm grad_clip=False: no clipping (max norm 1e12)
+    grad_force_finite: bool = True  # the default GradClip(force_finite=True) callback: nan/inf grads -> 0
     student_lora_rank: int = 0
     checkpoint_student_blocks: int = 0
     checkpoint_critic_blocks: int = 0
@@ -150,7 +151,7 @@ class WanDMAD(nn.Module):
         self.ema_coef = ema_exp_coefficient(cfg.ema_rate)
         if cfg.dp_optimizer == "sharded":
             kw = dict(betas=cfg.betas, eps=cfg.eps, weight_decay=cfg.weight_decay, use_multicast=cfg.dp_multicast,
-                      sync_timeout_s=cfg.dp_sync_timeout_s)
+                      sync_timeout_s=cfg.dp_sync_timeout_s, force_finite=cfg.grad_force_finite)
             self.opt_student = ShardedAdamW(s_params, lr=cfg.lr, ema=cfg.ema_enabled, **kw)
             self.opt_critic = ShardedAdamW(c_params, lr=cfg.critic_lr, **kw)
             self.ema_params = None

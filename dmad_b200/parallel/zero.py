@@ -81,7 +81,8 @@ class ShardedAdamW:
 
     def __init__(self, params: Iterable[torch.nn.Parameter], lr=1e-4, betas=(0.9, 0.999), eps=1e-8,
                  weight_decay=0.0, ema: bool = False, group=None, use_multicast: bool = True,
-                 sync_timeout_s: float = 120.0):
+                 sync_timeout_s: float = 120.0, force_finite: bool = False):
+        self.force_finite = force_finite
         self.params = [p for p in params]
         self.lr, self.betas, self.eps, self.weight_decay = lr, tuple(betas), eps, weight_decay
         self.step_count = 0
@@ -147,7 +148,7 @@ class ShardedAdamW:
             self._acc.zero_()
             for g in self.groups:
                 ext().dp_sumsq(g.gbuf.ptrs, g.pbuf.ptrs, g.gbuf.mc_ptr if mc else 0, g.pbuf.mc_ptr if mc else 0,
-                               g.pbuf.tensor.element_size(), g.off, g.len, self._acc)
+                               g.pbuf.tensor.element_size(), g.off, g.len, self._acc, self.force_finite)
             self.sync(self._acc)
             slots = self.sync.slots
         for g in self.groups:
@@ -156,7 +157,7 @@ class ShardedAdamW:
                            g.ema if ema_beta is not None else None, g.off, g.len, float(self.lr), float(b1),
                            float(b2), float(self.eps), float(self.weight_decay), int(self.step_count),
                            float(ema_beta) if ema_beta is not None else 0.0, slots,
-                           float(max_grad_norm) if clip else 0.0)
+                           float(max_grad_norm) if clip else 0.0, self.force_finite)
         self.sync()
 
     # ------------------------------------------------------------------ host path (gloo / CPU)
@@ -170,7 +171,10 @@ class ShardedAdamW:
             flat = g.gbuf.tensor.float()
             if dist_on:
                 dist.all_reduce(flat, group=self.group)
-            shards.append(flat[g.off:g.off + g.len] / self.world)
+            sh = flat[g.off:g.off + g.len] / self.world
+            if self.force_finite:
+                sh = torch.nan_to_num(sh, nan=0.0, posinf=0.0, neginf=0.0)
+            shards.append(sh)
         scale = 1.0
         if max_norm is not None:
             ss = torch.stack([(s * s).sum() for s in shards]).sum().reshape(1)

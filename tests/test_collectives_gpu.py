@@ -47,7 +47,7 @@ def test_dp_adamw_single_gpu(clip):
     scale = 1.0
     if clip is not None:
         acc = torch.zeros(1, device=dev)
-        ext().dp_sumsq([g.data_ptr()], [p.data_ptr()], 0, 0, 2, 0, n, acc)
+        ext().dp_sumsq([g.data_ptr()], [p.data_ptr()], 0, 0, 2, 0, n, acc, False)
         ref_ss = float((g.float() ** 2).sum())
         assert abs(float(acc) - ref_ss) / ref_ss < 1e-4
         sync = PeerSync(dev)
@@ -55,7 +55,7 @@ def test_dp_adamw_single_gpu(clip):
         slots = sync.slots
         scale = min(1.0, clip / (ref_ss ** 0.5 + 1e-6))
     ext().dp_adamw([g.data_ptr()], [p.data_ptr()], 0, 0, 2, master, m, v, ema, 0, n, 1e-3, 0.9, 0.99, 1e-8,
-                   0.01, 3, 0.95, slots, float(clip or 0.0))
+                   0.01, 3, 0.95, slots, float(clip or 0.0), False)
     torch.cuda.synchronize()
     check_device_status()
     rw, rm, rv, re = _adamw_ref(w0, g, m0, v0, 3, 1e-3, 0.9, 0.99, 1e-8, 0.01, scale, w0.clone(), 0.95)
@@ -83,7 +83,7 @@ def test_barrier_timeout_reports_and_blocks_update():
     g = torch.ones(n, dtype=torch.bfloat16, device=dev)
     master, m, v = torch.ones(n, device=dev), torch.zeros(n, device=dev), torch.zeros(n, device=dev)
     ext().dp_adamw([g.data_ptr()], [p.data_ptr()], 0, 0, 2, master, m, v, None, 0, n, 1e-2, 0.9, 0.99, 1e-8,
-                   0.0, 1, 0.0, None, 0.0)
+                   0.0, 1, 0.0, None, 0.0, False)
     torch.cuda.synchronize()
     assert int(fake_peer[0]) == 1  # our own flag reached the peer
     assert device_status(0, reset=True) == 5
