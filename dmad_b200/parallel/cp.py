@@ -118,13 +118,15 @@ class ContextParallel:
         if self.impl == "nccl" or not rows.is_cuda:
             return self.a2a_seq_to_head(rows, B, n, H, hd)
         from .. import ops
+        from ..runtime.nvtx import nvtx_range
 
         Hl = H // self.world
         L = rows.shape[0] // B * self.world
         slot, ptrs = self.slot(B * L * n * Hl * hd)
         rows = rows if (rows.stride(-1) == 1 and rows.stride(0) % 8 == 0) else rows.contiguous()
-        ops.ext().cp_seq_to_head(rows, ptrs, B, H * hd, n, hd, self.rank)
-        self.sync()
+        with nvtx_range("dmad.cp.seq_to_head"):
+            ops.ext().cp_seq_to_head(rows, ptrs, B, H * hd, n, hd, self.rank)
+            self.sync()
         return slot.view(B, L, n, Hl, hd)
 
     def head_to_seq(self, y: torch.Tensor, B: int) -> torch.Tensor:

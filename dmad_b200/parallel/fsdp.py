@@ -77,7 +77,9 @@ class ShardedFrozenBlocks:
         dst = self.slots[slot]
         if self.cuda:
             from ..ops import ext
-            ext().fsdp_gather([p + base * 2 for p in self.arena.ptrs], dst, ln, n)
+            from ..runtime.nvtx import nvtx_range
+            with nvtx_range(f"dmad.fsdp.gather[{i}]"):
+                ext().fsdp_gather([p + base * 2 for p in self.arena.ptrs], dst, ln, n)
         elif is_distributed() and self.world > 1:
             parts = [torch.empty(ln, dtype=torch.bfloat16) for _ in range(self.world)]
             dist.all_gather(parts, self.arena.tensor[base:base + ln].contiguous(), group=self.group)

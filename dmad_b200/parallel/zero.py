@@ -139,7 +139,12 @@ class ShardedAdamW:
             self._step_host(ema_beta, max_grad_norm if clip else None)
             return
         from ..ops import ext
+        from ..runtime.nvtx import nvtx_range
 
+        with nvtx_range("dmad.dp_step"):
+            self._step_device(ext, ema_beta, max_grad_norm, clip)
+
+    def _step_device(self, ext, ema_beta, max_grad_norm, clip):
         b1, b2 = self.betas
         mc = self.multicast
         self.sync()
