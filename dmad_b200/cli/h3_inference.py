@@ -45,6 +45,15 @@ def parse_args(argv=None):
     p.add_argument("--low-vram", nargs="?", const="auto", choices=["auto", "8", "12", "16", "24"], default=None)
     p.add_argument("--weights-in-ram", action="store_true")
     p.add_argument("--weights-int8", action="store_true")
+    p.add_argument("--weights-cache", default=None, help="accepted for flag compatibility (int8 weights are "
+                   "quantised in memory)")
+    p.add_argument("--chunk-rows", type=int, default=None, help="accepted for flag compatibility")
+    p.add_argument("--offload", action="store_true", help="same as --low-vram auto")
+    p.add_argument("--vae-offload", action="store_true", help="accepted for flag compatibility")
+    p.add_argument("--vae-dtype", default="bf16", choices=["bf16", "fp32"], help="accepted for flag compatibility")
+    p.add_argument("--cp", action="store_true", help="context parallel over all ranks (launch with torchrun): "
+                   "every rank holds a slice of the packed sequence")
+    p.add_argument("--cp-impl", default="fused", choices=["fused", "nccl"])
     return p.parse_args(argv)
 
 
@@ -64,11 +73,23 @@ def main(argv=None):
     if not prompts:
         prompts = ["synthetic prompt"]
     os.makedirs(args.output_dir, exist_ok=True)
-    device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
+    if args.offload and not args.low_vram:
+        args.low_vram = "auto"
+    cp = None
+    if args.cp:
+        from ..parallel.cp import ContextParallel
+        from ..parallel.dist import init_distributed
+        _, _, device = init_distributed()
+        cp = ContextParallel(impl=args.cp_impl, device=device)
+    else:
+        device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else \
+            torch.device("cpu")
+    rank0 = cp is None or cp.rank == 0
     t0 = time.time()
 
     def log(msg):
-        print(f"[{time.time() - t0:6.0f}s] {msg}", flush=True)
+        if rank0:
+            print(f"[{time.time() - t0:6.0f}s] {msg}", flush=True)
 
     def peak(stage):
         if device.type == "cuda":
@@ -110,6 +131,8 @@ def main(argv=None):
         log(f"streaming {streamed.streamer.bytes_per_pass / 2**30:.1f} GiB of weights per model evaluation")
     else:
         model.to(device)
+        if cp is not None:
+            model.enable_context_parallel(cp)
     outs = []
     for i, (c, lay) in enumerate(zip(conds, layouts)):
         t1 = time.time()
@@ -122,13 +145,19 @@ def main(argv=None):
     if streamed is not None:
         streamed.close()
     peak("sampling")
-    for i, ((v, a), prompt) in enumerate(zip(outs, prompts)):
-        torch.save({"video_rows": v, "audio_rows": a, "shape": shape}, os.path.join(args.output_dir, f"{i:04d}.pt"))
-        with open(os.path.join(args.output_dir, f"{i:04d}.txt"), "w", encoding="utf-8") as f:
-            f.write(prompt)
-    with open(os.path.join(args.output_dir, "settings.json"), "w") as f:
-        json.dump({k: v for k, v in vars(args).items() if k != "prompt"}, f, indent=2)
+    if rank0:
+        for i, ((v, a), prompt) in enumerate(zip(outs, prompts)):
+            torch.save({"video_rows": v, "audio_rows": a, "shape": shape},
+                       os.path.join(args.output_dir, f"{i:04d}.pt"))
+            with open(os.path.join(args.output_dir, f"{i:04d}.txt"), "w", encoding="utf-8") as f:
+                f.write(prompt)
+        with open(os.path.join(args.output_dir, "settings.json"), "w") as f:
+            json.dump({k: v for k, v in vars(args).items() if k != "prompt"}, f, indent=2)
     log("done")
+    if cp is not None:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
     return outs
 
 

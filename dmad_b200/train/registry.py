@@ -116,7 +116,13 @@ def _build_h3(cfg: dict, device, seed: int):
     hc = to_dataclass(H3DMADConfig, d)
     if isinstance(net, dict):
         hc.model = to_dataclass(H3Config, net)
-    model = H3DMAD(hc, device=device, dtype=_dtype(device), seed=seed)
+    pool = None
+    data = cfg.get("data", {})
+    if data.get("kind") == "h3_pool":  # the prepared real / teacher / prompt-cache files
+        from ..data.h3_pool import FileLatentPool
+        pool = FileLatentPool(data["real_latent_dir"], hc.num_frames, data["caption_map"], data["prompt_cache"],
+                              data["teacher_latent_dir"], seed=seed)
+    model = H3DMAD(hc, device=device, pool=pool, dtype=_dtype(device), seed=seed)
     return _IterationAdapter(model, lambda batch, it: model.train_iteration(),
                              {"student": model.student, "fake": model.fake, "heads": model.heads},
                              {"student": model.opt_s, "fake": model.opt_f})

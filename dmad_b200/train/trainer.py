@@ -101,7 +101,7 @@ class DistillTrainer:
 
         kind = d.get("kind", "synthetic")
         bs = int(d.get("batch_size", 1))
-        if kind == "internal":  # the model draws its own batches (H3 latent pool, EDM / SDXL synthetic inputs)
+        if kind in ("internal", "h3_pool"):  # the model draws its own batches (H3 pool, EDM / SDXL synthetic)
             import itertools
             return itertools.repeat(None)
         if kind == "synthetic":
