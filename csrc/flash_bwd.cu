@@ -254,11 +254,15 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         tmem_ld32(t_s + 32, r[1]);
         tmem_wait_ld();
         const float* lse = sm.lse[s] + c0;
+        // every second exponential on the FMA pipe (padded query columns have lse = +inf: the
+        // polynomial's clamp gives ~1e-38 there, against dO = 0)
 #pragma unroll
         for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            pv[c * 32 + e] = ex2_approx(fmaf(__uint_as_float(r[c][e]), scale_log2, -lse[c * 32 + e]));
+          for (int e = 0; e < 32; ++e) {
+            const float x = fmaf(__uint_as_float(r[c][e]), scale_log2, -lse[c * 32 + e]);
+            pv[c * 32 + e] = (e & 1) ? ex2_poly(x) : ex2_approx(x);
+          }
       }
       {
         uint32_t w[32];
@@ -465,12 +469,22 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&sm.s_free[s]);
+        if (kv_valid >= 64) {  // full columns: every second exponential on the FMA pipe
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
-            pv[c * 32 + e] = (c * 32 + e < kv_valid) ? ex2_approx(fmaf(__uint_as_float(r[c][e]), scale_log2, -lse2))
-                                                     : 0.f;
+            for (int e = 0; e < 32; ++e) {
+              const float x = fmaf(__uint_as_float(r[c][e]), scale_log2, -lse2);
+              pv[c * 32 + e] = (e & 1) ? ex2_poly(x) : ex2_approx(x);
+            }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              pv[c * 32 + e] =
+                  (c * 32 + e < kv_valid) ? ex2_approx(fmaf(__uint_as_float(r[c][e]), scale_log2, -lse2)) : 0.f;
+        }
       }
       ok = __all_sync(0xffffffffu, mbar_wait(&sm.dp_full, j & 1, kStatusTimeoutMma, abort_flag, p.status));
       if (!ok) break;

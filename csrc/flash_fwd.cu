@@ -294,7 +294,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         }
         // pass 2: P = exp2(S * scale - m) and the row sum, 32 columns at a time with the next
         // chunk's TMEM read in flight.  Chunk c writes bf16 P columns [16c, 16c+16), which
-        // only overlap S columns already read.  On full tiles one exponential in four runs on
+        // only overlap S columns already read.  On full tiles every second exponential runs on
         // the FMA pipe (ex2_poly); masked columns of the last tile give exactly 0 via MUFU.
         const float neg_m = -m_used;
         uint32_t buf[2][32];
@@ -315,7 +315,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
               x1 = col + 1 < kv_valid ? x1 : -INFINITY;
             }
             const float p0 = ex2_approx(x0);
-            const float p1 = (!kMasked && (i & 1)) ? ex2_poly(x1) : ex2_approx(x1);
+            const float p1 = !kMasked ? ex2_poly(x1) : ex2_approx(x1);
             rsum[c] += p0 + p1;
             pk[i] = pack_bf16x2(p0, p1);
           }
