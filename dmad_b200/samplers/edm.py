@@ -52,7 +52,7 @@ def frechet_distance(mu1, sigma1, mu2, sigma2) -> float:
     from scipy import linalg
 
     diff = np.asarray(mu1) - np.asarray(mu2)
-    covmean, _ = linalg.sqrtm(np.asarray(sigma1) @ np.asarray(sigma2), disp=False)
+    covmean = linalg.sqrtm(np.asarray(sigma1) @ np.asarray(sigma2))
     if not np.isfinite(covmean).all():
         eps = np.eye(len(mu1)) * 1e-6
         covmean = linalg.sqrtm((sigma1 + eps) @ (sigma2 + eps))
