@@ -40,3 +40,23 @@ def test_sdxl_tiny_step_and_full_size():
          "ctx": torch.randn(B, 7, 32), "pooled": torch.randn(B, 16)}
     out = d.train_step(b)
     assert all(torch.isfinite(v) for v in out.values())
+
+
+def test_fold_spectral_norm_matches_parametrized_forward():
+    import copy
+    from dmad_b200.distill.edm_dmad import sn_wrap
+    from dmad_b200.tools.export_unet import fold_spectral_norm, plain_state_dict
+
+    torch.manual_seed(0)
+    net = torch.nn.Sequential(torch.nn.Conv2d(3, 8, 3, padding=1), torch.nn.SiLU(), torch.nn.Conv2d(8, 3, 3, padding=1))
+    plain = copy.deepcopy(net)
+    for m in net:
+        if isinstance(m, torch.nn.Conv2d):
+            sn_wrap(m, power_iters=20)
+    net.eval()
+    x = torch.randn(2, 3, 8, 8)
+    ref = net(x)
+    sd = plain_state_dict(net, torch.float32)
+    assert not any("parametrizations" in k for k in sd)
+    plain.load_state_dict(sd)
+    torch.testing.assert_close(plain(x), ref, rtol=1e-4, atol=1e-5)
