@@ -286,6 +286,36 @@ class H3DMAD:
         return out
 
     # ------------------------------------------------------------------ checkpoint pieces
+    @torch.no_grad()
+    def export_loras(self, out_dir: str):
+        """The checkpoint's LoRA files in the Diffusers layout: the live student
+        (``pytorch_lora_weights.safetensors``), one directory per power-EMA bank (``ema_lora/``,
+        ``ema2_lora/``) and the critic (``fake_lora/``) (minimax_h3_dmad_trainer.py:543-595)."""
+        import os
+
+        from ..lora import lora_pairs_from_model, save_lora_file
+
+        os.makedirs(out_dir, exist_ok=True)
+        r = self.cfg.student_lora_rank
+        save_lora_file(os.path.join(out_dir, "pytorch_lora_weights.safetensors"),
+                       lora_pairs_from_model(self.student, torch.bfloat16), r, r)
+        for k, bank in enumerate(self.ema_banks):
+            live = [p.detach().clone() for p in bank.params]
+            for p, sh in zip(bank.params, bank.shadow):
+                p.copy_(sh.to(p.dtype))
+            d = os.path.join(out_dir, "ema_lora" if k == 0 else f"ema{k + 1}_lora")
+            os.makedirs(d, exist_ok=True)
+            save_lora_file(os.path.join(d, "pytorch_lora_weights.safetensors"),
+                           lora_pairs_from_model(self.student, torch.bfloat16), r, r,
+                           {"ema_gamma": str(bank.gamma), "ema_t": str(bank.t)})
+            for p, v in zip(bank.params, live):
+                p.copy_(v)
+        if self.cfg.fake_train_type == "lora":
+            d = os.path.join(out_dir, "fake_lora")
+            os.makedirs(d, exist_ok=True)
+            save_lora_file(os.path.join(d, "pytorch_lora_weights.safetensors"),
+                           lora_pairs_from_model(self.fake, torch.bfloat16), r, r)
+
     def critic_state(self):
         return {"heads": self.heads.state_dict(), "head_optimizer": self.opt_h.state_dict(),
                 "gap_ema": self.gap.gap_ema.cpu(), "gap_cnt": self.gap.gap_ready.cpu(),

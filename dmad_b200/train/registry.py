@@ -91,6 +91,12 @@ class _IterationAdapter:
             shared["critic_state"] = extra()
         return shared, None
 
+    def export_artifacts(self, ckpt_dir: str):
+        """Extra files of a published checkpoint (rank 0), e.g. the H3 LoRA exports."""
+        fn = getattr(self.model, "export_loras", None)
+        if fn is not None:
+            fn(ckpt_dir)
+
     def load_state_dicts(self, shared, per_rank):
         for k, m in self.modules.items():
             m.load_state_dict(shared[f"module/{k}"])

@@ -130,6 +130,11 @@ class DistillTrainer:
 
         text = yaml.safe_dump(self.cfg, sort_keys=False)
         self.ckpt.save(self.iteration, shared, per_rank, config_text=text)
+        export = getattr(self.model, "export_artifacts", None)
+        if export is not None and self.rank == 0:
+            from ..runtime.checkpoint import checkpoint_name
+            self.ckpt.finalize()
+            export(os.path.join(self.output_dir, checkpoint_name(self.iteration)))
         self.log.info("saved checkpoint iteration=%d in %s", self.iteration, self.output_dir)
 
     def maybe_resume(self) -> int:

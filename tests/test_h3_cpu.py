@@ -82,3 +82,25 @@ def test_h3_dmad_iterations_cpu():
     sd = m.critic_state()
     m.load_critic_state(sd)
     assert m.student_steps == 2 and m.ema_banks[0].t == 2
+
+
+def test_h3_checkpoint_exports_loras(tmp_path):
+    """The training CLI on the H3 family writes the student / EMA / critic LoRA files into each checkpoint."""
+    import os
+
+    from dmad_b200.cli.train import main
+    from dmad_b200.lora import read_lora_file
+
+    cfg = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "configs", "h3_dmad.yaml")
+    net = ("model.net={dim: 64, num_heads: 1, ffn_dim: 96, num_layers: 2, refiner_layers: 1, text_dim: 16, "
+           "time_embed_dim: 32}")
+    main(["--config", cfg, net, "model.distill.student_lora_rank=4", "model.distill.height=64",
+          "model.distill.width=64", "model.distill.num_frames=22", "model.distill.text_tokens=6",
+          "model.distill.gradient_checkpointing=false", f"training.output_dir={tmp_path}", "training.max_iters=1",
+          "training.save_every=1"])
+    ck = tmp_path / "checkpoint-000000001"
+    for f in ("pytorch_lora_weights.safetensors", "ema_lora/pytorch_lora_weights.safetensors",
+              "ema2_lora/pytorch_lora_weights.safetensors", "fake_lora/pytorch_lora_weights.safetensors"):
+        assert (ck / f).exists(), f
+    pairs, meta = read_lora_file(str(ck / "ema_lora" / "pytorch_lora_weights.safetensors"))
+    assert pairs and meta.get("ema_gamma") == "6.94"
