@@ -47,6 +47,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--count-launches", type=int, default=1)
     ap.add_argument("--profile", default=None, help="write a per-kernel time table of one cycle to this path")
+    ap.add_argument("--cp", type=int, default=1, help="context-parallel group size (config 3: 8)")
+    ap.add_argument("--cp-impl", default="fused", choices=["fused", "nccl", "ring"])
+    ap.add_argument("--lora", type=int, default=0, help="LoRA rank of the student (config 3: 128)")
     ap.add_argument("--dp-optimizer", default="sharded", choices=["sharded", "replicated"],
                     help="sharded: fused reduce-scatter/AdamW/all-gather kernel; replicated: NCCL all-reduce baseline")
     return ap.parse_args()
@@ -166,9 +169,19 @@ def main():
         over = {"num_layers": args.layers} if args.layers else {}
         cfg = WanDMADConfig(net=wan_config(args.model, **over), dp_optimizer=args.dp_optimizer)
         cfg.checkpoint_critic_blocks_student_phase = cfg.net.num_layers
+        if args.lora:
+            cfg.student_lora_rank = args.lora
+            cfg.shard_frozen = world > 1
+            cfg.checkpoint_student_blocks = cfg.net.num_layers
         trainer = WanDMAD(cfg, device=device, dtype=torch.bfloat16, seed=0)
+        if args.cp > 1:
+            from dmad_b200.parallel.cp import ContextParallel
+            from dmad_b200.train.trainer import make_cp_group
+            cpc = ContextParallel(make_cp_group(args.cp), impl=args.cp_impl, device=device)
+            for net in trainer.context_parallel_nets():
+                net.enable_context_parallel(cpc)
 
-    host = make_host_batch(args.frames, seed=1234 + rank)
+    host = make_host_batch(args.frames, seed=1234 + rank // max(1, args.cp))
     batch = to_device(host, device)
     l2buf = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=device)
     it = [0]
@@ -226,7 +239,7 @@ def main():
         e_ev.synchronize()
         wall = (time.perf_counter() - t0) * 1000 / args.steps
         e2e_ms = max_over_ranks(max(wall, s_ev.elapsed_time(e_ev) / args.steps))
-        e2e = {"value": world / (e2e_ms / 1000.0), "unit": "samples/s", "h2d_bytes_per_step": int(h2d),
+        e2e = {"value": (world // args.cp) / (e2e_ms / 1000.0), "unit": "samples/s", "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": int(loss_host.numel() * 4), "ms_per_step": e2e_ms}
 
     # ------------------------------------------------------------------ 4-step generation latency
@@ -274,9 +287,12 @@ def main():
             print(f"# device status: {e}", file=sys.stderr)
         raise
 
-    value = world / (dev_ms / 1000.0)
+    value = (world // args.cp) / (dev_ms / 1000.0)
     out = {
-        "metric": "DMAD train samples/s (Wan2.1-1.3B-shaped, device-timed max over ranks)",
+        # the metric named by BASELINE.json; "value" is the training throughput, the 4-step generation
+        # latency is "gen_latency_s_per_clip"
+        "metric": "DMAD train samples/s and 4-step video gen latency (s/clip), device-timed max over ranks, "
+                  "1/2/4/8 B200",
         "value": value,
         "unit": "samples/s",
         "n_gpus": world,
@@ -288,10 +304,13 @@ def main():
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic N(0,1) latents/context, random-init weights",
-        "config": {"model": f"{args.model}-shaped DiT (BASELINE config 2)" if headline_ok else "DEBUG (invalid)",
-                   "global_batch": world, "seq_len": SEQ_LEN if headline_ok else None,
+        "config": {"model": (f"{args.model}-shaped DiT (BASELINE config {'3' if '14b' in args.model else '2'})"
+                             if headline_ok else "DEBUG (invalid)"),
+                   "global_batch": world // args.cp, "seq_len": SEQ_LEN if headline_ok else None,
                    "latents": f"16x{args.frames}x60x104", "text": "512x4096",
-                   "parallelism": f"dp{world}", "step": "1 generator + 1 critic DMAD iteration",
+                   "parallelism": f"dp{world // args.cp}" + (f"-cp{args.cp}-{args.cp_impl}" if args.cp > 1 else ""),
+                   "student_lora_rank": args.lora or None,
+                   "step": "1 generator + 1 critic DMAD iteration",
                    "dp_optimizer": _dp_desc(trainer, args),
                    "l2": "flushed (write of a 252 MB buffer) before every timed step; inputs > L2"},
         "gen_latency_s_per_clip": gen_s,
