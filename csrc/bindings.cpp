@@ -45,6 +45,10 @@ void small_linear(const at::Tensor& x, const at::Tensor& w, c10::optional<at::Te
 void flash_jvp_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& tq,
                    c10::optional<at::Tensor> tk, c10::optional<at::Tensor> tv, at::Tensor& o, at::Tensor& to,
                    at::Tensor& lse, double scale);
+void flash_jvp_accumulate(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& tq,
+                          c10::optional<at::Tensor> tk, c10::optional<at::Tensor> tv, at::Tensor& o, at::Tensor& to,
+                          at::Tensor& lse, at::Tensor& acc_o, at::Tensor& acc_u, at::Tensor& acc_lse,
+                          at::Tensor& acc_mu, bool read, bool final_, double scale);
 void flash_fwd_scatter(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
                        double scale, std::vector<int64_t> scatter, int64_t ld, int64_t col);
 void cp_qkv_push(const at::Tensor& src, std::vector<int64_t> dst, const at::Tensor& wq, const at::Tensor& wk,
@@ -93,6 +97,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sinusoid_embed", &dmad::sinusoid_embed);
   m.def("small_linear", &dmad::small_linear);
   m.def("flash_jvp_fwd", &dmad::flash_jvp_fwd);
+  m.def("flash_jvp_accumulate", &dmad::flash_jvp_accumulate);
   m.def("flash_fwd_scatter", &dmad::flash_fwd_scatter);
   m.def("cp_qkv_push", &dmad::cp_qkv_push);
   m.def("cp_seq_to_head", &dmad::cp_seq_to_head);

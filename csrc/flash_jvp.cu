@@ -78,6 +78,13 @@ struct JvpParams {
   float scale_log2, scale;
   int has_tk, has_tv;
   int* status;
+  // accumulate mode (key blocks visited one launch at a time): acc_o / acc_u fp32 [B, Lq, H, 128] hold
+  // O and T~ / l of the blocks seen so far, acc_lse (log2) / acc_mu [B, H, Lpad] their LSE and r / l
+  float* acc_o;
+  float* acc_u;
+  float* acc_lse;
+  float* acc_mu;
+  int acc_read, acc_final;
 };
 
 // TMEM column map (lane = query row)
@@ -379,17 +386,88 @@ flash_jvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     if (ok)
       ok = __all_sync(0xffffffffu,
                       mbar_wait(&sm.acc_done, (nkv - 1) & 1, kStatusTimeoutMma, abort_flag, p.status));
+    const bool valid = q_row < p.Lq;
+    const int64_t lidx = ((int64_t)batch * p.H + head) * p.Lpad + q_row;
+    // the previous block's LSE / mu are read before fin_full: group 0 rewrites them only after both
+    // groups have arrived there
+    float lp = -INFINITY, mp = 0.f;
+    if (p.acc_o != nullptr && p.acc_read && valid) {
+      lp = p.acc_lse[lidx];
+      mp = p.acc_mu[lidx];
+    }
     sm.fin[0][g][row] = l_sum;
     sm.fin[1][g][row] = r_sum;
     mbar_arrive(&sm.fin_full);
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.fin_full, 0, kStatusTimeoutSoftmax, abort_flag, p.status));
-    if (ok && !*abort_flag) {
+    if (ok && !*abort_flag && p.acc_o != nullptr) {
+      // merge this key block: O = wa O_acc + wb O~, U = wa U_acc + wb T~, mu = wa mu_acc + wb r, with
+      // wa = 2^(lse_acc - lse_new), wb = 2^(m - lse_new); tO = U - mu O at the last block
+      tc_fence_after();
+      const float l_tot = sm.fin[0][0][row] + sm.fin[0][1][row];
+      const float r_tot = sm.fin[1][0][row] + sm.fin[1][1][row];
+      const float lse_j = m_used + __log2f(l_tot);
+      const float mx = fmaxf(lp, lse_j);
+      const float nl = mx + __log2f(exp2f(lp - mx) + exp2f(lse_j - mx));
+      const float wa = p.acc_read ? exp2f(lp - nl) : 0.f;
+      const float wb = exp2f(m_used - nl);
+      const float nmu = mp * wa + r_tot * wb;
+      const int64_t arow_off = (((int64_t)batch * p.Lq + q_row) * p.H + head) * 128 + c0;
+      float* arow = p.acc_o + arow_off;
+      float* urow = p.acc_u + arow_off;
+      __nv_bfloat16* orow = p.o + batch * p.o_sb + (int64_t)q_row * p.o_sl + head * p.o_sh + c0;
+      __nv_bfloat16* torow = p.to + batch * p.to_sb + (int64_t)q_row * p.to_sl + head * p.to_sh + c0;
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t ro[32], rt[32];
+        tmem_ld32(o_t + c * 32, ro);
+        tmem_ld32(t_t + c * 32, rt);
+        tmem_wait_ld();
+        if (valid) {
+          float4* a4 = reinterpret_cast<float4*>(arow + c * 32);
+          float4* u4 = reinterpret_cast<float4*>(urow + c * 32);
+#pragma unroll
+          for (int v = 0; v < 8; ++v) {
+            const float4 pa = p.acc_read ? a4[v] : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 pu = p.acc_read ? u4[v] : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 na, nu;
+            na.x = pa.x * wa + __uint_as_float(ro[4 * v + 0]) * wb;
+            na.y = pa.y * wa + __uint_as_float(ro[4 * v + 1]) * wb;
+            na.z = pa.z * wa + __uint_as_float(ro[4 * v + 2]) * wb;
+            na.w = pa.w * wa + __uint_as_float(ro[4 * v + 3]) * wb;
+            nu.x = pu.x * wa + __uint_as_float(rt[4 * v + 0]) * wb;
+            nu.y = pu.y * wa + __uint_as_float(rt[4 * v + 1]) * wb;
+            nu.z = pu.z * wa + __uint_as_float(rt[4 * v + 2]) * wb;
+            nu.w = pu.w * wa + __uint_as_float(rt[4 * v + 3]) * wb;
+            a4[v] = na;
+            u4[v] = nu;
+            if (p.acc_final) {
+              uint2 wo, wt;
+              wo.x = pack_bf16x2(na.x, na.y);
+              wo.y = pack_bf16x2(na.z, na.w);
+              wt.x = pack_bf16x2(nu.x - nmu * na.x, nu.y - nmu * na.y);
+              wt.y = pack_bf16x2(nu.z - nmu * na.z, nu.w - nmu * na.w);
+              reinterpret_cast<uint2*>(orow + c * 32)[v] = wo;
+              reinterpret_cast<uint2*>(torow + c * 32)[v] = wt;
+            }
+          }
+        }
+      }
+      if (g == 0 && q_row < p.Lpad) {
+        p.acc_lse[lidx] = valid ? nl : INFINITY;
+        p.acc_mu[lidx] = valid ? nmu : 0.f;
+        if (p.lse != nullptr) p.lse[lidx] = valid ? nl : INFINITY;
+        if (blockIdx.x == gridDim.x - 1 && q_row + kTileM < p.Lpad) {
+          p.acc_lse[lidx + kTileM] = INFINITY;
+          p.acc_mu[lidx + kTileM] = 0.f;
+          if (p.lse != nullptr) p.lse[lidx + kTileM] = INFINITY;
+        }
+      }
+    } else if (ok && !*abort_flag) {
       tc_fence_after();
       const float l_tot = sm.fin[0][0][row] + sm.fin[0][1][row];
       const float r_tot = sm.fin[1][0][row] + sm.fin[1][1][row];
       const float inv_l = 1.f / l_tot;
       const float rl = r_tot * inv_l;
-      const bool valid = q_row < p.Lq;
       __nv_bfloat16* orow = p.o + batch * p.o_sb + (int64_t)q_row * p.o_sl + head * p.o_sh + c0;
       __nv_bfloat16* torow = p.to + batch * p.to_sb + (int64_t)q_row * p.to_sl + head * p.to_sh + c0;
 #pragma unroll
@@ -444,11 +522,12 @@ CUtensorMap make_bhld_map(const at::Tensor& x) {
 
 size_t flash_jvp_smem_bytes() { return sizeof(JvpSmem) + 1024; }
 
-// q, k, v, tq: [B, L, H, 128] bf16 (last dim contiguous, strides multiples of 8 elements);
-// tk / tv optional (undefined = zero tangent).  Writes o, to (shape of q) and the log2 LSE.
-void flash_jvp_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& tq,
-                   c10::optional<at::Tensor> tk, c10::optional<at::Tensor> tv, at::Tensor& o, at::Tensor& to,
-                   at::Tensor& lse, double scale) {
+namespace {
+
+void jvp_launch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& tq,
+                const c10::optional<at::Tensor>& tk, const c10::optional<at::Tensor>& tv, at::Tensor& o,
+                at::Tensor& to, const at::Tensor& lse, double scale, float* acc_o, float* acc_u, float* acc_lse,
+                float* acc_mu, int acc_lpad, bool acc_read, bool acc_final) {
   check_bhld(q, "q");
   check_bhld(k, "k");
   check_bhld(v, "v");
@@ -492,17 +571,53 @@ void flash_jvp_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   p.Lq = Lq;
   p.Lk = Lk;
   p.H = H;
-  p.Lpad = has_lse ? (int)lse.size(2) : 0;
+  p.Lpad = acc_o != nullptr ? acc_lpad : (has_lse ? (int)lse.size(2) : 0);
   p.scale_log2 = (float)(scale * 1.4426950408889634);
   p.scale = (float)scale;
   p.has_tk = has_tk;
   p.has_tv = has_tv;
   p.status = device_status_ptr(q.get_device());
+  p.acc_o = acc_o;
+  p.acc_u = acc_u;
+  p.acc_lse = acc_lse;
+  p.acc_mu = acc_mu;
+  p.acc_read = acc_read ? 1 : 0;
+  p.acc_final = acc_final ? 1 : 0;
   const size_t smem = flash_jvp_smem_bytes();
   C10_CUDA_CHECK(cudaFuncSetAttribute(flash_jvp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((Lq + kTileM - 1) / kTileM, H, B);
   flash_jvp_kernel<<<grid, 384, smem, at::cuda::getCurrentCUDAStream()>>>(mq, mk, mv, mtq, mtk, mtv, p);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace
+
+// q, k, v, tq: [B, L, H, 128] bf16 (last dim contiguous, strides multiples of 8 elements);
+// tk / tv optional (undefined = zero tangent).  Writes o, to (shape of q) and the log2 LSE.
+void flash_jvp_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& tq,
+                   c10::optional<at::Tensor> tk, c10::optional<at::Tensor> tv, at::Tensor& o, at::Tensor& to,
+                   at::Tensor& lse, double scale) {
+  jvp_launch(q, k, v, tq, tk, tv, o, to, lse, scale, nullptr, nullptr, nullptr, nullptr, 0, false, false);
+}
+
+// One key block of a blockwise (ring) attention JVP: merges this block into acc_o / acc_u (contiguous
+// fp32 [B, Lq, H, 128]) and acc_lse / acc_mu (fp32 [B, H, round_up(Lq, 256)]); read = false starts a
+// fresh accumulation, final_ = true also writes the bf16 o and to.  lse (optional) receives the LSE.
+void flash_jvp_accumulate(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& tq,
+                          c10::optional<at::Tensor> tk, c10::optional<at::Tensor> tv, at::Tensor& o, at::Tensor& to,
+                          at::Tensor& lse, at::Tensor& acc_o, at::Tensor& acc_u, at::Tensor& acc_lse,
+                          at::Tensor& acc_mu, bool read, bool final_, double scale) {
+  for (const at::Tensor* a : {&acc_o, &acc_u})
+    TORCH_CHECK(a->is_cuda() && a->scalar_type() == at::kFloat && a->is_contiguous() && a->dim() == 4 &&
+                    a->size(0) == q.size(0) && a->size(1) == q.size(1) && a->size(2) == q.size(2) &&
+                    a->size(3) == 128,
+                "acc_o / acc_u must be contiguous fp32 [B, Lq, H, 128]");
+  for (const at::Tensor* a : {&acc_lse, &acc_mu})
+    TORCH_CHECK(a->is_cuda() && a->scalar_type() == at::kFloat && a->is_contiguous() && a->dim() == 3 &&
+                    a->size(0) == q.size(0) && a->size(1) == q.size(2) && a->size(2) == flash_lse_pad(q.size(1)),
+                "acc_lse / acc_mu must be fp32 [B, H, round_up(Lq, 256)]");
+  jvp_launch(q, k, v, tq, tk, tv, o, to, lse, scale, acc_o.data_ptr<float>(), acc_u.data_ptr<float>(),
+             acc_lse.data_ptr<float>(), acc_mu.data_ptr<float>(), (int)acc_lse.size(2), read, final_);
 }
 
 }  // namespace dmad

@@ -148,7 +148,10 @@ def block_jvp(blk, x, tx, e0, te0, context, cos, sin, B, L, rpg, cp=None):
     q, tq = ops.rope_apply(q, cos, sin, hd), ops.rope_apply(tq, cos, sin, hd)
     k, tk = ops.rope_apply(k, cos, sin, hd), ops.rope_apply(tk, cos, sin, hd)
     v, tv = qkv[:, 2 * D:], tqkv[:, 2 * D:]
-    if cp is not None and cp.world > 1:
+    if cp is not None and cp.world > 1 and cp.impl == "ring":
+        from ..parallel.cp import ring_attention_jvp
+        a, ta = ring_attention_jvp(q, k, v, tq, tk, tv, B, H, cp)
+    elif cp is not None and cp.world > 1:
         # the six primal / tangent tensors in one head exchange, the two outputs in one back
         # (the reference's _SeqAllToAllQKVWithT / _SeqAllToAllOutputWithT, jvp_helper.py:69-205)
         g = cp.seq_to_head(torch.cat([q, k, v, tq, tk, tv], dim=1), B, 6, H, hd)

@@ -352,14 +352,14 @@ class _A2AHeadToSeq(torch.autograd.Function):
 # its owner and summed there.  Parity: there is no ring attention in the reference (Ulysses only,
 # train/wan/rcm/utils/a2a_cp.py); this is the ring variant of the same context parallelism.
 
-def _ring_blocks(cp, slot_ptrs, R, D, stream, bufs, visit):
-    """Call ``visit(j, src, kv)`` for the key/value block of every rank ``src = rank + j`` (``kv`` None
-    for this rank's own block).  The block of step j + 1 is copied into ``bufs[(j + 1) % 2]`` on
-    ``stream`` while step j computes; a copy starts only after the work that last read its buffer."""
+def _ring_blocks(cp, slot_ptrs, nbytes, stream, bufs, visit):
+    """Call ``visit(j, src, kv)`` for the key/value block (``nbytes`` of each rank's slot) of every rank
+    ``src = rank + j`` (``kv`` None for this rank's own block).  The block of step j + 1 is copied into
+    ``bufs[(j + 1) % 2]`` on ``stream`` while step j computes; a copy starts only after the work that
+    last read its buffer."""
     from .. import ops
 
     e = ops.ext()
-    nbytes = 2 * R * D * 2
     cur = torch.cuda.current_stream()
     ready = {}
 
@@ -418,7 +418,7 @@ class _RingSelfAttn(torch.autograd.Function):
             e.flash_fwd_accumulate(q, blk[0].view(B, Ll, H, hd), blk[1].view(B, Ll, H, hd), o, lse, acc_o, acc_lse,
                                    j > 0, j == cp.world - 1, scale)
 
-        _ring_blocks(cp, ptrs, R, D, cp.ring_stream, bufs, visit)
+        _ring_blocks(cp, ptrs, 2 * R * D * 2, cp.ring_stream, bufs, visit)
         cp.sync()  # the peers have copied this rank's block before the slot is reused
         ctx.save_for_backward(qkv, wq, wk, cos, sin, rq, rk, o, lse)
         ctx.cfg = (B, H, eps, scale, cp)
@@ -463,7 +463,7 @@ class _RingSelfAttn(torch.autograd.Function):
                 e.peer_copy_to(pptrs[src] + cp.rank * 2 * R * D * 2, dkv, 2 * R * D * 2)
             # dkv is reused by the next block: wait for the copy (same stream, ordered)
 
-        _ring_blocks(cp, ptrs, R, D, cp.ring_stream, bufs, visit)
+        _ring_blocks(cp, ptrs, 2 * R * D * 2, cp.ring_stream, bufs, visit)
         cp.sync()  # every partial has landed
         g = part_v.float().sum(0)
         dqk = torch.cat([dq_acc, g[0]], dim=1).to(qkv.dtype)
@@ -511,3 +511,83 @@ def ring_self_attention(qkv, wq, wk, cos, sin, B, H, eps, cp: ContextParallel):
     if not qkv.is_cuda:
         return _ring_cpu(qkv, wq, wk, cos, sin, B, H, eps, cp)
     return _RingSelfAttn.apply(qkv, wq.float().contiguous(), wk.float().contiguous(), cos, sin, B, H, eps, cp)
+
+
+# ---------------------------------------------------------------------- ring attention JVP
+# The tangent pass of the student (sCM / rCM targets) on the ring: each rank's slot holds k, v, tk,
+# tv of its tokens; every block is merged by flash_jvp_accumulate, whose epilogue keeps O, T~/l, the
+# log-sum-exp and mu = rowsum(P * tS) / l of the blocks seen so far and writes tO = T~/l - mu O at the
+# last block.  Runs without autograd, as every JVP of the DMAD objectives does.  Parity: the Ulysses
+# form of the same exchange is the reference's _SeqAllToAllQKVWithT (train/wan/rcm/utils/
+# jvp_helper.py:69-205); the ring form is this build's.
+
+def ring_attention_jvp(q, k, v, tq, tk, tv, B: int, H: int, cp: ContextParallel):
+    """Local rows [R, D] of q, k, v and their tangents -> (O, tO) rows [R, D] of attention over the
+    sequence of the whole CP group (this rank's queries, every rank's keys)."""
+    if torch.is_grad_enabled() and any(t.requires_grad for t in (q, k, v)):
+        raise RuntimeError("ring_attention_jvp is forward-only: call it under torch.no_grad()")
+    if not q.is_cuda:
+        return _ring_jvp_cpu(q, k, v, tq, tk, tv, B, H, cp)
+    from .. import ops
+    from ..ops import attention as attn_ops
+
+    e = ops.ext()
+    R, D = q.shape
+    hd = D // H
+    Ll = R // B
+    scale = 1.0 / math.sqrt(hd)
+    slot, ptrs = cp.slot(4 * R * D)
+    own = slot.view(4, R, D)
+    for i, t in enumerate((k, v, tk, tv)):
+        own[i].copy_(t)
+    cp.sync()  # every rank's block is in place
+    shp = (B, Ll, H, hd)
+    q4, tq4 = q.contiguous().view(shp), tq.contiguous().view(shp)
+    o = torch.empty(shp, dtype=q.dtype, device=q.device)
+    to = torch.empty_like(o)
+    acc_o = torch.empty(shp, dtype=torch.float32, device=q.device)
+    acc_u = torch.empty_like(acc_o)
+    acc_lse = torch.empty((B, H, attn_ops._lse_pad(Ll)), dtype=torch.float32, device=q.device)
+    acc_mu = torch.empty_like(acc_lse)
+    no_lse = torch.empty(0, dtype=torch.float32, device=q.device)
+    bufs = cp.ring_buffers(4 * R * D)
+
+    def visit(j, src, kv):
+        blk = own if kv is None else kv[:4 * R * D].view(4, R, D)
+        e.flash_jvp_accumulate(q4, blk[0].view(shp), blk[1].view(shp), tq4, blk[2].view(shp), blk[3].view(shp),
+                               o, to, no_lse, acc_o, acc_u, acc_lse, acc_mu, j > 0, j == cp.world - 1, scale)
+
+    _ring_blocks(cp, ptrs, 4 * R * D * 2, cp.ring_stream, bufs, visit)
+    cp.sync()  # the peers have copied this rank's block before the slot is reused
+    return o.view(R, D), to.view(R, D)
+
+
+def _ring_jvp_cpu(q, k, v, tq, tk, tv, B, H, cp):
+    """fp32 restatement (gloo ranks): gather the blocks, merge (O, T~/l, mu) per block by LSE."""
+    R, D = q.shape
+    hd = D // H
+    Ll = R // B
+    blocks = cp.gather(torch.cat([k, v, tk, tv], dim=1).view(1, R, 4 * D), dim=1).view(cp.world, R, 4 * D)
+    hv = lambda t: t.float().reshape(B, Ll, H, hd).transpose(1, 2)  # noqa: E731
+    qf, tqf = hv(q), hv(tq)
+    scale = 1.0 / math.sqrt(hd)
+    O = U = mu = lse = None
+    for j in range(cp.world):
+        blk = blocks[(cp.rank + j) % cp.world]
+        kj, vj, tkj, tvj = (hv(blk[:, i * D:(i + 1) * D]) for i in range(4))
+        s = qf @ kj.transpose(-1, -2) * scale
+        ts = (tqf @ kj.transpose(-1, -2) + qf @ tkj.transpose(-1, -2)) * scale
+        l_j = torch.logsumexp(s, -1, keepdim=True)
+        p = torch.exp(s - l_j)
+        o_j = p @ vj
+        u_j = p @ tvj + (p * ts) @ vj
+        mu_j = (p * ts).sum(-1, keepdim=True)
+        if O is None:
+            O, U, mu, lse = o_j, u_j, mu_j, l_j
+        else:
+            nl = torch.logaddexp(lse, l_j)
+            wa, wb = torch.exp(lse - nl), torch.exp(l_j - nl)
+            O, U, mu, lse = O * wa + o_j * wb, U * wa + u_j * wb, mu * wa + mu_j * wb, nl
+    tO = U - mu * O
+    back = lambda t: t.transpose(1, 2).reshape(R, D).to(q.dtype)  # noqa: E731
+    return back(O), back(tO)

@@ -90,3 +90,38 @@ def test_flash_jvp_grad_of_o_matches_flash_attention():
     torch.testing.assert_close(o, o2, rtol=0, atol=1e-2)
     for a, b in zip(g1, g2):
         torch.testing.assert_close(a.float(), b.float(), rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("Lq,blocks,has_tk", [(999, (256, 300, 443), True), (512, (128, 77), False)])
+def test_flash_jvp_accumulate_over_key_blocks(Lq, blocks, has_tk):
+    """The blockwise (ring) form: key blocks visited one launch at a time and merged in the
+    epilogue reproduce the JVP over all keys."""
+    from dmad_b200 import ops
+
+    torch.manual_seed(1)
+    B, H, Lk = 1, 2, sum(blocks)
+    q, k, v = _rand(B, Lq, H, 128), _rand(B, Lk, H, 128), _rand(B, Lk, H, 128)
+    tq, tv = _rand(B, Lq, H, 128, s=0.5), _rand(B, Lk, H, 128, s=0.5)
+    tk = _rand(B, Lk, H, 128, s=0.5) if has_tk else None
+    scale = 1 / math.sqrt(128)
+    e = ops.ext()
+    o, to = torch.empty_like(q), torch.empty_like(q)
+    lse = torch.empty(B, H, e.flash_lse_pad(Lq), device=dev)
+    acc_o = torch.empty(B, Lq, H, 128, device=dev)
+    acc_u = torch.empty_like(acc_o)
+    acc_lse, acc_mu = torch.empty_like(lse), torch.empty_like(lse)
+    s0 = 0
+    for i, n in enumerate(blocks):
+        sl = slice(s0, s0 + n)
+        s0 += n
+        e.flash_jvp_accumulate(q, k[:, sl].contiguous(), v[:, sl].contiguous(), tq,
+                               tk[:, sl].contiguous() if tk is not None else None, tv[:, sl].contiguous(), o, to, lse,
+                               acc_o, acc_u, acc_lse, acc_mu, i > 0, i == len(blocks) - 1, scale)
+    torch.cuda.synchronize()
+    ops.check_device_status()
+    ro, rto, rlse = _oracle(q, k, v, tq, tk, tv, scale)
+    assert (o.float() - ro).abs().max().item() < 2e-2
+    t_err = (to.float() - rto).abs().max().item()
+    assert t_err < 3e-2 * max(1.0, rto.abs().max().item()), t_err
+    assert (lse[:, :, :Lq] / math.log2(math.e) - rlse).abs().max().item() < 2e-3
+    assert torch.isinf(lse[:, :, Lq:]).all()

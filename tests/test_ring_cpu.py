@@ -1,5 +1,5 @@
 """Ring attention (impl="ring") on 2 gloo CPU ranks: the per-block LSE merge reproduces the
-unsharded Wan forward."""
+unsharded Wan forward, and the per-block (O, T~/l, mu) merge its JVP."""
 import os
 import socket
 
@@ -29,6 +29,12 @@ def _inputs():
     return torch.randn(2, 16, 2, 4, 8, generator=g), torch.rand(2, 1, generator=g), torch.randn(2, 5, 32, generator=g)
 
 
+def _jvp_inputs():
+    g = torch.Generator().manual_seed(9)
+    x, t, ctx = _inputs()
+    return x, torch.randn(x.shape, generator=g), t, torch.rand(2, 1, generator=g), ctx
+
+
 def _worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank))
@@ -40,9 +46,12 @@ def _worker(rank, world, port, q):
         init_distributed(backend="gloo", timeout_s=120)
         m = _model()
         m.enable_context_parallel(ContextParallel(impl="ring"))
+        from dmad_b200.models.wan_jvp import wan_forward_jvp
+
         with torch.no_grad():
             out = m(*_inputs())
-        q.put((rank, out.numpy(), None))
+            jo, jt = wan_forward_jvp(m, *_jvp_inputs())
+        q.put((rank, (out.numpy(), jo.numpy(), jt.numpy()), None))
         dist.destroy_process_group()
     except Exception:  # pragma: no cover
         import traceback
@@ -60,9 +69,14 @@ def test_ring_matches_unsharded():
     res = [q.get(timeout=300) for _ in procs]
     for p in procs:
         p.join(timeout=60)
+    from dmad_b200.models.wan_jvp import wan_forward_jvp
+
     m = _model()
     with torch.no_grad():
         out = m(*_inputs())
+        jo, jt = wan_forward_jvp(m, *_jvp_inputs())
     for rank, o, err in res:
         assert err is None, err
-        torch.testing.assert_close(torch.from_numpy(o), out, rtol=1e-4, atol=1e-5)
+        torch.testing.assert_close(torch.from_numpy(o[0]), out, rtol=1e-4, atol=1e-5)
+        torch.testing.assert_close(torch.from_numpy(o[1]), jo, rtol=1e-4, atol=1e-5)
+        torch.testing.assert_close(torch.from_numpy(o[2]), jt, rtol=1e-3, atol=1e-5)
