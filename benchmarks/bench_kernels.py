@@ -80,7 +80,7 @@ def main():
     ap.add_argument("--H", type=int, default=12)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--only", default="all", choices=["all", "fwd", "bwd", "sdpa", "jvp", "ref_jvp", "gemm"])
+    ap.add_argument("--only", default="all", choices=["all", "fwd", "bwd", "bwd_fused", "sdpa", "jvp", "ref_jvp", "gemm"])
     ap.add_argument("--gemm", default="32760,8960,1536", help="M,N,K of the GEMM benchmark")
     ap.add_argument("--rank", type=int, default=128, help="LoRA rank of the GEMM benchmark")
     a = ap.parse_args()
@@ -108,6 +108,12 @@ def main():
         dq, dk, dv, dd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(lse)
         ms = timeit(lambda: e.flash_bwd(q, k, v, o, do, lse, dq, dk, dv, dd, scale), a.iters, a.warmup)
         res.append(("flash_bwd_sm100", ms, 2.5 * fl_fwd))
+    if a.only in ("all", "bwd", "bwd_fused"):
+        e.flash_fwd(q, k, v, o, lse, scale)
+        dq, dk, dv, dd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(lse)
+        acc = torch.empty(B * H * lse.shape[-1] * 128, device="cuda")
+        ms = timeit(lambda: e.flash_bwd_fused(q, k, v, o, do, lse, dq, dk, dv, dd, acc, scale), a.iters, a.warmup)
+        res.append(("flash_bwd_fused_sm100", ms, 2.5 * fl_fwd))
     if a.only in ("all", "sdpa"):
         from torch.nn.attention import SDPBackend, sdpa_kernel
 

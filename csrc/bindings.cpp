@@ -8,6 +8,9 @@ void flash_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at
 void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
                const at::Tensor& dout, const at::Tensor& lse2, at::Tensor& dq, at::Tensor& dk, at::Tensor& dv,
                at::Tensor& dd_scratch, double scale);
+void flash_bwd_fused(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+                     const at::Tensor& dout, const at::Tensor& lse2, at::Tensor& dq, at::Tensor& dk, at::Tensor& dv,
+                     at::Tensor& dd_scratch, at::Tensor& dq_acc, double scale);
 int64_t flash_lse_pad(int64_t L);
 int64_t device_status(int64_t device, bool reset);
 void ln_mod_fwd(const at::Tensor& x, at::Tensor& y, c10::optional<at::Tensor> mean, at::Tensor& rstd,
@@ -80,6 +83,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "dmad_b200 sm_100a kernels";
   m.def("flash_fwd", &dmad::flash_fwd);
   m.def("flash_bwd", &dmad::flash_bwd);
+  m.def("flash_bwd_fused", &dmad::flash_bwd_fused);
   m.def("flash_lse_pad", &dmad::flash_lse_pad);
   m.def("device_status", &dmad::device_status);
   m.def("ln_mod_fwd", &dmad::ln_mod_fwd);

@@ -524,6 +524,302 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   }
 }
 
+// ------------------------------------------------------------------ fused kernel: dK, dV and dQ
+// One CTA per 128-key tile, as kernel A, that also forms dQ_i = dS_i K for every query tile i and adds
+// it into an fp32 accumulator [B, H, Lpad, 128] with vector reductions (red.global.add.v4.f32): five
+// GEMMs per tile pair instead of seven.  TMEM: S^T / P^T 0..127, dP^T and then dQ_i 128..255,
+// dV 256..383, dK 384..511.  dS^T of tile i is written over dO_i once dV_i (its last reader) is done,
+// in the 128-byte-swizzled layout TMA gives a [128][64] box; dK += dS^T Q_i reads it as a K-major A
+// and dQ_i = dS K as an MN-major A.  Per tile the tensor pipe runs dP_i, dV_i, S_{i+1}, dK_i, dQ_i
+// and waits only while the softmax warps drain dQ_i out of TMEM (dP_{i+1} reuses its columns).
+struct FusedSmem {
+  uint8_t k[kTileBytes];
+  uint8_t v[kTileBytes];
+  uint8_t q[2][kTileBytes];
+  uint8_t g[2][kTileBytes];  // dO_i, then dS_i^T
+  float lse[2][128];
+  float dd[2][128];
+  uint64_t kv_full;
+  uint64_t q_full[2], q_empty[2];
+  uint64_t s_full, dp_full, p_full, dv_done, ds_full, dq_full, dq_free, done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c, float d) {
+  asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(384, 1)
+flash_bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_g,
+                       BwdParams p, float* __restrict__ dq_acc) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  FusedSmem& sm = *reinterpret_cast<FusedSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  volatile int* abort_flag = &sm.abort_flag;
+  const int warp = warp_id(), lane = lane_id();
+  const int head = blockIdx.y, batch = blockIdx.z;
+  const int k0 = blockIdx.x * 128;
+  const int nq = (p.Lq + 127) / 128;
+  const int64_t bh_off = ((int64_t)batch * p.H + head) * p.Lpad;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sm.q_full[s], 1);
+      mbar_init(&sm.q_empty[s], 1);
+    }
+    mbar_init(&sm.s_full, 1);
+    mbar_init(&sm.dp_full, 1);
+    mbar_init(&sm.p_full, 256);
+    mbar_init(&sm.dv_done, 1);
+    mbar_init(&sm.ds_full, 256);
+    mbar_init(&sm.dq_full, 1);
+    mbar_init(&sm.dq_free, 256);
+    mbar_init(&sm.done, 1);
+    sm.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(&sm.kv_full, 2 * kTileBytes);
+      for (int h = 0; h < 2; ++h) {
+        tma_load_4d(sm.k + h * kHalfBytes, &tm_k, &sm.kv_full, h * 64, head, k0, batch);
+        tma_load_4d(sm.v + h * kHalfBytes, &tm_v, &sm.kv_full, h * 64, head, k0, batch);
+      }
+      int last_s = -1;
+      uint32_t last_ph = 0;
+      for (int i = 0; i < nq; ++i) {
+        const int s = i & 1;
+        const uint32_t ph = (i >> 1) & 1;
+        if (!mbar_wait(&sm.q_empty[s], ph ^ 1, kStatusTimeoutEmpty, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(&sm.q_full[s], 2 * kTileBytes + 2 * 512);
+        for (int h = 0; h < 2; ++h) {
+          tma_load_4d(sm.q[s] + h * kHalfBytes, &tm_q, &sm.q_full[s], h * 64, head, i * 128, batch);
+          tma_load_4d(sm.g[s] + h * kHalfBytes, &tm_g, &sm.q_full[s], h * 64, head, i * 128, batch);
+        }
+        bulk_load(sm.lse[s], p.lse2 + bh_off + i * 128, 512, &sm.q_full[s]);
+        bulk_load(sm.dd[s], p.dd + bh_off + i * 128, 512, &sm.q_full[s]);
+        last_s = s;
+        last_ph = ph;
+      }
+      mbar_wait(&sm.kv_full, 0, kStatusTimeoutTmaFull, nullptr, p.status);
+      if (last_s >= 0) mbar_wait(&sm.q_full[last_s], last_ph, kStatusTimeoutTmaFull, nullptr, p.status);
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_kk = idesc_bf16_f32(128, 128, false, false);
+      constexpr uint32_t idesc_mn = idesc_bf16_f32(128, 128, false, true);
+      constexpr uint32_t idesc_dq = idesc_bf16_f32(128, 128, true, true);
+      const uint32_t ka = smem_u32(sm.k), va = smem_u32(sm.v);
+      const uint32_t t_s = tmem, t_y = tmem + 128, t_dv = tmem + 256, t_dk = tmem + 384;
+      auto gemm_kk = [&](uint32_t d, uint32_t a, uint32_t b) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          mma_bf16_ss(d, smem_desc_sw128(a + off, 16, 1024), smem_desc_sw128(b + off, 16, 1024), idesc_kk, kk > 0);
+        }
+      };
+      bool ok = mbar_wait(&sm.kv_full, 0, kStatusTimeoutTmaFull, abort_flag, p.status);
+      if (ok) ok = mbar_wait(&sm.q_full[0], 0, kStatusTimeoutTmaFull, abort_flag, p.status);
+      if (ok) {
+        tc_fence_after();
+        gemm_kk(t_s, ka, smem_u32(sm.q[0]));
+        mma_commit(&sm.s_full);
+        gemm_kk(t_y, va, smem_u32(sm.g[0]));
+        mma_commit(&sm.dp_full);
+      }
+      for (int i = 0; ok && i < nq; ++i) {
+        const int s = i & 1;
+        const bool has_next = i + 1 < nq;
+        const int s1 = (i + 1) & 1;
+        const uint32_t ph1 = ((i + 1) >> 1) & 1;
+        const uint32_t ga = smem_u32(sm.g[s]), qa = smem_u32(sm.q[s]);
+        if (i > 0) {  // dP_i into the columns dQ_{i-1} has left
+          if (!(ok = mbar_wait(&sm.dq_free, (i - 1) & 1, kStatusTimeoutSoftmax, abort_flag, p.status))) break;
+          tc_fence_after();
+          gemm_kk(t_y, va, ga);
+          mma_commit(&sm.dp_full);
+        }
+        if (!(ok = mbar_wait(&sm.p_full, i & 1, kStatusTimeoutSoftmax, abort_flag, p.status))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // dV += P^T dO_i
+          mma_bf16_ts(t_dv, t_s + split_a_col(kk), smem_desc_sw128(ga + kk * 2048, kHalfBytes, 1024), idesc_mn,
+                      (i > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&sm.dv_done);
+        if (has_next) {
+          if (!(ok = mbar_wait(&sm.q_full[s1], ph1, kStatusTimeoutTmaFull, abort_flag, p.status))) break;
+          tc_fence_after();
+          gemm_kk(t_s, ka, smem_u32(sm.q[s1]));
+          mma_commit(&sm.s_full);
+        }
+        if (!(ok = mbar_wait(&sm.ds_full, i & 1, kStatusTimeoutSoftmax, abort_flag, p.status))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // dK += dS^T Q_i (dS^T K-major over dO_i's buffer)
+          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          mma_bf16_ss(t_dk, smem_desc_sw128(ga + off, 16, 1024), smem_desc_sw128(qa + kk * 2048, kHalfBytes, 1024),
+                      idesc_mn, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)  // dQ_i = dS K (dS MN-major, K MN-major)
+          mma_bf16_ss(t_y, smem_desc_sw128(ga + kk * 2048, kHalfBytes, 1024),
+                      smem_desc_sw128(ka + kk * 2048, kHalfBytes, 1024), idesc_dq, kk > 0 ? 1u : 0u);
+        mma_commit(&sm.dq_full);
+        mma_commit(&sm.q_empty[s]);
+      }
+      mma_commit(&sm.done);
+      mbar_wait(&sm.done, 0, kStatusTimeoutMma, nullptr, p.status);
+    }
+  } else if (warp >= 4) {
+    const int g = (warp - 4) >> 2;  // column group: query columns (then dQ columns) [64g, 64g + 64)
+    const int c0 = 64 * g;
+    const int wq = warp & 3;
+    const int row = wq * 32 + lane;
+    const uint32_t lb = (uint32_t)(wq * 32) << 16;
+    const uint32_t t_s = tmem + lb + c0, t_y = tmem + lb + 128 + c0;
+    const float scale_log2 = p.scale_log2, scale = p.scale;
+    bool ok = true;
+    // dQ_j out of TMEM (lane = query row of tile j) into the fp32 accumulator
+    auto drain_dq = [&](int j) -> bool {
+      if (!__all_sync(0xffffffffu, mbar_wait(&sm.dq_full, j & 1, kStatusTimeoutMma, abort_flag, p.status)))
+        return false;
+      tc_fence_after();
+      uint32_t r[2][32];
+      tmem_ld32(t_y, r[0]);
+      tmem_ld32(t_y + 32, r[1]);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&sm.dq_free);
+      float* dst = dq_acc + (bh_off + (int64_t)j * 128 + row) * 128 + c0;
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int v = 0; v < 8; ++v)
+          red_add_v4(dst + c * 32 + 4 * v, __uint_as_float(r[c][4 * v]), __uint_as_float(r[c][4 * v + 1]),
+                     __uint_as_float(r[c][4 * v + 2]), __uint_as_float(r[c][4 * v + 3]));
+      return true;
+    };
+    for (int i = 0; i < nq; ++i) {
+      const int s = i & 1;
+      const uint32_t ph = (i >> 1) & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&sm.q_full[s], ph, kStatusTimeoutTmaFull, abort_flag, p.status));
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.s_full, i & 1, kStatusTimeoutMma, abort_flag, p.status));
+      if (!ok) break;
+      tc_fence_after();
+      float pv[64];
+      {
+        uint32_t r[2][32];
+        tmem_ld32(t_s, r[0]);
+        tmem_ld32(t_s + 32, r[1]);
+        tmem_wait_ld();
+        const float* lse = sm.lse[s] + c0;
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float x = fmaf(__uint_as_float(r[c][e]), scale_log2, -lse[c * 32 + e]);
+            pv[c * 32 + e] = (e & 1) ? ex2_poly(x) : ex2_approx(x);
+          }
+      }
+      {
+        uint32_t w[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) w[e] = pack_bf16x2(pv[2 * e], pv[2 * e + 1]);
+        tmem_st32(t_s, w);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&sm.p_full);
+      if (i > 0 && !(ok = drain_dq(i - 1))) break;
+
+      ok = __all_sync(0xffffffffu, mbar_wait(&sm.dp_full, i & 1, kStatusTimeoutMma, abort_flag, p.status));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t w[32];
+      {
+        uint32_t r[2][32];
+        tmem_ld32(t_y, r[0]);
+        tmem_ld32(t_y + 32, r[1]);
+        tmem_wait_ld();
+        const float* dd = sm.dd[s] + c0;
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int q = c * 32 + 2 * e;
+            const float d0 = pv[q] * (__uint_as_float(r[c][2 * e]) - dd[q]) * scale;
+            const float d1 = pv[q + 1] * (__uint_as_float(r[c][2 * e + 1]) - dd[q + 1]) * scale;
+            w[c * 16 + e] = pack_bf16x2(d0, d1);
+          }
+      }
+      // dO_i's buffer takes dS^T once dV_i has read it
+      ok = __all_sync(0xffffffffu, mbar_wait(&sm.dv_done, i & 1, kStatusTimeoutMma, abort_flag, p.status));
+      if (!ok) break;
+      {
+        uint8_t* dst = sm.g[s] + g * kHalfBytes + row * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(dst + ((c ^ (row & 7)) << 4)) =
+              make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&sm.ds_full);
+    }
+    if (ok && nq > 0) ok = drain_dq(nq - 1);
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.done, 0, kStatusTimeoutMma, abort_flag, p.status));
+    if (ok) {
+      tc_fence_after();
+      const int kr = k0 + row;
+      const bool valid = kr < p.Lk;
+      __nv_bfloat16* dv_row = valid ? p.out2 + batch * p.sb2 + (int64_t)kr * p.sl2 + head * p.sh2 : nullptr;
+      __nv_bfloat16* dk_row = valid ? p.out + batch * p.sb + (int64_t)kr * p.sl + head * p.sh : nullptr;
+      store_row_bf16(dv_row, tmem + lb + 256, 1.f, c0, 2);
+      store_row_bf16(dk_row, tmem + lb + 384, 1.f, c0, 2);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// dq (bf16, strided [B, Lq, H, 128]) from the fp32 accumulator [B, H, Lpad, 128]; 8 elements a thread
+__global__ void dq_from_acc_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq, int64_t sb,
+                                   int64_t sl, int64_t sh, int B, int H, int Lq, int Lpad) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = (int64_t)B * Lq * H * 16;
+  if (t >= total) return;
+  const int c8 = t & 15;
+  const int64_t r = t >> 4;  // (b, l, h) in dq's order
+  const int h = r % H;
+  const int l = (r / H) % Lq;
+  const int b = r / ((int64_t)H * Lq);
+  const float4* src = reinterpret_cast<const float4*>(acc + ((((int64_t)b * H + h) * Lpad + l) * 128 + c8 * 8));
+  const float4 x = src[0], y = src[1];
+  uint4 w;
+  w.x = pack_bf16x2(x.x, x.y);
+  w.y = pack_bf16x2(x.z, x.w);
+  w.z = pack_bf16x2(y.x, y.y);
+  w.w = pack_bf16x2(y.z, y.w);
+  *reinterpret_cast<uint4*>(dq + b * sb + (int64_t)l * sl + h * sh + c8 * 8) = w;
+}
+
 CUtensorMap make_map(const at::Tensor& x) {
   const uint64_t dims[4] = {128, (uint64_t)x.size(2), (uint64_t)x.size(1), (uint64_t)x.size(0)};
   const uint64_t strides[3] = {(uint64_t)x.stride(2) * 2, (uint64_t)x.stride(1) * 2, (uint64_t)x.stride(0) * 2};
@@ -606,6 +902,73 @@ void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, co
   }
 }
 
+
+// Single-kernel backward (dK, dV and an fp32 dQ accumulator in one pass over the tile pairs, then a
+// conversion of the accumulator into dq).  dq_acc: fp32, at least B * H * round_up(Lq, 256) * 128
+// elements, overwritten.
+void flash_bwd_fused(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
+                     const at::Tensor& dout, const at::Tensor& lse2, at::Tensor& dq, at::Tensor& dk, at::Tensor& dv,
+                     at::Tensor& dd_scratch, at::Tensor& dq_acc, double scale) {
+  check_bhld(q, "q");
+  check_bhld(k, "k");
+  check_bhld(v, "v");
+  check_bhld(o, "o");
+  check_bhld(dout, "dout");
+  check_bhld(dq, "dq");
+  check_bhld(dk, "dk");
+  check_bhld(dv, "dv");
+  const int B = q.size(0), Lq = q.size(1), H = q.size(2), Lk = k.size(1);
+  const int64_t Lpad = flash_lse_pad(Lq);
+  TORCH_CHECK(lse2.is_contiguous() && lse2.scalar_type() == at::kFloat && lse2.dim() == 3 && lse2.size(2) == Lpad,
+              "lse must be [B, H, round_up(Lq, 256)] fp32");
+  TORCH_CHECK(dd_scratch.is_contiguous() && dd_scratch.scalar_type() == at::kFloat &&
+                  dd_scratch.numel() >= (int64_t)B * H * Lpad,
+              "dd_scratch too small");
+  TORCH_CHECK(dq_acc.is_cuda() && dq_acc.is_contiguous() && dq_acc.scalar_type() == at::kFloat &&
+                  dq_acc.numel() >= (int64_t)B * H * Lpad * 128,
+              "dq_acc must be contiguous fp32 with at least B * H * round_up(Lq, 256) * 128 elements");
+  c10::cuda::CUDAGuard guard(q.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int64_t rows = (int64_t)B * H * Lpad;
+  {
+    const int warps = 8;
+    bwd_dot_kernel<<<(unsigned)((rows + warps - 1) / warps), warps * 32, 0, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
+        dd_scratch.data_ptr<float>(), o.stride(0), o.stride(1), o.stride(2), dout.stride(0), dout.stride(1),
+        dout.stride(2), B, H, Lq, (int)Lpad);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  C10_CUDA_CHECK(cudaMemsetAsync(dq_acc.data_ptr(), 0, (size_t)rows * 128 * sizeof(float), stream));
+  CUtensorMap tq = make_map(q), tk = make_map(k), tv = make_map(v), tg = make_map(dout);
+  BwdParams p;
+  p.lse2 = lse2.data_ptr<float>();
+  p.dd = dd_scratch.data_ptr<float>();
+  p.Lq = Lq;
+  p.Lk = Lk;
+  p.H = H;
+  p.Lpad = (int)Lpad;
+  p.scale = (float)scale;
+  p.scale_log2 = (float)(scale * 1.4426950408889634);
+  p.status = device_status_ptr(q.get_device());
+  p.out = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
+  p.sb = dk.stride(0);
+  p.sl = dk.stride(1);
+  p.sh = dk.stride(2);
+  p.out2 = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+  p.sb2 = dv.stride(0);
+  p.sl2 = dv.stride(1);
+  p.sh2 = dv.stride(2);
+  const size_t smem = sizeof(FusedSmem) + 1024;
+  C10_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  flash_bwd_fused_kernel<<<dim3((Lk + 127) / 128, H, B), 384, smem, stream>>>(tq, tk, tv, tg, p,
+                                                                               dq_acc.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const int64_t threads = (int64_t)B * Lq * H * 16;
+  dq_from_acc_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, stream>>>(
+      dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), dq.stride(0), dq.stride(1),
+      dq.stride(2), B, H, Lq, (int)Lpad);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 }  // namespace dmad
 
 // ============================================================================

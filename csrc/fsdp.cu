@@ -27,10 +27,12 @@ __global__ void fsdp_gather_kernel(Shards src, uint4* __restrict__ dst, int worl
                                    int64_t n_vec, int* status) {
   const int64_t total = len_vec * world;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    // visit the ranks in an order that starts at a different peer for every CTA
+    // (chunk, j) -> (rank, j) must be a bijection over the whole grid-stride range: the rank rotates
+    // with the 64 KB segment of j, so concurrent CTAs spread their loads over the peers while every
+    // (rank, j) is copied exactly once
     const int64_t chunk = i / len_vec;
-    const int r = (int)((chunk + blockIdx.x) % world);
     const int64_t j = i % len_vec;
+    const int r = (int)((chunk + (j >> 12)) % world);
     const int64_t g = (int64_t)r * len_vec + j;  // element-vector index in the gathered buffer
     DMAD_GUARD(r < world && j < len_vec, status)
     if (g < n_vec) dst[g] = reinterpret_cast<const uint4*>(src.p[r])[j];

@@ -306,7 +306,7 @@ class _SelfAttnCore(torch.autograd.Function):
         dqkv = torch.empty_like(qkv)
         dqk = torch.empty((R, 2 * D), dtype=qkv.dtype, device=qkv.device)
         dd = torch.empty_like(lse)
-        e.flash_bwd(qk[:, :D].view(B, L, H, hd), qk[:, D:].view(B, L, H, hd), qkv[:, 2 * D:].view(B, L, H, hd), o,
+        attn_ops.flash_bwd_into(qk[:, :D].view(B, L, H, hd), qk[:, D:].view(B, L, H, hd), qkv[:, 2 * D:].view(B, L, H, hd), o,
                     do.view(B, L, H, hd), lse, dqk[:, :D].view(B, L, H, hd), dqk[:, D:].view(B, L, H, hd),
                     dqkv[:, 2 * D:].view(B, L, H, hd), dd, scale)
         dwq = torch.zeros(D, dtype=torch.float32, device=qkv.device)
@@ -362,7 +362,7 @@ class _CrossAttnCore(torch.autograd.Function):
         dkn = torch.empty_like(kn)
         dckv = torch.empty_like(ckv)
         dd = torch.empty_like(lse)
-        e.flash_bwd(qn.view(B, L, H, hd), kn.view(B, Lc, H, hd), ckv[:, D:].view(B, Lc, H, hd), o,
+        attn_ops.flash_bwd_into(qn.view(B, L, H, hd), kn.view(B, Lc, H, hd), ckv[:, D:].view(B, Lc, H, hd), o,
                     do.view(B, L, H, hd), lse, dqn.view(B, L, H, hd), dkn.view(B, Lc, H, hd),
                     dckv[:, D:].view(B, Lc, H, hd), dd, scale)
         dcq = torch.empty_like(cq)

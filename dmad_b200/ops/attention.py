@@ -6,10 +6,28 @@ layout ``[B, L, H, D]`` in and out, softmax scale ``1/sqrt(D)`` by default.
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
 from . import ext
+
+# "fused": one kernel for dK, dV and dQ (fp32 dQ accumulator) where the key tiles fill the GPU;
+# "split": a dK/dV kernel and a dQ kernel (also used for short key sequences, e.g. cross-attention)
+BWD_IMPL = os.environ.get("DMAD_FLASH_BWD", "fused")
+_FUSED_MIN_CTAS = 296  # two waves of the 148 SMs
+
+
+def flash_bwd_into(q, k, v, o, do, lse, dq, dk, dv, dd, scale):
+    """dq, dk, dv of softmax(q k^T scale) v given o, do and the forward's log2 LSE ([B, L, H, 128] bf16,
+    strided outputs allowed; ``dd`` an fp32 [B, H, Lpad] work buffer)."""
+    e = ext()
+    B, Lq, H, _ = q.shape
+    if BWD_IMPL == "fused" and -(-k.shape[1] // 128) * H * B >= _FUSED_MIN_CTAS:
+        acc = torch.empty(B * H * lse.shape[-1] * 128, dtype=torch.float32, device=q.device)
+        e.flash_bwd_fused(q, k, v, o, do, lse, dq, dk, dv, dd, acc, float(scale))
+    else:
+        e.flash_bwd(q, k, v, o, do, lse, dq, dk, dv, dd, float(scale))
 
 
 def attention_reference(q, k, v, scale=None):
@@ -44,7 +62,7 @@ class _FlashAttn(torch.autograd.Function):
         dk = torch.empty(k.shape, dtype=k.dtype, device=k.device)
         dv = torch.empty(v.shape, dtype=v.dtype, device=v.device)
         dd = torch.empty_like(lse)
-        ext().flash_bwd(q, k, v, o, do, lse, dq, dk, dv, dd, float(ctx.scale))
+        flash_bwd_into(q, k, v, o, do, lse, dq, dk, dv, dd, ctx.scale)
         return dq, dk, dv, None
 
 
@@ -96,7 +114,7 @@ class _FlashAttnJvp(torch.autograd.Function):
         dk = torch.empty(k.shape, dtype=k.dtype, device=k.device)
         dv = torch.empty(v.shape, dtype=v.dtype, device=v.device)
         dd = torch.empty_like(lse)
-        ext().flash_bwd(q, k, v, o, do, lse, dq, dk, dv, dd, float(ctx.scale))
+        flash_bwd_into(q, k, v, o, do, lse, dq, dk, dv, dd, ctx.scale)
         return dq, dk, dv, None, None, None, None
 
 

@@ -256,6 +256,7 @@ class _SelfAttnCP(torch.autograd.Function):
     @staticmethod
     def backward(ctx, do):
         from .. import ops
+        from ..ops import attention as attn_ops
 
         qkv, wq, wk, cos, sin, rq, rk, qkv_g, o_g, lse = ctx.saved_tensors
         B, H, eps, scale, cp = ctx.cfg
@@ -276,7 +277,7 @@ class _SelfAttnCP(torch.autograd.Function):
             do_g = cp.a2a_seq_to_head(do, B, 1, H, hd)[:, :, 0]
         dqkv_g = torch.empty((B, L, 3, Hl, hd), dtype=qkv.dtype, device=qkv.device)
         dd = torch.empty_like(lse)
-        e.flash_bwd(qkv_g[:, :, 0], qkv_g[:, :, 1], qkv_g[:, :, 2], o_g, do_g, lse, dqkv_g[:, :, 0],
+        attn_ops.flash_bwd_into(qkv_g[:, :, 0], qkv_g[:, :, 1], qkv_g[:, :, 2], o_g, do_g, lse, dqkv_g[:, :, 0],
                     dqkv_g[:, :, 1], dqkv_g[:, :, 2], dd, scale)
         if cp.impl == "fused":
             gslot, gptrs = cp.slot(R * 3 * D)
@@ -427,6 +428,7 @@ class _RingSelfAttn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, do):
         from .. import ops
+        from ..ops import attention as attn_ops
         from ..ops import norm as norm_ops
 
         qkv, wq, wk, cos, sin, rq, rk, o, lse = ctx.saved_tensors
@@ -454,7 +456,7 @@ class _RingSelfAttn(torch.autograd.Function):
 
         def visit(j, src, kv):
             blk = own if kv is None else kv.view(2, R, D)
-            e.flash_bwd(q, blk[0].view(B, Ll, H, hd), blk[1].view(B, Ll, H, hd), o, do, lse, dq,
+            attn_ops.flash_bwd_into(q, blk[0].view(B, Ll, H, hd), blk[1].view(B, Ll, H, hd), o, do, lse, dq,
                         dkv[0].view(B, Ll, H, hd), dkv[1].view(B, Ll, H, hd), dd, scale)
             dq_acc.add_(dq.view(R, D).float())
             if src == cp.rank:

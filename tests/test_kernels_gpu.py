@@ -78,6 +78,36 @@ def test_flash_bwd(B, Lq, Lk, H):
         assert rel < 2e-2, (name, rel.item())
 
 
+@pytest.mark.parametrize("B,Lq,Lk,H", [(1, 128, 128, 1), (1, 384, 256, 2), (1, 999, 999, 1), (2, 300, 512, 2),
+                                        (1, 1000, 1300, 3)])
+def test_flash_bwd_fused(B, Lq, Lk, H):
+    """The single-kernel backward (fp32 dQ accumulator) against fp32 autograd, writing into strided
+    slices of one [B, L, 3, H, 128] buffer as the fused-QKV layers do."""
+    from dmad_b200 import ops
+    e = ops.ext()
+    torch.manual_seed(2)
+    q = torch.randn(B, Lq, H, 128, device=dev, dtype=torch.bfloat16)
+    k = torch.randn(B, Lk, H, 128, device=dev, dtype=torch.bfloat16)
+    v = torch.randn(B, Lk, H, 128, device=dev, dtype=torch.bfloat16)
+    g = torch.randn(B, Lq, H, 128, device=dev, dtype=torch.bfloat16)
+    scale = 1 / math.sqrt(128)
+    o = torch.empty_like(q)
+    lse = torch.empty(B, H, e.flash_lse_pad(Lq), device=dev)
+    e.flash_fwd(q, k, v, o, lse, scale)
+    dq = torch.empty(B, Lq, 3, H, 128, device=dev, dtype=torch.bfloat16)[:, :, 1]
+    dk, dv = torch.empty_like(k), torch.empty_like(v)
+    acc = torch.full((B * H * lse.shape[-1] * 128,), float("nan"), device=dev)
+    e.flash_bwd_fused(q, k, v, o, g, lse, dq, dk, dv, torch.empty_like(lse), acc, scale)
+    torch.cuda.synchronize()
+    ops.check_device_status()
+    qr, kr, vr = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+    ref, _ = _attn_ref(qr, kr, vr, scale)
+    ref.backward(g.float())
+    for a, b, name in ((dq, qr.grad, "dq"), (dk, kr.grad, "dk"), (dv, vr.grad, "dv")):
+        rel = (a.float() - b).norm() / b.norm()
+        assert rel < 2e-2, (name, rel.item())
+
+
 @pytest.mark.parametrize("D,R,G", [(1536, 1000, 2), (5120, 257, 1), (256, 64, 4)])
 @pytest.mark.parametrize("rms", [False, True])
 def test_ln_mod(D, R, G, rms):
@@ -247,3 +277,16 @@ def test_fsdp_gather_single_rank():
     e.fsdp_gather([shard.data_ptr()], dst, 1024, 1000)
     torch.cuda.synchronize()
     assert torch.equal(dst[:1000], shard[:1000])
+
+
+@pytest.mark.parametrize("world,ln", [(2, 1 << 20), (3, 40000), (8, 65536 + 8)])
+def test_fsdp_gather_many_shards(world, ln):
+    """Several shard addresses (here all on this GPU) and a grid-stride range larger than the grid:
+    every element of the gathered buffer comes from its own shard exactly once."""
+    e = _ext()
+    shards = [torch.randn(ln, device=dev).to(torch.bfloat16) for _ in range(world)]
+    n = ln * world - 8
+    dst = torch.full((ln * world,), float("nan"), device=dev, dtype=torch.bfloat16)
+    e.fsdp_gather([s.data_ptr() for s in shards], dst, ln, n)
+    torch.cuda.synchronize()
+    assert torch.equal(dst[:n], torch.cat(shards)[:n])
