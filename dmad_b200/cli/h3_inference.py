@@ -20,6 +20,7 @@ import torch
 
 from ..inference.h3 import (H3Geometry, build_packed_sequence, build_row_timesteps, latent_shape_of, rollout,
                             sigma_grid)
+from ..inference.text_encoder import read_prompts
 from ..models.h3 import H3Config, H3Model
 
 
@@ -57,16 +58,6 @@ def parse_args(argv=None):
     return p.parse_args(argv)
 
 
-def read_prompts(path):
-    out = []
-    for line in open(path, encoding="utf-8"):
-        line = line.strip()
-        if not line:
-            continue
-        out.append(json.loads(line)["prompt"] if path.endswith(".jsonl") else line)
-    return out
-
-
 def main(argv=None):
     args = parse_args(argv)
     prompts = list(args.prompt) + (read_prompts(args.prompt_file) if args.prompt_file else [])
@@ -102,8 +93,19 @@ def main(argv=None):
     shape = latent_shape_of(args.height, args.width, args.num_frames, geometry)
     vsig, asig = sigma_grid(args.steps, args.video_shift), sigma_grid(args.steps, args.audio_shift)
     g = torch.Generator().manual_seed(args.seed)
-    conds = [{"prompt_embeds": torch.randn(1, args.text_tokens, cfg.text_dim, generator=g).to(torch.bfloat16),
-              "text_token_tags": torch.ones(args.text_tokens, dtype=torch.long)} for _ in prompts]
+    te_dir = os.path.join(args.model_dir, "text_encoder") if args.model_dir else None
+    if te_dir and not args.random_init and os.path.isdir(te_dir):
+        # the Qwen3-VL conditioner (hidden layer 50, verbatim prompts); freed before the transformer loads
+        from ..inference.text_encoder import Qwen3VLConditioner
+        enc = Qwen3VLConditioner.from_pretrained(args.model_dir, device)
+        conds = enc.encode_all(prompts)
+        del enc
+        if device.type == "cuda":
+            torch.cuda.empty_cache()
+        log(f"encoded {len(conds)} prompt(s)")
+    else:
+        conds = [{"prompt_embeds": torch.randn(1, args.text_tokens, cfg.text_dim, generator=g).to(torch.bfloat16),
+                  "text_token_tags": torch.ones(args.text_tokens, dtype=torch.long)} for _ in prompts]
     layouts = [build_packed_sequence(c["text_token_tags"], shape["latent_frames"], shape["latent_height"],
                                      shape["latent_width"], shape["audio_latents"], geometry.patch_size) for c in conds]
     torch.manual_seed(args.seed)

@@ -2,12 +2,16 @@
 
     python -m dmad_b200.tools.h3_data prompt-list captions.jsonl prompts.jsonl [--min-words 3]
     python -m dmad_b200.tools.h3_data pool-indices --caption-map prompts.jsonl --real-latents real/ --out idx.txt
+    python -m dmad_b200.tools.h3_data encode-prompts prompts.jsonl --model-dir H3/ --out cache/ [--indices idx.txt]
+        [--shard R/W]          (then: python -m dmad_b200.tools.h3_data merge-prompt-shards cache/)
     python -m dmad_b200.tools.h3_data teacher-data --prompt-cache cache/ --indices idx.txt --out teacher/ \\
         [--model-dir ...] [--shard R/W] [--steps 31] [--video-shift 12] [--audio-shift 3]
 
 Parity: train/h3/data_process/build_prompt_list.py:30-59 (deduplicated caption list with the clip ids of
 every caption), build_pool_indices.py:29-47 (caption indices of the clips of the training frame tier, plus
-the first visualisation prompts) and gen_teacher_data.py:48-89 (31-step Euler teacher rollouts, shifts
+the first visualisation prompts), encode_prompts.py:51-144 (the prompt cache: Qwen3-VL layer-50 conditions
+``conditions/condition_<index:08d>.pt`` of the selected prompts, sharded by rank, resumable, one metadata
+file per shard merged at the end) and gen_teacher_data.py:48-89 (31-step Euler teacher rollouts, shifts
 12 / 3, seed = caption index, resumable, written to a temporary name and renamed).  The outputs are the
 files ``data.h3_pool.FileLatentPool`` reads.
 """
@@ -55,6 +59,55 @@ def pool_indices(caption_map: str, real_latents: str, num_frames: int, out: str,
     with open(out, "w") as f:
         f.write("".join(f"{i}\n" for i in sorted(idx)))
     return n, sorted(idx)
+
+
+def _write_jsonl(path, rows):
+    tmp = f"{path}.tmp{os.getpid()}"
+    with open(tmp, "w", encoding="utf-8") as f:
+        for r in rows:
+            f.write(json.dumps(r, ensure_ascii=False) + "\n")
+    os.replace(tmp, path)
+
+
+def encode_prompts(prompts_path: str, out_dir: str, encoder, indices: list[int] | None = None, shard: str = "",
+                   overwrite: bool = False) -> list[dict]:
+    """Conditions of the prompts (all, or the caption ``indices``) with ``encoder.encode(prompt)``; files
+    that exist are kept unless ``overwrite``.  Returns the metadata rows of this shard."""
+    from ..inference.text_encoder import read_prompts
+
+    indexed = list(enumerate(read_prompts(prompts_path)))
+    if indices is not None:
+        by_idx = dict(indexed)
+        indexed = [(i, by_idx[i]) for i in sorted(set(indices))]
+    if shard:
+        r, w = (int(x) for x in shard.split("/"))
+        indexed = indexed[r::w]
+    os.makedirs(os.path.join(out_dir, "conditions"), exist_ok=True)
+    rows = []
+    for index, prompt in indexed:
+        rel = os.path.join("conditions", f"condition_{index:08d}.pt")
+        path = os.path.join(out_dir, rel)
+        if overwrite or not os.path.isfile(path):
+            cond = encoder.encode(prompt)
+            tmp = f"{path}.tmp{os.getpid()}"
+            torch.save({"conditioning": {"positive": cond}, "prompt": prompt, "source_index": index}, tmp)
+            os.replace(tmp, path)
+        rows.append({"id": index, "caption": prompt, "condition_path": rel})
+    name = "metadata.jsonl" if not shard else f"metadata_shard{shard.replace('/', 'of')}.jsonl"
+    _write_jsonl(os.path.join(out_dir, name), rows)
+    return rows
+
+
+def merge_prompt_shards(out_dir: str) -> int:
+    import glob as _glob
+
+    rows = [json.loads(line) for f in sorted(_glob.glob(os.path.join(out_dir, "metadata_shard*.jsonl")))
+            for line in open(f, encoding="utf-8") if line.strip()]
+    rows.sort(key=lambda r: r["id"])
+    if len({r["id"] for r in rows}) != len(rows):
+        raise RuntimeError("duplicate ids across shards")
+    _write_jsonl(os.path.join(out_dir, "metadata.jsonl"), rows)
+    return len(rows)
 
 
 @torch.no_grad()
@@ -109,6 +162,15 @@ def main(argv=None):
     b.add_argument("--num-frames", type=int, default=124)
     b.add_argument("--out", required=True)
     b.add_argument("--num-viz-prompts", type=int, default=4)
+    e = sub.add_parser("encode-prompts")
+    e.add_argument("prompts")
+    e.add_argument("--model-dir", required=True)
+    e.add_argument("--out", required=True)
+    e.add_argument("--indices", default=None)
+    e.add_argument("--shard", default="")
+    e.add_argument("--overwrite", action="store_true")
+    mg = sub.add_parser("merge-prompt-shards")
+    mg.add_argument("out")
     c = sub.add_parser("teacher-data")
     c.add_argument("--prompt-cache", required=True)
     c.add_argument("--indices", required=True)
@@ -123,6 +185,15 @@ def main(argv=None):
     elif args.cmd == "pool-indices":
         n, idx = pool_indices(args.caption_map, args.real_latents, args.num_frames, args.out, args.num_viz_prompts)
         print(f"{n} clips -> {len(idx)} caption indices -> {args.out}")
+    elif args.cmd == "encode-prompts":
+        from ..inference.text_encoder import Qwen3VLConditioner
+        dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
+        idx = [int(x) for x in open(args.indices) if x.strip()] if args.indices else None
+        rows = encode_prompts(args.prompts, args.out, Qwen3VLConditioner.from_pretrained(args.model_dir, dev), idx,
+                              args.shard, args.overwrite)
+        print(f"{len(rows)} conditions under {args.out}")
+    elif args.cmd == "merge-prompt-shards":
+        print(merge_prompt_shards(args.out), "rows merged")
     else:
         idx = [int(x) for x in open(args.indices) if x.strip()]
         out = teacher_data(args.prompt_cache, idx, args.out, args.shard, args.steps, args.video_shift,
