@@ -69,6 +69,8 @@ class WanDMADConfig:
     checkpoint_student_blocks: int = 0
     checkpoint_critic_blocks: int = 0
     checkpoint_critic_blocks_student_phase: int | None = None
+    checkpoint_student_policy: str = "block_wise"  # "mm_only": keep matmul / attention outputs
+    checkpoint_critic_policy: str = "block_wise"
     rectified_flow_t_scaling_factor: float = 1000.0
     # rCM consistency term (0 = pure DMAD, as the reference's DMAD experiments; > 0 adds the sCM /
     # dCM loss of the rCM recipe in the student phase, which needs the teacher network)
@@ -129,6 +131,8 @@ class WanDMAD(nn.Module):
         self.critic_heads.to(device=device, dtype=torch.float32)
         self.net.checkpoint_blocks = cfg.checkpoint_student_blocks
         self.net_fake_score.checkpoint_blocks = cfg.checkpoint_critic_blocks
+        self.net.checkpoint_policy = cfg.checkpoint_student_policy
+        self.net_fake_score.checkpoint_policy = cfg.checkpoint_critic_policy
         broadcast_module(self.net)
         broadcast_module(self.net_fake_score)
         broadcast_module(self.critic_heads)

@@ -282,15 +282,12 @@ class _SelfAttnCore(torch.autograd.Function):
         R, D3 = qkv.shape
         D = D3 // 3
         hd = D // H
-        e = ops.ext()
         qk, rq, rk = norm_ops.qk_norm_rope(qkv, wq, wk, cos, sin, D, hd, eps)
         q = qk[:, :D].view(B, L, H, hd)
         k = qk[:, D:].view(B, L, H, hd)
         v = qkv[:, 2 * D:].view(B, L, H, hd)
-        o = torch.empty((B, L, H, hd), dtype=qkv.dtype, device=qkv.device)
-        lse = torch.empty((B, H, attn_ops._lse_pad(L)), dtype=torch.float32, device=qkv.device)
         scale = 1.0 / math.sqrt(hd)
-        e.flash_fwd(q, k, v, o, lse, scale)
+        o, lse = attn_ops.flash_attn_fwd(q, k, v, scale)
         ctx.save_for_backward(qkv, wq, wk, cos, sin, rq, rk, o, lse)
         ctx.cfg = (B, L, H, hd, D, eps, scale)
         return o.view(R, D)
@@ -339,13 +336,11 @@ class _CrossAttnCore(torch.autograd.Function):
     def forward(ctx, cq, ckv, wq, wk, B, L, Lc, H, eps):
         R, D = cq.shape
         hd = D // H
-        e = ops.ext()
         qn, rq = _rms_fwd(cq, wq, eps)
         kn, rk = _rms_fwd(ckv[:, :D], wk, eps)
-        o = torch.empty((B, L, H, hd), dtype=cq.dtype, device=cq.device)
-        lse = torch.empty((B, H, attn_ops._lse_pad(L)), dtype=torch.float32, device=cq.device)
         scale = 1.0 / math.sqrt(hd)
-        e.flash_fwd(qn.view(B, L, H, hd), kn.view(B, Lc, H, hd), ckv[:, D:].view(B, Lc, H, hd), o, lse, scale)
+        o, lse = attn_ops.flash_attn_fwd(qn.view(B, L, H, hd), kn.view(B, Lc, H, hd), ckv[:, D:].view(B, Lc, H, hd),
+                                         scale)
         ctx.save_for_backward(cq, ckv, wq, wk, rq, rk, o, lse)
         ctx.cfg = (B, L, Lc, H, hd, D, eps, scale)
         return o.view(R, D)

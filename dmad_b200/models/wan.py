@@ -21,7 +21,7 @@ from dataclasses import dataclass, field
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
-from torch.utils.checkpoint import checkpoint
+from .sac import checkpoint_block
 
 from .. import ops
 from ..ops import norm as norm_ops
@@ -199,6 +199,7 @@ class WanModel(nn.Module):
         self.blocks = nn.ModuleList([WanBlock(cfg) for _ in range(cfg.num_layers)])
         self.head = _Head(cfg)
         self.checkpoint_blocks = 0  # activation-checkpoint the first N blocks
+        self.checkpoint_policy = "block_wise"  # or "mm_only" (keep matmul / attention outputs)
         self._rope_cache: dict = {}
         self.cp = None  # ContextParallel (sequence sharding) or None
         self.init_weights()
@@ -312,7 +313,7 @@ class WanModel(nn.Module):
         for i in range(nblocks):
             blk = self.blocks[i]
             if self.training and torch.is_grad_enabled() and i < self.checkpoint_blocks:
-                x = checkpoint(blk, x, e0, context, cos, sin, B, Ll, rpg, cp, use_reentrant=False)
+                x = checkpoint_block(blk, x, e0, context, cos, sin, B, Ll, rpg, cp, policy=self.checkpoint_policy)
             else:
                 x = blk(x, e0, context, cos, sin, B, Ll, rpg, cp)
             if feature_hook_block is not None and i == (feature_hook_block % len(self.blocks)):

@@ -45,13 +45,27 @@ def _lse_pad(L: int) -> int:
     return (L + 255) // 256 * 256
 
 
+@torch.library.custom_op("dmad::flash_attn_fwd", mutates_args=(), device_types="cuda")
+def flash_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """(o [B, Lq, H, 128] bf16, log2 LSE [B, H, round_up(Lq, 256)] fp32) of one tcgen05 forward.  A
+    dispatcher op, so that selective activation checkpointing can keep its outputs."""
+    B, Lq, H, D = q.shape
+    o = torch.empty((B, Lq, H, D), dtype=q.dtype, device=q.device)
+    lse = torch.empty((B, H, _lse_pad(Lq)), dtype=torch.float32, device=q.device)
+    ext().flash_fwd(q, k, v, o, lse, float(scale))
+    return o, lse
+
+
+@flash_attn_fwd.register_fake
+def _(q, k, v, scale):
+    B, Lq, H, D = q.shape
+    return q.new_empty((B, Lq, H, D)), q.new_empty((B, H, _lse_pad(Lq)), dtype=torch.float32)
+
+
 class _FlashAttn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, scale):
-        B, Lq, H, D = q.shape
-        o = torch.empty((B, Lq, H, D), dtype=q.dtype, device=q.device)
-        lse = torch.empty((B, H, _lse_pad(Lq)), dtype=torch.float32, device=q.device)
-        ext().flash_fwd(q, k, v, o, lse, float(scale))
+        o, lse = flash_attn_fwd(q, k, v, float(scale))
         ctx.save_for_backward(q, k, v, o, lse)
         ctx.scale = scale
         return o

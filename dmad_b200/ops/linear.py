@@ -19,18 +19,33 @@ def _rows(t):
     return t.reshape(-1, t.shape[-1])
 
 
+@torch.library.custom_op("dmad::lora_linear_fwd", mutates_args=(), device_types="cuda")
+def lora_linear_fwd(x2: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, a: torch.Tensor, b: torch.Tensor,
+                    scale: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """(y, s x A^T) of the LoRA-fused linear on rows ``x2``.  A dispatcher op, so that selective
+    activation checkpointing can keep its outputs."""
+    M, N, r = x2.shape[0], w.shape[0], a.shape[0]
+    e = ext()
+    xa = torch.empty((M, r), dtype=x2.dtype, device=x2.device)
+    e.gemm_bf16(x2, a.contiguous(), None, None, None, xa, float(scale), 0)
+    y = torch.empty((M, N), dtype=x2.dtype, device=x2.device)
+    e.gemm_bf16(x2, w.contiguous(), xa, b.contiguous(), bias.float().contiguous() if bias is not None else None,
+                y, 1.0, 0)
+    return y, xa
+
+
+@lora_linear_fwd.register_fake
+def _(x2, w, bias, a, b, scale):
+    return x2.new_empty((x2.shape[0], w.shape[0])), x2.new_empty((x2.shape[0], a.shape[0]))
+
+
 class _LoraLinear(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, bias, a, b, scale):
         x2 = _rows(x)
         x2 = x2 if (x2.stride(-1) == 1 and x2.stride(0) % 8 == 0) else x2.contiguous()
-        M, N, r = x2.shape[0], w.shape[0], a.shape[0]
-        e = ext()
-        xa = torch.empty((M, r), dtype=x.dtype, device=x.device)
-        e.gemm_bf16(x2, a.contiguous(), None, None, None, xa, float(scale), 0)
-        y = torch.empty((M, N), dtype=x.dtype, device=x.device)
-        e.gemm_bf16(x2, w.contiguous(), xa, b.contiguous(), bias.float().contiguous() if bias is not None else None,
-                    y, 1.0, 0)
+        N = w.shape[0]
+        y, xa = lora_linear_fwd(x2, w, bias, a, b, float(scale))
         ctx.save_for_backward(x2, w, a, b, xa)
         ctx.scale = scale
         ctx.has_bias = bias is not None

@@ -68,3 +68,48 @@ def test_wan_forward_jvp_gpu_matches_cpu():
     out, tout = wan_forward_jvp(mg, x.cuda(), tx.cuda(), t.cuda(), tt.cuda(), c.cuda().bfloat16())
     assert ((out.cpu() - ref).norm() / ref.norm()).item() < 5e-2
     assert ((tout.cpu() - tref).norm() / tref.norm()).item() < 5e-2
+
+
+@pytest.mark.parametrize("lora", [0, 8])
+def test_mm_only_checkpoint_keeps_kernel_outputs(lora):
+    """mm_only on the CUDA path: the tcgen05 attention and LoRA-linear forwards are dispatcher ops whose
+    outputs the recomputation reuses; gradients equal the unchecked run's."""
+    from torch.utils._python_dispatch import TorchDispatchMode
+
+    from dmad_b200.models.wan import WanConfig, WanModel
+
+    class Count(TorchDispatchMode):
+        n = 0
+
+        def __torch_dispatch__(self, func, types, args=(), kwargs=None):
+            if func in (torch.ops.dmad.flash_attn_fwd.default, torch.ops.dmad.lora_linear_fwd.default):
+                Count.n += 1
+            return func(*args, **(kwargs or {}))
+
+    def run(policy):
+        torch.manual_seed(0)
+        m = WanModel(WanConfig(dim=256, ffn_dim=512, num_heads=2, num_layers=2, text_dim=64, freq_dim=64))
+        torch.nn.init.normal_(m.head.head.weight, std=0.05)
+        if lora:
+            m.enable_lora(lora)
+            for b in m.blocks:
+                for lin in b.linears():
+                    torch.nn.init.normal_(lin.lora_B, std=0.02)
+        m = m.cuda().to(torch.bfloat16).train()
+        if policy:
+            m.checkpoint_blocks, m.checkpoint_policy = 2, policy
+        g = torch.Generator().manual_seed(4)
+        x = torch.randn(1, 16, 2, 16, 16, generator=g).cuda()
+        t, ctx = torch.rand(1, 1, generator=g).cuda(), torch.randn(1, 8, 64, generator=g).cuda()
+        out = m(x, t, ctx)
+        Count.n = 0
+        with Count():
+            out.float().square().mean().backward()
+        return torch.cat([p.grad.float().reshape(-1) for p in m.parameters() if p.grad is not None]), Count.n
+
+    g0, n0 = run(None)
+    g1, n1 = run("mm_only")
+    g2, n2 = run("block_wise")
+    assert n0 == 0 and n1 == 0 and n2 > 0, (n0, n1, n2)
+    for g in (g1, g2):
+        assert ((g - g0).norm() / g0.norm()).item() < 1e-2
