@@ -131,9 +131,11 @@ class WanBlock(nn.Module):
         return [self.self_attn.qkv, self.self_attn.o, self.cross_attn.q, self.cross_attn.kv, self.cross_attn.o,
                 getattr(self.ffn, "0"), getattr(self.ffn, "2")]
 
-    def forward(self, x, e0, context, cos, sin, B, L, rpg, cp=None):
+    def forward(self, x, e0, context, cos, sin, B, L, rpg, cp=None, attn_ctx=None):
         """x: [B*L, D] bf16 (L = this rank's tokens under context parallelism); e0: [G, 6, D] fp32;
-        context: [B*Lc, D] bf16; rpg: rows per modulation group (int) or an int32 group index per row."""
+        context: [B*Lc, D] bf16; rpg: rows per modulation group (int) or an int32 group index per row;
+        attn_ctx: a block mask (``AttnMaskSpec``) or a KV-cache context (``AttnContext``) for the causal
+        and teacher-forcing modes (None: full attention)."""
         cfg = self.cfg
         D, H = cfg.dim, cfg.num_heads
         Lc = context.shape[0] // B
@@ -141,7 +143,9 @@ class WanBlock(nn.Module):
         e = self.modulation.float()[0] + e0  # [G, 6, D]
         h = ops.ln_mod(x, e[:, 1], e[:, 0], a_add=1.0, eps=cfg.eps, **grp)
         qkv = self.self_attn.qkv(h)
-        if cp is not None and cp.world > 1:
+        if attn_ctx is not None:
+            a = self._masked_self_attention(qkv, cos, sin, B, L, attn_ctx)
+        elif cp is not None and cp.world > 1:
             from ..parallel.cp import ring_self_attention, self_attention_cp
             attn = ring_self_attention if cp.impl == "ring" else self_attention_cp
             a = attn(qkv, self.self_attn.norm_q.weight, self.self_attn.norm_k.weight, cos, sin, B, H, cfg.eps, cp)
@@ -160,6 +164,33 @@ class WanBlock(nn.Module):
         f = ops.gelu_tanh(getattr(self.ffn, "0")(h2))
         y2 = getattr(self.ffn, "2")(f)
         return ops.gate_residual(x, y2, e[:, 5], **grp)
+
+
+    def _masked_self_attention(self, qkv, cos, sin, B, L, actx):
+        """Self-attention under a block mask and / or against the KV cache (causal modes)."""
+        from ..ops.block_attention import AttnMaskSpec, block_attention
+        from .kv_cache import KVCacheMode
+
+        cfg = self.cfg
+        D, H = cfg.dim, cfg.num_heads
+        hd = D // H
+        q = norm_ops.rope(ops.rms_norm(qkv[:, :D], self.self_attn.norm_q.weight, cfg.eps), cos, sin, hd)
+        k = norm_ops.rope(ops.rms_norm(qkv[:, D:2 * D], self.self_attn.norm_k.weight, cfg.eps), cos, sin, hd)
+        q4, k4, v4 = q.reshape(B, L, H, hd), k.reshape(B, L, H, hd), qkv[:, 2 * D:].reshape(B, L, H, hd)
+        if isinstance(actx, AttnMaskSpec):
+            return block_attention(q4, k4, v4, actx).reshape(B * L, D)
+        kk, vv = k4, v4
+        cache = actx.kv_cache
+        if actx.mode != KVCacheMode.DISABLED and cache is not None:
+            at = cache.get_prefix_end(actx.block_range)
+            if actx.mode == KVCacheMode.APPEND:
+                if at != cache.current_len:
+                    raise RuntimeError("an appended chunk must follow the whole committed prefix")
+                _, end = cache.append(k4, v4)
+                kk, vv = cache.k[:, :end], cache.v[:, :end]
+            else:
+                kk, vv = cache.write_transient(k4, v4, at)
+        return block_attention(q4, kk, vv, actx.mask).reshape(B * L, D)
 
 
 class _Head(nn.Module):
@@ -271,10 +302,13 @@ class WanModel(nn.Module):
 
     # --------------------------------------------------------------- forward
     def forward(self, x_B_C_T_H_W, timesteps_B_T, crossattn_emb, feature_hook_block: int | None = None,
-                stop_after_block: int | None = None, **unused):
+                stop_after_block: int | None = None, attn_meta=None, inference_state=None, **unused):
         """Returns the denoiser output; with ``feature_hook_block`` returns (output, features [B, L, D])
         where features is the token output of that block (the critic's feature tap).  With
-        ``stop_after_block`` the forward stops after that block and returns only its features."""
+        ``stop_after_block`` the forward stops after that block and returns only its features.
+        ``attn_meta`` (an ``AttnMaskSpec``) masks self-attention block-wise over the whole sequence;
+        ``inference_state`` (a ``CausalInferenceState``) runs the input as the chunk at its current
+        block against the per-layer KV caches, with RoPE at the chunk's frame offset."""
         cfg = self.cfg
         cp = self.cp if (self.cp is not None and self.cp.world > 1) else None
         if cp is not None and cp.broadcast_inputs:
@@ -290,7 +324,11 @@ class WanModel(nn.Module):
             timesteps_B_T = timesteps_B_T[:, None]
         uniform = timesteps_B_T.shape[1] == 1
         assert uniform or timesteps_B_T.shape[1] == T, "timesteps must be [B, 1] or [B, T]"
-        cos, sin = self.rope_tables(T, H, W, x.device)
+        masked = inference_state is not None or (attn_meta is not None and attn_meta.mode != "none")
+        if masked and cp is not None:
+            raise NotImplementedError("block masks / KV caches run without context parallelism")
+        t_off = inference_state.frame_offset() if inference_state is not None else 0
+        cos, sin = self.rope_tables(T, H, W, x.device, t_off)
         Ll, r0 = L, 0
         if cp is not None:
             assert L % cp.world == 0, f"L = T*H*W = {L} must be divisible by cp = {cp.world}"
@@ -312,10 +350,15 @@ class WanModel(nn.Module):
         nblocks = len(self.blocks) if stop_after_block is None else stop_after_block + 1
         for i in range(nblocks):
             blk = self.blocks[i]
+            actx = None
+            if inference_state is not None:
+                actx = inference_state.context(i)
+            elif masked:
+                actx = attn_meta
             if self.training and torch.is_grad_enabled() and i < self.checkpoint_blocks:
-                x = checkpoint_block(blk, x, e0, context, cos, sin, B, Ll, rpg, cp, policy=self.checkpoint_policy)
+                x = checkpoint_block(blk, x, e0, context, cos, sin, B, Ll, rpg, cp, actx, policy=self.checkpoint_policy)
             else:
-                x = blk(x, e0, context, cos, sin, B, Ll, rpg, cp)
+                x = blk(x, e0, context, cos, sin, B, Ll, rpg, cp, actx)
             if feature_hook_block is not None and i == (feature_hook_block % len(self.blocks)):
                 feats = x
         if stop_after_block is not None:
