@@ -99,6 +99,7 @@ class EDMDMADConfig:
     gap_tau: float = 2.0
     r1_gamma: float = 0.0
     r1_batch_size: int = 2
+    pretrained_critic: str = ""          # e.g. "vgg16_bn,tf_efficientnet_lite0": Projected-GAN feature critic
     teacher_loss_weight: float = 1.0
     real_loss_weight: float = 1.0
     generator_lr: float = 2e-6
@@ -113,17 +114,25 @@ class EDMCritic(nn.Module):
     def __init__(self, cfg: EDMDMADConfig, teacher: EDMPrecond):
         super().__init__()
         self.cfg = cfg
-        self.fake_unet = copy.deepcopy(teacher)
-        unet = self.fake_unet.model
-        unet.dec, unet.out_norm, unet.out_conv = None, None, None
-        c = unet.bottleneck_channels
-        spatial = cfg.resolution >> (len([k for k in unet.enc.keys() if k.endswith("_down")]))
-        self.head_real = make_binary_head(c, spatial)
-        self.head_teacher = make_binary_head(c, spatial)
-        if cfg.critic_spectral_norm:
-            for m in list(unet.enc.modules()) + list(self.head_real.modules()) + list(self.head_teacher.modules()):
-                if isinstance(m, nn.Conv2d):
-                    sn_wrap(m)
+        self.pg = None
+        if cfg.pretrained_critic:
+            # frozen feature networks + multi-scale heads instead of the teacher-encoder critic
+            # (edm_guidance.py:87-91); no noise-level input
+            from ..models.pg_critic import PGTwoHeadCritic
+
+            self.pg = PGTwoHeadCritic([b for b in cfg.pretrained_critic.split(",") if b], c_dim=cfg.label_dim)
+        else:
+            self.fake_unet = copy.deepcopy(teacher)
+            unet = self.fake_unet.model
+            unet.dec, unet.out_norm, unet.out_conv = None, None, None
+            c = unet.bottleneck_channels
+            spatial = cfg.resolution >> (len([k for k in unet.enc.keys() if k.endswith("_down")]))
+            self.head_real = make_binary_head(c, spatial)
+            self.head_teacher = make_binary_head(c, spatial)
+            if cfg.critic_spectral_norm:
+                for m in list(unet.enc.modules()) + list(self.head_real.modules()) + list(self.head_teacher.modules()):
+                    if isinstance(m, nn.Conv2d):
+                        sn_wrap(m)
         self.register_buffer("karras", torch.flip(get_sigmas_karras(cfg.num_train_timesteps, cfg.sigma_min,
                                                                     cfg.sigma_max, cfg.rho), dims=[0]))
         self.register_buffer("gap_ema", torch.zeros(NUM_GAP_BANDS))
@@ -147,9 +156,22 @@ class EDMCritic(nn.Module):
         idx = self.sample_timesteps(n, device)
         return idx, self.karras[idx]
 
+    def set_trainable(self, flag: bool):
+        """Critic parameters on / off for autograd; the feature networks of the pretrained critic stay frozen."""
+        self.requires_grad_(flag)
+        if self.pg is not None:
+            self.pg.features.requires_grad_(False)
+
     def logits(self, x, sigma, labels):
+        """(d_real, d_teacher): [N] each, or [N, K] per-pixel logits with the pretrained critic."""
+        if self.pg is not None:
+            return self.pg(x, labels)
         rep = self.fake_unet(x, sigma, labels, return_bottleneck=True).float()
         return self.head_real(rep).reshape(-1), self.head_teacher(rep).reshape(-1)
+
+    @staticmethod
+    def _per_sample(d):
+        return d if d.dim() == 1 else d.float().mean(1)
 
     @torch.no_grad()
     def update_gap(self, d_T, d_Q, idx_T, idx_Q):
@@ -190,6 +212,8 @@ class EDMCritic(nn.Module):
         d_r, d_t = self.logits(noisy, sig, labels)
         w = self.gap_weight(idx)
         x = -d_t
+        if w is not None and x.dim() == 2:  # per-pixel logits: the sample's weight on each of its logits
+            w = w[:, None].expand_as(x)
         tl = x.mean() if w is None else (x * w).sum() / w.sum().clamp(min=1.0) + x.sum() * 0.0
         return {"gen_teacher_loss": tl, "gen_real_loss": (-d_r).mean()}
 
@@ -197,10 +221,10 @@ class EDMCritic(nn.Module):
         k = max(1, min(xT.shape[0], self.cfg.r1_batch_size))
         a = xT[:k].detach().requires_grad_(True)
         dr, _ = self.logits(a, sT[:k], lT[:k])
-        g1 = torch.autograd.grad(dr.sum(), a, create_graph=True)[0]
+        g1 = torch.autograd.grad(self._per_sample(dr).sum(), a, create_graph=True)[0]
         b = xQ[:k].detach().requires_grad_(True)
         _, dq = self.logits(b, sQ[:k], lQ[:k])
-        g2 = torch.autograd.grad(dq.sum(), b, create_graph=True)[0]
+        g2 = torch.autograd.grad(self._per_sample(dq).sum(), b, create_graph=True)[0]
         return 0.5 * (g1.pow(2).flatten(1).sum(1).mean() + g2.pow(2).flatten(1).sum(1).mean())
 
     def critic_loss(self, fake, real, fake_l, real_l, teacher, teacher_l):
@@ -214,11 +238,17 @@ class EDMCritic(nn.Module):
             s4 = sig.reshape(-1, 1, 1, 1)
             xT, xG, xQ = real + s4 * torch.randn_like(real), fake + s4 * torch.randn_like(fake), \
                 teacher + s4 * torch.randn_like(teacher)
-        d_r, d_t = self.logits(torch.cat([xT, xG, xQ]), torch.cat([sig, sig, sig]), torch.cat([real_l, fake_l, teacher_l]))
+        if self.pg is not None:
+            # one forward per image set, so the heads' BatchNorms see the batches the generator step sees
+            parts = [self.logits(x, sig, lab) for x, lab in ((xT, real_l), (xG, fake_l), (xQ, teacher_l))]
+            d_r, d_t = torch.cat([p[0] for p in parts]), torch.cat([p[1] for p in parts])
+        else:
+            d_r, d_t = self.logits(torch.cat([xT, xG, xQ]), torch.cat([sig, sig, sig]),
+                                   torch.cat([real_l, fake_l, teacher_l]))
         dR_T, dR_G, dR_Q = d_r[:B], d_r[B:2 * B], d_r[2 * B:]
         dQ_G, dQ_Q = d_t[B:2 * B], d_t[2 * B:]
         if self.cfg.teacher_gap_route:
-            self.update_gap(dR_T.detach(), dR_Q.detach(), idx, idx)
+            self.update_gap(self._per_sample(dR_T.detach()), self._per_sample(dR_Q.detach()), idx, idx)
         loss = F.softplus(-dR_T).mean() + F.softplus(dR_G).mean() + F.softplus(-dQ_Q).mean() + F.softplus(dQ_G).mean()
         log = {"critic_acc_t": (dR_T > 0).float().mean().detach(), "critic_acc_q": (dQ_Q > 0).float().mean().detach(),
                "critic_acc_g": (0.5 * ((dR_G < 0).float().mean() + (dQ_G < 0).float().mean())).detach()}
@@ -268,9 +298,9 @@ class EDMDMAD:
         self.generator.train()
         self.critic.train()
         gen = self.generator(batch["noise"], sigma, batch["labels"])
-        self.critic.requires_grad_(False)
+        self.critic.set_trainable(False)
         gl = self.critic.generator_loss(gen, batch["labels"])
-        self.critic.requires_grad_(True)
+        self.critic.set_trainable(True)
         loss_g = gl["gen_teacher_loss"] * c.teacher_loss_weight + gl["gen_real_loss"] * c.real_loss_weight
         loss_g.backward()
         gnorm = torch.nn.utils.clip_grad_norm_(self.generator.parameters(), c.max_grad_norm)
