@@ -254,14 +254,21 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         tmem_ld32(t_s + 32, r[1]);
         tmem_wait_ld();
         const float* lse = sm.lse[s] + c0;
-        // every second exponential on the FMA pipe (padded query columns have lse = +inf: the
-        // polynomial's clamp gives ~1e-38 there, against dO = 0)
+        // every second exponential on the FMA pipe, two at a time as one packed polynomial
+        // (padded query columns have lse = +inf: the polynomial's clamp gives ~1e-38 there,
+        // against dO = 0)
 #pragma unroll
         for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float x = fmaf(__uint_as_float(r[c][e]), scale_log2, -lse[c * 32 + e]);
-            pv[c * 32 + e] = (e & 1) ? ex2_poly(x) : ex2_approx(x);
+          for (int e = 0; e < 32; e += 4) {
+            float x[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) x[u] = fmaf(__uint_as_float(r[c][e + u]), scale_log2, -lse[c * 32 + e + u]);
+            const float2 pp = ex2_poly2(x[1], x[3]);
+            pv[c * 32 + e] = ex2_approx(x[0]);
+            pv[c * 32 + e + 1] = pp.x;
+            pv[c * 32 + e + 2] = ex2_approx(x[2]);
+            pv[c * 32 + e + 3] = pp.y;
           }
       }
       {
@@ -283,15 +290,17 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         tmem_ld32(t_dp + 32, r[1]);
         tmem_wait_ld();
         const float* dd = sm.dd[s] + c0;
+        const uint64_t sc2 = f2(scale, scale);
         uint32_t w[32];
 #pragma unroll
         for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
+          for (int e = 0; e < 16; ++e) {  // dS = P (dP - D) scale, two columns per packed op
             const int q = c * 32 + 2 * e;
-            const float d0 = pv[q] * (__uint_as_float(r[c][2 * e]) - dd[q]) * scale;
-            const float d1 = pv[q + 1] * (__uint_as_float(r[c][2 * e + 1]) - dd[q + 1]) * scale;
-            w[c * 16 + e] = pack_bf16x2(d0, d1);
+            const uint64_t dp2 = f2(__uint_as_float(r[c][2 * e]), __uint_as_float(r[c][2 * e + 1]));
+            const uint64_t ds2 = f2_mul(f2_mul(f2_sub(dp2, f2(dd[q], dd[q + 1])), f2(pv[q], pv[q + 1])), sc2);
+            const float2 d = f2_split(ds2);
+            w[c * 16 + e] = pack_bf16x2(d.x, d.y);
           }
         tmem_st32(t_dp, w);
       }
@@ -469,13 +478,21 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(&sm.s_free[s]);
-        if (kv_valid >= 64) {  // full columns: every second exponential on the FMA pipe
+        if (kv_valid >= 64) {  // full columns: packed scale-and-shift, every second exponential as
+                               // half of a packed polynomial on the FMA pipe
+          const uint64_t sc2 = f2(scale_log2, scale_log2), nl2 = f2(-lse2, -lse2);
 #pragma unroll
           for (int c = 0; c < 2; ++c)
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const float x = fmaf(__uint_as_float(r[c][e]), scale_log2, -lse2);
-              pv[c * 32 + e] = (e & 1) ? ex2_poly(x) : ex2_approx(x);
+            for (int e = 0; e < 32; e += 4) {
+              const float2 xa = f2_split(f2_fma(f2(__uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1])), sc2, nl2));
+              const float2 xb =
+                  f2_split(f2_fma(f2(__uint_as_float(r[c][e + 2]), __uint_as_float(r[c][e + 3])), sc2, nl2));
+              const float2 pp = ex2_poly2(xa.y, xb.y);
+              pv[c * 32 + e] = ex2_approx(xa.x);
+              pv[c * 32 + e + 1] = pp.x;
+              pv[c * 32 + e + 2] = ex2_approx(xb.x);
+              pv[c * 32 + e + 3] = pp.y;
             }
         } else {
 #pragma unroll
@@ -494,14 +511,16 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         tmem_ld32(t_dp, r[0]);
         tmem_ld32(t_dp + 32, r[1]);
         tmem_wait_ld();
+        const uint64_t nd2 = f2(-dval, -dval), sc2 = f2(scale, scale);
         uint32_t w[32];
 #pragma unroll
         for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
+          for (int e = 0; e < 16; ++e) {  // dS = P (dP - D) scale, two columns per packed op
             const int kv = c * 32 + 2 * e;
-            w[c * 16 + e] = pack_bf16x2(pv[kv] * (__uint_as_float(r[c][2 * e]) - dval) * scale,
-                                        pv[kv + 1] * (__uint_as_float(r[c][2 * e + 1]) - dval) * scale);
+            const uint64_t dp2 = f2(__uint_as_float(r[c][2 * e]), __uint_as_float(r[c][2 * e + 1]));
+            const float2 d = f2_split(f2_mul(f2_mul(f2_add(dp2, nd2), f2(pv[kv], pv[kv + 1])), sc2));
+            w[c * 16 + e] = pack_bf16x2(d.x, d.y);
           }
         tmem_st32(t_dp, w);
       }

@@ -305,19 +305,37 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           if (c + 1 < 4) tmem_ld32(s_tmem + (c + 1) * 32, buf[(c + 1) & 1]);
           const uint32_t(&r)[32] = buf[c & 1];
           uint32_t pk[16];
+          if constexpr (!kMasked) {
+            // packed fp32x2 scale-and-shift and row sums; per four columns two exponentials on
+            // MUFU and two as one packed polynomial on the FMA pipe
+            const uint64_t sc2 = f2(scale_log2, scale_log2), nm2 = f2(neg_m, neg_m);
+            uint64_t acc2 = f2(0.f, 0.f);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int col = c * 32 + 2 * i;
-            float x0 = fmaf(__uint_as_float(r[2 * i]), scale_log2, neg_m);
-            float x1 = fmaf(__uint_as_float(r[2 * i + 1]), scale_log2, neg_m);
-            if (kMasked) {
+            for (int i = 0; i < 16; i += 2) {
+              const float2 xa = f2_split(f2_fma(f2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sc2, nm2));
+              const float2 xb =
+                  f2_split(f2_fma(f2(__uint_as_float(r[2 * i + 2]), __uint_as_float(r[2 * i + 3])), sc2, nm2));
+              const float2 pp = ex2_poly2(xa.y, xb.y);
+              const float pa = ex2_approx(xa.x), pb = ex2_approx(xb.x);
+              acc2 = f2_add(acc2, f2_add(f2(pa, pp.x), f2(pb, pp.y)));
+              pk[i] = pack_bf16x2(pa, pp.x);
+              pk[i + 1] = pack_bf16x2(pb, pp.y);
+            }
+            const float2 a2 = f2_split(acc2);
+            rsum[c] += a2.x + a2.y;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int col = c * 32 + 2 * i;
+              float x0 = fmaf(__uint_as_float(r[2 * i]), scale_log2, neg_m);
+              float x1 = fmaf(__uint_as_float(r[2 * i + 1]), scale_log2, neg_m);
               x0 = col < kv_valid ? x0 : -INFINITY;
               x1 = col + 1 < kv_valid ? x1 : -INFINITY;
+              const float p0 = ex2_approx(x0);
+              const float p1 = ex2_approx(x1);
+              rsum[c] += p0 + p1;
+              pk[i] = pack_bf16x2(p0, p1);
             }
-            const float p0 = ex2_approx(x0);
-            const float p1 = !kMasked ? ex2_poly(x1) : ex2_approx(x1);
-            rsum[c] += p0 + p1;
-            pk[i] = pack_bf16x2(p0, p1);
           }
           tmem_st16(s_tmem + c * 16, pk);
         }

@@ -323,6 +323,59 @@ __device__ __forceinline__ float ex2_poly(float x) {
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
+// ---------------------------------------------------------------- packed fp32x2 arithmetic (sm_100)
+// Two fp32 lanes per instruction (fma/add/sub/mul .f32x2, round-to-nearest unless named); each lane
+// rounds exactly as the scalar instruction does.
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 f2_split(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add_rm(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// ex2_poly of two values with the packed instructions: the same reduction and polynomial, lane by lane.
+__device__ __forceinline__ float2 ex2_poly2(float x0, float x1) {
+  const uint64_t C = f2(12582912.f, 12582912.f);
+  const uint64_t X = f2(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+  const uint64_t T = f2_add_rm(X, C);
+  const uint64_t F = f2_sub(X, f2_sub(T, C));
+  uint64_t P = f2_fma(f2(0.07802403f, 0.07802403f), F, f2(0.22606707f, 0.22606707f));
+  P = f2_fma(P, F, f2(0.69583398f, 0.69583398f));
+  P = f2_fma(P, F, f2(0.99992514f, 0.99992514f));
+  const float2 t = f2_split(T), q = f2_split(P);
+  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
+}
+
 // Packs two floats into one bf16x2 word: `lo` in bits [0,16), `hi` in [16,32).
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;

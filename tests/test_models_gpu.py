@@ -76,6 +76,7 @@ def test_mm_only_checkpoint_keeps_kernel_outputs(lora):
     outputs the recomputation reuses; gradients equal the unchecked run's."""
     from torch.utils._python_dispatch import TorchDispatchMode
 
+    import dmad_b200.ops.linear  # noqa: F401  (registers dmad::lora_linear_fwd)
     from dmad_b200.models.wan import WanConfig, WanModel
 
     class Count(TorchDispatchMode):
