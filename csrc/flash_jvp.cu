@@ -335,20 +335,26 @@ flash_jvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       // S columns are already in registers)
       const float neg_m = -m_used;
       float ls = 0.f;
+      {
+        // packed fp32x2 scale-and-shift and row sums (masked columns hold -inf: exp2 gives 0)
+        const uint64_t sc2 = f2(scale_log2, scale_log2), nm2 = f2(neg_m, neg_m);
+        uint64_t acc2 = f2(0.f, 0.f);
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t pk[16];
+        for (int c = 0; c < 2; ++c) {
+          uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int col = c * 32 + 2 * i;
-          const float e0 = ex2_approx(fmaf(pv[col], scale_log2, neg_m));
-          const float e1 = ex2_approx(fmaf(pv[col + 1], scale_log2, neg_m));
-          pv[col] = e0;
-          pv[col + 1] = e1;
-          ls += e0 + e1;
-          pk[i] = pack_bf16x2(e0, e1);
+          for (int i = 0; i < 16; ++i) {
+            const int col = c * 32 + 2 * i;
+            const float2 x = f2_split(f2_fma(f2(pv[col], pv[col + 1]), sc2, nm2));
+            pv[col] = ex2_approx(x.x);
+            pv[col + 1] = ex2_approx(x.y);
+            acc2 = f2_add(acc2, f2(pv[col], pv[col + 1]));
+            pk[i] = pack_bf16x2(pv[col], pv[col + 1]);
+          }
+          tmem_st16(s_t + c * 16, pk);
         }
-        tmem_st16(s_t + c * 16, pk);
+        const float2 a2 = f2_split(acc2);
+        ls = a2.x + a2.y;
       }
       l_sum = l_sum * alpha + ls;
       tmem_wait_st();
@@ -365,18 +371,25 @@ flash_jvp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         tmem_ld32(ts_t, tr[0]);
         tmem_ld32(ts_t + 32, tr[1]);
         tmem_wait_ld();
+        const uint64_t sc2 = f2(scale, scale);
+        uint64_t acc2 = f2(0.f, 0.f);
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float x0 = pv[c * 32 + 2 * i] * __uint_as_float(tr[c][2 * i]) * scale;
-            const float x1 = pv[c * 32 + 2 * i + 1] * __uint_as_float(tr[c][2 * i + 1]) * scale;
-            rs += x0 + x1;
-            pk[i] = pack_bf16x2(x0, x1);
+          for (int i = 0; i < 16; ++i) {  // P * tS * scale, two columns per packed op
+            const int col = c * 32 + 2 * i;
+            const uint64_t x2 = f2_mul(f2_mul(f2(pv[col], pv[col + 1]),
+                                              f2(__uint_as_float(tr[c][2 * i]), __uint_as_float(tr[c][2 * i + 1]))),
+                                       sc2);
+            acc2 = f2_add(acc2, x2);
+            const float2 x = f2_split(x2);
+            pk[i] = pack_bf16x2(x.x, x.y);
           }
           tmem_st16(ts_t + c * 16, pk);
         }
+        const float2 a2 = f2_split(acc2);
+        rs = a2.x + a2.y;
       }
       r_sum = r_sum * alpha + rs;
       tmem_wait_st();
