@@ -135,7 +135,7 @@ def _gelu_grad(x):
     return 0.5 * (1 + th) + 0.5 * x * (1 - th * th) * k0 * (1 + 3 * 0.044715 * x2)
 
 
-def block_jvp(blk, x, tx, e0, te0, context, cos, sin, B, L, rpg, cp=None):
+def block_jvp(blk, x, tx, e0, te0, context, cos, sin, B, L, rpg, cp=None, attn_meta=None):
     cfg = blk.cfg
     D, H = cfg.dim, cfg.num_heads
     hd = D // H
@@ -148,7 +148,13 @@ def block_jvp(blk, x, tx, e0, te0, context, cos, sin, B, L, rpg, cp=None):
     q, tq = ops.rope_apply(q, cos, sin, hd), ops.rope_apply(tq, cos, sin, hd)
     k, tk = ops.rope_apply(k, cos, sin, hd), ops.rope_apply(tk, cos, sin, hd)
     v, tv = qkv[:, 2 * D:], tqkv[:, 2 * D:]
-    if cp is not None and cp.world > 1 and cp.impl == "ring":
+    if attn_meta is not None and attn_meta.mode != "none":
+        from ..ops.block_attention import block_attention_jvp
+        shp = (B, L, H, hd)
+        a, ta = block_attention_jvp(q.reshape(shp), k.reshape(shp), v.reshape(shp), tq.reshape(shp), tk.reshape(shp),
+                                    tv.reshape(shp), attn_meta)
+        a, ta = a.reshape(B * L, D), ta.reshape(B * L, D)
+    elif cp is not None and cp.world > 1 and cp.impl == "ring":
         from ..parallel.cp import ring_attention_jvp
         a, ta = ring_attention_jvp(q, k, v, tq, tk, tv, B, H, cp)
     elif cp is not None and cp.world > 1:
@@ -211,9 +217,12 @@ def time_embed_jvp(model, t, tt):
 
 
 @torch.no_grad()
-def wan_forward_jvp(model, x, tx, timesteps, t_timesteps, crossattn_emb):
-    """(out, t_out) [B, 16, T, H, W] fp32 of ``model`` at (x, timesteps) along (tx, t_timesteps)."""
+def wan_forward_jvp(model, x, tx, timesteps, t_timesteps, crossattn_emb, attn_meta=None):
+    """(out, t_out) [B, 16, T, H, W] fp32 of ``model`` at (x, timesteps) along (tx, t_timesteps);
+    ``attn_meta`` (an ``AttnMaskSpec``) masks the self-attention block-wise (causal modes)."""
     cfg = model.cfg
+    if attn_meta is not None and attn_meta.mode != "none" and model.cp is not None and model.cp.world > 1:
+        raise NotImplementedError("block masks run without context parallelism")
     cp0 = model.cp if (model.cp is not None and model.cp.world > 1) else None
     if cp0 is not None and cp0.broadcast_inputs:  # rank 0's sample for the whole CP group
         x, tx, crossattn_emb = cp0.broadcast(x), cp0.broadcast(tx), cp0.broadcast(crossattn_emb)
@@ -246,7 +255,7 @@ def wan_forward_jvp(model, x, tx, timesteps, t_timesteps, crossattn_emb):
     e, e0, te, te0 = time_embed_jvp(model, timesteps.reshape(-1).float(), t_timesteps.reshape(-1).float())
     context = model.text_embed(crossattn_emb)
     for blk in model.blocks:
-        h, th = block_jvp(blk, h, th, e0, te0, context, cos, sin, B, Ll, rpg, cp)
+        h, th = block_jvp(blk, h, th, e0, te0, context, cos, sin, B, Ll, rpg, cp, attn_meta)
     m = model.head.modulation.float()[0]
     ho, tho = ln_mod_jvp(h, th, m[1][None] + e, te, m[0][None] + e, te, rpg, cfg.eps)
     hw = model.head.head

@@ -255,3 +255,64 @@ def block_attention(q, k, v, spec: AttnMaskSpec | None = None, scale: float | No
     if not q.is_cuda:
         return _attn_cpu(q, k, v, blocks, scale)
     return _BlockAttn.apply(q, k, v, blocks, scale)
+
+
+# ----------------------------------------------------------------------------- JVP under a block mask
+
+
+def _jvp_cpu(q, k, v, tq, tk, tv, blocks, scale):
+    ct = torch.promote_types(q.dtype, torch.float32)
+    O = torch.zeros(q.shape, dtype=ct, device=q.device)
+    tO = torch.zeros(q.shape, dtype=ct, device=q.device)
+    hv = lambda t: t.to(ct).transpose(1, 2)  # noqa: E731
+    for q0, q1, rng in blocks:
+        cat = lambda t: hv(torch.cat([t[:, a:b] for a, b in rng], dim=1))  # noqa: E731
+        kk, vv = cat(k), cat(v)
+        qq, tqq = hv(q[:, q0:q1]), hv(tq[:, q0:q1])
+        s = qq @ kk.transpose(-1, -2) * scale
+        ts = tqq @ kk.transpose(-1, -2)
+        if tk is not None:
+            ts = ts + qq @ cat(tk).transpose(-1, -2)
+        p = torch.softmax(s, -1)
+        pts = p * (ts * scale)
+        o = p @ vv
+        to = pts @ vv - pts.sum(-1, keepdim=True) * o
+        if tv is not None:
+            to = to + p @ cat(tv)
+        O[:, q0:q1] = o.transpose(1, 2)
+        tO[:, q0:q1] = to.transpose(1, 2)
+    return O.to(q.dtype), tO.to(q.dtype)
+
+
+@torch.no_grad()
+def block_attention_jvp(q, k, v, tq, tk=None, tv=None, spec: AttnMaskSpec | None = None, scale: float | None = None):
+    """(O, tO): attention under a block mask and its forward-mode derivative along (tq, tk, tv) (None =
+    zero tangent), [B, L, H, D].  Forward only; on CUDA one tcgen05 JVP launch per key range with the
+    ranges merged by (LSE, mu = rowsum(P * tS) / l) in the epilogue (``flash_jvp_accumulate``).
+    Parity: the reference's masked Triton JVP (flash_attention_jvp_triton.py:235-409)."""
+    spec = spec or AttnMaskSpec()
+    scale = float(scale) if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    blocks = mask_ranges(spec, q.shape[1], k.shape[1])
+    if not q.is_cuda:
+        return _jvp_cpu(q, k, v, tq, tk, tv, blocks, scale)
+    e = ext()
+    B, Q, H, D = q.shape
+    q, tq = q.contiguous(), tq.contiguous()
+    o, to = torch.zeros_like(q), torch.zeros_like(q)
+    no_lse = torch.empty(0, dtype=torch.float32, device=q.device)
+    sl = lambda t, a, b: t[:, a:b].contiguous() if t is not None else None  # noqa: E731
+    for q0, q1, rng in blocks:
+        qs, tqs, os_, tos = q[:, q0:q1], tq[:, q0:q1], o[:, q0:q1], to[:, q0:q1]
+        if len(rng) == 1:
+            a, b = rng[0]
+            e.flash_jvp_fwd(qs, k[:, a:b], v[:, a:b], tqs, sl(tk, a, b), sl(tv, a, b), os_, tos, no_lse, scale)
+            continue
+        n = q1 - q0
+        acc_o = torch.empty((B, n, H, D), dtype=torch.float32, device=q.device)
+        acc_u = torch.empty_like(acc_o)
+        acc_lse = torch.empty((B, H, _lse_pad(n)), dtype=torch.float32, device=q.device)
+        acc_mu = torch.empty_like(acc_lse)
+        for j, (a, b) in enumerate(rng):
+            e.flash_jvp_accumulate(qs, k[:, a:b], v[:, a:b], tqs, sl(tk, a, b), sl(tv, a, b), os_, tos, no_lse,
+                                   acc_o, acc_u, acc_lse, acc_mu, j > 0, j == len(rng) - 1, scale)
+    return o, to

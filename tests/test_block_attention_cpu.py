@@ -66,3 +66,56 @@ def test_block_attention_matches_masked_dense(mode):
     gr = torch.autograd.grad(ref, (q, k, v), g)
     for a, b in zip(gb, gr):
         torch.testing.assert_close(a, b)
+
+
+@pytest.mark.parametrize("mode", ["block_causal", "teacher_forcing"])
+def test_block_attention_jvp_matches_autodiff(mode):
+    """The masked JVP (per query block over its key ranges) equals torch.func.jvp of the masked
+    dense attention."""
+    from dmad_b200.ops.block_attention import block_attention_jvp
+
+    torch.manual_seed(1)
+    pat = BlockPattern(frame_tokens=4, first_chunk_frames=1, chunk_frames=2)
+    if mode == "teacher_forcing":
+        spec = AttnMaskSpec(mode, pat, local_attn_blocks=2, sink_blocks=1, clean_blocks=3)
+        Q = KV = 2 * pat.blocks_to_tokens(3)
+    else:
+        spec = AttnMaskSpec(mode, pat, local_attn_blocks=2, sink_blocks=1)
+        Q = KV = pat.blocks_to_tokens(4)
+    q, tq = torch.randn(1, Q, 2, 16, dtype=torch.float64), torch.randn(1, Q, 2, 16, dtype=torch.float64)
+    k, tk = torch.randn(1, KV, 2, 16, dtype=torch.float64), torch.randn(1, KV, 2, 16, dtype=torch.float64)
+    v, tv = torch.randn(1, KV, 2, 16, dtype=torch.float64), torch.randn(1, KV, 2, 16, dtype=torch.float64)
+    m = dense_mask(spec, Q, KV)
+
+    def f(q_, k_, v_):
+        s = torch.einsum("bqhd,bkhd->bhqk", q_, k_) / math.sqrt(16)
+        p = torch.nan_to_num(torch.softmax(s.masked_fill(~m, float("-inf")), -1))
+        return torch.einsum("bhqk,bkhd->bqhd", p, v_)
+
+    ro, rto = torch.func.jvp(f, (q, k, v), (tq, tk, tv))
+    o, to = block_attention_jvp(q, k, v, tq, tk, tv, spec)
+    torch.testing.assert_close(o, ro)
+    torch.testing.assert_close(to, rto)
+
+
+def test_wan_forward_jvp_with_block_mask_matches_autodiff():
+    from dmad_b200.models.wan import WanConfig, WanModel
+    from dmad_b200.models.wan_jvp import wan_forward_jvp
+
+    torch.manual_seed(0)
+    m = WanModel(WanConfig(dim=128, ffn_dim=256, num_heads=2, num_layers=2, text_dim=32, freq_dim=64)).double()
+    torch.nn.init.normal_(m.head.head.weight, std=0.05)
+    g = torch.Generator().manual_seed(2)
+    x, tx = torch.randn(1, 16, 3, 4, 8, generator=g).double(), torch.randn(1, 16, 3, 4, 8, generator=g).double()
+    t, tt = torch.rand(1, 1, generator=g).double(), torch.rand(1, 1, generator=g).double()
+    ctx = torch.randn(1, 6, 32, generator=g).double()
+    spec = AttnMaskSpec("block_causal", BlockPattern(frame_tokens=8, first_chunk_frames=1, chunk_frames=1))
+    out, tout = wan_forward_jvp(m, x, tx, t, tt, ctx, attn_meta=spec)
+    with torch.no_grad():
+        ref = m(x, t, ctx, attn_meta=spec)
+        eps = 1e-3  # central differences of the (fp32) network output
+        fd = (m(x + eps * tx, t + eps * tt, ctx, attn_meta=spec).double() -
+              m(x - eps * tx, t - eps * tt, ctx, attn_meta=spec).double()) / (2 * eps)
+    torch.testing.assert_close(out.double(), ref.double(), rtol=1e-5, atol=1e-6)  # parts of the JVP path run in fp32
+    rel = ((tout.double() - fd).norm() / fd.norm()).item()
+    assert rel < 1e-3, rel

@@ -42,3 +42,35 @@ def test_block_attention_cuda(mode, local, sink, qbo):
     for a, b, name in ((q.grad, qr.grad, "dq"), (k.grad, kr.grad, "dk"), (v.grad, vr.grad, "dv")):
         rel = ((a.float() - b).norm() / b.norm()).item()
         assert rel < 2e-2, (name, rel)
+
+
+@pytest.mark.parametrize("mode", ["block_causal", "teacher_forcing"])
+def test_block_attention_jvp_cuda(mode):
+    """Masked JVP on the tcgen05 JVP kernel (accumulated over key ranges) against fp32 torch.func.jvp of
+    masked dense attention."""
+    from dmad_b200 import ops
+    from dmad_b200.ops.block_attention import AttnMaskSpec, BlockPattern, block_attention_jvp, dense_mask
+
+    pat = BlockPattern(frame_tokens=96, first_chunk_frames=1, chunk_frames=2)
+    if mode == "teacher_forcing":
+        spec = AttnMaskSpec(mode, pat, 2, 1, 0, clean_blocks=3)
+        Q = KV = 2 * pat.blocks_to_tokens(3)
+    else:
+        spec = AttnMaskSpec(mode, pat, 2, 1)
+        Q = KV = pat.blocks_to_tokens(4)
+    torch.manual_seed(1)
+    mk = lambda n, s=1.0: (torch.randn(1, n, 2, 128, device="cuda") * s).to(torch.bfloat16)  # noqa: E731
+    q, k, v, tq, tk, tv = mk(Q), mk(KV), mk(KV), mk(Q, 0.5), mk(KV, 0.5), mk(KV, 0.5)
+    o, to = block_attention_jvp(q, k, v, tq, tk, tv, spec)
+    torch.cuda.synchronize()
+    ops.check_device_status()
+    m = dense_mask(spec, Q, KV, device="cuda")
+
+    def f(q_, k_, v_):
+        s = torch.einsum("bqhd,bkhd->bhqk", q_, k_) / math.sqrt(128)
+        p = torch.nan_to_num(torch.softmax(s.masked_fill(~m, float("-inf")), -1))
+        return torch.einsum("bhqk,bkhd->bqhd", p, v_)
+
+    ro, rto = torch.func.jvp(f, (q.float(), k.float(), v.float()), (tq.float(), tk.float(), tv.float()))
+    assert (o.float() - ro).abs().max().item() < 3e-2
+    assert ((to.float() - rto).norm() / rto.norm()).item() < 2e-2
