@@ -48,7 +48,8 @@ def parse():
     ap.add_argument("--count-launches", type=int, default=1)
     ap.add_argument("--profile", default=None, help="write a per-kernel time table of one cycle to this path")
     ap.add_argument("--cp", type=int, default=1, help="context-parallel group size (config 3: 8)")
-    ap.add_argument("--cp-impl", default="fused", choices=["fused", "nccl", "ring"])
+    ap.add_argument("--cp-impl", default="fused", choices=["fused", "nccl", "ring", "hybrid"])
+    ap.add_argument("--ulysses-size", type=int, default=None, help="hybrid CP: ranks per Ulysses group")
     ap.add_argument("--lora", type=int, default=0, help="LoRA rank of the student (config 3: 128)")
     ap.add_argument("--dp-optimizer", default="sharded", choices=["sharded", "replicated"],
                     help="sharded: fused reduce-scatter/AdamW/all-gather kernel; replicated: NCCL all-reduce baseline")
@@ -175,9 +176,10 @@ def main():
             cfg.checkpoint_student_blocks = cfg.net.num_layers
         trainer = WanDMAD(cfg, device=device, dtype=torch.bfloat16, seed=0)
         if args.cp > 1:
-            from dmad_b200.parallel.cp import ContextParallel
+            from dmad_b200.parallel.cp import make_context_parallel
             from dmad_b200.train.trainer import make_cp_group
-            cpc = ContextParallel(make_cp_group(args.cp), impl=args.cp_impl, device=device)
+            cpc = make_context_parallel(make_cp_group(args.cp), impl=args.cp_impl, device=device,
+                                        ulysses_size=args.ulysses_size)
             for net in trainer.context_parallel_nets():
                 net.enable_context_parallel(cpc)
 

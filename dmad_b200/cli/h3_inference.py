@@ -54,7 +54,10 @@ def parse_args(argv=None):
     p.add_argument("--vae-dtype", default="bf16", choices=["bf16", "fp32"], help="accepted for flag compatibility")
     p.add_argument("--cp", action="store_true", help="context parallel over all ranks (launch with torchrun): "
                    "every rank holds a slice of the packed sequence")
-    p.add_argument("--cp-impl", default="fused", choices=["fused", "nccl"])
+    p.add_argument("--cp-impl", default="fused", choices=["fused", "nccl", "hybrid"],
+                   help="hybrid: Ulysses inside groups of --ulysses-size ranks, ring attention across them "
+                        "(for head counts the CP size does not divide)")
+    p.add_argument("--ulysses-size", type=int, default=None)
     return p.parse_args(argv)
 
 
@@ -68,10 +71,10 @@ def main(argv=None):
         args.low_vram = "auto"
     cp = None
     if args.cp:
-        from ..parallel.cp import ContextParallel
+        from ..parallel.cp import make_context_parallel
         from ..parallel.dist import init_distributed
         _, _, device = init_distributed()
-        cp = ContextParallel(impl=args.cp_impl, device=device)
+        cp = make_context_parallel(impl=args.cp_impl, device=device, ulysses_size=args.ulysses_size)
     else:
         device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else \
             torch.device("cpu")

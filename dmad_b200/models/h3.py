@@ -100,6 +100,9 @@ class _H3Attention(nn.Module):
             q = ops.rope(q, cos, sin, hd)
             k = ops.rope(k, cos, sin, hd)
         v = qkv[:, 2 * D:]
+        if cp is not None and cp.world > 1 and cp.impl == "hybrid":
+            from ..parallel.cp import hybrid_attention_fwd
+            return getattr(self.to_out, "0")(hybrid_attention_fwd(q, k, v, 1, H, cp, L_valid))
         if cp is not None and cp.world > 1:
             # per-head q/k norms and RoPE are row-local, so they run before the head exchange
             g = cp.seq_to_head(torch.cat([q, k, v], dim=1), 1, 3, H, hd)       # [1, Lp, 3, H/cp, hd]

@@ -146,8 +146,8 @@ class WanBlock(nn.Module):
         if attn_ctx is not None:
             a = self._masked_self_attention(qkv, cos, sin, B, L, attn_ctx)
         elif cp is not None and cp.world > 1:
-            from ..parallel.cp import ring_self_attention, self_attention_cp
-            attn = ring_self_attention if cp.impl == "ring" else self_attention_cp
+            from ..parallel.cp import hybrid_self_attention, ring_self_attention, self_attention_cp
+            attn = {"ring": ring_self_attention, "hybrid": hybrid_self_attention}.get(cp.impl, self_attention_cp)
             a = attn(qkv, self.self_attn.norm_q.weight, self.self_attn.norm_k.weight, cos, sin, B, H, cfg.eps, cp)
         else:
             a = self_attention_core(qkv, self.self_attn.norm_q.weight, self.self_attn.norm_k.weight, cos, sin, B, L,

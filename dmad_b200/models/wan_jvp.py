@@ -154,6 +154,9 @@ def block_jvp(blk, x, tx, e0, te0, context, cos, sin, B, L, rpg, cp=None, attn_m
         a, ta = block_attention_jvp(q.reshape(shp), k.reshape(shp), v.reshape(shp), tq.reshape(shp), tk.reshape(shp),
                                     tv.reshape(shp), attn_meta)
         a, ta = a.reshape(B * L, D), ta.reshape(B * L, D)
+    elif cp is not None and cp.world > 1 and cp.impl == "hybrid":
+        from ..parallel.cp import hybrid_attention_jvp
+        a, ta = hybrid_attention_jvp(q, k, v, tq, tk, tv, B, H, cp)
     elif cp is not None and cp.world > 1 and cp.impl == "ring":
         from ..parallel.cp import ring_attention_jvp
         a, ta = ring_attention_jvp(q, k, v, tq, tk, tv, B, H, cp)

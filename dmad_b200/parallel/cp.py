@@ -180,6 +180,25 @@ class _GatherSeq(torch.autograd.Function):
         return g.narrow(ctx.dim, cp.rank * ll, ll).contiguous(), None, None
 
 
+class _GatherSum(torch.autograd.Function):
+    """All-gather along ``dim`` whose consumers differ per rank (attention over gathered keys): the
+    backward sums every rank's gradient of a slice and returns this rank's slice (reduce-scatter)."""
+
+    @staticmethod
+    def forward(ctx, x, dim, cp):
+        parts = [torch.empty_like(x) for _ in range(cp.world)]
+        dist.all_gather(parts, x.contiguous(), group=cp.group)
+        ctx.cfg = (dim, cp, x.shape[dim])
+        return torch.cat(parts, dim=dim)
+
+    @staticmethod
+    def backward(ctx, g):
+        dim, cp, n = ctx.cfg
+        g = g.contiguous()
+        dist.all_reduce(g, group=cp.group)
+        return g.narrow(dim, cp.rank * n, n).contiguous(), None, None
+
+
 class _Broadcast(torch.autograd.Function):
     @staticmethod
     def forward(ctx, t, src_in_group, cp):
@@ -490,7 +509,7 @@ def _ring_cpu(qkv, wq, wk, cos, sin, B, H, eps, cp):
     k = norm_ops.rope_reference(norm_ops.ln_mod_reference(qkv[:, D:2 * D], wk.reshape(1, -1), None, 0.0, None, None,
                                                           eps, True), cos, sin, hd)
     kv = torch.cat([k, qkv[:, 2 * D:]], dim=1)
-    blocks = _GatherSeq.apply(kv.view(1, R, 2 * D), 1, cp).view(cp.world, R, 2 * D)
+    blocks = _GatherSum.apply(kv.view(1, R, 2 * D), 1, cp).view(cp.world, R, 2 * D)
     qf = q.float().view(B, Ll, H, hd).transpose(1, 2)
     acc, lse = None, None
     for j in range(cp.world):
@@ -593,3 +612,242 @@ def _ring_jvp_cpu(q, k, v, tq, tk, tv, B, H, cp):
     tO = U - mu * O
     back = lambda t: t.transpose(1, 2).reshape(R, D).to(q.dtype)  # noqa: E731
     return back(O), back(tO)
+
+
+# ---------------------------------------------------------------------- hybrid: Ulysses inside, ring across
+# For head counts the CP size does not divide (H3's 40 heads at cp = 16, for instance) the group of
+# cp = u * r ranks is split into r Ulysses groups of u consecutive ranks and u ring groups of r ranks
+# with the same position.  A Ulysses group exchanges heads for sequence inside itself, so each rank
+# holds its group's whole span of L / r tokens for H / u heads; the ring then visits the spans of the
+# other groups for the same heads (key/value blocks through the copy engine, LSE merge in the flash
+# epilogue), and the Ulysses exchange runs back.  Parity: the reference has Ulysses only
+# (train/wan/rcm/utils/a2a_cp.py); the hybrid is this build's extension of it.
+
+class HybridContextParallel:
+    """``ContextParallel``-compatible group of ``u * r`` ranks: ``.ulysses`` (u consecutive ranks) and
+    ``.ring`` (r ranks with the same Ulysses position), each a ``ContextParallel``."""
+
+    impl = "hybrid"
+
+    def __init__(self, group=None, ulysses_size: int = 2, device=None, timeout_s: float = 120.0,
+                 ulysses_impl: str = "fused", broadcast_inputs: bool = True):
+        self.full = ContextParallel(group, impl="nccl", device=device, timeout_s=timeout_s,
+                                    broadcast_inputs=broadcast_inputs)
+        self.group, self.world, self.rank = self.full.group, self.full.world, self.full.rank
+        self.device, self.broadcast_inputs, self.timeout_s = self.full.device, broadcast_inputs, timeout_s
+        u = int(ulysses_size)
+        if u < 1 or self.world % u:
+            raise ValueError(f"ulysses_size {u} must divide the CP size {self.world}")
+        ranks = dist.get_process_group_ranks(self.group) if self.group is not None else list(range(self.world))
+        r = self.world // u
+        # only the members of a sub-group create it (so CP groups of different data-parallel replicas
+        # need not make the same calls)
+        i, j = self.rank // u, self.rank % u
+        mine_u = dist.new_group(ranks[i * u:(i + 1) * u], use_local_synchronization=True)
+        mine_r = dist.new_group(ranks[j::u], use_local_synchronization=True)
+        self.ulysses = ContextParallel(mine_u, impl=ulysses_impl, device=device, timeout_s=timeout_s,
+                                       broadcast_inputs=False)
+        self.ring = ContextParallel(mine_r, impl="ring", device=device, timeout_s=timeout_s, broadcast_inputs=False)
+        self.u, self.r = u, r
+
+    # whole-group helpers (token sharding, broadcasts, reductions) delegate to the full group
+    def split(self, x, dim=1):
+        return self.full.split(x, dim)
+
+    def gather(self, x, dim=1):
+        return self.full.gather(x, dim)
+
+    def all_reduce_sum(self, t):
+        return self.full.all_reduce_sum(t)
+
+    def broadcast(self, t, src_rank_in_group: int = 0):
+        return self.full.broadcast(t, src_rank_in_group)
+
+
+def _ring_core_fwd(q, kv_rows, cp: ContextParallel, valid: int | None = None):
+    """q [B, Lr, Hl, hd]; kv_rows [2, B*Lr, Hl*hd] (k, v of this rank's span) -> (o, lse) over the spans
+    of every rank of the ring group; ``valid`` (B = 1) = the global number of real keys, so the padded
+    tail of the last spans is left out."""
+    from .. import ops
+    from ..ops import attention as attn_ops
+
+    e = ops.ext()
+    B, Lr, Hl, hd = q.shape
+    R, D = B * Lr, Hl * hd
+    scale = 1.0 / math.sqrt(hd)
+    slot, ptrs = cp.slot(2 * R * D)
+    own = slot.view(2, R, D)
+    own.copy_(kv_rows)
+    cp.sync()
+    o = torch.empty((B, Lr, Hl, hd), dtype=q.dtype, device=q.device)
+    lse = torch.empty((B, Hl, attn_ops._lse_pad(Lr)), dtype=torch.float32, device=q.device)
+    acc_o = torch.empty((B, Lr, Hl, hd), dtype=torch.float32, device=q.device)
+    acc_lse = torch.empty_like(lse)
+    bufs = cp.ring_buffers(2 * R * D)
+    shp = (B, Lr, Hl, hd)
+    nkeys = [Lr if valid is None else max(0, min(Lr, valid - ((cp.rank + j) % cp.world) * Lr))
+             for j in range(cp.world)]
+    last = max((j for j in range(cp.world) if nkeys[j] > 0), default=-1)
+    first = min((j for j in range(cp.world) if nkeys[j] > 0), default=-1)
+
+    def visit(j, src, kv):
+        n = nkeys[j]
+        if n == 0:
+            return
+        blk = own if kv is None else kv[:2 * R * D].view(2, R, D)
+        e.flash_fwd_accumulate(q, blk[0].view(shp)[:, :n], blk[1].view(shp)[:, :n], o, lse, acc_o, acc_lse,
+                               j > first, j == last, scale)
+
+    _ring_blocks(cp, ptrs, 2 * R * D * 2, cp.ring_stream, bufs, visit)
+    cp.sync()
+    if last < 0:
+        o.zero_()
+    return o, lse
+
+
+def _ring_core_bwd(q, kv_rows, o, lse, do, cp: ContextParallel):
+    """(dq [B, Lr, Hl, hd], dkv [2, B*Lr, Hl*hd]) of the ring attention of ``_ring_core_fwd``."""
+    from .. import ops
+    from ..ops import attention as attn_ops
+
+    e = ops.ext()
+    B, Lr, Hl, hd = q.shape
+    R, D = B * Lr, Hl * hd
+    scale = 1.0 / math.sqrt(hd)
+    shp = (B, Lr, Hl, hd)
+    slot, ptrs = cp.slot(2 * R * D)
+    own = slot.view(2, R, D)
+    own.copy_(kv_rows)
+    part, pptrs = cp.slot(cp.world * 2 * R * D)
+    cp.sync()
+    dq_acc = torch.zeros((B, Lr, Hl, hd), dtype=torch.float32, device=q.device)
+    dq = torch.empty(shp, dtype=q.dtype, device=q.device)
+    dkv = torch.empty((2, R, D), dtype=q.dtype, device=q.device)
+    dd = torch.empty_like(lse)
+    bufs = cp.ring_buffers(2 * R * D)
+    part_v = part.view(cp.world, 2, R, D)
+
+    def visit(j, src, kv):
+        blk = own if kv is None else kv[:2 * R * D].view(2, R, D)
+        attn_ops.flash_bwd_into(q, blk[0].view(shp), blk[1].view(shp), o, do, lse, dq, dkv[0].view(shp),
+                                dkv[1].view(shp), dd, scale)
+        dq_acc.add_(dq.float())
+        if src == cp.rank:
+            part_v[cp.rank].copy_(dkv)
+        else:
+            e.peer_copy_to(pptrs[src] + cp.rank * 2 * R * D * 2, dkv, 2 * R * D * 2)
+
+    _ring_blocks(cp, ptrs, 2 * R * D * 2, cp.ring_stream, bufs, visit)
+    cp.sync()
+    return dq_acc.to(q.dtype), part_v.float().sum(0).to(q.dtype)
+
+
+class _HybridSelfAttn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, wq, wk, cos, sin, B, H, eps, hcp):
+        from ..ops import norm as norm_ops
+
+        R, D3 = qkv.shape
+        D = D3 // 3
+        hd = D // H
+        u = hcp.ulysses
+        qk, rq, rk = norm_ops.qk_norm_rope(qkv, wq, wk, cos, sin, D, hd, eps)
+        g = u.seq_to_head(torch.cat([qk, qkv[:, 2 * D:]], dim=1), B, 3, H, hd)  # [B, Lr, 3, Hl, hd]
+        q_h = g[:, :, 0].contiguous()
+        kv_rows = g[:, :, 1:].permute(2, 0, 1, 3, 4).reshape(2, -1, (H // u.world) * hd)
+        o_h, lse = _ring_core_fwd(q_h, kv_rows, hcp.ring)
+        out = u.head_to_seq(o_h.unsqueeze(2), B).clone()
+        ctx.save_for_backward(qkv, wq, wk, cos, sin, rq, rk, q_h, kv_rows, o_h, lse)
+        ctx.cfg = (B, H, eps, hcp)
+        return out
+
+    @staticmethod
+    def backward(ctx, do):
+        from .. import ops
+
+        qkv, wq, wk, cos, sin, rq, rk, q_h, kv_rows, o_h, lse = ctx.saved_tensors
+        B, H, eps, hcp = ctx.cfg
+        u = hcp.ulysses
+        R, D3 = qkv.shape
+        D = D3 // 3
+        hd = D // H
+        do_h = u.seq_to_head(do.contiguous(), B, 1, H, hd)[:, :, 0].contiguous()
+        dq_h, dkv = _ring_core_bwd(q_h, kv_rows, o_h, lse, do_h, hcp.ring)
+        Bq, Lr, Hl, _ = q_h.shape
+        grads = torch.stack([dq_h, dkv[0].view(Bq, Lr, Hl, hd), dkv[1].view(Bq, Lr, Hl, hd)], dim=2)
+        back = u.head_to_seq(grads, B)  # [R, 3D]: dq | dk | dv rows
+        dqkv = torch.empty_like(qkv)
+        dqkv[:, 2 * D:].copy_(back[:, 2 * D:])
+        dwq = torch.zeros(D, dtype=torch.float32, device=qkv.device)
+        dwk = torch.zeros(D, dtype=torch.float32, device=qkv.device)
+        dqk = back[:, :2 * D].contiguous()
+        ops.ext().qk_norm_rope_bwd(dqk[:, :D], dqk[:, D:], qkv, dqkv, wq, wk, cos, sin, rq, rk, dwq, dwk, D, hd)
+        return dqkv, dwq, dwk, None, None, None, None, None, None
+
+
+def _hybrid_cpu(qkv, wq, wk, cos, sin, B, H, eps, hcp):
+    """fp32 restatement on gloo ranks: Ulysses exchange (NCCL-style all-to-all), all-gather of the ring
+    group's keys / values, attention, exchange back (differentiable end to end)."""
+    from ..ops import attention as attn_ops
+    from ..ops import norm as norm_ops
+
+    R, D3 = qkv.shape
+    D = D3 // 3
+    hd = D // H
+    q, k = norm_ops.qk_norm_rope_reference(qkv, wq, wk, cos, sin, D, hd, eps)
+    u = hcp.ulysses
+    g = _A2ASeqToHead.apply(torch.cat([q, k, qkv[:, 2 * D:]], dim=1), B, 3, H, hd, u)  # [B, Lr, 3, Hl, hd]
+    kv = _GatherSum.apply(g[:, :, 1:].contiguous(), 1, hcp.ring)  # [B, L, 2, Hl, hd]
+    o = attn_ops.attention_reference(g[:, :, 0], kv[:, :, 0], kv[:, :, 1])
+    return _A2AHeadToSeq.apply(o.unsqueeze(2).contiguous(), B, 1, H, u)
+
+
+def hybrid_self_attention(qkv, wq, wk, cos, sin, B, H, eps, hcp: HybridContextParallel):
+    if not qkv.is_cuda:
+        return _hybrid_cpu(qkv, wq, wk, cos, sin, B, H, eps, hcp)
+    return _HybridSelfAttn.apply(qkv, wq.float().contiguous(), wk.float().contiguous(), cos, sin, B, H, eps, hcp)
+
+
+@torch.no_grad()
+def hybrid_attention_fwd(q, k, v, B: int, H: int, hcp: HybridContextParallel, valid: int | None = None):
+    """Forward-only hybrid attention of normalised / rotated rows ([B*Ll, D] each) -> [B*Ll, D];
+    ``valid`` leaves the padded tail of the global sequence out of every softmax (B = 1)."""
+    from ..ops import attention as attn_ops
+
+    R, D = q.shape
+    hd = D // H
+    u = hcp.ulysses
+    g = u.seq_to_head(torch.cat([q, k, v], dim=1), B, 3, H, hd)  # [B, Lr, 3, Hl, hd]
+    if not q.is_cuda:
+        kv = hcp.ring.gather(g[:, :, 1:].contiguous(), dim=1)
+        n = kv.shape[1] if valid is None else valid
+        o = attn_ops.attention_reference(g[:, :, 0], kv[:, :n, 0], kv[:, :n, 1])
+        return u.head_to_seq(o.unsqueeze(2).contiguous(), B)
+    q_h = g[:, :, 0].contiguous()
+    kv_rows = g[:, :, 1:].permute(2, 0, 1, 3, 4).reshape(2, -1, (H // u.world) * hd)
+    o_h, _ = _ring_core_fwd(q_h, kv_rows, hcp.ring, valid)
+    return u.head_to_seq(o_h.unsqueeze(2), B).clone()
+
+
+@torch.no_grad()
+def hybrid_attention_jvp(q, k, v, tq, tk, tv, B: int, H: int, hcp: HybridContextParallel):
+    """(O, tO) rows of the hybrid attention (Ulysses exchange of the six tensors, ring JVP, exchange back)."""
+    R, D = q.shape
+    hd = D // H
+    u = hcp.ulysses
+    Hl = H // u.world
+    g = u.seq_to_head(torch.cat([q, k, v, tq, tk, tv], dim=1), B, 6, H, hd)  # [B, Lr, 6, Hl, hd]
+    rows = [g[:, :, i].reshape(-1, Hl * hd).contiguous() for i in range(6)]
+    o, to = ring_attention_jvp(*rows, B, Hl, hcp.ring)
+    Lr = rows[0].shape[0] // B
+    back = u.head_to_seq(torch.stack([o.view(B, Lr, Hl, hd), to.view(B, Lr, Hl, hd)], dim=2).contiguous(), B)
+    return back[:, :D].clone(), back[:, D:].clone()
+
+
+def make_context_parallel(group=None, impl: str = "fused", device=None, ulysses_size: int | None = None,
+                          timeout_s: float = 120.0):
+    """``ContextParallel`` (impl fused / nccl / ring) or ``HybridContextParallel`` (impl "hybrid":
+    Ulysses groups of ``ulysses_size`` ranks, ring across them)."""
+    if impl == "hybrid":
+        return HybridContextParallel(group, ulysses_size or 2, device=device, timeout_s=timeout_s)
+    return ContextParallel(group, impl=impl, device=device, timeout_s=timeout_s)

@@ -67,9 +67,10 @@ class DistillTrainer:
         self.dp_rank = self.rank // cp
         self.model = build_model(cfg, self.device, seed=seed)
         if cp > 1:
-            from ..parallel.cp import ContextParallel
+            from ..parallel.cp import make_context_parallel
             grp = make_cp_group(cp)
-            self.cp = ContextParallel(grp, impl=get_dotted(cfg, "parallel.cp_impl", "fused"), device=self.device)
+            self.cp = make_context_parallel(grp, impl=get_dotted(cfg, "parallel.cp_impl", "fused"), device=self.device,
+                                            ulysses_size=get_dotted(cfg, "parallel.ulysses_size", None))
             for net in self.model.context_parallel_nets():
                 net.enable_context_parallel(self.cp)
         else:

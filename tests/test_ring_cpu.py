@@ -1,5 +1,5 @@
 """Ring attention (impl="ring") on 2 gloo CPU ranks: the per-block LSE merge reproduces the
-unsharded Wan forward, and the per-block (O, T~/l, mu) merge its JVP."""
+unsharded Wan forward and its gradients, and the per-block (O, T~/l, mu) merge its JVP."""
 import os
 import socket
 
@@ -48,10 +48,13 @@ def _worker(rank, world, port, q):
         m.enable_context_parallel(ContextParallel(impl="ring"))
         from dmad_b200.models.wan_jvp import wan_forward_jvp
 
+        out = m(*_inputs())
+        out.square().sum().backward()
+        grads = torch.cat([p.grad.reshape(-1) for p in m.parameters()])
+        dist.all_reduce(grads)  # parameter gradients summed over the CP group
         with torch.no_grad():
-            out = m(*_inputs())
             jo, jt = wan_forward_jvp(m, *_jvp_inputs())
-        q.put((rank, (out.numpy(), jo.numpy(), jt.numpy()), None))
+        q.put((rank, (out.detach().numpy(), jo.numpy(), jt.numpy(), grads.numpy()), None))
         dist.destroy_process_group()
     except Exception:  # pragma: no cover
         import traceback
@@ -72,11 +75,15 @@ def test_ring_matches_unsharded():
     from dmad_b200.models.wan_jvp import wan_forward_jvp
 
     m = _model()
+    out = m(*_inputs())
+    out.square().sum().backward()
+    grads = torch.cat([p.grad.reshape(-1) for p in m.parameters()])
+    out = out.detach()
     with torch.no_grad():
-        out = m(*_inputs())
         jo, jt = wan_forward_jvp(m, *_jvp_inputs())
     for rank, o, err in res:
         assert err is None, err
         torch.testing.assert_close(torch.from_numpy(o[0]), out, rtol=1e-4, atol=1e-5)
         torch.testing.assert_close(torch.from_numpy(o[1]), jo, rtol=1e-4, atol=1e-5)
         torch.testing.assert_close(torch.from_numpy(o[2]), jt, rtol=1e-3, atol=1e-5)
+        torch.testing.assert_close(torch.from_numpy(o[3]), grads, rtol=1e-3, atol=1e-5)
