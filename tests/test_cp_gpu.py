@@ -62,7 +62,11 @@ def _worker(rank, world, port, impl, per_frame, q):
 
         _, _, dev = init_distributed(timeout_s=60)
         m = _model(dev)
-        m.enable_context_parallel(ContextParallel(impl=impl, timeout_s=10.0))
+        if impl.startswith("hybrid"):  # hybrid-u2: one Ulysses group of 2; hybrid-u1: a ring of 2
+            from dmad_b200.parallel.cp import HybridContextParallel
+            m.enable_context_parallel(HybridContextParallel(ulysses_size=int(impl[-1]), timeout_s=10.0))
+        else:
+            m.enable_context_parallel(ContextParallel(impl=impl, timeout_s=10.0))
         out, feats, grads = _run(m, dev, per_frame)
         torch.cuda.synchronize()
         check_device_status()
@@ -83,7 +87,8 @@ def _worker(rank, world, port, impl, per_frame, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("impl,per_frame", [("fused", False), ("nccl", False), ("fused", True), ("ring", False)])
+@pytest.mark.parametrize("impl,per_frame", [("fused", False), ("nccl", False), ("fused", True), ("ring", False),
+                                            ("hybrid-u2", False), ("hybrid-u1", False)])
 def test_cp_two_gpus_matches_unsharded(impl, per_frame):
     world = 2
     ctx_mp = mp.get_context("spawn")
