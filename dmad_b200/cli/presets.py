@@ -25,6 +25,7 @@ register_experiment("dmad_wan2pt1_14b_cp8", {
     "model": {"family": "wan_dmad", "net": "wan2.1-14b",
               "distill": {"lr": 1e-6, "critic_lr": 1e-6, "betas": [0.0, 0.99], "student_update_freq": 2,
                           "student_lora_rank": 128, "checkpoint_student_blocks": 40, "shard_frozen": True,
+                          "checkpoint_student_policy": "mm_only",
                           "checkpoint_critic_blocks": 40, "checkpoint_critic_blocks_student_phase": 40}},
     "parallel": {"cp": 8, "cp_impl": "fused", "dp_optimizer": "sharded"},
 })
