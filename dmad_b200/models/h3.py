@@ -100,6 +100,8 @@ class _H3Attention(nn.Module):
             q = ops.rope(q, cos, sin, hd)
             k = ops.rope(k, cos, sin, hd)
         v = qkv[:, 2 * D:]
+        if cp is not None and cp.world > 1 and torch.is_grad_enabled() and x.requires_grad:
+            raise NotImplementedError("H3 context parallelism is inference-only (its exchanges carry no gradient)")
         if cp is not None and cp.world > 1 and cp.impl == "hybrid":
             from ..parallel.cp import hybrid_attention_fwd
             return getattr(self.to_out, "0")(hybrid_attention_fwd(q, k, v, 1, H, cp, L_valid))
