@@ -1,6 +1,8 @@
-"""CPU oracle: the reference's own Wan network (installed under baseline/_ref from the reference source)
-with random weights, loaded into this package's WanModel through the shared state-dict layout, gives the
-same output in fp32 -- uniform and per-frame timesteps (skipped when the reference is not installed)."""
+"""CPU oracles: the reference's own modules (installed under baseline/_ref from the reference source) with
+random weights, loaded into this package's modules through the shared state-dict layouts, give the same
+outputs in fp32 -- the Wan DiT (uniform and per-frame timesteps), the causal video VAE (encode and decode),
+the umT5 encoder with padding -- and the reference's block-mask predicates equal this package's key-range
+rectangles.  Skipped when the reference is not installed."""
 import os
 import sys
 
@@ -8,6 +10,27 @@ import pytest
 import torch
 
 REF = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+
+
+def _stub_io_deps():
+    """Stand-ins for packages the reference imports only for video IO, text cleaning and log colours."""
+    import types
+
+    if "imageio" not in sys.modules:
+        try:
+            import imageio  # noqa: F401
+        except ImportError:
+            pkg = types.ModuleType("imageio")
+            pkg.__path__ = []
+            sys.modules["imageio"] = pkg
+            sys.modules["imageio.v3"] = types.ModuleType("imageio.v3")
+    for name, attr in (("ftfy", "fix_text"), ("termcolor", "colored")):
+        try:
+            __import__(name)
+        except ImportError:
+            mod = types.ModuleType(name)
+            setattr(mod, attr, lambda text, *a, **k: text)
+            sys.modules[name] = mod
 
 
 @pytest.fixture(scope="module")
@@ -54,3 +77,113 @@ def test_wan_forward_matches_reference(ref_wan, per_frame):
         o = ours(x, t, ctx).float()
     assert r.shape == o.shape
     torch.testing.assert_close(o, r, rtol=2e-4, atol=2e-4)
+
+
+def test_wan_vae_matches_reference():
+    """The reference's chunked causal VAE (first frame, then 4-frame chunks with feature caches; one
+    latent frame at a time when decoding) against this package's whole-clip causal VAE, same weights."""
+    if not os.path.isdir(os.path.join(REF, "rcm")):
+        pytest.skip("reference not installed")
+    sys.path.insert(0, REF)
+    _stub_io_deps()
+    try:
+        from rcm.tokenizers.wan2pt1 import WanVAE_
+    except Exception as e:  # pragma: no cover
+        pytest.skip(f"reference VAE does not import here: {e}")
+    from dmad_b200.models.wan_vae import WanVAEModel
+
+    torch.manual_seed(0)
+    ref = WanVAE_(dim=16, z_dim=4, dim_mult=[1, 2, 4, 4], num_res_blocks=1, attn_scales=[],
+                  temperal_downsample=[False, True, True]).eval()
+    with torch.no_grad():
+        for p in ref.parameters():
+            p.add_(torch.randn_like(p) * 0.02)
+    ours = WanVAEModel(dim=16, z_dim=4, dim_mult=(1, 2, 4, 4), num_res_blocks=1,
+                       temporal_downsample=(False, True, True)).eval()
+    ours.load_state_dict(ref.state_dict())
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(1, 3, 9, 32, 32, generator=g)
+    z = torch.randn(1, 4, 3, 4, 4, generator=g)
+    scale = [torch.zeros(4), torch.ones(4)]
+    with torch.no_grad():
+        mu_ref = ref.encode(x, scale)
+        mu = ours.conv1(ours.encoder(x))[:, :4]
+        dec_ref = ref.decode(z, scale)
+        dec = ours.decoder(ours.conv2(z))
+    torch.testing.assert_close(mu, mu_ref, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(dec, dec_ref, rtol=1e-4, atol=1e-4)
+
+
+def test_umt5_encoder_matches_reference():
+    """The reference's umT5 encoder (per-layer relative position buckets, shared_pos=False as umT5 uses)
+    against this package's encoder with the same weights, with a padding mask."""
+    if not os.path.isdir(os.path.join(REF, "rcm")):
+        pytest.skip("reference not installed")
+    sys.path.insert(0, REF)
+    _stub_io_deps()
+    saved = torch.cuda.current_device
+    torch.cuda.current_device = lambda: 0  # a default argument of the reference's encoder wrapper (umt5.py:485)
+    try:
+        from rcm.utils.umt5 import T5Encoder
+    except Exception as e:  # pragma: no cover
+        pytest.skip(f"reference umT5 does not import here: {e}")
+    finally:
+        torch.cuda.current_device = saved
+    from dmad_b200.models.umt5 import UMT5Config, UMT5Encoder
+
+    torch.manual_seed(0)
+    ref = T5Encoder(vocab=300, dim=64, dim_attn=64, dim_ffn=128, num_heads=4, num_layers=2, num_buckets=32,
+                    shared_pos=False, dropout=0.0).eval()
+    ours = UMT5Encoder(UMT5Config(vocab=300, dim=64, dim_attn=64, dim_ffn=128, num_heads=4, num_layers=2,
+                                  num_buckets=32, text_len=16)).eval()
+    missing, unexpected = ours.load_state_dict(ref.state_dict(), strict=False)
+    assert not missing and not unexpected, (missing, unexpected)
+    ids = torch.randint(1, 300, (2, 16), generator=torch.Generator().manual_seed(3))
+    mask = torch.ones(2, 16, dtype=torch.long)
+    mask[1, 11:] = 0
+    with torch.no_grad():
+        r = ref(ids, mask)
+        o = ours(ids, mask)
+    torch.testing.assert_close(o, r, rtol=1e-4, atol=1e-4)
+
+
+def test_block_masks_match_reference_predicate():
+    """Key-range rectangles of ``mask_ranges`` against the reference's own mask functions
+    (blockmask.py ``_make_mask_fn``) for block-causal (windows, sinks, query offsets) and teacher forcing."""
+    import itertools
+
+    if not os.path.isdir(os.path.join(REF, "rcm")):
+        pytest.skip("reference not installed")
+    sys.path.insert(0, REF)
+    try:
+        from rcm.utils import blockmask as rb
+    except Exception as e:  # pragma: no cover
+        pytest.skip(f"reference block masks do not import here: {e}")
+    from dmad_b200.ops.block_attention import AttnMaskSpec, BlockPattern, mask_ranges
+
+    layer = rb.FlexOrSdpaLocalAttention.__new__(rb.FlexOrSdpaLocalAttention)  # only _make_mask_fn is used
+    n = 0
+    for ft, fc, cf, local, sink in itertools.product((3, 4), (1, 2), (1, 2), (0, 1, 2, 3), (0, 1, 2)):
+        cases = []
+        for qbo in (0, 1, 2):
+            pre = BlockPattern(ft, fc, cf).blocks_to_tokens(qbo)
+            Q = BlockPattern(ft, fc, cf).blocks_to_tokens(qbo + 3) - pre
+            cases.append(("block_causal", dict(q_block_offset=qbo), Q, pre + Q))
+        for clean in (2, 3):
+            L = 2 * BlockPattern(ft, fc, cf).blocks_to_tokens(clean)
+            cases.append(("teacher_forcing", dict(clean_blocks=clean), L, L))
+        for mode, extra, Q, KV in cases:
+            ref_spec = rb.AttnMaskSpec(mode=mode, pattern=rb.BlockPattern(ft, fc, cf), local_attn_blocks=local,
+                                       sink_blocks=sink, **extra)
+            fn, _ = layer._make_mask_fn(ref_spec, Q, KV)
+            qi = torch.arange(Q)[:, None]
+            ki = torch.arange(KV)[None, :]
+            ref = fn(0, 0, qi, ki).expand(Q, KV)
+            ours = torch.zeros(Q, KV, dtype=torch.bool)
+            spec = AttnMaskSpec(mode, BlockPattern(ft, fc, cf), local, sink, **extra)
+            for q0, q1, rng in mask_ranges(spec, Q, KV):
+                for a, b in rng:
+                    ours[q0:q1, a:b] = True
+            assert torch.equal(ours, ref), (mode, ft, fc, cf, local, sink, extra)
+            n += 1
+    assert n > 200
