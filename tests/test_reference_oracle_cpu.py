@@ -187,3 +187,37 @@ def test_block_masks_match_reference_predicate():
             assert torch.equal(ours, ref), (mode, ft, fc, cf, local, sink, extra)
             n += 1
     assert n > 200
+
+
+def test_kv_cache_matches_reference():
+    """The same sequence of cache operations on the reference's KVCache and this package's: appends,
+    prefixes by chunk count, transient writes and compaction leave identical contents."""
+    if not os.path.isdir(os.path.join(REF, "rcm")):
+        pytest.skip("reference not installed")
+    sys.path.insert(0, REF)
+    try:
+        from rcm.utils.kv_cache import KVCache as RefKV
+    except Exception as e:  # pragma: no cover
+        pytest.skip(f"reference KV cache does not import here: {e}")
+    from dmad_b200.models.kv_cache import KVCache
+
+    g = torch.Generator().manual_seed(0)
+    mk = lambda n: torch.randn(2, n, 3, 4, generator=g)  # noqa: E731
+    ref, ours = RefKV(20), KVCache(20)
+    for n in (4, 6, 5):
+        k, v = mk(n), mk(n)
+        assert ref.append(k, v) == ours.append(k, v)
+    for br in (None, 0, 1, 2, 3):
+        a, b = ref.get(br), ours.get(br)
+        assert (a[0] is None) == (b[0] is None)
+        if a[0] is not None:
+            assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+        assert ref.get_prefix_end(br) == ours.get_prefix_end(br)
+    k, v = mk(3), mk(3)
+    ra, oa = ref.write_transient(k, v, 10), ours.write_transient(k, v, 10)
+    assert torch.equal(ra[0], oa[0]) and ref.current_len == ours.current_len
+    keep = torch.tensor([0, 3, 7, 14])
+    ref.compact_(keep)
+    ours.compact_(keep)
+    assert ref.current_len == ours.current_len
+    assert torch.equal(ref.k[:, :ref.cur], ours.k[:, :ours.cur]) and torch.equal(ref.v[:, :ref.cur], ours.v[:, :ours.cur])
