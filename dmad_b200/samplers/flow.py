@@ -79,9 +79,15 @@ class FlowUniPCSampler:
         else:
             phi1 = math.expm1(hh)
         B = hh if self.kind == "bh1" else phi1
+        order = len(rks)
+        # first-order corrector and second-order predictor use the fixed weight 1/2 (also across the
+        # infinite log-SNR step out of sigma = 1)
+        if corrector and order == 1:
+            return phi1, B, [0.5]
+        if not corrector and order <= 2:
+            return phi1, B, ([] if order == 1 else [0.5])
         if math.isinf(hh):
             return phi1, B, [1.0] * len(rks)
-        order = len(rks)
         R, g = [], []
         phik = phi1 / hh - 1.0
         fact = 1.0
@@ -92,14 +98,8 @@ class FlowUniPCSampler:
             phik = phik / hh - 1.0 / fact
         if not corrector:
             m = order - 1  # the predictor has no term at r = 1
-            if m == 0:
-                return phi1, B, []
-            if m == 1:
-                return phi1, B, [0.5]
             Rm = torch.tensor([row[:m] for row in R[:m]], dtype=torch.float64)
             return phi1, B, torch.linalg.solve(Rm, torch.tensor(g[:m], dtype=torch.float64)).tolist()
-        if order == 1:
-            return phi1, B, [0.5]
         return phi1, B, torch.linalg.solve(torch.tensor(R, dtype=torch.float64),
                                            torch.tensor(g, dtype=torch.float64)).tolist()
 

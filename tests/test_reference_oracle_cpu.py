@@ -221,3 +221,38 @@ def test_kv_cache_matches_reference():
     ours.compact_(keep)
     assert ref.current_len == ours.current_len
     assert torch.equal(ref.k[:, :ref.cur], ours.k[:, :ours.cur]) and torch.equal(ref.v[:, :ref.cur], ours.v[:, :ours.cur])
+
+
+@pytest.mark.parametrize("kind,order,smax", [("euler", 1, 1.0), ("unipc", 2, 1.0), ("unipc", 3, 0.999)])
+def test_teacher_samplers_match_reference(kind, order, smax):
+    """Euler and UniPC (bh2) trajectories of a fixed velocity field through the reference's samplers and
+    this package's, 20 shifted steps.  (Third order starts below sigma = 1: from sigma = 1 the log-SNR of
+    the first step is infinite and the third-order corrector of the reference, like this one, is NaN.)"""
+    if not os.path.isdir(os.path.join(REF, "rcm")):
+        pytest.skip("reference not installed")
+    sys.path.insert(0, REF)
+    try:
+        from rcm.samplers.euler import FlowEulerSampler as RefEuler
+        from rcm.samplers.unipc import FlowUniPCMultistepSampler as RefUniPC
+    except Exception as e:  # pragma: no cover
+        pytest.skip(f"reference samplers do not import here: {e}")
+    from dmad_b200.samplers import FlowEulerSampler, FlowUniPCSampler
+
+    if kind == "euler":
+        ref, ours = RefEuler(sigma_max=smax), FlowEulerSampler(sigma_max=smax)
+        ref.set_timesteps(20, shift=3.0, device="cpu")
+    else:
+        ref, ours = RefUniPC(solver_order=order, sigma_max=smax), FlowUniPCSampler(solver_order=order, sigma_max=smax)
+        ref.set_timesteps(20, device="cpu", shift=3.0)
+    ours.set_timesteps(20, shift=3.0, device="cpu")
+
+    def vel(x, t):
+        return -0.3 * x + 0.1 * torch.sin(t / 1000.0 * 3.0)
+
+    x0 = torch.randn(2, 4, 6, generator=torch.Generator().manual_seed(0), dtype=torch.float64)
+    xr, xo = x0.clone(), x0.clone()
+    for t in ref.timesteps:
+        xr = ref.step(vel(xr, t), t, xr)
+    for t in ours.timesteps:
+        xo = ours.step(vel(xo, t), t, xo)
+    torch.testing.assert_close(xo.double(), xr.double(), rtol=1e-5, atol=2e-6)  # the reference runs in fp32
