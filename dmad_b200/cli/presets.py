@@ -10,7 +10,8 @@ from ..runtime.config import register_experiment
 _COMMON = {"data": {"kind": "synthetic", "batch_size": 1, "latent_shape": [16, 21, 60, 104],
                     "text_shape": [512, 4096]},
            "training": {"max_iters": 10000, "save_every": 500, "save_total_limit": 3, "log_every": 10,
-                        "auto_resume": True, "timeout_s": 3600, "heartbeat_s": 30}}
+                        "auto_resume": True, "timeout_s": 3600, "heartbeat_s": 30,
+                        "lr_schedule": "lambda_linear"}}  # the Wan stack's default scheduler
 
 register_experiment("dmad_wan2pt1_1pt3b", {
     **_COMMON,

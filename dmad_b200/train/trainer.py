@@ -80,7 +80,8 @@ class DistillTrainer:
         self.data = None  # built at train() time, after a resume has set the start iteration
         sched = tr.get("lr_schedule", "constant")
         warm = int(tr.get("lr_warmup", 0))
-        self.schedules = {name: LRSchedule(opt, sched, warm, self.max_iters) for name, opt in
+        cycles = tr.get("lr_cycles")  # lambda_* schedules: warm_up_steps / cycle_lengths / f_start / f_max / f_min
+        self.schedules = {name: LRSchedule(opt, sched, warm, self.max_iters, cycles=cycles) for name, opt in
                           self.model.optimizers().items()}
         self.ckpt = CheckpointManager(self.output_dir, tr.get("save_total_limit"), bool(tr.get("async_save", False)))
         self.metrics = MetricsWriter(get_dotted(cfg, "logging.metrics_file", os.path.join(self.output_dir,

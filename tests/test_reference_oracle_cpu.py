@@ -256,3 +256,57 @@ def test_teacher_samplers_match_reference(kind, order, smax):
     for t in ours.timesteps:
         xo = ours.step(vel(xo, t), t, xo)
     torch.testing.assert_close(xo.double(), xr.double(), rtol=1e-5, atol=2e-6)  # the reference runs in fp32
+
+
+def test_lr_schedules_match_reference():
+    """The Wan stack's LambdaLinear / LambdaWarmUpCosine multipliers (two cycles) against this package's."""
+    if not os.path.isdir(os.path.join(REF, "rcm")):
+        pytest.skip("reference not installed")
+    sys.path.insert(0, REF)
+    try:
+        from rcm.utils.lr_scheduler import LambdaLinearScheduler, LambdaWarmUpCosineScheduler
+    except Exception as e:  # pragma: no cover
+        pytest.skip(f"reference schedulers do not import here: {e}")
+    from dmad_b200.runtime.lr import LAMBDA_LINEAR_DEFAULT, lambda_factor
+
+    kw = dict(warm_up_steps=[10, 5], cycle_lengths=[50, 40], f_start=[0.01, 0.2], f_max=[1.0, 0.8], f_min=[0.1, 0.05])
+    lin, cos = LambdaLinearScheduler(**kw), LambdaWarmUpCosineScheduler(**kw)
+    for n in range(90):
+        assert abs(lambda_factor(n, **kw) - lin(n)) < 1e-12, n
+        assert abs(lambda_factor(n, cosine=True, **kw) - cos(n)) < 1e-12, n
+    default = LambdaLinearScheduler(**LAMBDA_LINEAR_DEFAULT)
+    for n in (0, 1, 50, 99, 100, 5000):
+        assert abs(lambda_factor(n, **LAMBDA_LINEAR_DEFAULT) - default(n)) < 1e-12, n
+
+
+def test_time_utilities_match_reference():
+    """RF / TrigFlow time conversions, the log-normal and shifted-uniform samplers (same seed, same draws
+    and inverse CDFs) and the rectified-flow TrigFlow scaling."""
+    if not os.path.isdir(os.path.join(REF, "rcm")):
+        pytest.skip("reference not installed")
+    sys.path.insert(0, REF)
+    try:
+        from rcm.utils import timestep_utils as rt
+        from rcm.utils.denoiser_scaling import RectifiedFlow_TrigFlowWrapper
+    except Exception as e:  # pragma: no cover
+        pytest.skip(f"reference time utilities do not import here: {e}")
+    from dmad_b200.algorithms import timesteps as ot
+
+    t = torch.linspace(0.01, 0.99, 37, dtype=torch.float64)
+    for name in ("rf_to_trig_time", "trig_to_rf_time", "sigma_to_rf_time", "rf_to_sigma"):
+        torch.testing.assert_close(getattr(ot, name)(t), getattr(rt, name)(t))
+    for s in (1.0, 3.0, 5.0):
+        torch.testing.assert_close(ot.shift_rf_time(t, s), rt.shift_rf_time(t, s))
+        torch.testing.assert_close(ot.inverse_shift_rf_time(t, s), rt.inverse_shift_rf_time(t, s))
+    for ours, ref in ((ot.LogNormal(-0.8, 1.6), rt.LogNormal(-0.8, 1.6)), (ot.UniformShift(5.0), rt.UniformShift(5.0))):
+        torch.manual_seed(3)
+        a = ours((64, 1), device="cpu")
+        torch.manual_seed(3)
+        b = ref((64, 1), device="cpu")
+        torch.testing.assert_close(a, b)
+        torch.testing.assert_close(ours.icdf_rf(t), ref.icdf_rf(t))
+        torch.testing.assert_close(ours.cdf_rf(t), ref.cdf_rf(t), rtol=1e-6, atol=1e-9)
+    trig = ot.rf_to_trig_time(t)
+    for a, b in zip(ot.TrigFlowScaling(t_scaling_factor=1000.0)(trig),
+                    RectifiedFlow_TrigFlowWrapper(t_scaling_factor=1000.0)(trig)):
+        torch.testing.assert_close(a, b)
