@@ -204,6 +204,11 @@ class WanDMAD(nn.Module):
         self.critic_heads.load_state_dict(shared["critic_heads"])
         self.gap.load_state_dict(shared["gap"])
         if isinstance(self.opt_student, ShardedAdamW):
+            if per_rank and "elastic_rank_states" in per_rank:  # saved with another world size
+                states = per_rank["elastic_rank_states"]
+                self.opt_student.load_resharded([st["opt_student"] for st in states])
+                self.opt_critic.load_resharded([st["opt_critic"] for st in states])
+                return
             if not per_rank or "opt_student" not in per_rank:
                 raise RuntimeError("checkpoint has no per-rank optimiser shards (saved with a replicated optimiser)")
             self.opt_student.load_state_dict(per_rank["opt_student"])

@@ -246,6 +246,29 @@ class ShardedAdamW:
                 "shards": [{"off": g.off, "len": g.len, "master": g.master, "exp_avg": g.exp_avg,
                             "exp_avg_sq": g.exp_avg_sq, "ema": g.ema} for g in self.groups]}
 
+    def load_resharded(self, rank_states: list[dict]):
+        """Elastic resume: load the shard states of every rank of a run with another world size (the flat
+        parameter layout is the same; only the shard boundaries move)."""
+        states = sorted(rank_states, key=lambda r: r["rank"])
+        if len(states) != int(states[0]["world"]):
+            raise ValueError(f"need the states of all {states[0]['world']} ranks, got {len(states)}")
+        self.step_count = int(states[0]["step"])
+        self.lr = states[0].get("lr", self.lr)
+        for gi, g in enumerate(self.groups):
+            for key in ("master", "exp_avg", "exp_avg_sq", "ema"):
+                dst = getattr(g, key)
+                parts = [st["shards"][gi].get(key) for st in states]
+                if dst is None or any(p is None for p in parts):
+                    continue
+                dst.copy_(reshard_flat(parts, g.total, g.off, g.len).to(dst.device, dst.dtype))
+            new = g.master.to(g.dtype)
+            if is_distributed() and self.world > 1:
+                parts = [torch.empty_like(new) for _ in range(self.world)]
+                dist.all_gather(parts, new, group=self.group)
+                g.pbuf.tensor.copy_(torch.cat(parts))
+            else:
+                g.pbuf.tensor[g.off:g.off + g.len].copy_(new)
+
     def load_state_dict(self, sd):
         if int(sd["world"]) != self.world:
             raise ValueError(f"sharded state was saved with world {sd['world']}, running with {self.world}")
@@ -264,6 +287,15 @@ class ShardedAdamW:
                 g.pbuf.tensor.copy_(torch.cat(parts))
             else:
                 g.pbuf.tensor[g.off:g.off + g.len].copy_(new)
+
+
+def reshard_flat(parts: list[torch.Tensor], total: int, off: int, length: int) -> torch.Tensor:
+    """This rank's ``[off, off + length)`` slice of the flat buffer that the old ranks' shards ``parts``
+    (in rank order) tile; the old and new flat lengths may differ only in the zero padding at the end."""
+    full = torch.cat([p.float().reshape(-1) for p in parts])
+    if full.numel() < total:
+        full = torch.cat([full, full.new_zeros(total - full.numel())])
+    return full[off:off + length].clone()
 
 
 def tensors_from_shards(layout: list[dict], rank_states: list[dict], key: str = "ema") -> dict:

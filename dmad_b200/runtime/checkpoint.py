@@ -193,8 +193,19 @@ class CheckpointManager:
     def latest(self) -> tuple[str | None, int]:
         return find_latest_checkpoint(self.output_dir)
 
-    def load(self, path: str, map_location="cpu") -> tuple[dict, dict | None, dict]:
-        """(shared, this rank's per-rank state or None, manifest); validates the world size."""
+    def load_all_ranks(self, path: str, map_location="cpu") -> list[dict]:
+        """Every rank's per-rank state of a checkpoint (elastic resume on another world size)."""
+        with open(os.path.join(path, "manifest.json")) as f:
+            manifest = json.load(f)
+        if not manifest.get("has_rank_files"):
+            return []
+        return [torch.load(os.path.join(path, f"rank{r:05d}.pt"), map_location=map_location, weights_only=False)
+                for r in range(int(manifest["world_size"]))]
+
+    def load(self, path: str, map_location="cpu", elastic: bool = False) -> tuple[dict, dict | None, dict]:
+        """(shared, this rank's per-rank state or None, manifest); validates the world size.  With
+        ``elastic`` a different world size is accepted and the per-rank state is
+        ``{"elastic_rank_states": [every old rank's state]}``."""
         with open(os.path.join(path, "manifest.json")) as f:
             manifest = json.load(f)
         if manifest.get("iteration") != parse_checkpoint_iteration(path):
@@ -207,9 +218,12 @@ class CheckpointManager:
         per_rank = None
         if manifest.get("has_rank_files"):
             world = get_world_size()
+            if manifest["world_size"] != world and elastic:
+                return shared, {"elastic_rank_states": self.load_all_ranks(path, map_location)}, manifest
             if manifest["world_size"] != world:
                 raise RuntimeError(f"checkpoint {path} was saved with world_size={manifest['world_size']}, "
-                                   f"resuming with world_size={world} (per-rank optimiser shards)")
+                                   f"resuming with world_size={world} (per-rank optimiser shards; set "
+                                   f"training.elastic_resume to reshard them)")
             per_rank = torch.load(os.path.join(path, f"rank{get_rank():05d}.pt"), map_location=map_location,
                                   weights_only=False)
         return shared, per_rank, manifest

@@ -146,11 +146,22 @@ class DistillTrainer:
             path, _ = self.ckpt.latest()
         if path is None:
             return 0
-        shared, per_rank, manifest = self.ckpt.load(path)
-        if shared["trainer"]["world_size"] != self.world:
-            raise RuntimeError(f"cannot resume {path}: saved with world_size={shared['trainer']['world_size']}, "
-                               f"running with {self.world}")
-        rng = (per_rank or {}).pop("rng", None) if per_rank else None
+        elastic = bool(tr.get("elastic_resume", False))
+        shared, per_rank, manifest = self.ckpt.load(path, elastic=elastic)
+        old_world = shared["trainer"]["world_size"]
+        if old_world != self.world and not elastic:
+            raise RuntimeError(f"cannot resume {path}: saved with world_size={old_world}, running with {self.world} "
+                               "(set training.elastic_resume to reshard)")
+        if per_rank and "elastic_rank_states" in per_rank:
+            # another world size: optimiser shards are resharded; a rank that existed keeps its RNG streams,
+            # a new rank starts from a fresh seed
+            states = per_rank["elastic_rank_states"]
+            rng = states[self.rank].get("rng") if self.rank < len(states) else None
+            if rng is None:
+                torch.manual_seed(int(tr.get("seed", 0)) + 104729 * (self.rank + 1) + int(shared["trainer"]["iteration"]))
+            self.log.info("elastic resume: world size %d -> %d", old_world, self.world)
+        else:
+            rng = (per_rank or {}).pop("rng", None) if per_rank else None
         self.model.load_state_dicts(shared, per_rank if per_rank else None)
         if rng is not None:
             torch.set_rng_state(rng["cpu"])

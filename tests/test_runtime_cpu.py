@@ -277,3 +277,22 @@ def test_train_cli_edm_family(tmp_path):
     assert "checkpoint-000000003" in os.listdir(out)
     lines = [json.loads(x) for x in open(os.path.join(out, "metrics.jsonl"))]
     assert lines[-1]["iteration"] == 3 and "generator_loss" in lines[-1]
+
+
+def test_elastic_resume_on_another_world_size(tmp_path):
+    """A 2-rank run's checkpoint (per-rank optimiser shards) resumes in one process only with
+    ``training.elastic_resume``; the shards are resharded and training continues."""
+    from dmad_b200.runtime.config import load_config
+    from dmad_b200.train.trainer import DistillTrainer
+
+    out, _ = _run_train(tmp_path, "c", [(4, False)])
+    cfg_path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "configs",
+                            "wan_1p3b_dmad.yaml")
+    base = _TINY + [f"training.output_dir={out}", "training.max_iters=6", "training.save_every=0",
+                    "training.auto_resume=true"]
+    with pytest.raises(RuntimeError, match="world_size"):
+        DistillTrainer(load_config(cfg_path, base)).train()
+    tr = DistillTrainer(load_config(cfg_path, base + ["training.elastic_resume=true"]))
+    tr.train()
+    assert tr.iteration == 6
+    assert all(torch.isfinite(p).all() for p in tr.model.net.parameters())

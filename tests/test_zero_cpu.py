@@ -110,3 +110,88 @@ def test_flat_views_single_process():
     opt.zero_grad()
     assert float(g.gbuf.tensor.abs().sum()) == 0.0
     assert all(p.grad is not None for p in params)
+
+
+def _np_tree(x):
+    if torch.is_tensor(x):
+        return ("__t__", x.detach().cpu().numpy())
+    if isinstance(x, dict):
+        return {k: _np_tree(v) for k, v in x.items()}
+    if isinstance(x, (list, tuple)):
+        return [_np_tree(v) for v in x]
+    return x
+
+
+def _torch_tree(x):
+    if isinstance(x, tuple) and len(x) == 2 and x[0] == "__t__":
+        return torch.from_numpy(x[1])
+    if isinstance(x, list) and len(x) == 2 and x[0] == "__t__":
+        return torch.from_numpy(x[1])
+    if isinstance(x, dict):
+        return {k: _torch_tree(v) for k, v in x.items()}
+    if isinstance(x, list):
+        return [_torch_tree(v) for v in x]
+    return x
+
+
+def _elastic_worker(rank, world, port, mode, states, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    try:
+        from dmad_b200.parallel.dist import init_distributed
+        from dmad_b200.parallel.zero import ShardedAdamW
+
+        init_distributed(backend="gloo", timeout_s=120)
+        params = _make_params(0 if mode == "train" else 5)
+        opt = ShardedAdamW(params, lr=1e-2, betas=(0.9, 0.99), weight_decay=0.05, ema=True)
+        if mode == "train":
+            for s in range(3):
+                opt.zero_grad()
+                for p, g in zip(params, _grads(rank, s, params)):
+                    p.grad.add_(g)
+                opt.step(ema_beta=0.9)
+        else:
+            opt.load_resharded([_torch_tree(st) for st in states])
+        out = (_np_tree(opt.state_dict()), [m.numpy() for m in opt.full_master()], [e.numpy() for e in opt.full_ema()],
+               [p.detach().numpy() for p in params], opt.step_count)
+        q.put((rank, out, None))
+        dist.destroy_process_group()
+    except Exception:  # pragma: no cover
+        import traceback
+        q.put((rank, None, traceback.format_exc()))
+
+
+def _spawn(world, mode, states=None):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_elastic_worker, args=(r, world, port, mode, states, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in procs], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+    for _, _, err in res:
+        assert err is None, err
+    return [r[1] for r in res]
+
+
+def test_elastic_resume_reshards_optimizer_state():
+    """Shard states of a 2-rank run reloaded on 3 ranks and on 1 process: the same full fp32 master and
+    EMA, the same bf16/fp32 weights and step count."""
+    from dmad_b200.parallel.zero import ShardedAdamW
+
+    old = _spawn(2, "train")
+    states = [o[0] for o in old]
+    full_m, full_e, weights, step = old[0][1], old[0][2], old[0][3], old[0][4]
+    new = _spawn(3, "load", states)
+    for _, m, e, w, st in new:
+        assert st == step
+        for a, b in zip(m + e + w, full_m + full_e + weights):
+            np_a, np_b = torch.from_numpy(a), torch.from_numpy(b)
+            torch.testing.assert_close(np_a, np_b)
+    params = _make_params(9)
+    opt = ShardedAdamW(params, lr=1e-2, ema=True)
+    opt.load_resharded([_torch_tree(st) for st in states])
+    for a, b in zip(opt.full_master() + [p.detach() for p in params], full_m + weights):
+        torch.testing.assert_close(a, torch.from_numpy(b))
