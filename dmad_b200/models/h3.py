@@ -29,11 +29,11 @@ from dataclasses import dataclass
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
-from torch.utils.checkpoint import checkpoint
 
 from .. import ops
 from ..ops import attention as attn_ops
 from .layers import SegLinear, install_segment_key_remap
+from .sac import checkpoint_block
 
 
 @dataclass
@@ -185,6 +185,7 @@ class H3Model(nn.Module):
         self.proj_out = nn.Linear(D, cfg.in_channels * math.prod(cfg.patch_size))
         self.audio_proj_out = nn.Linear(D, cfg.audio_in_channels)
         self.checkpoint_blocks = 0
+        self.checkpoint_policy = "block_wise"  # or "mm_only" (keep matmul / attention outputs)
         self._rope_cache = {}
         self.cp = None  # parallel.cp.ContextParallel: shard the packed sequence over a CP group
         self.init_weights()
@@ -262,7 +263,7 @@ class H3Model(nn.Module):
             blk = self.transformer_blocks[i]
             tables = adaln_tables[i] if adaln_tables is not None else blk.adaln_tables(temb)
             if self.training and torch.is_grad_enabled() and i < self.checkpoint_blocks:
-                h = checkpoint(blk, h, tables, adaln_idx, cos, sin, cp, L, use_reentrant=False)
+                h = checkpoint_block(blk, h, tables, adaln_idx, cos, sin, cp, L, policy=self.checkpoint_policy)
             else:
                 h = blk(h, tables, adaln_idx, cos, sin, cp, L)
         if cp is not None:

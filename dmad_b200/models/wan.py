@@ -21,11 +21,11 @@ from dataclasses import dataclass, field
 import torch
 import torch.nn as nn
 import torch.nn.functional as F
-from .sac import checkpoint_block
 
 from .. import ops
 from ..ops import norm as norm_ops
 from .layers import SegLinear, cross_attention_core, install_segment_key_remap, self_attention_core
+from .sac import checkpoint_block
 
 
 @dataclass
