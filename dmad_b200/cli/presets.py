@@ -5,7 +5,7 @@ Parity: the DMAD / rCM experiment configs of the Wan stack
 ``student_update_freq=2``, lr 2e-6, betas (0, 0.99); 14B on CP 8 with lr 1e-6) and the rCM
 experiments (experiments/rcm/wan2pt1_t2v.py, sCM loss on).
 """
-from ..runtime.config import register_experiment
+from ..runtime.config import experiment, merge, register_experiment
 
 _COMMON = {"data": {"kind": "synthetic", "batch_size": 1, "latent_shape": [16, 21, 60, 104],
                     "text_shape": [512, 4096]},
@@ -38,3 +38,11 @@ register_experiment("rcm_wan2pt1_1pt3b", {
                           "lr": 2e-6, "critic_lr": 2e-6}},
     "parallel": {"cp": 1, "dp_optimizer": "sharded"},
 })
+
+
+# ``<name>_debug`` twins of every experiment: 25 iterations, log every 2, checkpoint every 10, no resume,
+# tangent warm-up 8 (experiments/rcm/wan2pt1_t2v.py:23-58, registered for every job at :234)
+_DEBUG = {"training": {"max_iters": 25, "log_every": 2, "save_every": 10, "auto_resume": False},
+          "model": {"distill": {"tangent_warmup": 8}}}
+for _name in ("dmad_wan2pt1_1pt3b", "dmad_wan2pt1_14b_cp8", "rcm_wan2pt1_1pt3b"):
+    register_experiment(_name + "_debug", merge(experiment(_name), _DEBUG))

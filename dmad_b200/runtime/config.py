@@ -35,6 +35,11 @@ def experiments() -> list[str]:
     return sorted(_EXPERIMENTS)
 
 
+def experiment(name: str) -> dict:
+    """A copy of a registered experiment's overrides."""
+    return copy.deepcopy(_EXPERIMENTS[name])
+
+
 def merge(base: dict, over: dict) -> dict:
     """Recursive dict merge (``over`` wins; dicts merge, everything else replaces)."""
     out = copy.deepcopy(base)

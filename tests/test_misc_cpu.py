@@ -77,7 +77,8 @@ def test_presets_and_registry():
     from dmad_b200.runtime.config import experiments, load_config
     from dmad_b200.train.registry import registered_models
 
-    assert {"dmad_wan2pt1_1pt3b", "dmad_wan2pt1_14b_cp8", "rcm_wan2pt1_1pt3b"} <= set(experiments())
+    assert {"dmad_wan2pt1_1pt3b", "dmad_wan2pt1_14b_cp8", "rcm_wan2pt1_1pt3b", "dmad_wan2pt1_1pt3b_debug"} <= set(experiments())
+    assert load_config(None, ["experiment=dmad_wan2pt1_1pt3b_debug"])["training"]["max_iters"] == 25
     cfg = load_config(None, ["experiment=dmad_wan2pt1_14b_cp8", "training.max_iters=3"])
     assert cfg["parallel"]["cp"] == 8 and cfg["training"]["max_iters"] == 3
     assert cfg["model"]["distill"]["checkpoint_student_policy"] == "mm_only"
