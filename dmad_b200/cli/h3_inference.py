@@ -112,7 +112,17 @@ def main(argv=None):
     layouts = [build_packed_sequence(c["text_token_tags"], shape["latent_frames"], shape["latent_height"],
                                      shape["latent_width"], shape["audio_latents"], geometry.patch_size) for c in conds]
     torch.manual_seed(args.seed)
-    model = H3Model(cfg).to(torch.bfloat16)
+    if device.type == "cuda" and not args.low_vram:
+        # build the (33B) model directly on the GPU in bf16: no host copy in fp32
+        prev = torch.get_default_dtype()
+        torch.set_default_dtype(torch.bfloat16)
+        try:
+            with torch.device(device):
+                model = H3Model(cfg)
+        finally:
+            torch.set_default_dtype(prev)
+    else:
+        model = H3Model(cfg).to(torch.bfloat16)
     if args.lora:
         from ..lora import attach_lora, lora_rank_alpha, read_lora_file
 
