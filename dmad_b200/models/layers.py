@@ -232,10 +232,15 @@ class SegLinear(nn.Module):
                     elif strict:
                         missing_keys.append(k)
                 if self.sn_enabled and key + "sn_u" in state_dict:
-                    self.sn_u[sl].copy_(state_dict[key + "sn_u"])
-                    self.sn_v[i].copy_(state_dict[key + "sn_v"])
-                    self.sn_gain[i:i + 1].copy_(state_dict[key + "sn_gain"])
-                    self.sn_mask[i:i + 1].copy_(state_dict[key + "sn_mask"])
+                    u = state_dict[key + "sn_u"]
+                    self.sn_u[sl].copy_(u.reshape(-1))
+                    if key + "sn_v" in state_dict:
+                        self.sn_v[i].copy_(state_dict[key + "sn_v"])
+                    else:  # a source that stores only u (the reference's parametrization export)
+                        self.sn_v[i].copy_(_l2n(self.weight[sl].float().t() @ u.float().reshape(-1)))
+                    self.sn_gain[i:i + 1].copy_(state_dict[key + "sn_gain"].reshape(1))
+                    # a stored power-iteration state means the layer is spectrally normed
+                    self.sn_mask[i:i + 1].copy_(state_dict.get(key + "sn_mask", torch.ones(1, dtype=torch.bool)))
                     consumed.update(key + n for n in ("sn_u", "sn_v", "sn_gain", "sn_mask"))
                 if self.lora_rank and name in self.lora_segments:
                     r = self.lora_rank
