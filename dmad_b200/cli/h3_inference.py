@@ -7,7 +7,9 @@ Flag-compatible with the reference's ``inference.py`` (inference.py:50-98): --st
 Without real checkpoints (``--model-dir`` absent or ``--random-init``), the network is randomly
 initialised with the H3-shaped configuration (``--config 33b`` or ``tiny``) and prompts are replaced by
 N(0,1) embeddings of ``--text-tokens`` rows; latents are written instead of decoded video when no VAE
-is available.  Per-stage peak GPU memory is logged as the reference does.
+is available.  With ``--model-dir``, ``transformer/config.json`` sets the network's shape and its
+``*.safetensors`` shards (this package's parameter names) are loaded into it.  Per-stage peak GPU
+memory is logged as the reference does.
 """
 from __future__ import annotations
 
@@ -92,6 +94,14 @@ def main(argv=None):
 
     cfg = H3Config() if args.config == "33b" else H3Config(dim=512, num_heads=4, ffn_dim=1024, num_layers=4,
                                                             text_dim=512, time_embed_dim=256)
+    tf_dir = None
+    if args.model_dir and not args.random_init:
+        from ..inference.h3 import config_from_transformer_dir, resolve_transformer_dir
+        try:
+            tf_dir = resolve_transformer_dir(args.model_dir)
+            cfg = config_from_transformer_dir(tf_dir)
+        except FileNotFoundError:
+            tf_dir = None
     geometry = H3Geometry.from_model_dir(args.model_dir) if (args.model_dir and not args.random_init) else H3Geometry()
     shape = latent_shape_of(args.height, args.width, args.num_frames, geometry)
     vsig, asig = sigma_grid(args.steps, args.video_shift), sigma_grid(args.steps, args.audio_shift)
@@ -123,6 +133,10 @@ def main(argv=None):
             torch.set_default_dtype(prev)
     else:
         model = H3Model(cfg).to(torch.bfloat16)
+    if tf_dir is not None and any(tf_dir.glob("*.safetensors")):
+        from ..inference.h3 import load_transformer_weights
+        load_transformer_weights(model, tf_dir)
+        log(f"transformer weights loaded from {tf_dir}")
     if args.lora:
         from ..lora import attach_lora, lora_rank_alpha, read_lora_file
 

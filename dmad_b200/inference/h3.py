@@ -58,6 +58,94 @@ class H3Geometry:
                    int(math.prod(v["spatial_downsample_factors"])))
 
 
+def resolve_transformer_dir(path) -> Path:
+    """The model root (with ``transformer/``) or the transformer directory itself."""
+    path = Path(path).expanduser()
+    if (path / "transformer" / "config.json").is_file():
+        path = path / "transformer"
+    elif not (path / "config.json").is_file():
+        raise FileNotFoundError(f"no H3 transformer config below {path}")
+    cfg = json.load(open(path / "config.json"))
+    if cfg.get("_class_name") not in (None, "MiniMaxH3Transformer3DModel"):
+        raise ValueError(f"{path} is not a MiniMaxH3Transformer3DModel checkpoint")
+    return path
+
+
+def config_from_transformer_dir(path):
+    """``H3Config`` from a transformer ``config.json`` (keys the file does not name keep the 33B values)."""
+    from ..models.h3 import H3Config
+
+    c = json.load(open(resolve_transformer_dir(path) / "config.json"))
+    base = H3Config()
+    heads = int(c.get("num_attention_heads", base.num_heads))
+    hd = int(c.get("attention_head_dim", base.dim // base.num_heads))
+    return H3Config(dim=heads * hd, num_heads=heads, ffn_dim=int(c.get("ffn_dim", c.get("intermediate_size", base.ffn_dim))),
+                    num_layers=int(c.get("num_layers", base.num_layers)),
+                    refiner_layers=int(c.get("num_refiner_layers", base.refiner_layers)),
+                    in_channels=int(c.get("in_channels", base.in_channels)),
+                    audio_in_channels=int(c.get("audio_in_channels", base.audio_in_channels)),
+                    text_dim=int(c.get("text_embed_dim", c.get("text_dim", base.text_dim))),
+                    freq_dim=int(c.get("freq_dim", base.freq_dim)),
+                    time_embed_dim=int(c.get("time_embed_dim", base.time_embed_dim)),
+                    patch_size=tuple(int(p) for p in c.get("patch_size", base.patch_size)))
+
+
+def load_transformer_weights(model, path, strict: bool = True):
+    """Copies the ``*.safetensors`` shards of a transformer directory into ``model``, one shard at a
+    time (peak host memory is one shard, tensors land on the parameters' device).  Returns
+    ``(missing, unexpected)`` key lists; ``strict`` raises when either is non-empty."""
+    from safetensors.torch import load_file
+
+    root = resolve_transformer_dir(path)
+    idx = root / "diffusion_pytorch_model.safetensors.index.json"
+    if idx.is_file():
+        files = sorted({root / f for f in json.load(open(idx))["weight_map"].values()})
+    else:
+        files = sorted(root.glob("*.safetensors"))
+    if not files:
+        raise FileNotFoundError(f"no safetensors weights in {root}")
+    own = model.state_dict()
+    seen, unexpected = set(), []
+    with torch.no_grad():
+        for f in files:
+            for k, v in load_file(str(f)).items():
+                if k not in own:
+                    unexpected.append(k)
+                    continue
+                if own[k].shape != v.shape:
+                    raise ValueError(f"{k}: checkpoint shape {tuple(v.shape)} != model {tuple(own[k].shape)}")
+                own[k].copy_(v)
+                seen.add(k)
+    missing = [k for k in own if k not in seen]
+    if strict and (missing or unexpected):
+        raise KeyError(f"H3 weights do not match: {len(missing)} missing (e.g. {missing[:3]}), "
+                       f"{len(unexpected)} unexpected (e.g. {unexpected[:3]})")
+    return missing, unexpected
+
+
+def load_transformer(path, dtype=torch.bfloat16, device="cpu", strict: bool = True):
+    """This package's H3 network with the weights of a Diffusers-layout transformer directory
+    (``config.json`` plus ``*.safetensors`` shards, with or without an index), built on ``device``.
+
+    Parity: dmad_h3/model.py:33-54 (``resolve_transformer_dir`` / ``load_transformer``), which hands the
+    folder to the Diffusers class.  Here the tensors are read with ``safetensors`` into ``H3Model``
+    under this package's parameter names; a folder written with other names loads with ``strict=False``,
+    which returns ``(model, (missing, unexpected))`` instead of raising."""
+    from ..models.h3 import H3Model
+
+    cfg = config_from_transformer_dir(path)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(dtype)
+    try:
+        with torch.device(device):
+            model = H3Model(cfg)
+    finally:
+        torch.set_default_dtype(prev)
+    res = load_transformer_weights(model, path, strict)
+    model.requires_grad_(False).eval()
+    return model if strict else (model, res)
+
+
 @dataclass(frozen=True)
 class PackedSequence:
     sequence_length: int

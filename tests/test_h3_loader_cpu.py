@@ -1,0 +1,70 @@
+"""H3 transformer folder loading: config.json -> H3Config, safetensors shards (with an index) -> weights."""
+import json
+
+import pytest
+import torch
+
+from dmad_b200.inference.h3 import (config_from_transformer_dir, load_transformer, load_transformer_weights,
+                                    resolve_transformer_dir)
+from dmad_b200.models.h3 import H3Config, H3Model
+
+safetensors = pytest.importorskip("safetensors.torch")
+
+
+def _tiny_folder(tmp_path, shards=2):
+    cfg = H3Config(dim=64, num_heads=2, ffn_dim=128, num_layers=2, refiner_layers=1, text_dim=64,
+                   time_embed_dim=32)
+    torch.manual_seed(0)
+    src = H3Model(cfg)
+    tf = tmp_path / "transformer"
+    tf.mkdir()
+    json.dump({"_class_name": "MiniMaxH3Transformer3DModel", "num_attention_heads": 2, "attention_head_dim": 32,
+               "ffn_dim": 128, "num_layers": 2, "num_refiner_layers": 1, "text_embed_dim": 64, "time_embed_dim": 32,
+               "in_channels": cfg.in_channels, "audio_in_channels": cfg.audio_in_channels,
+               "patch_size": list(cfg.patch_size)}, open(tf / "config.json", "w"))
+    sd = {k: v.contiguous() for k, v in src.state_dict().items()}
+    keys = sorted(sd)
+    wm = {}
+    for i in range(shards):
+        name = f"diffusion_pytorch_model-{i + 1:05d}-of-{shards:05d}.safetensors"
+        part = {k: sd[k] for k in keys[i::shards]}
+        safetensors.save_file(part, str(tf / name))
+        wm.update({k: name for k in part})
+    json.dump({"weight_map": wm}, open(tf / "diffusion_pytorch_model.safetensors.index.json", "w"))
+    return cfg, src
+
+
+def test_resolve_and_config(tmp_path):
+    cfg, _ = _tiny_folder(tmp_path)
+    assert resolve_transformer_dir(tmp_path) == tmp_path / "transformer"
+    assert resolve_transformer_dir(tmp_path / "transformer") == tmp_path / "transformer"
+    got = config_from_transformer_dir(tmp_path)
+    assert (got.dim, got.num_heads, got.ffn_dim, got.num_layers, got.refiner_layers) == (64, 2, 128, 2, 1)
+    with pytest.raises(FileNotFoundError):
+        resolve_transformer_dir(tmp_path / "nothing")
+    json.dump({"_class_name": "Other"}, open(tmp_path / "transformer" / "config.json", "w"))
+    with pytest.raises(ValueError):
+        resolve_transformer_dir(tmp_path)
+
+
+def test_weights_roundtrip(tmp_path):
+    cfg, src = _tiny_folder(tmp_path)
+    dst = H3Model(H3Config(dim=64, num_heads=2, ffn_dim=128, num_layers=2, refiner_layers=1, text_dim=64,
+                           time_embed_dim=32))
+    missing, unexpected = load_transformer_weights(dst, tmp_path)
+    assert not missing and not unexpected
+    for k, v in src.state_dict().items():
+        torch.testing.assert_close(dst.state_dict()[k], v, rtol=0, atol=0)
+
+
+def test_strict_mismatch(tmp_path):
+    _, src = _tiny_folder(tmp_path, shards=1)
+    tf = tmp_path / "transformer"
+    (tf / "diffusion_pytorch_model.safetensors.index.json").unlink()
+    extra = {"not.a.param": torch.zeros(3)}
+    safetensors.save_file(extra, str(tf / "zz_extra.safetensors"))
+    with pytest.raises(KeyError):
+        load_transformer_weights(H3Model(H3Config(dim=64, num_heads=2, ffn_dim=128, num_layers=2, refiner_layers=1,
+                                                  text_dim=64, time_embed_dim=32)), tmp_path)
+    model, (missing, unexpected) = load_transformer(tmp_path, dtype=torch.float32, strict=False)
+    assert unexpected == ["not.a.param"] and not missing
