@@ -68,3 +68,19 @@ def test_strict_mismatch(tmp_path):
                                                   text_dim=64, time_embed_dim=32)), tmp_path)
     model, (missing, unexpected) = load_transformer(tmp_path, dtype=torch.float32, strict=False)
     assert unexpected == ["not.a.param"] and not missing
+
+
+def test_cli_loads_model_dir(tmp_path):
+    """The CLI takes the network shape and weights from ``--model-dir`` (no text encoder or VAE weights)."""
+    import os
+
+    from dmad_b200.cli.h3_inference import main
+
+    _tiny_folder(tmp_path)
+    (tmp_path / "vae").mkdir()
+    json.dump({"spatial_downsample_factors": [2, 2, 2, 2]}, open(tmp_path / "vae" / "config.json", "w"))
+    (tmp_path / "p.txt").write_text("a fox\n", encoding="utf-8")
+    main(["--model-dir", str(tmp_path), "--prompt-file", str(tmp_path / "p.txt"), "--output-dir",
+          str(tmp_path / "out"), "--steps", "1", "--height", "64", "--width", "64", "--num-frames", "22",
+          "--text-tokens", "4"])
+    assert os.listdir(tmp_path / "out")
