@@ -46,11 +46,14 @@ def parse_args(argv=None):
     p.add_argument("--width", type=int, default=1344)
     p.add_argument("--num-frames", type=int, default=124)
     p.add_argument("--low-vram", nargs="?", const="auto", choices=["auto", "8", "12", "16", "24"], default=None)
-    p.add_argument("--weights-in-ram", action="store_true")
-    p.add_argument("--weights-int8", action="store_true")
-    p.add_argument("--weights-cache", default=None, help="accepted for flag compatibility (int8 weights are "
-                   "quantised in memory)")
-    p.add_argument("--chunk-rows", type=int, default=None, help="accepted for flag compatibility")
+    p.add_argument("--weights-in-ram", action="store_true",
+                   help="with --low-vram: pinned host copies of the streamed weights instead of reading the "
+                        "memory-mapped shards on every pass")
+    p.add_argument("--weights-int8", action="store_true", help="with --low-vram: int8 per-row streamed weights")
+    p.add_argument("--weights-cache", default=None,
+                   help="directory of the int8 copy streamed from disk (default ~/.cache/dmad_b200/<id>/int8)")
+    p.add_argument("--chunk-rows", type=int, default=None,
+                   help="row-chunked blocks: at most this many rows of every intermediate except k / v")
     p.add_argument("--offload", action="store_true", help="same as --low-vram auto")
     p.add_argument("--vae-offload", action="store_true", help="accepted for flag compatibility")
     p.add_argument("--vae-dtype", default="bf16", choices=["bf16", "fp32"], help="accepted for flag compatibility")
@@ -71,6 +74,12 @@ def main(argv=None):
     os.makedirs(args.output_dir, exist_ok=True)
     if args.offload and not args.low_vram:
         args.low_vram = "auto"
+    if args.low_vram:  # GPU size preset -> rows per chunk (every preset gives the same samples up to rounding)
+        if args.low_vram == "auto":
+            total = torch.cuda.mem_get_info()[1] / 2**30 if torch.cuda.is_available() else 24
+            args.low_vram = "8" if total < 11 else "12" if total < 15 else "16" if total < 22 else "24"
+        if args.chunk_rows is None:
+            args.chunk_rows = {"8": 8192, "12": 8192, "16": 16384, "24": 16384}[args.low_vram]
     cp = None
     if args.cp:
         from ..parallel.cp import make_context_parallel
@@ -109,9 +118,15 @@ def main(argv=None):
     te_dir = os.path.join(args.model_dir, "text_encoder") if args.model_dir else None
     if te_dir and not args.random_init and os.path.isdir(te_dir):
         # the Qwen3-VL conditioner (hidden layer 50, verbatim prompts); freed before the transformer loads
-        from ..inference.text_encoder import Qwen3VLConditioner
-        enc = Qwen3VLConditioner.from_pretrained(args.model_dir, device)
-        conds = enc.encode_all(prompts)
+        if args.low_vram:  # decoder layers streamed from the shards, one ahead of compute
+            from ..inference.lowmem import LowMemTextEncoder
+            enc = LowMemTextEncoder(args.model_dir, device, cache_in_ram=args.weights_in_ram, log=log)
+            conds = enc.encode_all(prompts)
+            enc.close()
+        else:
+            from ..inference.text_encoder import Qwen3VLConditioner
+            enc = Qwen3VLConditioner.from_pretrained(args.model_dir, device)
+            conds = enc.encode_all(prompts)
         del enc
         if device.type == "cuda":
             torch.cuda.empty_cache()
@@ -122,7 +137,14 @@ def main(argv=None):
     layouts = [build_packed_sequence(c["text_token_tags"], shape["latent_frames"], shape["latent_height"],
                                      shape["latent_width"], shape["audio_latents"], geometry.patch_size) for c in conds]
     torch.manual_seed(args.seed)
-    if device.type == "cuda" and not args.low_vram:
+    source = None
+    has_weights = tf_dir is not None and any(tf_dir.glob("*.safetensors"))
+    if args.low_vram and has_weights:
+        # resident modules loaded now, blocks left on the meta device and streamed from the shards
+        from ..inference.lowmem import build_streamed_h3
+        model, source = build_streamed_h3(tf_dir, device)
+        log(f"resident transformer modules loaded from {tf_dir}; blocks stream from the shards")
+    elif device.type == "cuda" and not args.low_vram:
         # build the (33B) model directly on the GPU in bf16: no host copy in fp32
         prev = torch.get_default_dtype()
         torch.set_default_dtype(torch.bfloat16)
@@ -133,7 +155,7 @@ def main(argv=None):
             torch.set_default_dtype(prev)
     else:
         model = H3Model(cfg).to(torch.bfloat16)
-    if tf_dir is not None and any(tf_dir.glob("*.safetensors")):
+    if has_weights and source is None:
         from ..inference.h3 import load_transformer_weights
         load_transformer_weights(model, tf_dir)
         log(f"transformer weights loaded from {tf_dir}")
@@ -143,17 +165,22 @@ def main(argv=None):
         pairs, meta = read_lora_file(args.lora)
         rank, alpha = lora_rank_alpha(pairs, meta, args.lora_alpha)
         attach_lora(model, pairs, rank, alpha)
-        model.to(torch.bfloat16)
+        if source is None:
+            model.to(torch.bfloat16)
         log(f"LoRA attached: {len(pairs)} modules, rank {rank}, alpha {alpha:g}")
     model.eval().requires_grad_(False)
     streamed = None
     text_feats = [None] * len(conds)
     tables = None
     if args.low_vram:
-        from ..inference.lowmem import LowMemH3
+        from ..inference.lowmem import LowMemH3, default_cache_dir
 
         ts = [build_row_timesteps(layouts[0], vsig[s], asig[s])[0] for s in range(args.steps)]
-        streamed = LowMemH3(model, device, ts, codec="int8" if args.weights_int8 else None)
+        codec = "int8" if args.weights_int8 else None
+        in_ram = args.weights_in_ram or source is None  # a randomly initialised model lives in host memory
+        cache_dir = args.weights_cache or (default_cache_dir(tf_dir) if codec and not in_ram else None)
+        streamed = LowMemH3(model, device, ts, codec=codec, source=source, cache_in_ram=in_ram, cache_dir=cache_dir,
+                            chunk_rows=args.chunk_rows, log=log)
         streamed.precompute_text([c["prompt_embeds"] for c in conds])
         text_feats = [streamed.text_features(c["prompt_embeds"]) for c in conds]
         tables = streamed.tables

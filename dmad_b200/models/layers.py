@@ -155,7 +155,8 @@ class SegLinear(nn.Module):
         self.lora_alpha = float(alpha if alpha is not None else rank)
         self.lora_scale = self.lora_alpha / self.lora_rank
         self.lora_segments = [n for n, _ in self.segments] if segments is None else list(segments)
-        dev = self.weight.device
+        # a weight left on the meta device (streamed from a checkpoint) gets host adapters
+        dev = self.weight.device if self.weight.device.type != "meta" else torch.device("cpu")
         nseg = len(self.lora_segments)
         self.lora_A = nn.Parameter(torch.empty(nseg * rank, self.in_features, device=dev, dtype=self.weight.dtype))
         self.lora_B = nn.Parameter(torch.zeros(self.out_features, nseg * rank, device=dev, dtype=self.weight.dtype))
@@ -173,6 +174,21 @@ class SegLinear(nn.Module):
         return self.lora_scale * (self.lora_B * self.lora_mask) @ self.lora_A
 
     # ------------------------------------------------------------------ forward
+    def forward_rows(self, x, start: int, stop: int):
+        """Output columns ``[start, stop)`` of ``forward(x)``, computed from those weight rows only
+        (one segment of a fused projection, for instance)."""
+        w = self.effective_weight()[start:stop]
+        b = None if self.bias is None else self.bias[start:stop]
+        if x.dtype != w.dtype:
+            x = x.to(w.dtype)
+        if self.lora_rank:
+            bm = (self.lora_B * self.lora_mask)[start:stop]
+            if x.is_cuda:
+                from ..ops.linear import lora_linear
+                return lora_linear(x, w, b, self.lora_A, bm, self.lora_scale)
+            return F.linear(x, w, b) + self.lora_scale * F.linear(F.linear(x, self.lora_A), bm)
+        return F.linear(x, w, b)
+
     def forward(self, x):
         w = self.effective_weight()
         b = self.bias

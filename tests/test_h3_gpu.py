@@ -63,3 +63,38 @@ def test_lowmem_streamed_is_bit_identical():
                   text_features=lm.text_features(pe), adaln_tables_per_step=lm.tables)
     lm.close()
     assert torch.equal(out[0], ref[0]) and torch.equal(out[1], ref[1])
+
+
+@pytest.mark.parametrize("layers", [3, 4])
+def test_lowmem_streamed_from_shards_is_bit_identical(tmp_path, layers):
+    """Blocks streamed from memory-mapped safetensors through pinned staging buffers (odd and even block
+    counts, so the slot rotation wraps both ways) give the resident rollout bit for bit."""
+    import json
+
+    from safetensors.torch import save_file
+
+    from dmad_b200.inference.h3 import build_row_timesteps, rollout, sigma_grid
+    from dmad_b200.inference.lowmem import LowMemH3, build_streamed_h3
+    from dmad_b200.models.h3 import H3Config, H3Model
+    torch.manual_seed(0)
+    m = H3Model(H3Config(dim=256, num_heads=2, ffn_dim=512, num_layers=layers, text_dim=128, time_embed_dim=128))
+    for p in m.parameters():
+        p.data.normal_(0, 0.03)
+    m = m.to(torch.bfloat16).eval().requires_grad_(False)
+    tf = tmp_path / "transformer"
+    tf.mkdir()
+    json.dump({"num_attention_heads": 2, "attention_head_dim": 128, "ffn_dim": 512, "num_layers": layers,
+               "text_embed_dim": 128, "time_embed_dim": 128}, open(tf / "config.json", "w"))
+    save_file({k: v.contiguous() for k, v in m.state_dict().items()}, str(tf / "model.safetensors"))
+    geo, shape, lay = _inputs("cuda")
+    vs, as_ = sigma_grid(4, 12.0), sigma_grid(4, 2.0)
+    pe = torch.randn(1, 20, 128).to(torch.bfloat16)
+    ref = rollout(copy.deepcopy(m).cuda(), pe.cuda(), lay, shape, geo, vs, as_, 7, torch.device("cuda"))
+    ts = [build_row_timesteps(lay, vs[s], as_[s])[0] for s in range(4)]
+    model, source = build_streamed_h3(tmp_path, torch.device("cuda"))
+    lm = LowMemH3(model, torch.device("cuda"), ts, source=source, cache_in_ram=False)
+    lm.precompute_text([pe])
+    out = rollout(lm.model, pe.cuda(), lay, shape, geo, vs, as_, 7, torch.device("cuda"),
+                  text_features=lm.text_features(pe), adaln_tables_per_step=lm.tables)
+    lm.close()
+    assert torch.equal(out[0], ref[0]) and torch.equal(out[1], ref[1])
