@@ -55,8 +55,10 @@ def parse_args(argv=None):
     p.add_argument("--chunk-rows", type=int, default=None,
                    help="row-chunked blocks: at most this many rows of every intermediate except k / v")
     p.add_argument("--offload", action="store_true", help="same as --low-vram auto")
-    p.add_argument("--vae-offload", action="store_true", help="accepted for flag compatibility")
-    p.add_argument("--vae-dtype", default="bf16", choices=["bf16", "fp32"], help="accepted for flag compatibility")
+    # the H3 video / audio VAEs are Diffusers modules that this package does not rebuild; latents are
+    # written instead of decoded video, and these two flags only keep reference command lines parsing
+    p.add_argument("--vae-offload", action="store_true", help="no effect (the H3 VAEs are external)")
+    p.add_argument("--vae-dtype", default="bf16", choices=["bf16", "fp32"], help="no effect (the H3 VAEs are external)")
     p.add_argument("--cp", action="store_true", help="context parallel over all ranks (launch with torchrun): "
                    "every rank holds a slice of the packed sequence")
     p.add_argument("--cp-impl", default="fused", choices=["fused", "nccl", "hybrid"],
