@@ -22,6 +22,7 @@ from __future__ import annotations
 import copy
 import math
 from dataclasses import dataclass, field
+from pathlib import Path
 
 import torch
 import torch.distributed as dist
@@ -63,6 +64,7 @@ class H3DMADConfig:
     head_wd: float = 0.01
     gradient_checkpointing: bool = True
     text_tokens: int = 256
+    model_dir: str | None = None      # H3 release folder: transformer/config.json sets ``model``, shards load
 
 
 class SyntheticH3Pool:
@@ -91,9 +93,19 @@ class H3DMAD:
     def __init__(self, cfg: H3DMADConfig, device, pool=None, dtype=torch.bfloat16, seed=0):
         self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
         self.geo = H3Geometry()
+        if cfg.model_dir:
+            # the pretrained transformer (reference: model_zoo/minimax_h3_t2av.py:15-60 loads it from the
+            # Diffusers folder); the network's shape comes from its config.json
+            from ..inference.h3 import config_from_transformer_dir
+            cfg.model = config_from_transformer_dir(cfg.model_dir)
+            if (Path(cfg.model_dir) / "vae" / "config.json").is_file():
+                self.geo = H3Geometry.from_model_dir(cfg.model_dir)
         self.shape = latent_shape_of(cfg.height, cfg.width, cfg.num_frames, self.geo)
         torch.manual_seed(seed)
         base = H3Model(cfg.model)
+        if cfg.model_dir:
+            from ..inference.h3 import load_transformer_weights
+            load_transformer_weights(base, cfg.model_dir)
         self.student = base
         self.fake = copy.deepcopy(base)
         self.student.enable_lora(cfg.student_lora_rank)

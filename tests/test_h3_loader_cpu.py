@@ -103,3 +103,21 @@ def test_cli_low_vram_streams_from_model_dir(tmp_path, extra):
     for (v, a), (rv, ra) in zip(out, ref):
         torch.testing.assert_close(v.float(), rv.float(), rtol=0.05, atol=0.05)
         torch.testing.assert_close(a.float(), ra.float(), rtol=0.05, atol=0.05)
+
+
+def test_h3_dmad_trainer_starts_from_model_dir(tmp_path):
+    """``model_dir`` in the H3 DMAD config: the student and the critic start from the folder's weights."""
+    from dmad_b200.distill.h3_dmad import H3DMAD, H3DMADConfig
+
+    cfg, src = _tiny_folder(tmp_path)
+    hc = H3DMADConfig(height=64, width=64, num_frames=22, student_lora_rank=4, text_tokens=4,
+                      model_dir=str(tmp_path))
+    m = H3DMAD(hc, "cpu", dtype=torch.float32)
+    assert m.cfg.model.dim == 64 and len(m.student.transformer_blocks) == 2
+    want = src.state_dict()
+    for net in (m.student, m.fake):
+        got = net.state_dict()
+        for k in ("proj_in.weight", "transformer_blocks.1.attn.to_k.weight", "transformer_blocks.0.ff.net.2.bias"):
+            torch.testing.assert_close(got[k], want[k], rtol=0, atol=0)
+    out = m.train_iteration()
+    assert all(torch.isfinite(torch.tensor(v)) for v in out["student"].values())
