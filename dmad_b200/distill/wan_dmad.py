@@ -96,6 +96,9 @@ class WanDMADConfig:
     dp_optimizer: str = "sharded"
     dp_multicast: bool = True
     dp_sync_timeout_s: float = 120.0
+    # pretrained teacher: a DCP directory, a release / plain .pth or a .safetensors file; student and
+    # critic backbone start from it (rcm :197-251); None = random init
+    teacher_ckpt: str | None = None
 
 
 class WanDMAD(nn.Module):
@@ -106,6 +109,12 @@ class WanDMAD(nn.Module):
         device = torch.device(device) if device is not None else torch.device("cpu")
         torch.manual_seed(seed)
         teacher = WanModel(cfg.net)
+        if cfg.teacher_ckpt:
+            from ..tools.import_reference_checkpoint import read_pretrained
+            res = teacher.load_state_dict(read_pretrained(cfg.teacher_ckpt), strict=False)
+            if res.missing_keys:
+                raise KeyError(f"teacher checkpoint {cfg.teacher_ckpt} lacks {len(res.missing_keys)} weights, "
+                               f"e.g. {res.missing_keys[:3]}")
         # student and critic backbone both start from the teacher weights (rcm :247-251)
         self.net = teacher
         self.net_fake_score = copy.deepcopy(teacher)

@@ -51,6 +51,26 @@ def to_package_keys(sd: dict, prefix: str = "net_ema.") -> dict:
     return out
 
 
+def read_pretrained(path: str) -> dict:
+    """A network state dict from a DCP checkpoint directory (the ``net_ema.`` sub-module when present,
+    else ``net.``), a ``.safetensors`` file, or a torch file (a release ``net.*`` file or a plain state
+    dict), with spectral-norm parametrization keys renamed to this package's."""
+    if os.path.isdir(path):
+        sd = read_dcp(path)
+        prefix = "net_ema." if any(k.startswith("net_ema.") for k in sd) else "net."
+        return to_package_keys(sd, prefix)
+    if path.endswith(".safetensors"):
+        from safetensors.torch import load_file
+        sd = load_file(path)
+    else:
+        sd = torch.load(path, map_location="cpu", weights_only=False)
+        for key in ("model", "state_dict", "module"):
+            if isinstance(sd, dict) and isinstance(sd.get(key), dict):
+                sd = sd[key]
+    prefix = "net." if sd and all(k.startswith("net.") for k in sd) else ""
+    return to_package_keys(sd, prefix)
+
+
 def fold_spectral_norm(sd: dict) -> dict:
     """Plain weights: W g / sigma for every layer with ``sn_u`` / ``sn_gain`` (sigma after one power iteration
     from the stored u), other entries unchanged."""

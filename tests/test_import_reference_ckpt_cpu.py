@@ -2,6 +2,7 @@
 stored as torch parametrizations) into this package's WanModel, and the SN-folded release file."""
 import os
 
+import pytest
 import torch
 
 
@@ -74,3 +75,40 @@ def test_cli_writes_state_and_release(tmp_path):
     rel = torch.load(tmp_path / "rel.pth")
     assert all(k.startswith("net.") for k in rel) and rel["net.head.head.weight"].dtype == torch.bfloat16
     assert os.path.getsize(tmp_path / "out.pt") > 0
+
+
+@pytest.mark.parametrize("fmt", ["release_pth", "plain_pt", "safetensors", "dcp"])
+def test_wan_dmad_starts_from_teacher_ckpt(tmp_path, fmt):
+    """``teacher_ckpt``: student, critic backbone (and the teacher, when kept) start from the checkpoint
+    in any of the formats the reference's runs produce (rcm :197-251)."""
+    from dmad_b200.distill.wan_dmad import WanDMAD, WanDMADConfig
+    from dmad_b200.models.wan import WanConfig, WanModel
+
+    cfg = WanConfig(dim=64, ffn_dim=128, num_heads=1, num_layers=2, text_dim=16)
+    torch.manual_seed(11)
+    src = WanModel(cfg)
+    sd = {k: v.clone().contiguous() for k, v in src.state_dict().items()}
+    if fmt == "release_pth":
+        path = str(tmp_path / "teacher.pth")
+        torch.save({f"net.{k}": v for k, v in sd.items()}, path)
+    elif fmt == "plain_pt":
+        path = str(tmp_path / "teacher.pt")
+        torch.save({"model": sd}, path)
+    elif fmt == "safetensors":
+        from safetensors.torch import save_file
+        path = str(tmp_path / "teacher.safetensors")
+        save_file(sd, path)
+    else:
+        import torch.distributed.checkpoint as dcp
+        path = str(tmp_path / "dcp")
+        dcp.save({f"net_ema.{k}": v for k, v in sd.items()}, checkpoint_id=path, no_dist=True)
+    m = WanDMAD(WanDMADConfig(net=cfg, teacher_ckpt=path, critic_mode="dmd", critic_spectral_norm=False,
+                              generator_spectral_norm=False), device="cpu", dtype=torch.float32)
+    for net in (m.net, m.net_fake_score, m.net_teacher):
+        got = net.state_dict()
+        for k in ("patch_embedding.weight", "blocks.1.self_attn.k.weight", "head.head.bias"):
+            if k in sd:
+                torch.testing.assert_close(got[k], sd[k], rtol=0, atol=0)
+    with pytest.raises(KeyError):
+        torch.save({"net.patch_embedding.weight": sd["patch_embedding.weight"]}, str(tmp_path / "bad.pth"))
+        WanDMAD(WanDMADConfig(net=cfg, teacher_ckpt=str(tmp_path / "bad.pth")), device="cpu", dtype=torch.float32)
