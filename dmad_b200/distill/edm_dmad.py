@@ -25,7 +25,7 @@ import torch.nn.functional as F
 
 from ..algorithms.dmad import NUM_GAP_BANDS
 from ..algorithms.ema import kimg_halflife_beta
-from ..models.edm import EDMPrecond, config1_unet
+from ..models.edm import EDMPrecond, config1_unet, load_edm_teacher
 
 
 def get_sigmas_karras(n, sigma_min, sigma_max, rho=7.0):
@@ -100,6 +100,7 @@ class EDMDMADConfig:
     r1_gamma: float = 0.0
     r1_batch_size: int = 2
     pretrained_critic: str = ""          # e.g. "vgg16_bn,tf_efficientnet_lite0": Projected-GAN feature critic
+    model_id: str = ""                   # pretrained EDM teacher (.pkl release pickle, .pt / .safetensors)
     teacher_loss_weight: float = 1.0
     real_loss_weight: float = 1.0
     generator_lr: float = 2e-6
@@ -264,7 +265,10 @@ class EDMDMAD:
 
     def __init__(self, cfg: EDMDMADConfig = EDMDMADConfig(), teacher: EDMPrecond | None = None, device="cpu"):
         self.cfg, self.device = cfg, torch.device(device)
-        teacher = teacher or config1_unet(cfg.label_dim)
+        if teacher is None:
+            teacher = config1_unet(cfg.label_dim)
+            if cfg.model_id:  # it initialises the generator and the critic backbone (edm_unified_model.py:13-30)
+                load_edm_teacher(teacher, cfg.model_id)
         self.critic = EDMCritic(cfg, teacher).to(self.device)
         self.generator = copy.deepcopy(teacher).to(self.device)
         if cfg.generator_spectral_norm:

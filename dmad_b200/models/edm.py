@@ -183,3 +183,115 @@ def imagenet_unet(label_dim=1000, use_fp16=False):
     """The reference's ImageNet-64 configuration (train/image/main/edm/edm_network.py:3-31)."""
     return EDMPrecond(64, 3, label_dim=label_dim, use_fp16=use_fp16, model_channels=192, channel_mult=(1, 2, 3, 4),
                       channel_mult_emb=4, num_blocks=3, attn_resolutions=(32, 16, 8))
+
+
+# ----------------------------------------------------------------------------- pretrained teachers
+
+
+class _Record:
+    """Stands in for a class of a pickled network: keeps the instance's attribute dict, runs nothing."""
+
+    def __init__(self, *args, **kwargs):
+        pass
+
+    def __setstate__(self, state):
+        if isinstance(state, tuple):  # (dict, slots) form
+            state = state[0] or {}
+        if isinstance(state, dict):
+            self.__dict__.update(state)
+
+
+def _persistent_record(meta):
+    """An EDM ``torch_utils.persistence`` record: the object's state is kept, its embedded module source
+    is never executed."""
+    obj = _Record()
+    obj.__setstate__(meta.get("state", {}) if isinstance(meta, dict) else {})
+    return obj
+
+
+def _storage_from_bytes(b):
+    """A tensor storage serialised inside a plain pickle, read with torch's weights-only loader."""
+    import io
+
+    return torch.load(io.BytesIO(b), weights_only=True)
+
+
+_TORCH_REBUILD = {"_rebuild_tensor_v2", "_rebuild_parameter", "_rebuild_parameter_with_state"}
+_PLAIN = {("collections", "OrderedDict"), ("builtins", "set"), ("builtins", "frozenset")}
+
+
+def _net_unpickler(f):
+    """A ``pickle.Unpickler`` that rebuilds tensors and containers but replaces every other class by
+    ``_Record``: no code of the pickle runs (torch's tensor rebuild functions, a weights-only storage
+    loader, ``OrderedDict`` and plain builtin containers are the only callables it resolves)."""
+    import pickle
+
+    class Unpickler(pickle.Unpickler):
+        def find_class(self, module, name):
+            if module == "torch._utils" and name in _TORCH_REBUILD:
+                return super().find_class(module, name)
+            if (module, name) in _PLAIN:
+                return super().find_class(module, name)
+            if (module, name) == ("torch.storage", "_load_from_bytes"):
+                return _storage_from_bytes
+            if module.endswith("persistence") and name == "_reconstruct_persistent_obj":
+                return _persistent_record
+            if (module, name) == ("copyreg", "_reconstructor"):
+                return lambda *a: _Record()
+            return type(name, (_Record,), {})
+
+        def persistent_load(self, pid):
+            raise pickle.UnpicklingError("persistent ids are not supported")
+
+    return Unpickler(f)
+
+
+def _record_state_dict(obj, prefix="", out=None):
+    """``state_dict`` of a module rebuilt from ``_Record`` objects: its ``_parameters`` / ``_buffers`` /
+    ``_modules`` attribute dicts, walked recursively (non-persistent buffers skipped)."""
+    out = {} if out is None else out
+    d = obj.__dict__ if not isinstance(obj, nn.Module) else {
+        "_parameters": obj._parameters, "_buffers": obj._buffers, "_modules": obj._modules,
+        "_non_persistent_buffers_set": obj._non_persistent_buffers_set}
+    skip = d.get("_non_persistent_buffers_set") or set()
+    for k, v in (d.get("_parameters") or {}).items():
+        if v is not None:
+            out[prefix + k] = v.detach()
+    for k, v in (d.get("_buffers") or {}).items():
+        if v is not None and k not in skip:
+            out[prefix + k] = v
+    for k, v in (d.get("_modules") or {}).items():
+        if v is not None:
+            _record_state_dict(v, f"{prefix}{k}.", out)
+    return out
+
+
+def read_edm_teacher(path: str) -> dict:
+    """The state dict of a pretrained EDM network.
+
+    ``.pkl``: an EDM release pickle (its ``"ema"`` entry), read with ``_net_unpickler``, so neither the
+    EDM code nor the source embedded in the pickle is needed or run (the reference unpickles it with the
+    EDM code importable: train/image/main/edm/edm_unified_model.py:13-21).  ``.safetensors`` or a torch
+    file: a state dict (an ``"ema"`` / ``"model"`` / ``"state_dict"`` entry is unwrapped)."""
+    if path.endswith(".pkl"):
+        with open(path, "rb") as f:
+            data = _net_unpickler(f).load()
+        return _record_state_dict(data["ema"] if isinstance(data, dict) else data)
+    if path.endswith(".safetensors"):
+        from safetensors.torch import load_file
+        return load_file(path)
+    sd = torch.load(path, map_location="cpu", weights_only=True)
+    for key in ("ema", "model", "state_dict"):
+        if isinstance(sd, dict) and isinstance(sd.get(key), dict):
+            sd = sd[key]
+    return sd
+
+
+def load_edm_teacher(net: "EDMPrecond", path: str) -> "EDMPrecond":
+    """Loads a pretrained EDM teacher into ``net``: every key must match, except the augmentation
+    mapping, which the distillation drops (edm_unified_model.py:18-20)."""
+    sd = {k: v for k, v in read_edm_teacher(path).items() if ".map_augment." not in k}
+    res = net.load_state_dict(sd, strict=False)
+    if res.missing_keys or res.unexpected_keys:
+        raise KeyError(f"EDM teacher {path}: missing {res.missing_keys[:3]}, unexpected {res.unexpected_keys[:3]}")
+    return net
