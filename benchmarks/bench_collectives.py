@@ -5,8 +5,9 @@
 
 Every figure is timed with CUDA events on the launching stream between barriers and reported as the
 maximum over ranks.  Roofline = the bytes that must cross NVLink per GPU and direction divided by
-770 GB/s (this pool's measured peer-copy bandwidth per direction); compute and HBM time are far below
-it for these kernels.
+770 GB/s (this pool's measured peer-copy bandwidth per direction).  Compute is far below it for all
+three; the AdamW kernel also moves its fp32 shard state through HBM (12 bytes read and written per shard
+element), which at 2 GPUs is about two thirds of the NVLink time.
 
 * ``adamw``: ``ShardedAdamW.step`` on N bf16 parameters (one kernel: pull or NVLS ``ld_reduce`` of the
   gradient shard, AdamW on the fp32 shard, push or ``multimem.st`` of the new weights).  Bytes per GPU
