@@ -21,6 +21,7 @@ BCE is identical), so activations of only one forward are alive at once.
 """
 from __future__ import annotations
 
+import contextlib
 import copy
 import math
 from dataclasses import dataclass, field
@@ -160,6 +161,7 @@ class WanDMAD(nn.Module):
         self.device = device
         # optimisers; the student's optimiser also advances the fp32 EMA copy in the same kernel pass
         s_params = [p for p in self.net.parameters() if p.requires_grad]
+        self._student_params = s_params  # the EMA's order
         c_params = [p for p in self.net_fake_score.parameters() if p.requires_grad] + list(self.critic_heads.parameters())
         self.ema_coef = ema_exp_coefficient(cfg.ema_rate)
         if cfg.dp_optimizer == "sharded":
@@ -400,7 +402,30 @@ class WanDMAD(nn.Module):
 
     # ------------------------------------------------------------------ sampling (rcm :830-895)
     @torch.no_grad()
+    @contextlib.contextmanager
+    def ema_scope(self):
+        """The student runs with its EMA weights inside (rcm ``ema_scope``); collective when the optimiser
+        state is sharded, so every rank enters together."""
+        ema = self.ema_weights()
+        if ema is None:
+            yield
+            return
+        params = self._student_params
+        saved = [p.detach().clone() for p in params]
+        with torch.no_grad():
+            for p, e in zip(params, ema):
+                p.copy_(e.to(device=p.device, dtype=p.dtype).view_as(p))
+        try:
+            yield
+        finally:
+            with torch.no_grad():
+                for p, s_ in zip(params, saved):
+                    p.copy_(s_)
+
     def generate(self, context, shape, num_steps: int = 4, mid_t=None, generator=None, use_ema=False):
+        if use_ema:
+            with self.ema_scope():
+                return self.generate(context, shape, num_steps, mid_t, generator, use_ema=False)
         cfg = self.cfg
         mid_t = list(mid_t) if mid_t is not None else list(cfg.backward_timesteps[: num_steps - 1])
         t_steps = [math.atan(cfg.sigma_max)] + mid_t + [0.0]

@@ -148,3 +148,49 @@ class ForceFiniteLoss(Callback):
             if torch.is_tensor(v) and v.is_floating_point() and not torch.isfinite(v).all():
                 bad += 1
         return {"health/nonfinite_outputs": float(bad)}
+
+
+class EveryNDrawSample(Callback):
+    """Every ``every`` iterations, few-step samples of the current batch's prompts (1, 2 and
+    ``num_steps`` steps, live or EMA student) saved as latents to ``<out_dir>/samples``.
+
+    Parity: train/wan/rcm/callbacks/every_n_draw_distill.py:102-247 (1-, 2- and N-step samples of the
+    training batch, ``is_ema`` tag, only the first ``n_sample_to_save`` data-parallel ranks write).  Every
+    rank samples, so context-parallel groups stay in step; the latents are written instead of decoded
+    video (decode them with ``cli.wan_sample``'s VAE path)."""
+
+    def __init__(self, out_dir: str, every: int, num_steps: int = 4, is_ema: bool = False, n_ranks_to_save: int = 1,
+                 run_at_start: bool = False, seed: int = 0):
+        self.out_dir, self.every, self.num_steps = out_dir, int(every), int(num_steps)
+        self.is_ema, self.n_ranks, self.run_at_start, self.seed = is_ema, int(n_ranks_to_save), run_at_start, seed
+        self.written: list = []
+
+    def on_train_start(self, trainer, iteration):
+        self._start = iteration
+
+    def on_step_end(self, trainer, iteration, out):
+        if self.every <= 0 or iteration % self.every or (iteration == self._start and not self.run_at_start):
+            return None
+        gen = getattr(trainer.model, "generate", None)
+        batch = getattr(trainer, "last_batch", None)
+        if gen is None or not isinstance(batch, dict) or "latents" not in batch or "context" not in batch:
+            return None
+        import os
+
+        lat, ctx = batch["latents"], batch["context"]
+        device = lat.device
+        g = torch.Generator(device=device).manual_seed(self.seed)
+        samples = {}
+        with torch.no_grad():
+            for n in sorted({1, 2, self.num_steps}):
+                g.manual_seed(self.seed)
+                samples[f"steps_{n}"] = gen(ctx, tuple(lat.shape), num_steps=n, generator=g,
+                                            use_ema=self.is_ema).float().cpu()
+        rank = getattr(trainer, "rank", 0)
+        if rank < self.n_ranks:
+            tag = "ema" if self.is_ema else "reg"
+            os.makedirs(os.path.join(self.out_dir, "samples"), exist_ok=True)
+            path = os.path.join(self.out_dir, "samples", f"iter_{iteration:09d}_{tag}_rank{rank:03d}.pt")
+            torch.save({"iteration": iteration, "tag": tag, **samples}, path)
+            self.written.append(path)
+        return None

@@ -93,8 +93,13 @@ class DistillTrainer:
         if hb > 0 and self.world > 1:
             self.callbacks.append(cbs.HeartBeatCallback(Heartbeat(self.rank, self.world, hb),
                                                         float(tr.get("heartbeat_max_age_s", 10 * hb))))
+        if int(tr.get("sample_every", 0) or 0) > 0:
+            self.callbacks.append(cbs.EveryNDrawSample(self.output_dir, int(tr["sample_every"]),
+                                                       int(tr.get("sample_steps", 4)), bool(tr.get("sample_ema", False)),
+                                                       int(tr.get("sample_ranks", 1))))
         self.timeout = IterationTimeout(tr.get("timeout_s"))
         self.dryrun = dryrun
+        self.last_batch = None
         self.iteration = 0
 
     # ------------------------------------------------------------------ data
@@ -194,6 +199,7 @@ class DistillTrainer:
                 batch = next(data)
                 for c in self.callbacks:
                     c.on_after_dataloading(self, self.iteration)
+                self.last_batch = batch
                 out = self.model.training_step(batch, self.iteration)
                 phase = self.model.phase_of(self.iteration)
                 if phase in self.schedules:

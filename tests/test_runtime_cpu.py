@@ -296,3 +296,30 @@ def test_elastic_resume_on_another_world_size(tmp_path):
     tr.train()
     assert tr.iteration == 6
     assert all(torch.isfinite(p).all() for p in tr.model.net.parameters())
+
+
+def test_every_n_draw_sample_and_ema_scope(tmp_path):
+    """``training.sample_every``: 1-, 2- and 4-step samples of the batch saved as latents; with
+    ``sample_ema`` the student runs with its EMA weights and gets its own weights back afterwards."""
+    from dmad_b200.runtime.config import load_config
+    from dmad_b200.train.trainer import DistillTrainer
+
+    cfg_path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "configs",
+                            "wan_1p3b_dmad.yaml")
+    cfg = load_config(cfg_path, _TINY + [f"training.output_dir={tmp_path}", "training.max_iters=4",
+                                         "training.save_every=100", "model.distill.ema_rate=0.5",
+                                         "training.sample_every=2", "training.sample_ema=true"])
+    tr = DistillTrainer(cfg)
+    tr.train()
+    files = sorted(os.listdir(tmp_path / "samples"))
+    assert files == ["iter_000000002_ema_rank000.pt", "iter_000000004_ema_rank000.pt"]
+    rec = torch.load(tmp_path / "samples" / files[-1])
+    assert set(rec) >= {"steps_1", "steps_2", "steps_4"} and rec["steps_4"].shape == (1, 16, 2, 4, 4)
+    assert all(torch.isfinite(rec[k]).all() for k in ("steps_1", "steps_2", "steps_4"))
+    m = tr.model
+    before = [p.detach().clone() for p in m._student_params]
+    ema = m.ema_weights()
+    with m.ema_scope():
+        assert all(torch.equal(p, e.to(p.dtype).view_as(p)) for p, e in zip(m._student_params, ema))
+    assert all(torch.equal(p, b) for p, b in zip(m._student_params, before))
+    assert not all(torch.equal(b, e.to(b.dtype).view_as(b)) for b, e in zip(before, ema))
