@@ -71,33 +71,26 @@ def _sn_wrap_linear(mod, power_iters=30, allow_frozen=False):
     return 1
 
 
-class _MasterAdamW:
-    """bf16 parameters, fp32 master weights and moments (the reference's master-weight AdamW
-    fallback when Transformer Engine is absent), with the low-precision copy-back."""
+def _stub_log_colours():
+    """``termcolor`` (log colours only) is not in this image; the reference's ``imaginaire.utils.misc``
+    imports it at module level.  A stand-in that returns the text uncoloured lets the reference's own
+    optimiser module import unmodified."""
+    import types
 
-    def __init__(self, params, lr, betas, eps, weight_decay):
-        self.params = [p for p in params]
-        self.master = [p.detach().float().clone().requires_grad_(True) for p in self.params]
-        self.opt = torch.optim.AdamW(self.master, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay,
-                                     foreach=True)
-
-    def step(self):
-        for p, m in zip(self.params, self.master):
-            m.grad = None if p.grad is None else p.grad.float()
-        self.opt.step()
-        with torch.no_grad():
-            torch._foreach_copy_([p.data for p in self.params], [m.detach() for m in self.master])
-
-    def zero_grad(self):
-        for p in self.params:
-            p.grad = None
-        self.opt.zero_grad(set_to_none=True)
+    try:
+        import termcolor  # noqa: F401
+    except ImportError:
+        mod = types.ModuleType("termcolor")
+        mod.colored = lambda text, *a, **k: text
+        sys.modules["termcolor"] = mod
 
 
 class ReferenceWanDMAD:
     def __init__(self, device, layers=None, seed=0):
         sys.path.insert(0, REF)
+        _stub_log_colours()
         from imaginaire.utils.ema import FastEmaModelUpdater
+        from rcm.utils.fused_adam_dtensor import MasterWeightAdamW
         from rcm.networks.wan2pt1 import WanModel
         from rcm.utils.denoiser_scaling import RectifiedFlow_TrigFlowWrapper
         from rcm.utils.selective_activation_checkpoint import SACConfig
@@ -151,9 +144,13 @@ class ReferenceWanDMAD:
         self._gap_ema = torch.zeros(NUM_GAP_BANDS, device=device)
         self._gap_ready = torch.zeros(NUM_GAP_BANDS, device=device)
         kw = dict(lr=2e-6, betas=(0.0, 0.99), eps=1e-8, weight_decay=0.01)
-        self.opt_net = _MasterAdamW([p for p in self.net.parameters() if p.requires_grad], **kw)
-        self.opt_fake = _MasterAdamW([p for p in self.net_fake_score.parameters() if p.requires_grad]
-                                     + list(self.heads.parameters()), **kw)
+        # the reference's own master-weight AdamW (fused_adam_dtensor.py:372-416), which its optimiser
+        # factory selects when Transformer Engine is absent (as here)
+        self.opt_net = MasterWeightAdamW([p for p in self.net.parameters() if p.requires_grad], **kw)
+        self.opt_fake = MasterWeightAdamW([p for p in self.net_fake_score.parameters() if p.requires_grad]
+                                          + list(self.heads.parameters()), **kw)
+        self.params_net = [p for g in self.opt_net.param_groups for p in g["params"]]
+        self.params_fake = [p for g in self.opt_fake.param_groups for p in g["params"]]
         self.world = torch.distributed.get_world_size() if torch.distributed.is_initialized() else 1
 
     # ------------------------------------------------------------------ rcm model pieces
@@ -257,12 +254,12 @@ class ReferenceWanDMAD:
             loss.sum().backward()
             self.net_fake_score.requires_grad_(True)
             self.heads.requires_grad_(True)
-            self._sync_grads(self.opt_net.params)
-            torch.nn.utils.clip_grad_norm_(self.opt_net.params, 1e12, foreach=True)
+            self._sync_grads(self.params_net)
+            torch.nn.utils.clip_grad_norm_(self.params_net, 1e12, foreach=True)
             self.opt_net.step()
             beta = 0.0 if eff < 1 else (1 - 1 / (eff + 1)) ** (self.ema_coef + 1)
             self.ema.update_average(self.net, self.net_ema, beta=beta)
-            self.opt_net.zero_grad()
+            self.opt_net.zero_grad(set_to_none=True)
             return {"dmad_g_loss": loss.detach().mean()}
         eff_fake = it - it // 2 - 1
         n_sim = eff_fake % 4 + 1
@@ -275,10 +272,10 @@ class ReferenceWanDMAD:
         bce = F.softplus(-d_t_Q) + F.softplus(d_t_G) + F.softplus(-d_r_T) + F.softplus(d_r_G)
         bce.sum().backward()
         self.update_gap(d_r_T.detach(), d_r_Q.detach(), D, D)
-        self._sync_grads(self.opt_fake.params)
-        torch.nn.utils.clip_grad_norm_(self.opt_fake.params, 1e12, foreach=True)
+        self._sync_grads(self.params_fake)
+        torch.nn.utils.clip_grad_norm_(self.params_fake, 1e12, foreach=True)
         self.opt_fake.step()
-        self.opt_fake.zero_grad()
+        self.opt_fake.zero_grad(set_to_none=True)
         return {"dmad_d_loss": bce.detach().mean()}
 
     @torch.no_grad()

@@ -138,6 +138,36 @@ def count_my_kernels(fn, prefixes=("dmad",)) -> int:
     return n
 
 
+# ---------------------------------------------------------------------- process-group plumbing
+# (plain torch.distributed, so the reference arm imports nothing of this package)
+
+
+def init_distributed(timeout_s: float):
+    import datetime
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1 and not torch.distributed.is_initialized():
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=timeout_s), device_id=device)
+    return rank, world, device
+
+
+def barrier():
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+
+
+def max_over_ranks(x: float) -> float:
+    if not torch.distributed.is_initialized():
+        return float(x)
+    t = torch.tensor([float(x)], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
 def _dp_desc(trainer, args):
     if args.impl == "reference":
         return "reference: NCCL gradient all-reduce + master-weight AdamW"
@@ -150,8 +180,6 @@ def _dp_desc(trainer, args):
 
 def main():
     args = parse()
-    from dmad_b200.parallel.dist import barrier, get_rank, get_world_size, init_distributed, max_over_ranks
-
     rank, world, device = init_distributed(timeout_s=900)
     assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE {world}"
     torch.backends.cuda.matmul.allow_tf32 = True
@@ -194,11 +222,33 @@ def main():
         it[0] += 2
         return o1, o2
 
+    def mem(phase):
+        """Peak device memory of the phase just finished (stderr), then a fresh peak for the next one."""
+        if torch.cuda.is_available() and rank == 0:
+            print(f"# memory after {phase}: peak {torch.cuda.max_memory_allocated() / 2**30:.1f} GiB, "
+                  f"now {torch.cuda.memory_allocated() / 2**30:.1f} GiB", file=sys.stderr, flush=True)
+        if torch.cuda.is_available():
+            torch.cuda.reset_peak_memory_stats()
+
+    def optional(phase, fn):
+        """Runs an optional phase; its failure nulls its own field, not the timed result."""
+        try:
+            return fn()
+        except Exception as e:  # noqa: BLE001 - reported, then the line is printed without this field
+            if rank == 0:
+                print(f"# {phase} failed: {e!r}", file=sys.stderr, flush=True)
+            torch.cuda.empty_cache()
+            return None
+        finally:
+            mem(phase)
+
+    mem("setup")
     # ------------------------------------------------------------------ warm-up
     for _ in range(args.warmup):
         cycle(batch)
     torch.cuda.synchronize()
     barrier()
+    mem("warm-up")
 
     # ------------------------------------------------------------------ device-timed loop
     clocks = ClockSampler(torch.cuda.current_device())
@@ -218,11 +268,11 @@ def main():
     barrier()
     clk = clocks.stop()
     dev_ms = max_over_ranks(sum(per_step) / len(per_step))
+    mem("timed loop")
 
     # ------------------------------------------------------------------ end-to-end loop (public API,
     # pinned H2D of the step's inputs and D2H of the step's losses inside the timed region)
-    e2e = None
-    if not args.no_e2e:
+    def run_e2e():
         h2d = sum(v.numel() * v.element_size() for v in host.values())
         loss_host = torch.empty(2, dtype=torch.float32).pin_memory()
         barrier()
@@ -241,12 +291,13 @@ def main():
         e_ev.synchronize()
         wall = (time.perf_counter() - t0) * 1000 / args.steps
         e2e_ms = max_over_ranks(max(wall, s_ev.elapsed_time(e_ev) / args.steps))
-        e2e = {"value": (world // args.cp) / (e2e_ms / 1000.0), "unit": "samples/s", "h2d_bytes_per_step": int(h2d),
-               "d2h_bytes_per_step": int(loss_host.numel() * 4), "ms_per_step": e2e_ms}
+        return {"value": (world // args.cp) / (e2e_ms / 1000.0), "unit": "samples/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(loss_host.numel() * 4), "ms_per_step": e2e_ms}
+
+    e2e = None if args.no_e2e else optional("e2e loop", run_e2e)
 
     # ------------------------------------------------------------------ 4-step generation latency
-    gen_s = None
-    if args.gen_runs > 0:
+    def run_gen():
         ctx = batch["context"]
         shp = (1,) + (LATENT_SHAPE[0], args.frames, LATENT_SHAPE[2], LATENT_SHAPE[3])
         trainer.generate(ctx, shp, num_steps=4)
@@ -259,7 +310,9 @@ def main():
             e2.record()
             e2.synchronize()
             times.append(s2.elapsed_time(e2) / 1000.0)
-        gen_s = max_over_ranks(min(times))
+        return max_over_ranks(min(times))
+
+    gen_s = optional("4-step generation", run_gen) if args.gen_runs > 0 else None
 
     if args.profile and rank == 0:
         from torch.profiler import ProfilerActivity, profile
@@ -269,25 +322,20 @@ def main():
             torch.cuda.synchronize()
         with open(args.profile, "w") as f:
             f.write(prof.key_averages().table(sort_by="cuda_time_total", row_limit=60, max_name_column_width=90))
-        print(f"# peak memory {torch.cuda.max_memory_allocated() / 2**30:.1f} GiB", file=sys.stderr)
 
     launches = None
     if args.count_launches and args.impl == "dmad_b200":
-        try:
-            launches = count_my_kernels(lambda: cycle(batch)) * args.steps
-        except Exception as e:  # pragma: no cover
-            launches = None
-            if rank == 0:
-                print(f"# launch count failed: {e!r}", file=sys.stderr)
+        per_cycle = optional("launch count", lambda: count_my_kernels(lambda: cycle(batch)))
+        launches = None if per_cycle is None else per_cycle * args.steps
 
-    try:
+    if args.impl == "dmad_b200":
         from dmad_b200 import ops
-        if args.impl == "dmad_b200":
+        try:
             ops.check_device_status()
-    except Exception as e:
-        if rank == 0:
-            print(f"# device status: {e}", file=sys.stderr)
-        raise
+        except Exception as e:
+            if rank == 0:
+                print(f"# device status: {e}", file=sys.stderr)
+            raise
 
     value = (world // args.cp) / (dev_ms / 1000.0)
     out = {

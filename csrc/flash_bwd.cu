@@ -1055,6 +1055,27 @@ extern "C" int dmad_flash_attn_bwd_noalloc(const void* q, const void* k, const v
     fprintf(stderr, "dmad_flash_attn_bwd_noalloc: sizes must be positive\n");
     return DMAD_NOALLOC_ERR_ARGS;
   }
+  // every tensor is moved with 16-byte vector accesses or bulk copies: a misaligned base would fault on the
+  // GPU, so it is rejected here instead
+  for (int i = 0; i < 9; ++i)
+    if (reinterpret_cast<uintptr_t>(ptrs[i]) % 16 != 0) {
+      fprintf(stderr, "dmad_flash_attn_bwd_noalloc: pointer argument %d is not 16-byte aligned\n", i);
+      return DMAD_NOALLOC_ERR_ARGS;
+    }
+  {
+    // the static array's address is per device: the stream must belong to the current device
+    int cur = -1, sdev = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess ||
+        cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev) != cudaSuccess) {
+      fprintf(stderr, "dmad_flash_attn_bwd_noalloc: cannot query the current device or the stream's device\n");
+      return DMAD_NOALLOC_ERR_CUDA;
+    }
+    if (cur != sdev) {
+      fprintf(stderr, "dmad_flash_attn_bwd_noalloc: stream belongs to device %d but device %d is current\n", sdev,
+              cur);
+      return DMAD_NOALLOC_ERR_ARGS;
+    }
+  }
   for (int i = 0; i < 24; ++i)
     if (strides[i] <= 0 || strides[i] % 8 != 0) {
       fprintf(stderr, "dmad_flash_attn_bwd_noalloc: stride %d must be a positive multiple of 8 elements\n", i);
@@ -1134,5 +1155,23 @@ extern "C" int dmad_flash_attn_bwd_noalloc(const void* q, const void* k, const v
     return DMAD_NOALLOC_ERR_CUDA;
   flash_bwd_dq_kernel<<<dim3((Lq + 127) / 128, H, B), 384, smem_b, s>>>(tq, tk, tv, tg, p);
   if (cudaGetLastError() != cudaSuccess) return DMAD_NOALLOC_ERR_CUDA;
+  return DMAD_NOALLOC_OK;
+}
+
+extern "C" int dmad_flash_attn_bwd_noalloc_status(void* stream, int* out) {
+  using namespace dmad;
+  if (out == nullptr) return DMAD_NOALLOC_ERR_ARGS;
+  int cur = -1, sdev = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess ||
+      cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev) != cudaSuccess)
+    return DMAD_NOALLOC_ERR_CUDA;
+  if (cur != sdev) return DMAD_NOALLOC_ERR_ARGS;
+  // host code names the status word only through the symbol API (the name is a host-side stand-in)
+  int v = 0;
+  if (cudaMemcpyFromSymbolAsync(&v, g_noalloc_status, sizeof(int), 0, cudaMemcpyDeviceToHost,
+                                static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return DMAD_NOALLOC_ERR_CUDA;
+  if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return DMAD_NOALLOC_ERR_CUDA;
+  *out = v;
   return DMAD_NOALLOC_OK;
 }

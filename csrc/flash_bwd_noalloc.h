@@ -20,16 +20,22 @@
 //   * B * H * round_up(Lq, 256) must not exceed DMAD_NOALLOC_MAX_ROWS; larger
 //     problems are rejected with DMAD_NOALLOC_ERR_TOO_LARGE and a message on
 //     stderr, nothing is launched.
-//   * The first call on a device (with that device current) looks up the
-//     device address of the static arrays with cudaGetSymbolAddress; make that
-//     first call before any stream capture begins.
+//   * Every call needs the stream's device current (a stream of another device
+//     is rejected with DMAD_NOALLOC_ERR_ARGS).  The first call on a device looks
+//     up the device address of the static arrays with cudaGetSymbolAddress;
+//     make that first call before any stream capture begins.
+//   * q, k, v, o, dout, lse2, dq, dk and dv must start on 16-byte boundaries
+//     (they are moved with 16-byte accesses); others are rejected with
+//     DMAD_NOALLOC_ERR_ARGS before anything is launched.
 //   * Every call shares the one array.  Calls that overlap on the GPU (other
 //     streams, other host threads) race on it; serialise them.  The array keeps
 //     the last call's contents; each call rewrites every element it reads, so
 //     nothing has to start at zero.
 //   * The kernels' bounded waits report failures in a status word of the same
 //     file, cleared at the start of each call; the return value covers argument
-//     and launch errors only (the launch is asynchronous on `stream`).
+//     and launch errors only (the launch is asynchronous on `stream`).  Read the
+//     word with dmad_flash_attn_bwd_noalloc_status after a call: non-zero means
+//     a wait gave up and dq / dk / dv are not valid.
 #pragma once
 #include <cstdint>
 
@@ -54,6 +60,11 @@ extern "C" {
 int dmad_flash_attn_bwd_noalloc(const void* q, const void* k, const void* v, const void* o, const void* dout,
                                 const float* lse2, void* dq, void* dk, void* dv, int B, int Lq, int Lk, int H,
                                 const int64_t* strides, float scale, void* stream);
+
+// Waits for `stream` and stores the status word of the last call in *out: 0 when every bounded wait of
+// the kernels completed, otherwise the code of the wait that gave up.  Allocates nothing.  Returns
+// DMAD_NOALLOC_OK, or an error code when the stream is not of the current device or a CUDA call failed.
+int dmad_flash_attn_bwd_noalloc_status(void* stream, int* out);
 
 #ifdef __cplusplus
 }

@@ -25,6 +25,7 @@ import torch.nn.functional as F
 
 from ..algorithms.dmad import NUM_GAP_BANDS
 from ..algorithms.ema import kimg_halflife_beta
+from ..algorithms.spectral import attach_spectral_norm
 from ..models.edm import EDMPrecond, config1_unet, load_edm_teacher
 
 
@@ -35,33 +36,9 @@ def get_sigmas_karras(n, sigma_min, sigma_max, rho=7.0):
 
 
 def sn_wrap(module, power_iters=30):
-    """Frozen-gain spectral norm on a Linear / Conv weight (gain fixed at the initial sigma_max)."""
-    from torch.nn.utils import parametrize
-    from torch.nn.utils.parametrizations import spectral_norm
-
-    w = getattr(module, "weight", None)
-    if not isinstance(w, nn.Parameter) or w.dim() < 2:
-        return 0
-    if float(torch.linalg.matrix_norm(w.detach().flatten(1).float(), ord=2)) < 1e-8:
-        return 0
-    w0 = w.detach().clone()
-    spectral_norm(module, name="weight", n_power_iterations=1)
-    with torch.no_grad():
-        for _ in range(power_iters):
-            _ = module.weight
-        wn = module.weight.detach()
-        gain = (w0.flatten().float() @ wn.flatten().float()) / (wn.flatten().float() @ wn.flatten().float())
-
-    class _Gain(nn.Module):
-        def __init__(self, g):
-            super().__init__()
-            self.register_buffer("gain", g)
-
-        def forward(self, x):
-            return x * self.gain
-
-    parametrize.register_parametrization(module, "weight", _Gain(gain.to(w0.dtype)))
-    return 1
+    """Frozen-gain spectral norm on one Linear / Conv layer (gain fixed at its initial sigma_max,
+    edm_guidance.py:54-80); the normalisation itself is ``algorithms.spectral``."""
+    return int(attach_spectral_norm(module, power_iters))
 
 
 def make_binary_head(channels, spatial):

@@ -19,46 +19,15 @@ import torch
 import torch.distributed as dist
 import torch.nn as nn
 import torch.nn.functional as F
-from torch.nn.utils import parametrize
-
 from ..algorithms.dmad import NUM_GAP_BANDS
+from ..algorithms.spectral import apply_spectral_norm
 from ..models.sdxl import SDXLUNet, ddpm_alphas_cumprod
 
 
-class ScaledSN(nn.Module):
-    """weight -> gain * W / sigma_max(W), one power iteration per forward, gain frozen at set-up."""
-
-    def __init__(self, weight, iters=200):
-        super().__init__()
-        w2 = weight.detach().float().reshape(weight.shape[0], -1)
-        u = torch.randn(w2.shape[0], device=weight.device)
-        v = torch.randn(w2.shape[1], device=weight.device)
-        for _ in range(iters):
-            v = F.normalize(w2.t() @ u, dim=0)
-            u = F.normalize(w2 @ v, dim=0)
-        self.register_buffer("u", u.clone())
-        self.register_buffer("v", v.clone())
-        v1 = F.normalize(w2.t() @ u, dim=0)
-        u1 = F.normalize(w2 @ v1, dim=0)
-        self.register_buffer("gain", torch.sum(u1 * (w2 @ v1)).clone())
-
-    def forward(self, w):
-        w2 = w.reshape(w.shape[0], -1).float()
-        with torch.no_grad():
-            self.v.copy_(F.normalize(w2.t() @ self.u, dim=0))
-            self.u.copy_(F.normalize(w2 @ self.v, dim=0))
-        u, v = self.u.clone(), self.v.clone()
-        sigma = torch.sum(u * (w2 @ v)).clamp(min=1e-12)
-        return w * (self.gain / sigma).to(w.dtype)
-
-
 def apply_scaled_spectral_norm(module, iters=200):
-    n = 0
-    for m in module.modules():
-        if isinstance(m, nn.Conv2d) and m.weight.requires_grad and m.weight.detach().abs().max() >= 1e-8:
-            parametrize.register_parametrization(m, "weight", ScaledSN(m.weight, iters))
-            n += 1
-    return n
+    """Frozen-gain spectral norm on every trainable conv of ``module`` with ``iters`` power steps at
+    set-up and one per forward in every mode (sd_guidance.py:51-89); ``algorithms.spectral`` does it."""
+    return apply_spectral_norm(module, iters, update="always", types=(nn.Conv2d,))
 
 
 def make_head(ch=1280, spatial=32):

@@ -32,6 +32,7 @@ import torch.nn as nn
 from ..algorithms import (CriticHeads, GapRouter, TrigFlowScaling, UniformShift, LogNormal, critic_bce_loss,
                           ema_exp_coefficient, generator_linear_loss, rf_to_trig_time, trig_to_rf_time)
 from ..algorithms.dmad import band_of_cdf, critic_accuracies
+from ..algorithms.spectral import apply_spectral_norm
 from ..models.wan import WanConfig, WanModel, WAN_1P3B
 from ..ops.optim import FusedAdamW
 from ..parallel.dist import broadcast_module
@@ -124,10 +125,7 @@ class WanDMAD(nn.Module):
         self.critic_heads = CriticHeads(cfg.net.dim)
         if cfg.critic_spectral_norm:
             self.net_fake_score.enable_spectral_norm(range(cfg.net.num_layers), cfg.sn_power_iters)
-            for head in (self.critic_heads.real, self.critic_heads.teacher):
-                for i, m in enumerate(head):
-                    if isinstance(m, nn.Linear):
-                        _sn_wrap_torch_linear(m, cfg.sn_power_iters)
+            apply_spectral_norm(self.critic_heads, cfg.sn_power_iters, types=(nn.Linear,))
         if cfg.generator_spectral_norm:
             nb = math.ceil(cfg.net.num_layers * cfg.sn_generator_frac)
             self.net.enable_spectral_norm(range(nb), cfg.sn_power_iters)
@@ -401,7 +399,6 @@ class WanDMAD(nn.Module):
         return self.student_step(batch, it) if cfg.critic_mode == "dmad" else rcm.student_dmd_step(self, batch, it, True)
 
     # ------------------------------------------------------------------ sampling (rcm :830-895)
-    @torch.no_grad()
     @contextlib.contextmanager
     def ema_scope(self):
         """The student runs with its EMA weights inside (rcm ``ema_scope``); collective when the optimiser
@@ -422,6 +419,7 @@ class WanDMAD(nn.Module):
                 for p, s_ in zip(params, saved):
                     p.copy_(s_)
 
+    @torch.no_grad()
     def generate(self, context, shape, num_steps: int = 4, mid_t=None, generator=None, use_ema=False):
         if use_ema:
             with self.ema_scope():
@@ -439,31 +437,3 @@ class WanDMAD(nn.Module):
         self.net.train(was)
         return torch.nan_to_num(x.float())
 
-
-def _sn_wrap_torch_linear(lin: nn.Linear, power_iters: int):
-    """Frozen-gain spectral norm on a plain nn.Linear (the critic heads), via torch parametrizations
-    exactly as the reference registers it (t2v_model_distill_dmad.py:488-507)."""
-    from torch.nn.utils import parametrize
-    from torch.nn.utils.parametrizations import spectral_norm
-
-    w = lin.weight
-    if float(torch.linalg.matrix_norm(w.detach().float(), ord=2)) < 1e-8:
-        return 0
-    w_orig = w.detach().clone()
-    spectral_norm(lin, name="weight", n_power_iterations=1)
-    with torch.no_grad():
-        for _ in range(power_iters):
-            _ = lin.weight
-        wn = lin.weight.detach()
-        gain = (w_orig.flatten().float() @ wn.flatten().float()) / (wn.flatten().float() @ wn.flatten().float())
-
-    class _Gain(nn.Module):
-        def __init__(self, g):
-            super().__init__()
-            self.register_buffer("gain", g)
-
-        def forward(self, x):
-            return x * self.gain
-
-    parametrize.register_parametrization(lin, "weight", _Gain(gain.to(w_orig.dtype)))
-    return 1

@@ -26,6 +26,11 @@ class _Gelu(torch.autograd.Function):
 
 
 def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
-    if not x.is_cuda or x.dtype != torch.bfloat16 or x.numel() % 8:
+    """GELU-tanh; the CPU path is the PyTorch restatement, the CUDA path is this package's kernel only
+    (bf16, element count a multiple of 8: anything else on CUDA is an error, not a silent fallback)."""
+    if not x.is_cuda:
         return F.gelu(x.float(), approximate="tanh").to(x.dtype)
+    if x.dtype != torch.bfloat16 or x.numel() % 8:
+        raise ValueError(f"gelu_tanh on CUDA takes bf16 tensors with numel % 8 == 0, got {x.dtype} "
+                         f"with {x.numel()} elements")
     return _Gelu.apply(x.contiguous())

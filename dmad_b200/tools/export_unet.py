@@ -4,9 +4,9 @@
 
 Parity: train/image/main/sdxl/export_unet.py (SN-folded fp16 UNet state dict) and the FID path of
 train/image/main/edm/test_folder_edm.py, which folds the SN of the EMA generator before sampling.
-``fold_spectral_norm`` replaces every parametrised weight by its current effective value (one more
-power iteration from the stored vectors for the frozen-gain parametrisations) and removes the
-parametrisation, so the plain network class loads the result.
+``fold_spectral_norm`` (``algorithms.spectral``) replaces every normalised weight by the effective
+weight of the network in eval mode and turns the layer back into its plain class, so the plain
+network class loads the result.
 """
 from __future__ import annotations
 
@@ -14,18 +14,7 @@ import argparse
 import copy
 
 import torch
-from torch.nn.utils import parametrize
-
-
-@torch.no_grad()
-def fold_spectral_norm(module: torch.nn.Module) -> int:
-    n = 0
-    for m in list(module.modules()):
-        if parametrize.is_parametrized(m):
-            for name in list(m.parametrizations.keys()):
-                parametrize.remove_parametrizations(m, name, leave_parametrized=True)
-                n += 1
-    return n
+from ..algorithms.spectral import fold_spectral_norm
 
 
 def plain_state_dict(module: torch.nn.Module, dtype=torch.float16) -> dict:

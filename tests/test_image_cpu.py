@@ -42,7 +42,7 @@ def test_sdxl_tiny_step_and_full_size():
     assert all(torch.isfinite(v) for v in out.values())
 
 
-def test_fold_spectral_norm_matches_parametrized_forward():
+def test_fold_spectral_norm_matches_normalised_forward():
     import copy
     from dmad_b200.distill.edm_dmad import sn_wrap
     from dmad_b200.tools.export_unet import fold_spectral_norm, plain_state_dict
@@ -57,6 +57,35 @@ def test_fold_spectral_norm_matches_parametrized_forward():
     x = torch.randn(2, 3, 8, 8)
     ref = net(x)
     sd = plain_state_dict(net, torch.float32)
-    assert not any("parametrizations" in k for k in sd)
+    assert not any("parametrizations" in k or k.endswith(("sn_u", "sn_v", "sn_gain")) for k in sd)
     plain.load_state_dict(sd)
     torch.testing.assert_close(plain(x), ref, rtol=1e-4, atol=1e-5)
+
+
+def test_frozen_gain_spectral_norm_properties():
+    """At set-up the normalised layer computes what the plain one did; after the weight changes its
+    spectral norm is pulled back to the set-up value; the module deep-copies and round-trips its state."""
+    import copy
+    from dmad_b200.algorithms.spectral import SNLinear, apply_spectral_norm
+
+    torch.manual_seed(0)
+    net = torch.nn.Sequential(torch.nn.Linear(12, 9), torch.nn.SiLU(), torch.nn.Conv2d(3, 4, 3))
+    plain = copy.deepcopy(net)
+    assert apply_spectral_norm(net, power_iters=50) == 2
+    assert isinstance(net[0], SNLinear)
+    x = torch.randn(5, 12)
+    torch.testing.assert_close(net[0](x), plain[0](x), rtol=1e-4, atol=1e-5)
+    s0 = torch.linalg.matrix_norm(plain[0].weight, ord=2)
+    with torch.no_grad():
+        net[0].weight.mul_(3.0).add_(0.1 * torch.randn_like(net[0].weight))
+    for _ in range(60):  # power steps in training mode converge to the new sigma
+        w_eff = net[0].sn_weight()
+    torch.testing.assert_close(torch.linalg.matrix_norm(w_eff.detach(), ord=2), s0, rtol=1e-3, atol=1e-4)
+    twin = copy.deepcopy(net)
+    twin.load_state_dict(net.state_dict())
+    net.eval(), twin.eval()
+    torch.testing.assert_close(twin[0](x), net[0](x))
+    # gradients reach the raw weight through sigma
+    net.train()
+    net[0](x).sum().backward()
+    assert net[0].weight.grad is not None and torch.isfinite(net[0].weight.grad).all()

@@ -46,3 +46,15 @@ def test_rcm_objectives_run(kw):
     for it in range(3):
         out = m.training_step(b, it)
         assert all(torch.isfinite(torch.as_tensor(float(v))) for v in out.values())
+
+
+@pytest.mark.parametrize("use_ema", [False, True])
+def test_generate_records_no_autograd_graph(use_ema):
+    """Few-step sampling runs without autograd, with and without the EMA weights swapped in."""
+    from dmad_b200.distill.wan_dmad import WanDMAD, WanDMADConfig
+
+    cfg = WanConfig(dim=128, ffn_dim=256, num_heads=1, num_layers=2, text_dim=32)
+    m = WanDMAD(WanDMADConfig(net=cfg, sn_power_iters=2), device="cpu", dtype=torch.float32)
+    x = m.generate(torch.randn(1, 8, 32), (1, 16, 2, 4, 6), num_steps=2, use_ema=use_ema)
+    assert x.shape == (1, 16, 2, 4, 6)
+    assert not x.requires_grad and x.grad_fn is None

@@ -25,6 +25,23 @@ def _symbol():
     return fn
 
 
+def _status_symbol():
+    import dmad_b200._C as C
+
+    lib = ctypes.CDLL(C.__file__)
+    fn = lib.dmad_flash_attn_bwd_noalloc_status
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]
+    return fn
+
+
+def _read_status(stream):
+    st = ctypes.c_int(-1)
+    rc = _status_symbol()(stream.cuda_stream, ctypes.byref(st))
+    assert rc == 0, rc
+    return st.value
+
+
 def _strides(*ts):
     vals = []
     for t in ts:
@@ -61,6 +78,8 @@ def test_noalloc_backward_matches_regular_entry_point():
                 dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), B, Lq, Lk, H,
                 ctypes.cast(_strides(q, k, v, o, dout, dq, dk, dv), ctypes.c_void_p), scale, stream.cuda_stream)
         assert rc == 0, rc
+        # the entry point's own status word: 0 means every bounded wait of its kernels completed
+        assert _read_status(stream) == 0
         torch.cuda.synchronize()
         ops.check_device_status()
         for a, b, name in zip((dq, dk, dv), ref, ("dq", "dk", "dv")):
@@ -78,3 +97,16 @@ def test_noalloc_rejects_oversize():
             q.data_ptr(), q.data_ptr(), 64, 1 << 16, 128, 64, ctypes.cast(st, ctypes.c_void_p), 0.1,
             torch.cuda.current_stream().cuda_stream)
     assert rc == 2
+
+
+def test_noalloc_rejects_misaligned_pointer():
+    fn = _symbol()
+    q = torch.zeros(1, 256, 1, 128, device="cuda", dtype=torch.bfloat16)
+    lse = torch.zeros(1, 1, 260, device="cuda")
+    st = _strides(*([q] * 8))
+    p = q.data_ptr()
+    # an lse pointer 4 bytes past a 16-byte boundary is rejected before any launch
+    rc = fn(p, p, p, p, p, lse.data_ptr() + 4, p, p, p, 1, 256, 256, 1, ctypes.cast(st, ctypes.c_void_p), 0.1,
+            torch.cuda.current_stream().cuda_stream)
+    assert rc == 1
+    assert _read_status(torch.cuda.current_stream()) == 0
