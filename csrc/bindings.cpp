@@ -3,6 +3,7 @@
 #include <vector>
 
 namespace dmad {
+void register_h2d_stream(pybind11::module& m);
 void flash_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
                double scale);
 void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
@@ -114,4 +115,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_barrier", &dmad::symm_barrier);
   m.def("dp_sumsq", &dmad::dp_sumsq);
   m.def("dp_adamw", &dmad::dp_adamw);
+  dmad::register_h2d_stream(m);
 }

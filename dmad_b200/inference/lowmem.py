@@ -1,104 +1,120 @@
-"""Low-VRAM inference: stream transformer blocks host -> device one layer ahead of compute.
+"""Low-VRAM inference: the transformer's repeated blocks stream host -> device while the GPU computes.
 
-Parity with dmad_h3/lowmem.py (ShardIndex :41-76, Streamer :176-331, LowMemTextEncoder :337-393,
-AdaLNTables :400-413, _chunked_block_forward :416-461, TextLookup :464-475, LowMemTransformer :478-574):
-* each block's weights (minus its adaLN projection) form one group with a fixed byte layout; the groups
-  come from a tensor source: the memory-mapped safetensors shards of a checkpoint (``ShardIndex``) or
-  the weights of a model already in host memory (``StateSource``);
-* the bytes reach the GPU either from pinned host copies made once (``cache_in_ram``) or, per pass,
-  from the source through two pinned staging buffers (host memory stays at two blocks);
-* two rotating GPU slots; a worker thread issues ``cudaMemcpyAsync`` (``copy_(non_blocking=True)``) of
-  block i+2 on a side stream once the compute stream has recorded that the slot's previous occupant is
-  done; a forward pre-hook makes the compute stream wait on the copy and binds the parameters as views
-  into the slot, the post-hook records ``compute_done`` and unbinds;
-* the adaLN projections (the bulk of the parameters) depend only on the sampling step, so their outputs
-  are tabulated per step up front and the projections are never streamed;
-* the token refiner sees only the text, so its output is computed once per prompt;
-* optional int8 per-output-row codec, dequantised to bf16 on the GPU right before use (changes the
-  samples; off by default); streamed from disk it is written once to a cache directory validated by a
-  manifest of the shards it came from;
-* ``chunked_block_forward``: a block forward that holds at most ``rows`` rows of every intermediate
-  except the keys and values (the attention still sees the whole sequence).
-The kernels and their order are those of the resident model, so without the codec and the row chunking
-the output is bit-identical to the resident run.  On a CPU device the same code runs with synchronous
-copies (no streams or events), which is how the bookkeeping is tested without a GPU.
+What it reproduces (dmad_h3/lowmem.py: the ``--low-vram`` path of the H3 CLI): the blocks' weights
+stay on the host and only a few blocks' worth of device memory holds them, one block ahead of compute,
+with the sampled output bit-identical to the resident run; optional int8 weights; the adaLN
+projections tabulated per sampling step instead of streamed; the text refiner run once per prompt; a
+row-chunked block forward; the Qwen3-VL text encoder streamed layer by layer.
+
+How (this library's design):
+* ``SafetensorsCatalog`` parses the shards' headers itself, so every tensor is a (file, byte offset,
+  length) triple.  A block whose stored dtypes match the model's streams straight from those byte
+  ranges: the native engine ``pread``s them into a pinned staging buffer, no Python on the path.
+* ``BlockLayout`` packs one block's streamed parameters into a fixed byte layout (each 256-byte
+  aligned; fused projections stored as several checkpoint entries map to several extents of one
+  parameter) and knows where every byte comes from.
+* ``LayerStreamer`` drives the native engine ``dmad_b200._C.H2DStreamer`` (csrc/h2d_stream.cpp): K
+  device slots, one copy stream, events, a C++ worker thread issuing ``cudaMemcpyAsync`` from pinned
+  memory on the side stream.  A forward pre-hook ``acquire``s the block's slot (the compute stream waits
+  on the copy's event, never the host on the GPU) and binds the parameters as views into it; the post-
+  hook unbinds and ``release``s, which queues the block K positions later in the cyclic schedule.
+* Groups come from pinned RAM copies made once (``cache_in_ram``), straight from the shards, or from an
+  int8 cache directory (one file per block, per-output-row absmax scales, checked against a
+  fingerprint of the shards it was made from).
+On a CPU device the engine runs the same schedule with synchronous memcpy into host slots, which is
+how the bookkeeping is tested without a GPU.
 """
 from __future__ import annotations
 
 import contextlib
 import hashlib
 import json
-import queue
-import threading
+import mmap
+import os
+import struct
 from pathlib import Path
 
 import torch
 import torch.nn as nn
 
 _ALIGN = 256
+_ST_DTYPES = {"BF16": torch.bfloat16, "F16": torch.float16, "F32": torch.float32, "F64": torch.float64,
+              "I64": torch.int64, "I32": torch.int32, "I16": torch.int16, "I8": torch.int8, "U8": torch.uint8,
+              "BOOL": torch.bool}
 
 
-def _aligned(n):
-    return -(-n // _ALIGN) * _ALIGN
+def _round_up(n: int) -> int:
+    return (n + _ALIGN - 1) // _ALIGN * _ALIGN
 
 
-def _quantize_rows(w):
+def int8_rows(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Symmetric per-output-row int8 code: q = round(w / s), s = max|w_row| / 127 (s = 1 for a zero row)."""
     w32 = w.float()
-    s = w32.abs().amax(dim=1) / 127.0
-    s = torch.where(s > 0, s, torch.ones_like(s))
-    return (w32 / s[:, None]).round_().clamp_(-127, 127).to(torch.int8), s
+    scale = w32.abs().amax(dim=1).div(127.0)
+    scale = scale.masked_fill(scale == 0, 1.0)
+    return torch.clamp(torch.round(w32 / scale.unsqueeze(1)), -127, 127).to(torch.int8), scale
 
 
-# ----------------------------------------------------------------------------------------------- sources
+# ----------------------------------------------------------------------------------------------- weights on disk
 
 
-class ShardIndex:
-    """Tensor name -> shard of a safetensors directory (with or without an index file); shards are
-    memory-mapped once touched, and ``tensor`` reads one entry."""
+class SafetensorsCatalog:
+    """Every tensor of a directory of ``*.safetensors`` shards as (file, byte offset, length, dtype, shape),
+    read from the shards' own headers (8-byte little-endian header length, then a JSON table of
+    ``dtype`` / ``shape`` / ``data_offsets`` relative to the end of the header)."""
 
     def __init__(self, directory):
-        from safetensors import safe_open
-
         self.directory = Path(directory).expanduser()
-        self.where: dict = {}
-        index = sorted(self.directory.glob("*.safetensors.index.json"))
-        if index:
-            for key, fname in json.load(open(index[0]))["weight_map"].items():
-                self.where[key] = self.directory / fname
-        else:
-            for path in sorted(self.directory.glob("*.safetensors")):
-                with safe_open(str(path), "pt") as f:
-                    for key in f.keys():
-                        self.where[key] = path
-        if not self.where:
-            raise FileNotFoundError(f"no safetensors in {self.directory}")
-        self._open: dict = {}
-        self._lock = threading.Lock()
-
-    def _handle(self, path):
-        from safetensors import safe_open
-
-        with self._lock:
-            h = self._open.get(path)
-            if h is None:
-                h = self._open[path] = safe_open(str(path), "pt")
-            return h
+        self.entries: dict = {}
+        self.shards = sorted(self.directory.glob("*.safetensors"))
+        for path in self.shards:
+            with open(path, "rb") as f:
+                (hlen,) = struct.unpack("<Q", f.read(8))
+                header = json.loads(f.read(hlen))
+            base = 8 + hlen
+            for key, meta in header.items():
+                if key == "__metadata__":
+                    continue
+                start, end = meta["data_offsets"]
+                dtype = _ST_DTYPES.get(meta["dtype"])
+                if dtype is None:
+                    raise ValueError(f"{path.name}: tensor {key} has unsupported dtype {meta['dtype']}")
+                self.entries[key] = (path, base + int(start), int(end) - int(start), dtype, tuple(meta["shape"]))
+        if not self.entries:
+            raise FileNotFoundError(f"{self.directory}: no tensors found in *.safetensors files")
+        self._maps: dict = {}
 
     def keys(self):
-        return self.where.keys()
+        return self.entries.keys()
 
     def __contains__(self, key):
-        return key in self.where
+        return key in self.entries
 
-    def tensor(self, key):
-        return self._handle(self.where[key]).get_tensor(key)
+    def location(self, key):
+        """(path, byte offset, byte length, dtype, shape) of one tensor."""
+        return self.entries[key]
 
-    def files(self):
-        return sorted(set(self.where.values()))
+    def tensor(self, key) -> torch.Tensor:
+        """A read-only CPU view of one tensor over the memory-mapped shard."""
+        path, off, n, dtype, shape = self.entries[key]
+        mm = self._maps.get(path)
+        if mm is None:
+            with open(path, "rb") as f:
+                mm = self._maps[path] = mmap.mmap(f.fileno(), 0, access=mmap.ACCESS_READ)
+        if n == 0:
+            return torch.empty(shape, dtype=dtype)
+        import warnings
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore")  # the view is read-only; callers copy out of it
+            raw = torch.frombuffer(mm, dtype=torch.uint8, count=n, offset=off)
+        return raw.view(dtype).reshape(shape)
+
+    def fingerprint(self) -> list:
+        return [[p.name, p.stat().st_size, p.stat().st_mtime_ns] for p in self.shards]
 
 
-class StateSource:
-    """An in-memory state dict (a model's own weights) as a tensor source."""
+class _DictSource:
+    """A state dict held in memory, behind the same ``keys`` / ``tensor`` interface."""
 
     def __init__(self, state):
         self.state = state
@@ -111,9 +127,6 @@ class StateSource:
 
     def tensor(self, key):
         return self.state[key]
-
-    def files(self):
-        return []
 
 
 @contextlib.contextmanager
@@ -153,115 +166,127 @@ def _buffers_to(module: nn.Module, device):
                 m._buffers[k] = buf.to(device)
 
 
-# ----------------------------------------------------------------------------------------------- groups
+# ----------------------------------------------------------------------------------------------- block layout
 
 
-def _param_pieces(module: nn.Module, prefix: str, source) -> dict:
-    """id(parameter) -> [(source key, element offset, numel)]: the state-dict entries of ``module`` the
-    source holds that are contiguous pieces of one parameter (a fused projection is stored as one entry
-    per segment, each a row range of the fused weight)."""
-    params = {id(p) for p in module.parameters()}
-    pieces: dict = {}
-    for key, t in module.state_dict(prefix=prefix, keep_vars=True).items():
-        if key not in source:
-            continue
-        base = t if id(t) in params else getattr(t, "_base", None)
-        if base is None or id(base) not in params or not t.is_contiguous():
-            continue
-        pieces.setdefault(id(base), []).append((key, t.storage_offset() - base.storage_offset(), t.numel()))
-    return pieces
+class _Param:
+    __slots__ = ("module", "name", "shape", "dtype", "numel", "nbytes", "int8", "offset", "wide_offset", "parts")
 
 
-class _Item:
-    __slots__ = ("module", "attr", "shape", "dtype", "numel", "nbytes", "quant", "off", "raw_off", "pieces")
+class BlockLayout:
+    """One block's streamed parameters in a fixed byte layout, and where each byte comes from.
 
+    ``parts`` of a parameter: (source key, element offset in the parameter, element count), because a
+    checkpoint may store one fused parameter as several entries (the q / k / v rows of a fused
+    projection are views of one weight).  An int8 parameter stores its rows, then its fp32 row scales;
+    ``wide_offset`` is its place in the bf16 scratch it is decoded into.  Parameters the source does not
+    cover (adapters) stay resident."""
 
-class _Group:
-    """The streamed parameters of one block in a fixed byte layout (each item 256-byte aligned; an int8
-    item stores its rows then the fp32 row scales).  Parameters the source does not cover (adapters,
-    for instance) stay resident."""
-
-    def __init__(self, block: nn.Module, prefix: str, source, codec=None, skip=("adaln_proj",)):
-        pieces = _param_pieces(block, prefix, source)
-        self.items, self.resident = [], []
-        off = raw = 0
-        for mname, mod in block.named_modules():
-            if any(mname == s or mname.startswith(s + ".") for s in skip):
+    def __init__(self, block: nn.Module, prefix: str, source, int8: bool = False, skip=("adaln_proj",)):
+        owner = {id(p): (m, n) for m in block.modules() for n, p in m._parameters.items() if p is not None}
+        skipped = {id(p) for s in skip if hasattr(block, s) and getattr(block, s) is not None
+                   for p in getattr(block, s).parameters()}
+        parts: dict = {}
+        for key, t in block.state_dict(prefix=prefix, keep_vars=True).items():
+            base = t if id(t) in owner else t._base
+            if key in source and base is not None and id(base) in owner and t.is_contiguous():
+                parts.setdefault(id(base), []).append((key, t.storage_offset() - base.storage_offset(), t.numel()))
+        self.params, self.resident = [], []
+        cursor = wide = 0
+        for pid, (mod, name) in owner.items():
+            if pid in skipped:
                 continue
-            for pname, p in list(mod._parameters.items()):
-                if p is None:
-                    continue
-                pc = pieces.get(id(p))
-                if pc is None or sum(n for _, _, n in pc) != p.numel():
-                    self.resident.append((mod, pname))
-                    continue
-                it = _Item()
-                it.module, it.attr, it.shape, it.dtype = mod, pname, tuple(p.shape), p.dtype
-                it.numel = p.numel()
-                it.nbytes = p.numel() * p.element_size()
-                it.quant = codec == "int8" and p.dim() == 2 and p.numel() >= 2 ** 16
-                it.off, it.raw_off, it.pieces = off, raw, sorted(pc, key=lambda x: x[1])
-                off += _aligned(p.numel() + 4 * p.shape[0] if it.quant else it.nbytes)
-                raw += _aligned(it.nbytes)
-                self.items.append(it)
-        if not self.items:
-            raise ValueError(f"no parameter of the block under {prefix!r} is in the weight source")
-        self.nbytes, self.raw_bytes = off, raw
+            p = mod._parameters[name]
+            pc = sorted(parts.get(pid, []), key=lambda x: x[1])
+            if sum(n for _, _, n in pc) != p.numel():
+                self.resident.append((mod, name))
+                continue
+            it = _Param()
+            it.module, it.name, it.shape, it.dtype, it.numel = mod, name, tuple(p.shape), p.dtype, p.numel()
+            it.nbytes = p.numel() * p.element_size()
+            it.int8 = bool(int8) and p.dim() == 2 and p.numel() >= 1 << 16
+            it.offset, it.wide_offset, it.parts = cursor, wide, pc
+            cursor += _round_up(it.numel + 4 * it.shape[0] if it.int8 else it.nbytes)
+            wide += _round_up(it.nbytes)
+            self.params.append(it)
+        if not self.params:
+            raise ValueError(f"block {prefix!r}: none of its parameters is in the weight source")
+        self.nbytes, self.wide_bytes = cursor, wide
+        self.int8 = any(it.int8 for it in self.params)
 
-    def read(self, source, flat, quant_device="cpu"):
-        """Fills ``flat`` (uint8, at least ``nbytes``) with this group in its stored layout."""
-        with torch.no_grad():
-            for it in self.items:
-                if it.quant:
-                    w = torch.empty(it.numel, dtype=it.dtype, device=quant_device)
-                    for key, o, n in it.pieces:
-                        w[o:o + n].copy_(source.tensor(key).reshape(-1))
-                    q, s = _quantize_rows(w.view(it.shape))
-                    flat[it.off:it.off + it.numel].view(torch.int8).copy_(q.reshape(-1))
-                    flat[it.off + it.numel:it.off + it.numel + 4 * it.shape[0]].view(torch.float32).copy_(s)
-                else:
-                    dst = flat[it.off:it.off + it.nbytes].view(it.dtype)
-                    for key, o, n in it.pieces:
-                        dst[o:o + n].copy_(source.tensor(key).reshape(-1))
-        return flat
+    def file_extents(self, catalog: SafetensorsCatalog):
+        """[(path, file offset, bytes, layout offset)] when every byte can be read from the shards as stored
+        (no int8 code, stored dtype = parameter dtype), else None."""
+        if self.int8 or not isinstance(catalog, SafetensorsCatalog):
+            return None
+        out = []
+        for it in self.params:
+            esz = it.nbytes // it.numel
+            for key, elem_off, n in it.parts:
+                path, off, nbytes, dtype, _ = catalog.location(key)
+                if dtype != it.dtype or nbytes != n * esz:
+                    return None
+                out.append((path, off, nbytes, it.offset + elem_off * esz))
+        return out
 
-    def bind(self, slot, scratch):
-        for it in self.items:
-            if it.quant:
-                q = slot[it.off:it.off + it.numel].view(torch.int8).view(it.shape)
-                s = slot[it.off + it.numel:it.off + it.numel + 4 * it.shape[0]].view(torch.float32)
-                w = scratch[it.raw_off:it.raw_off + it.nbytes].view(it.dtype).view(it.shape)
-                w.copy_(q.float().mul_(s[:, None]))
+    @torch.no_grad()
+    def pack(self, source, out: torch.Tensor, work_device="cpu") -> torch.Tensor:
+        """Writes the layout into ``out`` (uint8, at least ``nbytes``); int8 coding runs on ``work_device``."""
+        for it in self.params:
+            if it.int8:
+                w = torch.empty(it.numel, dtype=it.dtype, device=work_device)
+                for key, o, n in it.parts:
+                    w[o:o + n].copy_(source.tensor(key).reshape(-1))
+                q, scale = int8_rows(w.view(it.shape))
+                out[it.offset:it.offset + it.numel].view(torch.int8).copy_(q.reshape(-1))
+                out[it.offset + it.numel:it.offset + it.numel + 4 * it.shape[0]].view(torch.float32).copy_(scale)
             else:
-                w = slot[it.off:it.off + it.nbytes].view(it.dtype).view(it.shape)
-            it.module._parameters[it.attr] = nn.Parameter(w, requires_grad=False)
+                dst = out[it.offset:it.offset + it.nbytes].view(it.dtype)
+                for key, o, n in it.parts:
+                    dst[o:o + n].copy_(source.tensor(key).reshape(-1))
+        return out
 
-    def unbind(self):
-        for it in self.items:
-            it.module._parameters[it.attr] = nn.Parameter(torch.empty(it.shape, dtype=it.dtype, device="meta"),
+    def attach(self, slot: torch.Tensor, wide: torch.Tensor | None):
+        """Points the block's parameters at their bytes in ``slot`` (int8 ones decoded into ``wide``)."""
+        for it in self.params:
+            if it.int8:
+                q = slot[it.offset:it.offset + it.numel].view(torch.int8).view(it.shape)
+                scale = slot[it.offset + it.numel:it.offset + it.numel + 4 * it.shape[0]].view(torch.float32)
+                w = wide[it.wide_offset:it.wide_offset + it.nbytes].view(it.dtype).view(it.shape)
+                w.copy_(q.float().mul_(scale.unsqueeze(1)))
+            else:
+                w = slot[it.offset:it.offset + it.nbytes].view(it.dtype).view(it.shape)
+            it.module._parameters[it.name] = nn.Parameter(w, requires_grad=False)
+
+    def detach(self):
+        for it in self.params:
+            it.module._parameters[it.name] = nn.Parameter(torch.empty(it.shape, dtype=it.dtype, device="meta"),
                                                           requires_grad=False)
 
 
 # --------------------------------------------------------------------------------------------- streamer
 
 
-class BlockStreamer:
-    """Streams the parameters of ``blocks`` through two device slots, one block ahead of compute.
+class LayerStreamer:
+    """Streams the parameters of ``blocks`` through ``slots`` device buffers in the blocks' order.
 
-    ``source``/``prefixes``: where each block's weights come from (default: the blocks' own weights,
-    which must then be real host tensors).  ``cache_in_ram``: pinned host copies made once, else read
-    from the source on every pass through two pinned staging buffers.  ``codec="int8"`` without
-    ``cache_in_ram`` needs ``cache_dir`` for the quantised copy."""
+    ``source`` / ``prefixes``: where each block's weights come from (default: the blocks' own weights,
+    which must then be real host tensors).  ``cache_in_ram``: pinned host copies made once; otherwise
+    every pass reads the shards (or the int8 cache directory) through two pinned staging buffers, so
+    host memory holds two blocks.  ``codec="int8"`` without ``cache_in_ram`` needs ``cache_dir``."""
 
     def __init__(self, blocks, device, codec=None, source=None, prefixes=None, cache_in_ram=True, cache_dir=None,
-                 log=None):
+                 slots: int = 2, timeout_s: float = 600.0, log=None):
+        from .. import ops
+
         self.blocks = list(blocks)
         if len(self.blocks) < 2:
-            raise ValueError("need at least two streamed blocks")
+            raise ValueError("layer streaming needs at least two blocks")
         if codec not in (None, "int8"):
-            raise ValueError(f"unknown weight codec {codec!r}")
-        if codec is not None and not cache_in_ram and cache_dir is None:
-            raise ValueError("int8 weights streamed from disk need a cache_dir for the quantised copy")
+            raise ValueError(f"weight codec must be None or 'int8', not {codec!r}")
+        if codec and not cache_in_ram and cache_dir is None:
+            raise ValueError("int8 weights read from disk on every pass are read from a cache directory of the "
+                             "coded weights: pass cache_dir (or cache_in_ram=True)")
         self.device = torch.device(device)
         if self.device.type == "cuda" and self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
@@ -269,164 +294,130 @@ class BlockStreamer:
         self.codec = codec
         if source is None:
             if any(p.device.type == "meta" for b in self.blocks for p in b.parameters()):
-                raise ValueError("blocks on the meta device need a weight source (ShardIndex)")
-            sources = [StateSource(b.state_dict()) for b in self.blocks]
+                raise ValueError("blocks whose weights are on the meta device need a weight source "
+                                 "(a SafetensorsCatalog of the checkpoint)")
+            sources = [_DictSource(b.state_dict()) for b in self.blocks]
             prefixes = [""] * len(self.blocks)
         else:
             sources = [source] * len(self.blocks)
             prefixes = list(prefixes)
-        self.groups = [_Group(b, p, s, codec) for b, p, s in zip(self.blocks, prefixes, sources)]
-        for b, g in zip(self.blocks, self.groups):  # adapters, norm statistics, masks stay resident
-            for mod, name in g.resident:
+        self.layouts = [BlockLayout(b, p, s, int8=codec == "int8") for b, p, s in zip(self.blocks, prefixes, sources)]
+        for b, lay in zip(self.blocks, self.layouts):  # adapters and buffers stay on the device
+            for mod, name in lay.resident:
                 p = mod._parameters[name]
                 if p.device.type == "meta":
-                    raise ValueError(f"{type(mod).__name__}.{name} is neither in the weight source nor loaded")
+                    raise ValueError(f"{type(mod).__name__}.{name}: not in the weight source and never loaded")
                 mod._parameters[name] = nn.Parameter(p.detach().to(self.device), requires_grad=False)
             _buffers_to(b, self.device)
-        slot_bytes = max(g.nbytes for g in self.groups)
-        self.bytes_per_pass = sum(g.nbytes for g in self.groups)
-        self.sources, self.host, self.staging, self.cache_files = sources, None, None, None
+        slot_bytes = max(lay.nbytes for lay in self.layouts)
+        self.bytes_per_pass = sum(lay.nbytes for lay in self.layouts)
+        self.host = None       # pinned RAM copies (cache_in_ram)
+        self.staging = []      # pinned staging buffers (groups read from files)
+        self.engine = ops.ext().H2DStreamer  # fails loudly without the native extension
+        extents = [None] * len(self.layouts)
         if cache_in_ram:
             self.host = []
-            for i, g in enumerate(self.groups):
-                self.host.append(g.read(sources[i], self._host_buffer(g.nbytes), self.device))
+            for i, lay in enumerate(self.layouts):
+                self.host.append(lay.pack(sources[i], self._host_bytes(lay.nbytes), self.device))
                 if log and (i + 1) % 10 == 0:
-                    log(f"cached {i + 1}/{len(self.groups)} blocks in host memory")
-            self.sources = None  # the in-memory weights can go
+                    log(f"{i + 1} of {len(self.layouts)} blocks copied to pinned host memory")
+        elif codec:
+            files = self._coded_cache(Path(cache_dir).expanduser(), sources, log)
+            extents = [[(str(f), 0, lay.nbytes, 0)] for f, lay in zip(files, self.layouts)]
         else:
-            self.staging = [self._host_buffer(slot_bytes) for _ in range(2)]
-            if codec is not None:
-                self.cache_files = self._disk_cache(Path(cache_dir).expanduser(), sources, log)
-        for g in self.groups:
-            g.unbind()
-        self.slots = [torch.empty(slot_bytes, dtype=torch.uint8, device=self.device) for _ in range(2)]
-        self.scratch = (torch.empty(max(g.raw_bytes for g in self.groups), dtype=torch.uint8, device=self.device)
-                        if codec else None)
-        self.stream = torch.cuda.Stream(device=self.device) if self.cuda else None
-        self.compute_done = [torch.cuda.Event() for _ in range(2)] if self.cuda else [None, None]
-        self.staged = [None, None]  # per staging buffer: the event of the copy that last read it
-        # the k-th requested group goes to slot k % 2 (groups are consumed in request order), so with an
-        # odd block count the wrap-around from the last block to the first still alternates slots
-        self.bound_slot = [0] * len(self.blocks)
-        self.ready: dict = {}
-        self.cond = threading.Condition()
-        self.requests: queue.Queue = queue.Queue()
-        self.error = None
+            for i, lay in enumerate(self.layouts):
+                extents[i] = lay.file_extents(sources[i])
+                if extents[i] is None:
+                    raise ValueError(f"block {i}: its stored tensors do not match the model's dtypes, so they "
+                                     f"cannot stream as stored; use cache_in_ram=True")
+        for lay in self.layouts:
+            lay.detach()
+        self.slots = [torch.empty(slot_bytes, dtype=torch.uint8, device=self.device) for _ in range(int(slots))]
+        self.wide = (torch.empty(max(lay.wide_bytes for lay in self.layouts), dtype=torch.uint8, device=self.device)
+                     if codec else None)
+        if self.host is None:
+            self.staging = [self._host_bytes(slot_bytes) for _ in range(2)]
+        self.native = self.engine([t.data_ptr() for t in self.slots], slot_bytes,
+                                  self.device.index if self.cuda else -1,
+                                  [t.data_ptr() for t in self.staging], slot_bytes if self.staging else 0,
+                                  float(timeout_s))
+        file_ids: dict = {}
+        for i, lay in enumerate(self.layouts):
+            if self.host is not None:
+                self.native.add_ram_group(self.host[i].data_ptr(), lay.nbytes)
+            else:
+                ext = []
+                for path, off, n, dst in extents[i]:
+                    if path not in file_ids:
+                        file_ids[str(path)] = self.native.add_file(str(path))
+                    ext.append([file_ids[str(path)], int(off), int(n), int(dst)])
+                self.native.add_file_group(ext, lay.nbytes)
         self.hooks = []
         for i, b in enumerate(self.blocks):
-            self.hooks.append(b.register_forward_pre_hook(self._pre(i)))
-            self.hooks.append(b.register_forward_hook(self._post(i)))
-        self.worker = threading.Thread(target=self._run, daemon=True)
-        self.worker.start()
-        self.requests.put(0)
-        self.requests.put(1)
+            self.hooks.append(b.register_forward_pre_hook(self._before(i)))
+            self.hooks.append(b.register_forward_hook(self._after(i)))
+        self.native.start(list(range(len(self.blocks))))
 
-    def _host_buffer(self, n):
+    # the int8 cache: one file per block, reused while the shards' fingerprint is unchanged
+    def _coded_cache(self, cache_dir: Path, sources, log):
+        cache_dir.mkdir(parents=True, exist_ok=True)
+        catalog = sources[0] if isinstance(sources[0], SafetensorsCatalog) else None
+        stamp = {"format": "dmad_b200 int8 rows v1", "blocks": [lay.nbytes for lay in self.layouts],
+                 "source": catalog.fingerprint() if catalog else None}
+        files = [cache_dir / f"block{i:04d}.i8" for i in range(len(self.layouts))]
+        index = cache_dir / "index.json"
+        reuse = (catalog is not None and index.is_file() and json.loads(index.read_text()) == stamp
+                 and all(f.is_file() and f.stat().st_size == lay.nbytes for f, lay in zip(files, self.layouts)))
+        if not reuse:
+            if log:
+                log(f"coding {len(files)} blocks to int8 in {cache_dir}; later runs reuse them")
+            index.unlink(missing_ok=True)
+            for i, (f, lay) in enumerate(zip(files, self.layouts)):
+                buf = lay.pack(sources[i], torch.zeros(lay.nbytes, dtype=torch.uint8), self.device)
+                tmp = f.with_suffix(".tmp")
+                with open(tmp, "wb") as h:
+                    h.write(buf.numpy().tobytes())
+                os.replace(tmp, f)
+            index.write_text(json.dumps(stamp))
+        return files
+
+    def _host_bytes(self, n):
         t = torch.empty(n, dtype=torch.uint8)
         return t.pin_memory() if self.cuda else t
 
-    def _disk_cache(self, cache_dir, sources, log):
-        """One file per group in the stored layout, written once and validated against a manifest of the
-        shards it was built from (an in-memory source has no shards and is rewritten every time)."""
-        cache_dir.mkdir(parents=True, exist_ok=True)
-        shard_files = sources[0].files()
-        manifest = {"codec": self.codec, "groups": [g.nbytes for g in self.groups],
-                    "shards": [[p.name, p.stat().st_size] for p in shard_files]}
-        files = [cache_dir / f"group_{i:03d}.bin" for i in range(len(self.groups))]
-        mpath = cache_dir / "manifest.json"
-        valid = (bool(shard_files) and mpath.is_file() and json.load(open(mpath)) == manifest
-                 and all(f.is_file() and f.stat().st_size == g.nbytes for f, g in zip(files, self.groups)))
-        if not valid:
-            if log:
-                log(f"writing the {self.codec} copy of the streamed weights to {cache_dir} (once)")
-            if mpath.exists():
-                mpath.unlink()
-            for i, (f, g) in enumerate(zip(files, self.groups)):
-                flat = g.read(sources[i], torch.zeros(g.nbytes, dtype=torch.uint8), self.device)
-                with open(f, "wb") as h:
-                    h.write(memoryview(flat.numpy()))
-            json.dump(manifest, open(mpath, "w"))
-        return files
+    def _stream_handle(self):
+        return torch.cuda.current_stream(self.device).cuda_stream if self.cuda else 0
 
-    def _fill_staging(self, g, buf):
-        if self.cache_files is not None:
-            with open(self.cache_files[g], "rb") as h:
-                h.readinto(memoryview(buf.numpy())[:self.groups[g].nbytes])
-        else:
-            self.groups[g].read(self.sources[g], buf, self.device)
-        return buf
-
-    def _run(self):
-        if self.cuda:
-            torch.cuda.set_device(self.device)
-        seq = 0
-        try:
-            while True:
-                g = self.requests.get()
-                if g is None:
-                    return
-                slot = seq % 2
-                seq += 1
-                n = self.groups[g].nbytes
-                if self.host is not None:
-                    src = self.host[g]
-                else:
-                    if self.staged[slot] is not None:  # the copy that last read this staging buffer
-                        self.staged[slot].synchronize()
-                    src = self._fill_staging(g, self.staging[slot])
-                ev = None
-                if self.cuda:
-                    with torch.cuda.stream(self.stream):
-                        self.stream.wait_event(self.compute_done[slot])
-                        self.slots[slot][:n].copy_(src[:n], non_blocking=True)
-                        ev = torch.cuda.Event()
-                        ev.record(self.stream)
-                    if self.host is None:
-                        self.staged[slot] = ev
-                else:
-                    self.slots[slot][:n].copy_(src[:n])
-                with self.cond:
-                    self.ready[g] = (ev, slot)
-                    self.cond.notify_all()
-        except Exception as e:  # surfaced in the compute thread instead of hanging it
-            with self.cond:
-                self.error = e
-                self.cond.notify_all()
-
-    def _pre(self, i):
+    def _before(self, i):
         def hook(module, args):
-            with self.cond:
-                while i not in self.ready and self.error is None:
-                    self.cond.wait(timeout=60.0)
-                    if i not in self.ready and self.error is None and not self.worker.is_alive():
-                        self.error = RuntimeError("streaming worker died")
-                if self.error is not None:
-                    raise RuntimeError("weight streaming failed") from self.error
-                ev, slot = self.ready.pop(i)
-            if ev is not None:
-                torch.cuda.current_stream(self.device).wait_event(ev)
-            self.bound_slot[i] = slot
-            self.groups[i].bind(self.slots[slot], self.scratch)
+            slot, group = self.native.acquire(self._stream_handle())
+            if group != i:
+                raise RuntimeError(f"layer streaming: block {i} ran where the schedule expected block {group} "
+                                   f"(blocks must run in order, every pass)")
+            self.layouts[i].attach(self.slots[slot], self.wide)
 
         return hook
 
-    def _post(self, i):
+    def _after(self, i):
         def hook(module, args, output):
-            if self.cuda:
-                self.compute_done[self.bound_slot[i]].record(torch.cuda.current_stream(self.device))
-            self.groups[i].unbind()
-            self.requests.put((i + 2) % len(self.groups))
+            self.layouts[i].detach()
+            self.native.release(self._stream_handle())
 
         return hook
+
+    def stats(self) -> dict:
+        return dict(self.native.stats())
 
     def close(self):
         for h in self.hooks:
             h.remove()
-        self.requests.put(None)
-        self.worker.join(timeout=60)
+        self.hooks = []
+        if self.native is not None:
+            self.native.close()
         if self.cuda:
             torch.cuda.synchronize(self.device)
-        self.slots = self.scratch = self.host = self.staging = self.sources = None
+        self.native = None
+        self.slots = self.wide = self.host = self.staging = None
 
 
 # ------------------------------------------------------------------------------------ row-chunked block
@@ -486,7 +477,7 @@ _H3_RESIDENT = ("proj_in", "audio_proj_in", "context_embedder", "time_embedder",
 
 
 def build_streamed_h3(model_dir, device, dtype=torch.bfloat16):
-    """(H3Model, ShardIndex) for a transformer directory: the resident modules loaded on ``device``,
+    """(H3Model, SafetensorsCatalog) for a transformer directory: the resident modules loaded on ``device``,
     the blocks left on the meta device for ``LowMemH3`` to stream from the shards."""
     from ..models.h3 import H3Model
     from .h3 import config_from_transformer_dir, resolve_transformer_dir
@@ -494,7 +485,7 @@ def build_streamed_h3(model_dir, device, dtype=torch.bfloat16):
     root = resolve_transformer_dir(model_dir)
     with torch.device("meta"):
         model = H3Model(config_from_transformer_dir(root)).to(dtype)
-    source = ShardIndex(root)
+    source = SafetensorsCatalog(root)
     for name in _H3_RESIDENT:
         load_resident(getattr(model, name), name + ".", source, device)
     return model.eval().requires_grad_(False), source
@@ -510,7 +501,7 @@ class LowMemH3:
 
     ``timesteps_per_step``: the distinct-timestep tensors the sampler will pass at each step, so the
     adaLN tables are built before sampling and the projections dropped.  Without ``source`` the model
-    holds real weights in host memory; with a ``ShardIndex`` (``build_streamed_h3``) its blocks are on
+    holds real weights in host memory; with a ``SafetensorsCatalog`` (``build_streamed_h3``) its blocks are on
     the meta device and read from the shards (adaLN projections one block at a time)."""
 
     def __init__(self, model, device, timesteps_per_step, codec=None, source=None, cache_in_ram=True, cache_dir=None,
@@ -538,7 +529,7 @@ class LowMemH3:
             for b in blocks:
                 b.forward = chunked_block_forward(b, int(chunk_rows))
         prefixes = [f"transformer_blocks.{i}." for i in range(len(blocks))] if source is not None else None
-        self.streamer = BlockStreamer(blocks, self.device, codec=codec, source=source, prefixes=prefixes,
+        self.streamer = LayerStreamer(blocks, self.device, codec=codec, source=source, prefixes=prefixes,
                                       cache_in_ram=cache_in_ram, cache_dir=cache_dir, log=log)
         self._text_cache = []
 
@@ -591,12 +582,12 @@ class LowMemTextEncoder:
         self.lm.layers = nn.ModuleList(list(self.lm.layers)[:self.layer])
         self.lm.norm = nn.Identity()
         _buffers_to(self.model, self.device)
-        self.source = ShardIndex(tdir)
+        self.source = SafetensorsCatalog(tdir)
         names = {id(m): n for n, m in model.named_modules()}
         lm_prefix = names[id(self.lm)] + "."
         emb = self.lm.embed_tokens
         load_resident(emb, lm_prefix + "embed_tokens.", self.source, self.device)
-        self.streamer = BlockStreamer(list(self.lm.layers), self.device, source=self.source,
+        self.streamer = LayerStreamer(list(self.lm.layers), self.device, source=self.source,
                                       prefixes=[f"{lm_prefix}layers.{i}." for i in range(len(self.lm.layers))],
                                       cache_in_ram=cache_in_ram, log=log)
         self.tokenizer = tokenizer or AutoTokenizer.from_pretrained(str(root / "tokenizer"), local_files_only=True)

@@ -1,7 +1,8 @@
-"""Low-VRAM streaming on a CPU device (synchronous copies): the streamed rollout equals the resident one,
-weights stream from memory-mapped safetensors shards or from an int8 disk cache validated by a manifest,
-row-chunked blocks match the full-width forward, and the streamed text encoder equals the resident
-conditioner (dmad_h3/lowmem.py:41-76, 176-331, 337-393, 416-461)."""
+"""Low-VRAM streaming on a CPU device (the native engine in host mode: synchronous copies, the same
+schedule): the streamed rollout equals the resident one, weights stream from byte ranges of the
+safetensors shards or from an int8 cache directory checked against the shards' fingerprint, row-chunked
+blocks match the full-width forward, and the streamed text encoder equals the resident conditioner
+(parity: dmad_h3/lowmem.py, the --low-vram path)."""
 import copy
 import json
 import os
@@ -11,7 +12,7 @@ import torch
 
 from dmad_b200.inference.h3 import (H3Geometry, build_packed_sequence, build_row_timesteps, latent_shape_of,
                                     load_transformer, rollout, sigma_grid)
-from dmad_b200.inference.lowmem import BlockStreamer, LowMemH3, build_streamed_h3, chunked_block_forward
+from dmad_b200.inference.lowmem import LayerStreamer, LowMemH3, build_streamed_h3, chunked_block_forward
 from dmad_b200.models.h3 import H3Config, H3Model
 
 safetensors = pytest.importorskip("safetensors.torch")
@@ -85,7 +86,11 @@ def test_streamed_from_shards_equals_resident(tmp_path, in_ram):
     assert (lm.streamer.host is None) == (not in_ram)
     out = _run(lm.model, case, lm)
     out2 = _run(lm.model, case, lm)  # a second pass re-reads the shards through the staging buffers
+    st = lm.streamer.stats()
     lm.close()
+    # every block evaluation copied one block's layout; read from the shards when not cached in RAM
+    assert st["copies"] >= 2 * 2 * CFG["num_layers"]
+    assert (st["bytes_read_from_files"] > 0) == (not in_ram)
     assert torch.equal(out[0], ref[0]) and torch.equal(out[1], ref[1])
     assert torch.equal(out2[0], ref[0])
 
@@ -100,13 +105,13 @@ def test_int8_disk_cache_manifest(tmp_path):
     with pytest.raises(ValueError):
         LowMemH3(copy.deepcopy(model), "cpu", case[5], codec="int8", source=source, cache_in_ram=False)
     lm = LowMemH3(model, "cpu", case[5], codec="int8", source=source, cache_in_ram=False, cache_dir=cache)
-    assert any(it.quant for g in lm.streamer.groups for it in g.items)
+    assert any(it.int8 for lay in lm.streamer.layouts for it in lay.params)
     out = _run(lm.model, case, lm)
     lm.close()
     rel = (out[0] - ref[0]).norm() / ref[0].norm()
     assert 0 < rel < 0.05  # quantised weights: close, not equal
-    man = json.load(open(cache / "manifest.json"))
-    assert man["codec"] == "int8" and len(man["groups"]) == CFG["num_layers"] and len(man["shards"]) == 2
+    index = json.load(open(cache / "index.json"))
+    assert len(index["blocks"]) == CFG["num_layers"] and len(index["source"]) == 2
     stamp = {f: os.stat(cache / f).st_mtime_ns for f in os.listdir(cache)}
     model, source = build_streamed_h3(tmp_path, "cpu", dtype=torch.float32)
     lm = LowMemH3(model, "cpu", case[5], codec="int8", source=source, cache_in_ram=False, cache_dir=cache)
@@ -153,7 +158,7 @@ def test_streamer_rejects_unloaded_parameters():
     with torch.device("meta"):
         m = H3Model(H3Config(**CFG))
     with pytest.raises(ValueError):
-        BlockStreamer(list(m.transformer_blocks), "cpu")
+        LayerStreamer(list(m.transformer_blocks), "cpu")
 
 
 transformers = pytest.importorskip("transformers")
