@@ -315,21 +315,22 @@ class LayerStreamer:
         self.staging = []      # pinned staging buffers (groups read from files)
         self.engine = ops.ext().H2DStreamer  # fails loudly without the native extension
         extents = [None] * len(self.layouts)
+        if source is None:
+            cache_in_ram = True  # the weights are in host memory already
+        if not cache_in_ram and not codec:
+            extents = [lay.file_extents(src) for lay, src in zip(self.layouts, sources)]
         if cache_in_ram:
             self.host = []
             for i, lay in enumerate(self.layouts):
                 self.host.append(lay.pack(sources[i], self._host_bytes(lay.nbytes), self.device))
                 if log and (i + 1) % 10 == 0:
                     log(f"{i + 1} of {len(self.layouts)} blocks copied to pinned host memory")
-        elif codec:
-            files = self._coded_cache(Path(cache_dir).expanduser(), sources, log)
+        elif codec or any(e is None for e in extents):
+            # int8 code, or stored dtypes that differ from the model's: a converted copy on disk, made once
+            kind = codec or "converted"
+            where = Path(cache_dir).expanduser() if cache_dir else default_cache_dir(sources[0].directory, kind)
+            files = self._disk_copy(where, kind, sources, log)
             extents = [[(str(f), 0, lay.nbytes, 0)] for f, lay in zip(files, self.layouts)]
-        else:
-            for i, lay in enumerate(self.layouts):
-                extents[i] = lay.file_extents(sources[i])
-                if extents[i] is None:
-                    raise ValueError(f"block {i}: its stored tensors do not match the model's dtypes, so they "
-                                     f"cannot stream as stored; use cache_in_ram=True")
         for lay in self.layouts:
             lay.detach()
         self.slots = [torch.empty(slot_bytes, dtype=torch.uint8, device=self.device) for _ in range(int(slots))]
@@ -358,19 +359,21 @@ class LayerStreamer:
             self.hooks.append(b.register_forward_hook(self._after(i)))
         self.native.start(list(range(len(self.blocks))))
 
-    # the int8 cache: one file per block, reused while the shards' fingerprint is unchanged
-    def _coded_cache(self, cache_dir: Path, sources, log):
+    # a copy of the blocks in their streamed layout (int8-coded or dtype-converted): one file per block,
+    # reused while the shards' fingerprint is unchanged
+    def _disk_copy(self, cache_dir: Path, kind: str, sources, log):
         cache_dir.mkdir(parents=True, exist_ok=True)
         catalog = sources[0] if isinstance(sources[0], SafetensorsCatalog) else None
-        stamp = {"format": "dmad_b200 int8 rows v1", "blocks": [lay.nbytes for lay in self.layouts],
+        stamp = {"format": f"dmad_b200 {kind} layout v1", "blocks": [lay.nbytes for lay in self.layouts],
+                 "dtypes": sorted({str(it.dtype) for lay in self.layouts for it in lay.params}),
                  "source": catalog.fingerprint() if catalog else None}
-        files = [cache_dir / f"block{i:04d}.i8" for i in range(len(self.layouts))]
+        files = [cache_dir / f"block{i:04d}.bin" for i in range(len(self.layouts))]
         index = cache_dir / "index.json"
         reuse = (catalog is not None and index.is_file() and json.loads(index.read_text()) == stamp
                  and all(f.is_file() and f.stat().st_size == lay.nbytes for f, lay in zip(files, self.layouts)))
         if not reuse:
             if log:
-                log(f"coding {len(files)} blocks to int8 in {cache_dir}; later runs reuse them")
+                log(f"writing the {kind} layout of {len(files)} blocks to {cache_dir}; later runs reuse it")
             index.unlink(missing_ok=True)
             for i, (f, lay) in enumerate(zip(files, self.layouts)):
                 buf = lay.pack(sources[i], torch.zeros(lay.nbytes, dtype=torch.uint8), self.device)
