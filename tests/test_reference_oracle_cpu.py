@@ -2,14 +2,15 @@
 random weights, loaded into this package's modules through the shared state-dict layouts, give the same
 outputs in fp32 -- the Wan DiT (uniform and per-frame timesteps), the causal video VAE (encode and decode),
 the umT5 encoder with padding -- and the reference's block-mask predicates equal this package's key-range
-rectangles.  Skipped when the reference is not installed."""
+rectangles.  The reference comes from baseline/_ref or the reference checkout; the tests fail when
+neither is present (tests/_reference_src.py)."""
 import os
 import sys
 
 import pytest
 import torch
 
-REF = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+from _reference_src import wan_tree
 
 
 def _stub_io_deps():
@@ -35,14 +36,14 @@ def _stub_io_deps():
 
 @pytest.fixture(scope="module")
 def ref_wan():
-    if not os.path.isdir(os.path.join(REF, "rcm")):
-        pytest.skip("reference not installed")
-    sys.path.insert(0, REF)
+    REF = wan_tree()
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
     try:
         import rcm.utils.rope as ref_rope
         from rcm.networks.wan2pt1 import WanModel
     except Exception as e:  # pragma: no cover - depends on the installed reference
-        pytest.skip(f"reference Wan network does not import here: {e}")
+        pytest.fail(f"reference Wan network does not import: {e}")
     # the reference rotates with flash-attn's GPU kernel when that package imports; on CPU it must take
     # its own PyTorch fallback (rope.py:65-70)
     ref_rope.flash_apply_rotary_emb = None
@@ -82,14 +83,14 @@ def test_wan_forward_matches_reference(ref_wan, per_frame):
 def test_wan_vae_matches_reference():
     """The reference's chunked causal VAE (first frame, then 4-frame chunks with feature caches; one
     latent frame at a time when decoding) against this package's whole-clip causal VAE, same weights."""
-    if not os.path.isdir(os.path.join(REF, "rcm")):
-        pytest.skip("reference not installed")
-    sys.path.insert(0, REF)
+    REF = wan_tree()
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
     _stub_io_deps()
     try:
         from rcm.tokenizers.wan2pt1 import WanVAE_
     except Exception as e:  # pragma: no cover
-        pytest.skip(f"reference VAE does not import here: {e}")
+        pytest.fail(f"reference VAE does not import: {e}")
     from dmad_b200.models.wan_vae import WanVAEModel
 
     torch.manual_seed(0)
@@ -117,16 +118,16 @@ def test_wan_vae_matches_reference():
 def test_umt5_encoder_matches_reference():
     """The reference's umT5 encoder (per-layer relative position buckets, shared_pos=False as umT5 uses)
     against this package's encoder with the same weights, with a padding mask."""
-    if not os.path.isdir(os.path.join(REF, "rcm")):
-        pytest.skip("reference not installed")
-    sys.path.insert(0, REF)
+    REF = wan_tree()
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
     _stub_io_deps()
     saved = torch.cuda.current_device
     torch.cuda.current_device = lambda: 0  # a default argument of the reference's encoder wrapper (umt5.py:485)
     try:
         from rcm.utils.umt5 import T5Encoder
     except Exception as e:  # pragma: no cover
-        pytest.skip(f"reference umT5 does not import here: {e}")
+        pytest.fail(f"reference umT5 does not import: {e}")
     finally:
         torch.cuda.current_device = saved
     from dmad_b200.models.umt5 import UMT5Config, UMT5Encoder
@@ -152,9 +153,9 @@ def test_block_masks_match_reference_predicate():
     (blockmask.py ``_make_mask_fn``) for block-causal (windows, sinks, query offsets) and teacher forcing."""
     import itertools
 
-    if not os.path.isdir(os.path.join(REF, "rcm")):
-        pytest.skip("reference not installed")
-    sys.path.insert(0, REF)
+    REF = wan_tree()
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
     try:
         from rcm.utils import blockmask as rb
     except Exception as e:  # pragma: no cover
@@ -192,13 +193,13 @@ def test_block_masks_match_reference_predicate():
 def test_kv_cache_matches_reference():
     """The same sequence of cache operations on the reference's KVCache and this package's: appends,
     prefixes by chunk count, transient writes and compaction leave identical contents."""
-    if not os.path.isdir(os.path.join(REF, "rcm")):
-        pytest.skip("reference not installed")
-    sys.path.insert(0, REF)
+    REF = wan_tree()
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
     try:
         from rcm.utils.kv_cache import KVCache as RefKV
     except Exception as e:  # pragma: no cover
-        pytest.skip(f"reference KV cache does not import here: {e}")
+        pytest.fail(f"reference KV cache does not import: {e}")
     from dmad_b200.models.kv_cache import KVCache
 
     g = torch.Generator().manual_seed(0)
@@ -228,9 +229,9 @@ def test_teacher_samplers_match_reference(kind, order, smax):
     """Euler and UniPC (bh2) trajectories of a fixed velocity field through the reference's samplers and
     this package's, 20 shifted steps.  (Third order starts below sigma = 1: from sigma = 1 the log-SNR of
     the first step is infinite and the third-order corrector of the reference, like this one, is NaN.)"""
-    if not os.path.isdir(os.path.join(REF, "rcm")):
-        pytest.skip("reference not installed")
-    sys.path.insert(0, REF)
+    REF = wan_tree()
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
     try:
         from rcm.samplers.euler import FlowEulerSampler as RefEuler
         from rcm.samplers.unipc import FlowUniPCMultistepSampler as RefUniPC
@@ -260,9 +261,9 @@ def test_teacher_samplers_match_reference(kind, order, smax):
 
 def test_lr_schedules_match_reference():
     """The Wan stack's LambdaLinear / LambdaWarmUpCosine multipliers (two cycles) against this package's."""
-    if not os.path.isdir(os.path.join(REF, "rcm")):
-        pytest.skip("reference not installed")
-    sys.path.insert(0, REF)
+    REF = wan_tree()
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
     try:
         from rcm.utils.lr_scheduler import LambdaLinearScheduler, LambdaWarmUpCosineScheduler
     except Exception as e:  # pragma: no cover
@@ -282,9 +283,9 @@ def test_lr_schedules_match_reference():
 def test_time_utilities_match_reference():
     """RF / TrigFlow time conversions, the log-normal and shifted-uniform samplers (same seed, same draws
     and inverse CDFs) and the rectified-flow TrigFlow scaling."""
-    if not os.path.isdir(os.path.join(REF, "rcm")):
-        pytest.skip("reference not installed")
-    sys.path.insert(0, REF)
+    REF = wan_tree()
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
     try:
         from rcm.utils import timestep_utils as rt
         from rcm.utils.denoiser_scaling import RectifiedFlow_TrigFlowWrapper
