@@ -311,3 +311,43 @@ def test_time_utilities_match_reference():
     for a, b in zip(ot.TrigFlowScaling(t_scaling_factor=1000.0)(trig),
                     RectifiedFlow_TrigFlowWrapper(t_scaling_factor=1000.0)(trig)):
         torch.testing.assert_close(a, b)
+
+
+def test_edm_unet_matches_reference():
+    """The config-1 EDM U-Net against the reference's own EDMPrecond / DhariwalUNet
+    (train/image/third_party/edm/training/networks.py), weights moved through the shared state dict:
+    the denoised output and the critic's bottleneck features agree in fp32."""
+    from _reference_src import image_tree
+
+    from dmad_b200.models.edm import config1_unet
+
+    tree = image_tree()
+    for p in (tree, os.path.join(tree, "third_party", "edm")):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    from third_party.edm.training.networks import EDMPrecond as RefPrecond
+
+    torch.manual_seed(0)
+    ref = RefPrecond(img_resolution=64, img_channels=3, label_dim=1000, use_fp16=False, sigma_min=0,
+                     sigma_max=float("inf"), sigma_data=0.5, model_type="DhariwalUNet", augment_dim=0,
+                     model_channels=64, channel_mult=[1, 2, 2], channel_mult_emb=4, num_blocks=1,
+                     attn_resolutions=[16], dropout=0.0, label_dropout=0)
+    del ref.model.map_augment
+    ref.model.map_augment = None
+    with torch.no_grad():
+        for p in ref.parameters():  # the reference zero-initialises its output layers; make every part count
+            p.add_(torch.randn_like(p) * 0.02)
+    ours = config1_unet(1000)
+    missing, unexpected = ours.load_state_dict(ref.state_dict(), strict=False)
+    # the reference stores its fixed [1, 1] resampling filter as a buffer; here it is a constant
+    assert not missing and all(k.endswith("resample_filter") for k in unexpected), (missing, unexpected)
+    ref.eval(), ours.eval()
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(2, 3, 64, 64, generator=g)
+    sigma = torch.tensor([0.3, 11.0])
+    labels = torch.eye(1000)[torch.tensor([5, 999])]
+    with torch.no_grad():
+        torch.testing.assert_close(ours(x, sigma, labels), ref(x, sigma, labels), rtol=2e-4, atol=2e-4)
+        rb = ref(x, sigma, labels, return_bottleneck=True)
+        ob = ours(x, sigma, labels, return_bottleneck=True)
+    torch.testing.assert_close(ob, rb, rtol=2e-4, atol=2e-4)
