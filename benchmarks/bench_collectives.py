@@ -96,9 +96,37 @@ def bench_ring(tokens, heads, hd, iters, warmup):
             "nvlink_gb_per_gpu_dir": round(gb, 4), "roofline_ms": round(roof, 4), "frac_of_roofline": round(roof / ms, 3)}
 
 
+def bench_nccl_baselines(n, tokens, heads, hd, iters, warmup):
+    """The NCCL-only paths the fused kernels replace, on the same bytes: reduce-scatter + all-gather of the
+    bf16 gradients / weights (then AdamW would run between them), and the Ulysses all-to-all."""
+    w = dist.get_world_size()
+    g = torch.randn(n, device="cuda", dtype=torch.bfloat16)
+    shard = torch.empty(n // w, device="cuda", dtype=torch.bfloat16)
+    full = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+
+    def rs_ag():
+        dist.reduce_scatter_tensor(shard, g)
+        dist.all_gather_into_tensor(full, shard)
+
+    ms = _time(rs_ag, iters, warmup)
+    gb = 2 * 2 * n * (w - 1) / w / 1e9
+    out = [{"op": "nccl_reduce_scatter+all_gather", "params": n, "world": w, "ms": round(ms, 4),
+            "nvlink_gb_per_gpu_dir": round(gb, 4), "roofline_ms": round(gb / LINK_GBS * 1e3, 4),
+            "frac_of_roofline": round(gb / LINK_GBS * 1e3 / ms, 3)}]
+    R, D = tokens // w, heads * hd
+    src = torch.randn(3 * R * D, device="cuda", dtype=torch.bfloat16)
+    dst = torch.empty_like(src)
+    ms = _time(lambda: dist.all_to_all_single(dst, src), iters, warmup)
+    gb = 3 * R * D * 2 * (w - 1) / w / 1e9
+    out.append({"op": "nccl_all_to_all (Ulysses q/k/v bytes)", "tokens": tokens, "heads": heads, "world": w,
+                "ms": round(ms, 4), "nvlink_gb_per_gpu_dir": round(gb, 4), "roofline_ms": round(gb / LINK_GBS * 1e3, 4),
+                "frac_of_roofline": round(gb / LINK_GBS * 1e3 / ms, 3)})
+    return out
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", default="all", choices=["all", "adamw", "a2a", "ring"])
+    ap.add_argument("--op", default="all", choices=["all", "adamw", "a2a", "ring", "nccl"])
     ap.add_argument("--params", type=int, default=1 << 28)
     ap.add_argument("--tokens", type=int, default=32760)
     ap.add_argument("--heads", type=int, default=40)
@@ -119,6 +147,8 @@ def main(argv=None):
             res.append(bench_a2a(tok, a.heads, 128, a.iters, a.warmup))
         if a.op in ("all", "ring"):
             res.append(bench_ring(tok, a.heads, 128, a.iters, a.warmup))
+        if a.op in ("all", "nccl"):
+            res += bench_nccl_baselines(a.params, tok, a.heads, 128, a.iters, a.warmup)
         from dmad_b200.ops import check_device_status
         torch.cuda.synchronize()
         check_device_status()

@@ -110,7 +110,14 @@ class WanDMAD(nn.Module):
         self.dtype = dtype
         device = torch.device(device) if device is not None else torch.device("cpu")
         torch.manual_seed(seed)
-        teacher = WanModel(cfg.net)
+        if device.type == "cuda":
+            # built on the device in the compute dtype: a 14B net is 28 GB there, and three fp32 host copies
+            # per rank would not fit in host memory
+            with torch.device(device):
+                teacher = WanModel(cfg.net)
+            teacher.to(dtype)
+        else:
+            teacher = WanModel(cfg.net)
         if cfg.teacher_ckpt:
             from ..tools.import_reference_checkpoint import read_pretrained
             res = teacher.load_state_dict(read_pretrained(cfg.teacher_ckpt), strict=False)
