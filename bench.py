@@ -51,6 +51,12 @@ def parse():
     ap.add_argument("--cp-impl", default="fused", choices=["fused", "nccl", "ring", "hybrid"])
     ap.add_argument("--ulysses-size", type=int, default=None, help="hybrid CP: ranks per Ulysses group")
     ap.add_argument("--lora", type=int, default=0, help="LoRA rank of the student (config 3: 128)")
+    ap.add_argument("--cm-loss-scale", type=float, default=None,
+                    help="weight of the sCM consistency term (flash-attention JVP path); default 100 for the 14B "
+                         "config (BASELINE config 3), 0 for the 1.3B DMAD config (the reference's DMAD recipe)")
+    ap.add_argument("--dp-path", default="auto", choices=["auto", "nvls", "p2p"],
+                    help="fused optimiser transport: NVLS multimem or P2P peer loads/stores (auto: P2P up to 2 "
+                         "GPUs, NVLS above, as measured by benchmarks/bench_collectives.py)")
     ap.add_argument("--dp-optimizer", default="sharded", choices=["sharded", "replicated"],
                     help="sharded: fused reduce-scatter/AdamW/all-gather kernel; replicated: NCCL all-reduce baseline")
     return ap.parse_args()
@@ -196,8 +202,14 @@ def main():
         from dmad_b200.models.wan import wan_config
 
         over = {"num_layers": args.layers} if args.layers else {}
-        cfg = WanDMADConfig(net=wan_config(args.model, **over), dp_optimizer=args.dp_optimizer)
+        multicast = {"nvls": True, "p2p": False, "auto": world > 2}[args.dp_path]
+        cfg = WanDMADConfig(net=wan_config(args.model, **over), dp_optimizer=args.dp_optimizer, dp_multicast=multicast)
         cfg.checkpoint_critic_blocks_student_phase = cfg.net.num_layers
+        big = "14b" in args.model.lower()
+        cfg.loss_scale = args.cm_loss_scale if args.cm_loss_scale is not None else (100.0 if big else 0.0)
+        if big:  # the reference's 14B DMAD experiment: critic checkpointed block-wise, lr 1e-6
+            cfg.checkpoint_critic_blocks = cfg.net.num_layers
+            cfg.lr = cfg.critic_lr = 1e-6
         if args.lora:
             cfg.student_lora_rank = args.lora
             cfg.shard_frozen = world > 1
@@ -360,6 +372,7 @@ def main():
                    "latents": f"16x{args.frames}x60x104", "text": "512x4096",
                    "parallelism": f"dp{world // args.cp}" + (f"-cp{args.cp}-{args.cp_impl}" if args.cp > 1 else ""),
                    "student_lora_rank": args.lora or None,
+                   "scm_loss_scale": (None if args.impl == "reference" else trainer.cfg.loss_scale),
                    "step": "1 generator + 1 critic DMAD iteration",
                    "dp_optimizer": _dp_desc(trainer, args),
                    "l2": "flushed (write of a 252 MB buffer) before every timed step; inputs > L2"},
