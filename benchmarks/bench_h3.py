@@ -52,10 +52,16 @@ def _case(args, cfg):
     return geo, shape, lay, vs, as_, pe
 
 
+def sigma_grid_n(steps):
+    from dmad_b200.inference.h3 import sigma_grid
+
+    return sigma_grid(steps, 12.0), sigma_grid(steps, 2.0)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(description="config-5 H3 33B-shaped sampling")
     ap.add_argument("--mode", default="resident", choices=["resident", "cp", "lowvram"])
-    ap.add_argument("--steps", type=int, default=4)
+    ap.add_argument("--steps", default="4", help="comma-separated step counts, each timed (e.g. 4,8)")
     ap.add_argument("--runs", type=int, default=1)
     ap.add_argument("--layers", type=int, default=None, help="debug only: fewer blocks (invalid for the headline)")
     ap.add_argument("--height", type=int, default=768)
@@ -68,6 +74,10 @@ def main(argv=None):
     from dmad_b200.inference.h3 import build_row_timesteps, rollout
     from dmad_b200.models.h3 import H3Config, H3Model
 
+    step_counts = [int(x) for x in str(a.steps).split(",")]
+    a.steps = max(step_counts)
+    if a.mode == "lowvram" and len(step_counts) > 1:
+        raise SystemExit("lowvram precomputes the adaLN tables of one step count: pass one --steps value")
     cfg = H3Config() if a.layers is None else H3Config(num_layers=a.layers)
     cp = None
     if a.mode == "cp":
@@ -129,34 +139,39 @@ def main(argv=None):
         model.eval().requires_grad_(False)
     build_s = time.time() - t_build
 
-    def one():
-        return rollout(model, pe.to(device), lay, shape, geo, vs, as_, 7, device, text_features=text_features,
-                       adaln_tables_per_step=tables)
+    results = []
+    for steps in step_counts:
+        vs_n, as_n = sigma_grid_n(steps)
+        tab = None if tables is None else tables[:steps]
 
-    with torch.no_grad():
-        one()  # warm-up rollout
-        torch.cuda.synchronize()
-        torch.cuda.reset_peak_memory_stats()
-        times = []
-        for _ in range(a.runs):
-            if cp is not None:
-                torch.distributed.barrier()
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
-            one()
-            e.record()
-            e.synchronize()
-            times.append(s.elapsed_time(e) / 1000.0)
-    t = min(times)
-    peak = torch.cuda.max_memory_allocated() / 2 ** 30
-    if cp is not None:
-        v = torch.tensor([t, peak], device=device, dtype=torch.float64)
-        torch.distributed.all_reduce(v, op=torch.distributed.ReduceOp.MAX)
-        t, peak = float(v[0]), float(v[1])
+        def one():
+            return rollout(model, pe.to(device), lay, shape, geo, vs_n, as_n, 7, device, text_features=text_features,
+                           adaln_tables_per_step=tab)
+
+        with torch.no_grad():
+            one()  # warm-up rollout
+            torch.cuda.synchronize()
+            torch.cuda.reset_peak_memory_stats()
+            times = []
+            for _ in range(a.runs):
+                if cp is not None:
+                    torch.distributed.barrier()
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                one()
+                e.record()
+                e.synchronize()
+                times.append(s.elapsed_time(e) / 1000.0)
+        t = min(times)
+        peak = torch.cuda.max_memory_allocated() / 2 ** 30
+        if cp is not None:
+            v = torch.tensor([t, peak], device=device, dtype=torch.float64)
+            torch.distributed.all_reduce(v, op=torch.distributed.ReduceOp.MAX)
+            t, peak = float(v[0]), float(v[1])
+        results.append({"steps": steps, "s_per_video": t, "s_per_evaluation": t / steps, "peak_sampling_gib": round(peak, 2)})
     out = {"metric": "H3 33B-shaped sampling: s per video and s per model evaluation (device-timed, max over ranks)",
-           "mode": a.mode, "steps": a.steps, "s_per_video": t, "s_per_evaluation": t / a.steps,
-           "tokens": int(lay.sequence_length),
-           "gpus": cp.world if cp is not None else 1, "peak_sampling_gib": round(peak, 2), "build_s": round(build_s, 1),
+           "mode": a.mode, "results": results, "tokens": int(lay.sequence_length),
+           "gpus": cp.world if cp is not None else 1, "build_s": round(build_s, 1),
            "config": {"model": f"H3-shaped DiT, {cfg.num_layers} blocks, hidden {cfg.dim}, ffn {cfg.ffn_dim}",
                       "video": f"{a.num_frames} frames at {a.height}x{a.width}", "text_tokens": a.text_tokens,
                       "dtype": "bf16", "weights": "random init"},
