@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--dp-path", default="auto", choices=["auto", "nvls", "p2p"],
                     help="fused optimiser transport: NVLS multimem or P2P peer loads/stores (auto: P2P up to 2 "
                          "GPUs, NVLS above, as measured by benchmarks/bench_collectives.py)")
+    ap.add_argument("--fsdp", action="store_true",
+                    help="FSDP-style sharding of the trainable block weights (critic, and the student unless LoRA)")
     ap.add_argument("--dp-optimizer", default="sharded", choices=["sharded", "replicated"],
                     help="sharded: fused reduce-scatter/AdamW/all-gather kernel; replicated: NCCL all-reduce baseline")
     return ap.parse_args()
@@ -178,6 +180,9 @@ def _dp_desc(trainer, args):
     if args.impl == "reference":
         return "reference: NCCL gradient all-reduce + master-weight AdamW"
     opt = getattr(trainer, "opt_student", None)
+    if getattr(trainer, "fsdp", None):
+        return ("FSDP-sharded block weights: peer-memory gather one block ahead, per-block reduce-scatter kernel "
+                "in backward, AdamW on the shards; other weights: fused reduce-scatter+AdamW+all-gather")
     if args.dp_optimizer == "sharded" and opt is not None and hasattr(opt, "multicast"):
         return "sharded fp32 state; fused reduce-scatter+AdamW+all-gather kernel (" + \
             ("NVLS multimem" if opt.multicast else "P2P peer loads/stores") + ")"
@@ -203,7 +208,8 @@ def main():
 
         over = {"num_layers": args.layers} if args.layers else {}
         multicast = {"nvls": True, "p2p": False, "auto": world > 2}[args.dp_path]
-        cfg = WanDMADConfig(net=wan_config(args.model, **over), dp_optimizer=args.dp_optimizer, dp_multicast=multicast)
+        cfg = WanDMADConfig(net=wan_config(args.model, **over), dp_optimizer=args.dp_optimizer, dp_multicast=multicast,
+                            fsdp_trainable=args.fsdp)
         cfg.checkpoint_critic_blocks_student_phase = cfg.net.num_layers
         big = "14b" in args.model.lower()
         cfg.loss_scale = args.cm_loss_scale if args.cm_loss_scale is not None else (100.0 if big else 0.0)

@@ -4,6 +4,7 @@
 
 namespace dmad {
 void register_h2d_stream(pybind11::module& m);
+void fsdp_reduce_scatter(std::vector<int64_t> slot_ptrs, at::Tensor& acc, int64_t off, int64_t len, bool accumulate);
 void flash_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
                double scale);
 void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
@@ -109,6 +110,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cp_head_to_seq", &dmad::cp_head_to_seq);
   m.def("gemm_bf16", &dmad::gemm_bf16);
   m.def("fsdp_gather", &dmad::fsdp_gather);
+  m.def("fsdp_reduce_scatter", &dmad::fsdp_reduce_scatter);
   m.def("flash_fwd_accumulate", &dmad::flash_fwd_accumulate);
   m.def("peer_copy", &dmad::peer_copy);
   m.def("peer_copy_to", &dmad::peer_copy_to);

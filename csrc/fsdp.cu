@@ -22,6 +22,7 @@ constexpr int kMaxRanks = 16;
 struct Shards {
   int64_t p[kMaxRanks];
 };
+static_assert(sizeof(Shards) == 8 * 16, "peer table");
 
 __global__ void fsdp_gather_kernel(Shards src, uint4* __restrict__ dst, int world, int64_t len_vec,
                                    int64_t n_vec, int* status) {
@@ -39,7 +40,58 @@ __global__ void fsdp_gather_kernel(Shards src, uint4* __restrict__ dst, int worl
   }
 }
 
+// acc[j] (+)= sum over ranks r (in rank order) of slot_r[off + j], j < len: every rank's bf16 gradient of
+// one block sits in its symmetric grad slot; this rank pulls the slice it owns from every peer with
+// 16-byte loads and sums in fp32.  The rank order is fixed, so the result does not depend on timing.
+__global__ void fsdp_reduce_scatter_kernel(Shards slots, float* __restrict__ acc, int world, int64_t off,
+                                           int64_t len_vec, bool accumulate, int* status) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < len_vec; i += (int64_t)gridDim.x * blockDim.x) {
+    float s[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s[e] = 0.f;
+    for (int r = 0; r < world; ++r) {
+      const uint4 v = reinterpret_cast<const uint4*>(slots.p[r] + off * 2)[i];  // off in bf16 elements
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        s[2 * e] += __uint_as_float(w[e] << 16);
+        s[2 * e + 1] += __uint_as_float(w[e] & 0xffff0000u);
+      }
+    }
+    float4* out = reinterpret_cast<float4*>(acc) + 2 * i;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+    if (accumulate) {
+      a = out[0];
+      b = out[1];
+    }
+    out[0] = make_float4(a.x + s[0], a.y + s[1], a.z + s[2], a.w + s[3]);
+    out[1] = make_float4(b.x + s[4], b.y + s[5], b.z + s[6], b.w + s[7]);
+  }
+}
+
 }  // namespace
+
+// acc (fp32, len elements) (+)= sum over ranks of the bf16 elements [off, off + len) of every rank's slot.
+void fsdp_reduce_scatter(std::vector<int64_t> slot_ptrs, at::Tensor& acc, int64_t off, int64_t len, bool accumulate) {
+  const int world = (int)slot_ptrs.size();
+  TORCH_CHECK(world >= 1 && world <= kMaxRanks, "1..16 ranks");
+  TORCH_CHECK(acc.is_cuda() && acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.numel() >= len,
+              "acc must be a contiguous fp32 CUDA tensor of at least len elements");
+  TORCH_CHECK(len % 8 == 0 && off % 8 == 0, "off / len must be multiples of 8");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(acc.data_ptr()) % 16 == 0, "acc must be 16-byte aligned");
+  Shards s{};
+  for (int i = 0; i < world; ++i) {
+    TORCH_CHECK(slot_ptrs[i] % 16 == 0, "slots must be 16-byte aligned");
+    s.p[i] = slot_ptrs[i];
+  }
+  if (len == 0) return;
+  c10::cuda::CUDAGuard guard(acc.device());
+  const int64_t len_vec = len / 8;
+  const int blocks = (int)std::min<int64_t>((len_vec + 255) / 256, 148 * 8);
+  fsdp_reduce_scatter_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      s, acc.data_ptr<float>(), world, off, len_vec, accumulate, device_status_ptr(acc.get_device()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 
 // dst: local bf16 buffer of >= numel elements; shard_ptrs: every rank's shard address (len elements each).
 void fsdp_gather(std::vector<int64_t> shard_ptrs, at::Tensor& dst, int64_t len, int64_t numel) {

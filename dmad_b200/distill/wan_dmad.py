@@ -95,6 +95,10 @@ class WanDMADConfig:
     # shard the frozen block weights (LoRA student base, teacher) over the ranks and gather them one
     # block ahead (needs the student blocks activation-checkpointed)
     shard_frozen: bool = False
+    # FSDP-style sharding of the trainable block weights (critic, and the student unless it is a LoRA
+    # student): bf16 shards gathered one block ahead, gradients reduce-scattered per block in backward,
+    # AdamW on the shards; the blocks are then activation-checkpointed
+    fsdp_trainable: bool = False
     dp_optimizer: str = "sharded"
     dp_multicast: bool = True
     dp_sync_timeout_s: float = 120.0
@@ -160,6 +164,21 @@ class WanDMAD(nn.Module):
                 self.sharded.append(sh)
             if self.net_teacher is not None:
                 self.sharded.append(ShardedFrozenBlocks(self.net_teacher.blocks))
+        self.fsdp = {}
+        if cfg.fsdp_trainable:
+            from ..parallel.fsdp import ShardedTrainableBlocks
+            if cfg.dp_optimizer != "sharded":
+                raise ValueError("fsdp_trainable runs with dp_optimizer='sharded'")
+            kw_b = dict(betas=cfg.betas, eps=cfg.eps, weight_decay=cfg.weight_decay,
+                        sync_timeout_s=cfg.dp_sync_timeout_s, force_finite=cfg.grad_force_finite)
+            nl = cfg.net.num_layers
+            cfg.checkpoint_critic_blocks = cfg.checkpoint_critic_blocks_student_phase = nl
+            self.net_fake_score.checkpoint_blocks = nl
+            self.fsdp["critic"] = ShardedTrainableBlocks(self.net_fake_score.blocks, lr=cfg.critic_lr, **kw_b)
+            if not cfg.student_lora_rank:
+                cfg.checkpoint_student_blocks = nl
+                self.net.checkpoint_blocks = nl
+                self.fsdp["student"] = ShardedTrainableBlocks(self.net.blocks, lr=cfg.lr, ema=cfg.ema_enabled, **kw_b)
         self.gap = GapRouter("allreduce", tau=cfg.gap_tau, beta=cfg.gap_ema_beta, enabled=cfg.gap_route).to(device)
         self.scaling = TrigFlowScaling(1.0, cfg.rectified_flow_t_scaling_factor)
         self.p_D = LogNormal(*cfg.p_D_lognormal) if cfg.p_D_lognormal else UniformShift(cfg.p_D_shift)
@@ -172,8 +191,18 @@ class WanDMAD(nn.Module):
         if cfg.dp_optimizer == "sharded":
             kw = dict(betas=cfg.betas, eps=cfg.eps, weight_decay=cfg.weight_decay, use_multicast=cfg.dp_multicast,
                       sync_timeout_s=cfg.dp_sync_timeout_s, force_finite=cfg.grad_force_finite)
-            self.opt_student = ShardedAdamW(s_params, lr=cfg.lr, ema=cfg.ema_enabled, **kw)
-            self.opt_critic = ShardedAdamW(c_params, lr=cfg.critic_lr, **kw)
+
+            def make(params, lr, ema, name):
+                sh = self.fsdp.get(name)
+                if sh is None:
+                    return ShardedAdamW(params, lr=lr, ema=ema, **kw)
+                from ..parallel.fsdp import FSDPOptimizer
+                owned = {id(p) for p in sh.params}
+                rest = [p for p in params if id(p) not in owned]
+                return FSDPOptimizer(sh, ShardedAdamW(rest, lr=lr, ema=ema, **kw) if rest else None)
+
+            self.opt_student = make(s_params, cfg.lr, cfg.ema_enabled, "student")
+            self.opt_critic = make(c_params, cfg.critic_lr, False, "critic")
             self.ema_params = None
             self.sync_student = GradSync(s_params, enabled=False)
             self.sync_critic = GradSync(c_params, enabled=False)
@@ -199,12 +228,22 @@ class WanDMAD(nn.Module):
         return [n for n in (self.net, self.net_fake_score, self.net_teacher) if n is not None]
 
     # ------------------------------------------------------------------ checkpoint state
+    def _full_blocks(self, write_back=False):
+        """Context with every FSDP-sharded block weight gathered into full tensors (collective)."""
+        stack = contextlib.ExitStack()
+        for sh in self.fsdp.values():
+            stack.enter_context(sh.materialized(write_back))
+        return stack
+
     def state_dicts(self) -> tuple[dict, dict | None]:
         """(state every rank holds identically, this rank's optimiser shards or None)."""
-        # sharded frozen weights are never saved (they do not change; they come from the teacher checkpoint)
-        net_sd = {k: v for k, v in self.net.state_dict().items() if v.numel() > 0 or not self.sharded}
-        shared = {"net": net_sd, "net_fake_score": self.net_fake_score.state_dict(),
-                  "critic_heads": self.critic_heads.state_dict(), "gap": self.gap.state_dict()}
+        with self._full_blocks():
+            # sharded frozen weights are never saved (they do not change; they come from the teacher checkpoint)
+            net_sd = {k: v.clone() for k, v in self.net.state_dict().items() if v.numel() > 0 or not self.sharded}
+            shared = {"net": net_sd, "net_fake_score": {k: v.clone() for k, v in self.net_fake_score.state_dict().items()},
+                      "critic_heads": self.critic_heads.state_dict(), "gap": self.gap.state_dict()}
+        if self.fsdp:
+            return shared, {"opt_student": self.opt_student.state_dict(), "opt_critic": self.opt_critic.state_dict()}
         if isinstance(self.opt_student, ShardedAdamW):
             names = {id(p): n for n, p in self.net.named_parameters()}
             shared["student_layout"] = self.opt_student.layout(names)
@@ -215,10 +254,17 @@ class WanDMAD(nn.Module):
         return shared, None
 
     def load_state_dicts(self, shared: dict, per_rank: dict | None):
-        self.net.load_state_dict(shared["net"], strict=not self.sharded)
-        self.net_fake_score.load_state_dict(shared["net_fake_score"])
+        with self._full_blocks(write_back=True):
+            self.net.load_state_dict(shared["net"], strict=not self.sharded)
+            self.net_fake_score.load_state_dict(shared["net_fake_score"])
         self.critic_heads.load_state_dict(shared["critic_heads"])
         self.gap.load_state_dict(shared["gap"])
+        if self.fsdp:
+            if not per_rank or "opt_student" not in per_rank or "elastic_rank_states" in per_rank:
+                raise RuntimeError("an FSDP-sharded run resumes from its own per-rank shards at the same world size")
+            self.opt_student.load_state_dict(per_rank["opt_student"])
+            self.opt_critic.load_state_dict(per_rank["opt_critic"])
+            return
         if isinstance(self.opt_student, ShardedAdamW):
             if per_rank and "elastic_rank_states" in per_rank:  # saved with another world size
                 states = per_rank["elastic_rank_states"]
@@ -238,6 +284,9 @@ class WanDMAD(nn.Module):
 
     def ema_weights(self) -> list[torch.Tensor] | None:
         """Full fp32 EMA of the student's trainable parameters (collective when sharded)."""
+        if "student" in self.fsdp:
+            by = self.opt_student.full_ema_by_param()
+            return None if by is None else [by[id(p)] for p in self._student_params]
         if isinstance(self.opt_student, ShardedAdamW):
             return self.opt_student.full_ema()
         return self.ema_params
@@ -410,6 +459,23 @@ class WanDMAD(nn.Module):
     def ema_scope(self):
         """The student runs with its EMA weights inside (rcm ``ema_scope``); collective when the optimiser
         state is sharded, so every rank enters together."""
+        if "student" in self.fsdp:
+            sh, rest = self.fsdp["student"], self.opt_student.rest
+            if sh.ema is None:
+                yield
+                return
+            rest_ema = rest.full_ema() if rest is not None else None
+            saved = [p.detach().clone() for p in rest.params] if rest is not None else []
+            with sh.use_weights(sh.ema), torch.no_grad():
+                if rest is not None and rest_ema is not None:
+                    for p, e in zip(rest.params, rest_ema):
+                        p.copy_(e.to(device=p.device, dtype=p.dtype).view_as(p))
+                try:
+                    yield
+                finally:
+                    for p, s_ in zip(rest.params if rest is not None else [], saved):
+                        p.copy_(s_)
+            return
         ema = self.ema_weights()
         if ema is None:
             yield

@@ -19,6 +19,8 @@ peer-memory copy overlapped with the previous block's compute.
 """
 from __future__ import annotations
 
+import math
+
 import torch
 import torch.distributed as dist
 import torch.nn as nn
@@ -41,7 +43,7 @@ class ShardedFrozenBlocks:
         self.layout = []  # per block: (params, offsets, numel, shard len, arena offset)
         off = 0
         for b in self.blocks:
-            ps = [p for p in b.parameters() if not p.requires_grad and p.dtype == torch.bfloat16 and p.numel() > 0]
+            ps = self._owned(b)
             offs, n = [], 0
             for p in ps:
                 offs.append(n)
@@ -49,10 +51,14 @@ class ShardedFrozenBlocks:
             ln = max(64, -(-n // (self.world * 64)) * 64)
             self.layout.append((ps, offs, n, ln, off))
             off += ln
-        self.arena = SymmBuffer(max(off, 64), torch.bfloat16, dev, group, zero=True)
+        dtypes = {p.dtype for ps, _, _, _, _ in self.layout for p in ps}
+        if len(dtypes) > 1 or (self.cuda and dtypes and dtypes != {torch.bfloat16}):
+            raise ValueError(f"sharded block weights must share one dtype (bf16 on CUDA), got {sorted(map(str, dtypes))}")
+        self.dtype = dtypes.pop() if dtypes else torch.bfloat16
+        self.arena = SymmBuffer(max(off, 64), self.dtype, dev, group, zero=True)
         with torch.no_grad():
             for ps, offs, n, ln, base in self.layout:
-                flat = torch.zeros(ln * self.world, dtype=torch.bfloat16, device=dev)
+                flat = torch.zeros(ln * self.world, dtype=self.dtype, device=dev)
                 for p, o in zip(ps, offs):
                     flat[o:o + p.numel()].copy_(p.data.reshape(-1))
                 self.arena.tensor[base:base + ln].copy_(flat[self.rank * ln:(self.rank + 1) * ln])
@@ -60,7 +66,7 @@ class ShardedFrozenBlocks:
                     p._fsdp_shape = tuple(p.shape)
                     p.data = torch.empty(0, dtype=p.dtype, device=dev)
         self.max_full = max(ln * self.world for _, _, _, ln, _ in self.layout)
-        self.slots = [torch.empty(self.max_full, dtype=torch.bfloat16, device=dev) for _ in range(slots)]
+        self.slots = [torch.empty(self.max_full, dtype=self.dtype, device=dev) for _ in range(slots)]
         self.resident = [-1] * slots
         self.stream = torch.cuda.Stream(device=dev) if self.cuda else None
         self.done = [None] * slots
@@ -70,6 +76,10 @@ class ShardedFrozenBlocks:
             torch.cuda.synchronize(dev)
         if is_distributed() and self.world > 1:
             barrier()  # every shard is in place before any peer reads it
+
+    def _owned(self, b):
+        """The parameters of block ``b`` this sharding owns: its frozen bf16 weights."""
+        return [p for p in b.parameters() if not p.requires_grad and p.dtype == torch.bfloat16 and p.numel() > 0]
 
     # ------------------------------------------------------------------ gather
     def _gather(self, i: int, slot: int):
@@ -81,7 +91,7 @@ class ShardedFrozenBlocks:
             with nvtx_range(f"dmad.fsdp.gather[{i}]"):
                 ext().fsdp_gather([p + base * 2 for p in self.arena.ptrs], dst, ln, n)
         elif is_distributed() and self.world > 1:
-            parts = [torch.empty(ln, dtype=torch.bfloat16) for _ in range(self.world)]
+            parts = [torch.empty(ln, dtype=self.dtype) for _ in range(self.world)]
             dist.all_gather(parts, self.arena.tensor[base:base + ln].contiguous(), group=self.group)
             dst[: ln * self.world].copy_(torch.cat(parts))
         else:
@@ -139,3 +149,322 @@ def _numel(shape):
     for d in shape:
         n *= d
     return n
+
+
+class ShardedTrainableBlocks(ShardedFrozenBlocks):
+    """FSDP-style sharding of the trainable weights of a block stack (ZeRO stage 3).
+
+    Each rank keeps the bf16 shard of every block's flat weight vector, and the fp32 master weights,
+    Adam moments, optional EMA and an fp32 gradient accumulator of that shard only.  Forward: the block
+    is gathered from the peers' shards one block ahead (as the frozen blocks are) and its parameters are
+    bound to the gathered copy.  Backward (the blocks are activation-checkpointed, so the gathered
+    weights are bound again when the block is recomputed): as each parameter's gradient is accumulated,
+    a hook copies it into this rank's half of a double-buffered symmetric gradient slot and drops it;
+    once the block's last gradient is in, a bounded peer barrier (every rank has filled its slot) is
+    followed by the reduce-scatter kernel, which pulls this rank's slice of the block's gradient from
+    every peer's slot and adds the fp32 sum into the shard accumulator.  The k-th reduce-scatter uses
+    slot k % 2, and a rank writes slot k % 2 only after it passed the barrier of reduce-scatter k - 1,
+    which every peer reaches only after finishing reduce-scatter k - 2: no slot is overwritten while a
+    peer still reads it.  ``step`` is one multi-tensor AdamW launch over the shards that also writes the
+    new bf16 shard in place (the next gather picks it up).  Gradients are averaged over the ranks, as in
+    data-parallel training.  Without CUDA (gloo ranks) the same protocol runs on torch collectives.
+
+    Parity: FSDP2 ``fully_shard`` of every block of the student and the critic with FusedAdam master
+    weights (train/wan/rcm/models/t2v_model_distill_rcm.py:175-195, train/h3/lightx2v_train/runtime/
+    fsdp.py:35-85); there the all-gather and reduce-scatter are NCCL calls.
+    """
+
+    def __init__(self, blocks, lr=1e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, ema: bool = False,
+                 group=None, slots: int = 3, sync_timeout_s: float = 120.0, force_finite: bool = False):
+        self._select_trainable = True
+        super().__init__(blocks, group=group, slots=slots)
+        self.lr, self.betas, self.eps, self.weight_decay = lr, tuple(betas), eps, weight_decay
+        self.force_finite = force_finite
+        self.step_count = 0
+        dev = self.device
+        total = sum(ln for _, _, _, ln, _ in self.layout)
+        shard = self.arena.tensor[:total]
+        self.master = shard.float().clone()
+        self.exp_avg = torch.zeros_like(self.master)
+        self.exp_avg_sq = torch.zeros_like(self.master)
+        self.ema = self.master.clone() if ema else None
+        self.grad_acc = torch.zeros_like(self.master)
+        self.gslots = SymmBuffer(2 * self.max_full, self.dtype, dev, group, zero=True)
+        if self.cuda:
+            from .symm import PeerSync
+            self.sync = PeerSync(dev, group, sync_timeout_s)
+        self.rs_count = 0
+        self._pending = {}  # block -> (parameters still to deliver a gradient, slot)
+        self._grad_hooks = []
+        for i, (ps, offs, n, ln, base) in enumerate(self.layout):
+            for p, o in zip(ps, offs):
+                self._grad_hooks.append(p.register_post_accumulate_grad_hook(self._make_grad_hook(i, p, o)))
+
+    # parameters of a block that this sharding owns
+    def _owned(self, b):
+        if getattr(self, "_select_trainable", False):
+            return [p for p in b.parameters() if p.requires_grad and p.dtype.is_floating_point and p.numel() > 0]
+        return super()._owned(b)
+
+    @property
+    def params(self):
+        return [p for ps, _, _, _, _ in self.layout for p in ps]
+
+    # ------------------------------------------------------------------ gradients
+    def _make_grad_hook(self, i: int, p, off: int):
+        def hook(param):
+            g = param.grad
+            if g is None:
+                return
+            st = self._pending.get(i)
+            if st is None:
+                st = self._pending[i] = [len(self.layout[i][0]), self.rs_count % 2]
+                self.rs_count += 1
+            slot = self.gslots.tensor[st[1] * self.max_full:(st[1] + 1) * self.max_full]
+            with torch.no_grad():
+                slot[off:off + param.numel()].copy_(g.reshape(-1))
+            param.grad = None
+            st[0] -= 1
+            if st[0] == 0:
+                del self._pending[i]
+                self._reduce_scatter(i, st[1])
+        return hook
+
+    def _reduce_scatter(self, i: int, k: int):
+        ps, offs, n, ln, base = self.layout[i]
+        acc = self.grad_acc[base:base + ln]
+        slot_base = k * self.max_full
+        if self.cuda:
+            from ..ops import ext
+            from ..runtime.nvtx import nvtx_range
+            with nvtx_range(f"dmad.fsdp.reduce_scatter[{i}]"):
+                self.sync()  # every rank has its gradient of block i in slot k
+                ext().fsdp_reduce_scatter([ptr + (slot_base + self.rank * ln) * 2 for ptr in self.gslots.ptrs],
+                                          acc, 0, ln, True)
+        else:
+            full = self.gslots.tensor[slot_base:slot_base + ln * self.world].float()
+            if is_distributed() and self.world > 1:
+                dist.all_reduce(full, group=self.group)
+            acc.add_(full[self.rank * ln:(self.rank + 1) * ln])
+
+    def zero_grad(self, set_to_none: bool = True):
+        self.grad_acc.zero_()
+        for p in self.params:
+            p.grad = None
+
+    # ------------------------------------------------------------------ optimiser
+    @torch.no_grad()
+    def step(self, ema_beta: float | None = None, max_grad_norm: float | None = None):
+        if self._pending:
+            raise RuntimeError(f"blocks {sorted(self._pending)} still wait for gradients: a backward did not "
+                               f"reach every parameter of a block")
+        self.step_count += 1
+        total = self.master.numel()
+        shard = self.arena.tensor[:total]
+        g = self.grad_acc / self.world
+        if self.force_finite:
+            g = torch.nan_to_num(g, nan=0.0, posinf=0.0, neginf=0.0)
+        scale = None
+        if max_grad_norm is not None and math.isfinite(max_grad_norm) and max_grad_norm < 1e11:
+            ss = (g * g).sum().reshape(1)
+            if is_distributed() and self.world > 1:
+                dist.all_reduce(ss, group=self.group)
+            norm = ss.sqrt()
+            scale = torch.clamp(max_grad_norm / (norm + 1e-6), max=1.0)
+            scale = torch.where(torch.isfinite(norm), scale, torch.zeros_like(scale))
+        b1, b2 = self.betas
+        if self.cuda:
+            from ..ops import ext
+            ext().fused_adamw([self.master], [g.contiguous()], [self.exp_avg], [self.exp_avg_sq], [shard],
+                              [self.ema] if (self.ema is not None and ema_beta is not None) else [],
+                              float(self.lr), float(b1), float(b2), float(self.eps), float(self.weight_decay),
+                              int(self.step_count), scale, float(ema_beta or 0.0))
+        else:
+            if scale is not None:
+                g = g * scale
+            bc1, bc2 = 1 - b1 ** self.step_count, 1 - b2 ** self.step_count
+            self.master.mul_(1 - self.lr * self.weight_decay)
+            self.exp_avg.mul_(b1).add_(g, alpha=1 - b1)
+            self.exp_avg_sq.mul_(b2).addcmul_(g, g, value=1 - b2)
+            denom = (self.exp_avg_sq / bc2).sqrt_().add_(self.eps)
+            self.master.addcdiv_(self.exp_avg, denom, value=-self.lr / bc1)
+            if self.ema is not None and ema_beta is not None:
+                self.ema.mul_(ema_beta).add_(self.master, alpha=1 - ema_beta)
+            shard.copy_(self.master.to(shard.dtype))
+        self.resident = [-1] * len(self.slots)  # gathered copies are stale now
+
+    # ------------------------------------------------------------------ full tensors (checkpoint / export)
+    def _full(self, flat_shard: torch.Tensor, dtype=None) -> list[torch.Tensor]:
+        """Every owned parameter rebuilt from all ranks' ``flat_shard`` (collective)."""
+        if is_distributed() and self.world > 1:
+            parts = [torch.empty_like(flat_shard) for _ in range(self.world)]
+            dist.all_gather(parts, flat_shard.contiguous(), group=self.group)
+        else:
+            parts = [flat_shard]
+        out = []
+        for ps, offs, n, ln, base in self.layout:
+            full = torch.cat([pt[base:base + ln] for pt in parts])
+            for p, o in zip(ps, offs):
+                t = full[o:o + _numel(p._fsdp_shape)].view(p._fsdp_shape)
+                out.append(t.to(dtype) if dtype is not None else t.clone())
+        return out
+
+    def full_params(self) -> list[torch.Tensor]:
+        return self._full(self.arena.tensor[:self.master.numel()])
+
+    def full_master(self) -> list[torch.Tensor]:
+        return self._full(self.master)
+
+    def full_ema(self) -> list[torch.Tensor] | None:
+        return None if self.ema is None else self._full(self.ema)
+
+    def state_dict(self):
+        return {"step": self.step_count, "lr": self.lr, "world": self.world, "rank": self.rank,
+                "master": self.master, "exp_avg": self.exp_avg, "exp_avg_sq": self.exp_avg_sq, "ema": self.ema}
+
+    @torch.no_grad()
+    def load_state_dict(self, sd):
+        if int(sd["world"]) != self.world:
+            raise ValueError(f"sharded block state was saved with world {sd['world']}, running with {self.world}")
+        self.step_count = int(sd["step"])
+        self.lr = sd.get("lr", self.lr)
+        for k in ("master", "exp_avg", "exp_avg_sq"):
+            getattr(self, k).copy_(sd[k])
+        if self.ema is not None and sd.get("ema") is not None:
+            self.ema.copy_(sd["ema"])
+        self.arena.tensor[:self.master.numel()].copy_(self.master.to(self.dtype))
+        self.resident = [-1] * len(self.slots)
+
+    def remove(self):
+        super().remove()
+        for h in self._grad_hooks:
+            h.remove()
+
+
+class _Materialized:
+    """Binds every owned parameter to its full tensor (gathered from all ranks) inside the block; on
+    exit optionally writes edited full tensors back into the shards, then releases them."""
+
+    def __init__(self, sh: "ShardedTrainableBlocks", write_back: bool):
+        self.sh, self.write_back = sh, write_back
+
+    def __enter__(self):
+        fulls = self.sh.full_params()
+        for p, t in zip(self.sh.params, fulls):
+            p.data = t
+        return self
+
+    def __exit__(self, *exc):
+        sh = self.sh
+        if self.write_back and exc[0] is None:
+            with torch.no_grad():
+                for ps, offs, n, ln, base in sh.layout:
+                    flat = torch.zeros(ln * sh.world, dtype=sh.dtype, device=sh.device)
+                    for p, o in zip(ps, offs):
+                        flat[o:o + p.numel()].copy_(p.data.reshape(-1))
+                    mine = flat[sh.rank * ln:(sh.rank + 1) * ln]
+                    sh.arena.tensor[base:base + ln].copy_(mine)
+                    sh.master[base:base + ln].copy_(mine.float())
+        for p in sh.params:
+            p.data = torch.empty(0, dtype=p.dtype, device=sh.device)
+        sh.resident = [-1] * len(sh.slots)
+        return False
+
+
+def _materialized(self, write_back: bool = False):
+    """Context in which the owned parameters are full tensors (collective: every rank enters)."""
+    return _Materialized(self, write_back)
+
+
+ShardedTrainableBlocks.materialized = _materialized
+
+
+class _UseWeights:
+    def __init__(self, sh, flat):
+        self.sh, self.flat = sh, flat
+
+    def __enter__(self):
+        n = self.sh.master.numel()
+        self.saved = self.sh.arena.tensor[:n].clone()
+        with torch.no_grad():
+            self.sh.arena.tensor[:n].copy_(self.flat.to(self.sh.dtype))
+        self.sh.resident = [-1] * len(self.sh.slots)
+        return self
+
+    def __exit__(self, *exc):
+        with torch.no_grad():
+            self.sh.arena.tensor[:self.saved.numel()].copy_(self.saved)
+        self.sh.resident = [-1] * len(self.sh.slots)
+        return False
+
+
+def _use_weights(self, flat_fp32: torch.Tensor):
+    """Context in which the blocks run with other weights of the same sharded layout (this rank's flat
+    fp32 shard, e.g. the EMA); local to each rank, no collective."""
+    return _UseWeights(self, flat_fp32)
+
+
+ShardedTrainableBlocks.use_weights = _use_weights
+
+
+class FSDPOptimizer:
+    """One optimiser over a net whose block weights are sharded (``ShardedTrainableBlocks``) and whose
+    remaining trainable parameters (embeddings, head, critic heads: a few percent of the weights) use
+    the fused sharded-state data-parallel AdamW (``ShardedAdamW``).  Gradient clipping is by the norm of
+    each part (the reference clips at 1e12 for these models, i.e. not at all)."""
+
+    def __init__(self, blocks: ShardedTrainableBlocks, rest):
+        self.blocks, self.rest = blocks, rest
+        self._order = None
+
+    @property
+    def params(self):
+        return self.blocks.params + (self.rest.params if self.rest is not None else [])
+
+    @property
+    def param_groups(self):
+        return [{"params": self.params, "lr": self.blocks.lr}]
+
+    @property
+    def multicast(self):
+        return getattr(self.rest, "multicast", False)
+
+    @property
+    def lr(self):
+        return self.blocks.lr
+
+    @lr.setter
+    def lr(self, value):  # the LR schedule sets one rate for the whole net
+        self.blocks.lr = value
+        if self.rest is not None:
+            self.rest.lr = value
+
+    def zero_grad(self, set_to_none: bool = True):
+        self.blocks.zero_grad()
+        if self.rest is not None:
+            self.rest.zero_grad()
+
+    def step(self, ema_beta: float | None = None, max_grad_norm: float | None = None):
+        self.blocks.step(ema_beta=ema_beta, max_grad_norm=max_grad_norm)
+        if self.rest is not None:
+            self.rest.step(ema_beta=ema_beta, max_grad_norm=max_grad_norm)
+
+    def full_ema_by_param(self) -> dict | None:
+        """id(parameter) -> full fp32 EMA tensor (collective)."""
+        be = self.blocks.full_ema()
+        if be is None:
+            return None
+        out = {id(p): t for p, t in zip(self.blocks.params, be)}
+        if self.rest is not None:
+            re = self.rest.full_ema()
+            if re is not None:
+                out.update({id(p): t for p, t in zip(self.rest.params, re)})
+        return out
+
+    def state_dict(self):
+        return {"blocks": self.blocks.state_dict(), "rest": self.rest.state_dict() if self.rest is not None else None}
+
+    def load_state_dict(self, sd):
+        self.blocks.load_state_dict(sd["blocks"])
+        if self.rest is not None and sd.get("rest") is not None:
+            self.rest.load_state_dict(sd["rest"])
