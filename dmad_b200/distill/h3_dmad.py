@@ -65,6 +65,11 @@ class H3DMADConfig:
     gradient_checkpointing: bool = True
     text_tokens: int = 256
     model_dir: str | None = None      # H3 release folder: transformer/config.json sets ``model``, shards load
+    # shard the block weights over the ranks (FSDP-style, the reference's fully_shard per block,
+    # train/h3/lightx2v_train/runtime/fsdp.py:35-85): the frozen bases of the LoRA student and critic,
+    # and in full-critic mode the critic's trainable blocks (gathered one block ahead, gradients
+    # reduce-scattered per block, AdamW on the shards); needs gradient_checkpointing
+    shard_weights: bool = False
 
 
 class SyntheticH3Pool:
@@ -102,7 +107,18 @@ class H3DMAD:
                 self.geo = H3Geometry.from_model_dir(cfg.model_dir)
         self.shape = latent_shape_of(cfg.height, cfg.width, cfg.num_frames, self.geo)
         torch.manual_seed(seed)
-        base = H3Model(cfg.model)
+        if self.device.type == "cuda":
+            # built on the device in the compute dtype: two 33B nets are 132 GB in bf16, far beyond what
+            # fp32 host copies per rank could hold
+            prev = torch.get_default_dtype()
+            torch.set_default_dtype(dtype)
+            try:
+                with torch.device(self.device):
+                    base = H3Model(cfg.model)
+            finally:
+                torch.set_default_dtype(prev)
+        else:
+            base = H3Model(cfg.model)
         if cfg.model_dir:
             from ..inference.h3 import load_transformer_weights
             load_transformer_weights(base, cfg.model_dir)
@@ -127,12 +143,34 @@ class H3DMAD:
         self.fb = cfg.feature_block % len(self.fake.transformer_blocks)
         self.s_params = [p for p in self.student.parameters() if p.requires_grad]
         self.f_params = [p for p in self.fake.parameters() if p.requires_grad]
+        self.sharded = []
+        owned = set()
+        if cfg.shard_weights:
+            from ..parallel.fsdp import ShardedFrozenBlocks, ShardedTrainableBlocks
+            if not cfg.gradient_checkpointing:
+                raise ValueError("shard_weights needs gradient_checkpointing (the blocks are gathered per use)")
+            self.sharded.append(ShardedFrozenBlocks(self.student.transformer_blocks))
+            fblocks = list(self.fake.transformer_blocks)
+            if cfg.fake_train_type == "lora":
+                self.sharded.append(ShardedFrozenBlocks(fblocks))
+            else:
+                k = min(cfg.critic_freeze_blocks, len(fblocks))
+                if k > 0:
+                    self.sharded.append(ShardedFrozenBlocks(fblocks[:k]))
+                if k < len(fblocks):
+                    self.fake_fsdp = ShardedTrainableBlocks(fblocks[k:], lr=cfg.fake_lr, betas=cfg.betas, eps=cfg.eps,
+                                                            weight_decay=cfg.weight_decay)
+                    self.sharded.append(self.fake_fsdp)
+                    owned = {id(p) for p in self.fake_fsdp.params}
         self.opt_s = FusedAdamW(self.s_params, lr=cfg.lr, betas=cfg.betas, eps=cfg.eps, weight_decay=cfg.weight_decay)
-        self.opt_f = FusedAdamW(self.f_params, lr=cfg.fake_lr, betas=cfg.betas, eps=cfg.eps,
-                                weight_decay=cfg.weight_decay)
+        f_rest = [p for p in self.f_params if id(p) not in owned]
+        self.opt_f = FusedAdamW(f_rest, lr=cfg.fake_lr, betas=cfg.betas, eps=cfg.eps, weight_decay=cfg.weight_decay)
+        if owned:
+            from ..parallel.fsdp import FSDPOptimizer
+            self.opt_f = FSDPOptimizer(self.fake_fsdp, self.opt_f)
         self.opt_h = torch.optim.AdamW(self.heads.parameters(), lr=cfg.head_lr, betas=cfg.betas,
                                        weight_decay=cfg.head_wd, eps=cfg.eps)
-        self.sync_s, self.sync_f = GradSync(self.s_params), GradSync(self.f_params)
+        self.sync_s, self.sync_f = GradSync(self.s_params), GradSync(f_rest)
         self.gap = GapRouter("local", tau=cfg.gap_tau, beta=0.99, min_ready=5, band_min_count=10).to(self.device)
         self.ema_banks = [PowerEMA(self.s_params, g) for g in cfg.ema_gammas]
         self.pool = pool or SyntheticH3Pool(self.shape, cfg.text_tokens, cfg.model.text_dim, self.geo, seed=seed)

@@ -440,7 +440,9 @@ def chunked_block_forward(block, rows: int):
     D = H * hd
     to_out = getattr(attn.to_out, "0")
 
-    def forward(h, tables, adaln_idx, cos, sin, cp=None, L_valid=None):
+    def forward(h, tables, adaln_idx, cos, sin, cp=None, L_valid=None, temb=None):
+        if tables is None:
+            tables = block.adaln_tables(temb)
         if cp is not None or not block.modulated:
             raise NotImplementedError("row chunking runs the modulated blocks of a single-GPU forward")
         sh1, sc1, g1, sh2, sc2, g2 = tables

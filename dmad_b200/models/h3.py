@@ -151,9 +151,13 @@ class H3Block(nn.Module):
         return m.view(T, 6, self.cfg.num_tags, self.cfg.dim).permute(1, 0, 2, 3).reshape(6, T * self.cfg.num_tags,
                                                                                           self.cfg.dim)
 
-    def forward(self, h, tables, adaln_idx, cos, sin, cp=None, L_valid=None):
+    def forward(self, h, tables, adaln_idx, cos, sin, cp=None, L_valid=None, temb=None):
+        """``tables``: the block's adaLN tables, or None to compute them here from ``temb`` (so that block
+        weights bound only while the block runs, as when they are sharded, include the adaLN projection)."""
         L = h.shape[0]
         if self.modulated:
+            if tables is None:
+                tables = self.adaln_tables(temb)
             sh1, sc1, g1, sh2, sc2, g2 = tables
             x = ops.ln_mod(h, sc1, sh1, a_add=1.0, gidx=adaln_idx, eps=self.cfg.eps)
             h = ops.gate_residual(h, self.attn(x, cos, sin, L, cp, L_valid), g1, gidx=adaln_idx)
@@ -261,11 +265,11 @@ class H3Model(nn.Module):
         n = len(self.transformer_blocks) if stop_after_block is None else stop_after_block + 1
         for i in range(n):
             blk = self.transformer_blocks[i]
-            tables = adaln_tables[i] if adaln_tables is not None else blk.adaln_tables(temb)
+            tables = adaln_tables[i] if adaln_tables is not None else None
             if self.training and torch.is_grad_enabled() and i < self.checkpoint_blocks:
-                h = checkpoint_block(blk, h, tables, adaln_idx, cos, sin, cp, L, policy=self.checkpoint_policy)
+                h = checkpoint_block(blk, h, tables, adaln_idx, cos, sin, cp, L, temb, policy=self.checkpoint_policy)
             else:
-                h = blk(h, tables, adaln_idx, cos, sin, cp, L)
+                h = blk(h, tables, adaln_idx, cos, sin, cp, L, temb)
         if cp is not None:
             h = cp.gather(h[None], dim=1)[0, :L]
             adaln_idx = full_idx
