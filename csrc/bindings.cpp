@@ -64,6 +64,9 @@ void cp_seq_to_head(const at::Tensor& src, std::vector<int64_t> dst, int64_t B, 
 void cp_head_to_seq(std::vector<at::Tensor> srcs, std::vector<int64_t> dst, int64_t ld, int64_t D, int64_t rank);
 void gemm_bf16(const at::Tensor& a, const at::Tensor& b, c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2,
                c10::optional<at::Tensor> bias, at::Tensor& d, double alpha, int64_t act);
+void gemm_bf16_ex(const at::Tensor& a, const at::Tensor& b, c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2,
+                  c10::optional<at::Tensor> bias, c10::optional<at::Tensor> d, c10::optional<at::Tensor> d32,
+                  double alpha, int64_t act, bool a_mn, bool b_mn, int64_t split);
 void fsdp_gather(std::vector<int64_t> shard_ptrs, at::Tensor& dst, int64_t len, int64_t numel);
 void flash_fwd_accumulate(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
                           at::Tensor& lse, at::Tensor& acc_o, at::Tensor& acc_lse, bool read, bool final_,
@@ -109,6 +112,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cp_seq_to_head", &dmad::cp_seq_to_head);
   m.def("cp_head_to_seq", &dmad::cp_head_to_seq);
   m.def("gemm_bf16", &dmad::gemm_bf16);
+  m.def("gemm_bf16_ex", &dmad::gemm_bf16_ex);
   m.def("fsdp_gather", &dmad::fsdp_gather);
   m.def("fsdp_reduce_scatter", &dmad::fsdp_reduce_scatter);
   m.def("flash_fwd_accumulate", &dmad::flash_fwd_accumulate);

@@ -27,6 +27,19 @@ inline EncodeTiledFn get_encode_tiled() {
   return fn;
 }
 
+// The encode call is a driver API function and needs a current context.  A host thread that has made
+// no runtime call yet (the autograd engine's device thread running a backward, for instance) has
+// none: cudaSetDevice on the current device makes its primary context current (it allocates nothing),
+// once per thread.
+inline void ensure_context() {
+  static thread_local bool done = false;
+  if (!done) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaSetDevice(dev);
+    done = true;
+  }
+}
+
 // bf16 tensor map with a 128-byte swizzle.  dims/strides are innermost-first;
 // strides are in bytes for dims 1..rank-1 (dim 0 is contiguous).  Every
 // stride must be a multiple of 16 bytes and the base 16-byte aligned.
@@ -34,6 +47,7 @@ inline CUtensorMap make_tmap_bf16(const void* base, int rank, const uint64_t* di
                                   const uint32_t* box, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   CUtensorMap m;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) throw std::runtime_error("dmad: TMA base not 16B aligned");
+  ensure_context();
   cuuint64_t d[5];
   cuuint64_t s[4];
   cuuint32_t b[5];

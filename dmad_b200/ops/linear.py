@@ -3,10 +3,13 @@
     y = x W^T + bias + s (x A^T) (B o mask)^T
 
 Forward = two launches of the same kernel: ``xa = s x A^T`` (N = r), then one GEMM over the
-concatenated K panels ``[x | xa] [W | B o mask]^T`` with the bias in the epilogue.  Backward uses
-the library GEMMs (cuBLAS through torch): dX = dY W + (dY B) (s A), dA = s (dY B)^T x,
-dB = dY^T xa, dW = dY^T x when W is trainable.  Parity: PEFT's LoraLayer on nn.Linear, as the
-reference's LoRA students use it (train/h3/lightx2v_train/model_zoo/base.py:16-114).
+concatenated K panels ``[x | xa] [W | B o mask]^T`` with the bias in the epilogue.  Backward on the
+same kernel, with operands read transposed in place (MN-major tiles) instead of materialised:
+``g_s = s dY B`` (N = r), then ``dX = [dY | g_s] [W^T | A^T]^T`` as one GEMM over two K panels (the
+forward's trick again), and the weight gradients ``dA = g_s^T x``, ``dB = dY^T xa`` (and ``dW = dY^T x``
+when W trains) as split-K GEMMs over the token dimension (few output tiles, a long K: the K loop is
+spread over the SMs and the fp32 partial sums are reduced in the epilogue).  Parity: PEFT's LoraLayer on
+nn.Linear, as the reference's LoRA students use it (train/h3/lightx2v_train/model_zoo/base.py:16-114).
 """
 from __future__ import annotations
 
@@ -55,14 +58,37 @@ class _LoraLinear(torch.autograd.Function):
     @staticmethod
     def backward(ctx, gy):
         x2, w, a, b, xa = ctx.saved_tensors
-        g = _rows(gy)
-        gxa = g @ b                                   # [M, r]
-        dx = g @ w + (gxa * ctx.scale) @ a
-        da = (gxa.t() @ x2) * ctx.scale if ctx.needs_input_grad[3] else None
-        db = g.t() @ xa if ctx.needs_input_grad[4] else None
-        dw = g.t() @ x2 if ctx.needs_input_grad[1] else None
+        g = _rows(gy).contiguous()
+        e = ext()
+        M, N = g.shape
+        r, K = a.shape
+        b = b.contiguous()
+        gxa = torch.empty((M, r), dtype=g.dtype, device=g.device)   # s dY B
+        e.gemm_bf16_ex(g, b, None, None, None, gxa, None, float(ctx.scale), 0, False, True, 1)
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.empty((M, K), dtype=g.dtype, device=g.device)
+            e.gemm_bf16_ex(g, w.contiguous(), gxa, a.contiguous(), None, dx, None, 1.0, 0, False, True, 1)
+            dx = dx.view(ctx.xshape)
+        da = _grad_gemm(gxa, x2) if ctx.needs_input_grad[3] else None    # [r, K] = g_s^T x
+        db = _grad_gemm(g, xa) if ctx.needs_input_grad[4] else None      # [N, r] = dY^T xa
+        dw = _grad_gemm(g, x2) if ctx.needs_input_grad[1] else None      # [N, K] = dY^T x
         dbias = g.float().sum(0).to(gy.dtype) if (ctx.has_bias and ctx.needs_input_grad[2]) else None
-        return dx.view(ctx.xshape), dw, dbias, da, db, None
+        return dx, dw, dbias, da, db, None
+
+
+def _grad_gemm(p: torch.Tensor, q: torch.Tensor) -> torch.Tensor:
+    """``p^T q`` for p [T, m], q [T, n] (T = tokens): both read MN-major; the T loop is split over enough
+    CTAs to fill the GPU and the fp32 partial sums are reduced in the kernel's epilogue."""
+    T, m = p.shape
+    n = q.shape[1]
+    tiles = -(-m // 128) * -(-n // 256)
+    ksteps = -(-T // 64)
+    sms = torch.cuda.get_device_properties(p.device).multi_processor_count
+    split = max(1, min(ksteps // 4, -(-sms // tiles)))
+    out = torch.zeros((m, n), dtype=torch.float32, device=p.device)
+    ext().gemm_bf16_ex(p, q, None, None, None, None, out, 1.0, 0, True, True, split)
+    return out.to(p.dtype)
 
 
 def lora_linear(x, w, bias, a, b, scale: float):

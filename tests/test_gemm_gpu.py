@@ -79,3 +79,61 @@ def test_seglinear_lora_uses_fused_path():
     ref = x.float() @ w.t() + lin.bias.float() + lin.lora_scale * (x.float() @ lin.lora_A.float().t()) @ \
         (lin.lora_B * lin.lora_mask).float().t()
     assert (y.float() - ref).abs().max().item() < 3e-2
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (304, 520, 1000), (384, 1536, 4099)])
+def test_gemm_transposed_operands(a_mn, b_mn, M, N, K):
+    """Operands read MN-major (stored transposed) give A B^T as the K-major ones do."""
+    from dmad_b200 import ops
+
+    torch.manual_seed(3)
+    a, b = _r(M, K), _r(N, K, scale=K ** -0.5)
+    d = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    ops.ext().gemm_bf16_ex(a.t().contiguous() if a_mn else a, b.t().contiguous() if b_mn else b, None, None, None,
+                           d, None, 1.0, 0, a_mn, b_mn, 1)
+    torch.cuda.synchronize()
+    ops.check_device_status()
+    ref = a.float() @ b.float().t()
+    assert (d.float() - ref).abs().max().item() < 3e-2 * max(1.0, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("split", [1, 3, 16, 40])
+def test_gemm_split_k_fp32(split):
+    """Split-K with fp32 reduction in the epilogue: p^T q over a long token dimension (the LoRA weight
+    gradients), including splits that get no K steps."""
+    from dmad_b200 import ops
+
+    torch.manual_seed(4)
+    T, m, n = 4100, 128, 1536
+    p, q = _r(T, m, scale=0.1), _r(T, n, scale=0.1)
+    out = torch.zeros(m, n, device=dev)
+    ops.ext().gemm_bf16_ex(p, q, None, None, None, None, out, 2.0, 0, True, True, split)
+    torch.cuda.synchronize()
+    ops.check_device_status()
+    ref = 2.0 * p.float().t() @ q.float()
+    assert (out - ref).abs().max().item() < 1e-2 * max(1.0, ref.abs().max().item())
+
+
+def test_lora_linear_backward_on_tcgen05_matches_fp32_at_wan_shape():
+    """The LoRA-linear backward (dX with the extra K panel, dA / dB split-K) at a Wan FFN shape."""
+    from dmad_b200.ops.linear import lora_linear
+
+    torch.manual_seed(5)
+    M, N, K, r, s = 4096, 8960, 1536, 128, 1.0
+    x = _r(M, K).requires_grad_(True)
+    w = _r(N, K, scale=K ** -0.5)
+    a = _r(r, K, scale=K ** -0.5).requires_grad_(True)
+    b = _r(N, r, scale=0.02).requires_grad_(True)
+    y = lora_linear(x, w, None, a, b, s)
+    g = _r(*y.shape, scale=0.1)
+    dx, da, db = torch.autograd.grad(y, (x, a, b), g)
+    torch.cuda.synchronize()
+    from dmad_b200 import ops
+    ops.check_device_status()
+    xf, af, bf = (t.detach().float().requires_grad_(True) for t in (x, a, b))
+    yf = xf @ w.float().t() + s * (xf @ af.t()) @ bf.t()
+    rdx, rda, rdb = torch.autograd.grad(yf, (xf, af, bf), g.float())
+    for got, ref in ((dx, rdx), (da, rda), (db, rdb)):
+        rel = ((got.float() - ref).norm() / ref.norm()).item()
+        assert rel < 2e-2, rel
