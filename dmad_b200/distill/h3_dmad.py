@@ -168,8 +168,9 @@ class H3DMAD:
         if owned:
             from ..parallel.fsdp import FSDPOptimizer
             self.opt_f = FSDPOptimizer(self.fake_fsdp, self.opt_f)
-        self.opt_h = torch.optim.AdamW(self.heads.parameters(), lr=cfg.head_lr, betas=cfg.betas,
-                                       weight_decay=cfg.head_wd, eps=cfg.eps)
+        # the heads' AdamW is the same multi-tensor kernel (fp32 parameters act as their own master copy)
+        self.opt_h = FusedAdamW(list(self.heads.parameters()), lr=cfg.head_lr, betas=cfg.betas,
+                                weight_decay=cfg.head_wd, eps=cfg.eps)
         self.sync_s, self.sync_f = GradSync(self.s_params), GradSync(f_rest)
         self.gap = GapRouter("local", tau=cfg.gap_tau, beta=0.99, min_ready=5, band_min_count=10).to(self.device)
         self.ema_banks = [PowerEMA(self.s_params, g) for g in cfg.ema_gammas]
@@ -323,7 +324,7 @@ class H3DMAD:
                     dist.all_reduce(p.grad)
                     p.grad.div_(get_world_size())
         self.opt_h.step()
-        self.opt_h.zero_grad(set_to_none=True)
+        self.opt_h.zero_grad()
         self.opt_f.step()
         self.opt_f.zero_grad()
         return {"gan_d": float(bce), "acc_t": float((d_t > 0).float().mean()), "acc_q": float((d_q > 0).float().mean()),
