@@ -61,6 +61,10 @@ class SDXLDMADConfig:
     gradient_checkpointing: bool = True
     unet_kwargs: dict | None = None
     batch_size: int = 4  # per GPU (config 4)
+    # data-parallel optimiser: "sharded" = fp32 state sharded over the ranks, one fused reduce-scatter /
+    # AdamW / all-gather kernel per step; "nccl" = NCCL all-reduce of the gradients, then torch's AdamW
+    # on every rank (the library path, as the reference's accelerate DDP + AdamW)
+    dp_optimizer: str = "sharded"
 
 
 class SDXLDMAD:
@@ -94,9 +98,23 @@ class SDXLDMAD:
         self.gap_ema = torch.zeros(NUM_GAP_BANDS, device=self.device)
         self.gap_ready = torch.zeros(NUM_GAP_BANDS, device=self.device)
         cp = list(self.critic.parameters()) + list(self.head_real.parameters()) + list(self.head_teacher.parameters())
-        self.opt_g = torch.optim.AdamW(self.generator.parameters(), lr=cfg.generator_lr, betas=cfg.betas, foreach=True)
-        self.opt_c = torch.optim.AdamW([p for p in cp if p.requires_grad], lr=cfg.guidance_lr, betas=cfg.betas,
-                                       foreach=True)
+        gp = [p for p in self.generator.parameters() if p.requires_grad]
+        cp = [p for p in cp if p.requires_grad]
+        from ..parallel.dist import broadcast_module
+        for m in (self.generator, self.critic, self.head_real, self.head_teacher):
+            broadcast_module(m)
+        if cfg.dp_optimizer == "sharded":
+            from ..parallel.zero import ShardedAdamW
+            self.opt_g = ShardedAdamW(gp, lr=cfg.generator_lr, betas=cfg.betas)
+            self.opt_c = ShardedAdamW(cp, lr=cfg.guidance_lr, betas=cfg.betas)
+            self.sync_g = self.sync_c = None
+        elif cfg.dp_optimizer == "nccl":
+            from ..parallel.dp import GradSync
+            self.opt_g = torch.optim.AdamW(gp, lr=cfg.generator_lr, betas=cfg.betas, foreach=True)
+            self.opt_c = torch.optim.AdamW(cp, lr=cfg.guidance_lr, betas=cfg.betas, foreach=True)
+            self.sync_g, self.sync_c = GradSync(gp), GradSync(cp)
+        else:
+            raise ValueError(f"unknown dp_optimizer {cfg.dp_optimizer!r}")
         self.time_ids = torch.tensor([[cfg.resolution, cfg.resolution, 0, 0, cfg.resolution, cfg.resolution]],
                                      device=self.device, dtype=torch.float32)
 
@@ -191,6 +209,8 @@ class SDXLDMAD:
         tl = (-dt).mean() if w is None else (-dt * w).sum() / w.sum().clamp(min=1.0) + (-dt).sum() * 0.0
         loss_g = cfg.teacher_loss_weight * tl + cfg.real_loss_weight * (-dr).mean()
         loss_g.backward()
+        if self.sync_g is not None:
+            self.sync_g.sync()
         self.opt_g.step()
         self.opt_g.zero_grad(set_to_none=True)
         for p in self._critic_params():
@@ -202,6 +222,8 @@ class SDXLDMAD:
         loss_c = F.softplus(-dR_T).mean() + F.softplus(dR_G).mean() + F.softplus(-dQ_Q).mean() + F.softplus(dQ_G).mean()
         self.update_gap(dR_T.detach(), dR_Q.detach(), tc)
         loss_c.backward()
+        if self.sync_c is not None:
+            self.sync_c.sync()
         self.opt_c.step()
         self.opt_c.zero_grad(set_to_none=True)
         return {"generator_loss": loss_g.detach(), "critic_loss": loss_c.detach()}

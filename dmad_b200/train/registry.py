@@ -83,13 +83,19 @@ class _IterationAdapter:
     def context_parallel_nets(self) -> list:
         return []
 
+    @staticmethod
+    def _per_rank(o) -> bool:
+        """Optimisers whose state is this rank's shard (sharded data-parallel / FSDP) save per rank."""
+        return hasattr(o, "layout") or hasattr(o, "blocks")
+
     def state_dicts(self):
         shared = {f"module/{k}": m.state_dict() for k, m in self.modules.items()}
-        shared.update({f"optim/{k}": o.state_dict() for k, o in self.optims.items()})
+        shared.update({f"optim/{k}": o.state_dict() for k, o in self.optims.items() if not self._per_rank(o)})
+        per_rank = {f"optim/{k}": o.state_dict() for k, o in self.optims.items() if self._per_rank(o)}
         extra = getattr(self.model, "critic_state", None)
         if extra is not None:
             shared["critic_state"] = extra()
-        return shared, None
+        return shared, (per_rank or None)
 
     def export_artifacts(self, ckpt_dir: str):
         """Extra files of a published checkpoint (rank 0), e.g. the H3 LoRA exports."""
@@ -101,7 +107,12 @@ class _IterationAdapter:
         for k, m in self.modules.items():
             m.load_state_dict(shared[f"module/{k}"])
         for k, o in self.optims.items():
-            o.load_state_dict(shared[f"optim/{k}"])
+            if self._per_rank(o):
+                if not per_rank or f"optim/{k}" not in per_rank:
+                    raise RuntimeError(f"checkpoint has no per-rank state of the sharded optimiser {k!r}")
+                o.load_state_dict(per_rank[f"optim/{k}"])
+            else:
+                o.load_state_dict(shared[f"optim/{k}"])
         if "critic_state" in shared and hasattr(self.model, "load_critic_state"):
             self.model.load_critic_state(shared["critic_state"])
 
