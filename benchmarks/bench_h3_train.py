@@ -41,6 +41,10 @@ def main(argv=None):
     cfg = H3DMADConfig(model=model, fake_train_type=a.critic, shard_weights=world > 1)
     t0 = time.time()
     m = H3DMAD(cfg, device, dtype=torch.bfloat16, seed=0)
+    with torch.no_grad():  # the output projections start at zero; random weights so gradients flow
+        for net in (m.student, m.fake):
+            for lin in (net.proj_out, net.audio_proj_out):
+                lin.weight.normal_(0.0, 0.02, generator=torch.Generator(device=lin.weight.device).manual_seed(3))
     torch.cuda.synchronize()
     build_s = time.time() - t0
     for _ in range(a.warmup):

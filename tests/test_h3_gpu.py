@@ -109,6 +109,15 @@ def _h3_train_cfg(shard=False, full=False):
                         shard_weights=shard)
 
 
+def _nonzero_outputs(m):
+    """The H3 output projections start at zero (as in the reference), which keeps every gradient upstream
+    of them at zero on a random-init model; give them small weights so the test sees the updates."""
+    with torch.no_grad():
+        for net in (m.student, m.fake):
+            for lin in (net.proj_out, net.audio_proj_out):
+                lin.weight.normal_(0.0, 0.02, generator=torch.Generator(device=lin.weight.device).manual_seed(3))
+
+
 @pytest.mark.parametrize("full", [False, True])
 def test_h3_dmad_training_on_gpu(full):
     """Two H3 DMAD iterations (student and critic stages, LoRA or full critic) run on the GPU kernels with
@@ -117,6 +126,7 @@ def test_h3_dmad_training_on_gpu(full):
     from dmad_b200.distill.h3_dmad import H3DMAD
 
     m = H3DMAD(_h3_train_cfg(full=full), "cuda", dtype=torch.bfloat16)
+    _nonzero_outputs(m)
     before = [p.detach().clone() for p in m.s_params]
     fbefore = [p.detach().clone() for p in m.f_params]
     for _ in range(2):
@@ -141,6 +151,7 @@ def _h3_shard_worker(rank, world, port, q):
 
         _, _, dev = init_distributed(timeout_s=60)
         m = H3DMAD(_h3_train_cfg(shard=True, full=True), dev, dtype=torch.bfloat16)
+        _nonzero_outputs(m)
         losses = []
         for _ in range(2):
             out = m.train_iteration()
