@@ -545,46 +545,32 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   }
 }
 
-// ------------------------------------------------------------------ kernel B': dQ with Q and dO held in TMEM
-// Same work as kernel B.  The query tile's Q and dO are the A operands of every S = Q K^T and dP = dO V^T of
-// the CTA, so they are copied once from shared memory into TMEM (bf16 pairs, 64 columns each) and those
-// GEMMs take A from TMEM: per key tile the tensor core reads 96 KB of shared memory instead of 160 KB
-// (the shared-memory bandwidth, shared with the TMA writes, is what the split kernels run against).
-// The price is a single S buffer: S_{j+1} starts once the softmax warps have loaded S_j, which they do
-// first.  TMEM: S 0..127, dP / dS 128..255, dQ 256..383, Q 384..447, dO 448..511.
-struct DqSmemT {
+// ------------------------------------------------------------------ kernel B': dQ with dS staged in shared memory
+// Same work as kernel B, but dS goes from the softmax warps into a shared-memory tile (128-byte-swizzled,
+// K-major: query rows, key columns) instead of back over dP in TMEM, and dQ += dS K reads it from there.
+// That frees dP's TMEM columns as soon as the softmax warps have loaded dP_j, so the MMA thread issues
+// dP_{j+1} (and S_{j+1}) while tile j's dS is still being formed: the tensor pipe no longer waits for the
+// elementwise work of every tile.  TMEM: S double-buffered 0..255, dP 256..383, dQ 384..511.
+struct DqSmem2 {
   uint8_t q[kTileBytes];
   uint8_t g[kTileBytes];
   uint8_t k[2][kTileBytes];
   uint8_t v[2][kTileBytes];
-  uint64_t q_full, qo_ready;
+  uint8_t ds[kTileBytes];
+  uint64_t q_full;
   uint64_t kv_full[2], kv_empty[2];
-  uint64_t s_full, s_free, dp_full, ds_full, done;
+  uint64_t s_full[2], s_free[2];
+  uint64_t dp_full, dp_free, ds_full, ds_empty, done;
   uint32_t tmem_base;
   int abort_flag;
 };
 
-// Row `row` (this thread's TMEM lane) of a [128][64] 128-byte-swizzled bf16 half tile into 32 TMEM columns.
-__device__ __forceinline__ void half_row_to_tmem(const uint8_t* half_tile, int row, uint32_t taddr) {
-  uint32_t w[32];
-  const uint8_t* src = half_tile + row * 128;
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    const uint4 v = *reinterpret_cast<const uint4*>(src + ((c ^ (row & 7)) << 4));
-    w[4 * c] = v.x;
-    w[4 * c + 1] = v.y;
-    w[4 * c + 2] = v.z;
-    w[4 * c + 3] = v.w;
-  }
-  tmem_st32(taddr, w);
-}
-
 __global__ void __launch_bounds__(384, 1)
-flash_bwd_dq_tq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_g,
-                       BwdParams p) {
+flash_bwd_dq_smem_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_g,
+                         BwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  DqSmemT& sm = *reinterpret_cast<DqSmemT*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  DqSmem2& sm = *reinterpret_cast<DqSmem2*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   volatile int* abort_flag = &sm.abort_flag;
   const int warp = warp_id(), lane = lane_id();
   const int head = blockIdx.y, batch = blockIdx.z;
@@ -593,15 +579,16 @@ flash_bwd_dq_tq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 1);
-    mbar_init(&sm.qo_ready, 256);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sm.kv_full[s], 1);
       mbar_init(&sm.kv_empty[s], 1);
+      mbar_init(&sm.s_full[s], 1);
+      mbar_init(&sm.s_free[s], 256);
     }
-    mbar_init(&sm.s_full, 1);
-    mbar_init(&sm.s_free, 256);
     mbar_init(&sm.dp_full, 1);
+    mbar_init(&sm.dp_free, 256);
     mbar_init(&sm.ds_full, 256);
+    mbar_init(&sm.ds_empty, 1);
     mbar_init(&sm.done, 1);
     sm.abort_flag = 0;
     fence_barrier_init();
@@ -643,21 +630,22 @@ flash_bwd_dq_tq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
     if (elect_one()) {
       constexpr uint32_t idesc_kk = idesc_bf16_f32(128, 128, false, false);
       constexpr uint32_t idesc_mn = idesc_bf16_f32(128, 128, false, true);
-      const uint32_t t_s = tmem, t_dp = tmem + 128, t_dq = tmem + 256, t_q = tmem + 384, t_g = tmem + 448;
-      auto gemm_ts_k = [&](uint32_t d, uint32_t a_tmem, uint32_t b) {  // D = A[tmem] B^T, B K-major in smem
+      const uint32_t qa = smem_u32(sm.q), ga = smem_u32(sm.g), dsa = smem_u32(sm.ds);
+      const uint32_t t_dp = tmem + 256, t_dq = tmem + 384;
+      auto gemm_kk = [&](uint32_t d, uint32_t a, uint32_t b) {
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          mma_bf16_ts(d, a_tmem + kk * 8, smem_desc_sw128(b + off, 16, 1024), idesc_kk, kk > 0 ? 1u : 0u);
+          mma_bf16_ss(d, smem_desc_sw128(a + off, 16, 1024), smem_desc_sw128(b + off, 16, 1024), idesc_kk, kk > 0);
         }
       };
-      bool ok = mbar_wait(&sm.qo_ready, 0, kStatusTimeoutSoftmax, abort_flag, p.status);
+      bool ok = mbar_wait(&sm.q_full, 0, kStatusTimeoutTmaFull, abort_flag, p.status);
       if (ok) ok = mbar_wait(&sm.kv_full[0], 0, kStatusTimeoutTmaFull, abort_flag, p.status);
       if (ok) {
         tc_fence_after();
-        gemm_ts_k(t_s, t_q, smem_u32(sm.k[0]));
-        mma_commit(&sm.s_full);
-        gemm_ts_k(t_dp, t_g, smem_u32(sm.v[0]));
+        gemm_kk(tmem, qa, smem_u32(sm.k[0]));
+        mma_commit(&sm.s_full[0]);
+        gemm_kk(t_dp, ga, smem_u32(sm.v[0]));
         mma_commit(&sm.dp_full);
       }
       for (int j = 0; ok && j < nkv; ++j) {
@@ -667,61 +655,60 @@ flash_bwd_dq_tq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
         const uint32_t ph1 = ((j + 1) >> 1) & 1;
         if (has_next) {
           if (!(ok = mbar_wait(&sm.kv_full[s1], ph1, kStatusTimeoutTmaFull, abort_flag, p.status))) break;
-          if (!(ok = mbar_wait(&sm.s_free, j & 1, kStatusTimeoutSoftmax, abort_flag, p.status))) break;
+          if (j >= 1 && !(ok = mbar_wait(&sm.s_free[s1], ((j - 1) >> 1) & 1, kStatusTimeoutSoftmax, abort_flag, p.status)))
+            break;
           tc_fence_after();
-          gemm_ts_k(t_s, t_q, smem_u32(sm.k[s1]));
-          mma_commit(&sm.s_full);
+          gemm_kk(tmem + s1 * 128, qa, smem_u32(sm.k[s1]));
+          mma_commit(&sm.s_full[s1]);
+          // dP_{j+1} as soon as the softmax warps have loaded dP_j (not after dS_j is formed)
+          if (!(ok = mbar_wait(&sm.dp_free, j & 1, kStatusTimeoutSoftmax, abort_flag, p.status))) break;
+          tc_fence_after();
+          gemm_kk(t_dp, ga, smem_u32(sm.v[s1]));
+          mma_commit(&sm.dp_full);
         }
         if (!(ok = mbar_wait(&sm.ds_full, j & 1, kStatusTimeoutSoftmax, abort_flag, p.status))) break;
         tc_fence_after();
         const uint32_t kb = smem_u32(sm.k[s]);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)  // dQ += dS K (dS over dP in TMEM, K MN-major)
-          mma_bf16_ts(t_dq, t_dp + split_a_col(kk), smem_desc_sw128(kb + kk * 2048, kHalfBytes, 1024), idesc_mn,
-                      (j > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(&sm.kv_empty[s]);
-        if (has_next) {
-          gemm_ts_k(t_dp, t_g, smem_u32(sm.v[s1]));
-          mma_commit(&sm.dp_full);
+        for (int kk = 0; kk < 8; ++kk) {  // dQ += dS K (dS K-major in shared memory, K MN-major)
+          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          mma_bf16_ss(t_dq, smem_desc_sw128(dsa + off, 16, 1024), smem_desc_sw128(kb + kk * 2048, kHalfBytes, 1024),
+                      idesc_mn, (j > 0 || kk > 0) ? 1u : 0u);
         }
+        mma_commit(&sm.ds_empty);
+        mma_commit(&sm.kv_empty[s]);
       }
       mma_commit(&sm.done);
       mbar_wait(&sm.done, 0, kStatusTimeoutMma, nullptr, p.status);
     }
   } else if (warp >= 4) {
-    const int g = (warp - 4) >> 2;  // column group: key columns [64g, 64g + 64); Q / dO dims [64g, 64g + 64)
+    const int g = (warp - 4) >> 2;  // column group: key columns [64g, 64g + 64)
     const int c0 = 64 * g;
     const int wq = warp & 3;
     const int row = wq * 32 + lane;
     const int q_row = q0 + row;
     const uint32_t lb = (uint32_t)(wq * 32) << 16;
-    const uint32_t t_s = tmem + lb + c0, t_dp = tmem + lb + 128 + c0;
+    const uint32_t t_dp = tmem + lb + 256 + c0;
     const float scale_log2 = p.scale_log2, scale = p.scale;
     const int64_t bh_off = ((int64_t)batch * p.H + head) * p.Lpad;
     const float lse2 = p.lse2[bh_off + q_row];
     const float dval = p.dd[bh_off + q_row];
-    // this row's Q and dO into TMEM once (dims [64g, 64g + 64) -> 32 columns per group)
-    bool ok = __all_sync(0xffffffffu, mbar_wait(&sm.q_full, 0, kStatusTimeoutTmaFull, abort_flag, p.status));
-    if (ok) {
-      half_row_to_tmem(sm.q + g * kHalfBytes, row, tmem + lb + 384 + 32 * g);
-      half_row_to_tmem(sm.g + g * kHalfBytes, row, tmem + lb + 448 + 32 * g);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&sm.qo_ready);
-    }
-    for (int j = 0; ok && j < nkv; ++j) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&sm.s_full, j & 1, kStatusTimeoutMma, abort_flag, p.status));
+    uint8_t* ds_row = sm.ds + g * kHalfBytes + row * 128;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      const int s = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&sm.s_full[s], (j >> 1) & 1, kStatusTimeoutMma, abort_flag, p.status));
       if (!ok) break;
       tc_fence_after();
       float pv[64];
       const int kv_valid = p.Lk - j * 128 - c0;
       {
         uint32_t r[2][32];
-        tmem_ld32(t_s, r[0]);
-        tmem_ld32(t_s + 32, r[1]);
+        tmem_ld32(tmem + lb + s * 128 + c0, r[0]);
+        tmem_ld32(tmem + lb + s * 128 + c0 + 32, r[1]);
         tmem_wait_ld();
         tc_fence_before();
-        mbar_arrive(&sm.s_free);
+        mbar_arrive(&sm.s_free[s]);
         if (kv_valid >= 64) {
           const uint64_t sc2 = f2(scale_log2, scale_log2), nl2 = f2(-lse2, -lse2);
 #pragma unroll
@@ -749,13 +736,15 @@ flash_bwd_dq_tq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
       ok = __all_sync(0xffffffffu, mbar_wait(&sm.dp_full, j & 1, kStatusTimeoutMma, abort_flag, p.status));
       if (!ok) break;
       tc_fence_after();
+      uint32_t w[32];
       {
         uint32_t r[2][32];
         tmem_ld32(t_dp, r[0]);
         tmem_ld32(t_dp + 32, r[1]);
         tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&sm.dp_free);
         const uint64_t nd2 = f2(-dval, -dval), sc2 = f2(scale, scale);
-        uint32_t w[32];
 #pragma unroll
         for (int c = 0; c < 2; ++c)
 #pragma unroll
@@ -765,9 +754,17 @@ flash_bwd_dq_tq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
             const float2 d = f2_split(f2_mul(f2_mul(f2_add(dp2, nd2), f2(pv[kv], pv[kv + 1])), sc2));
             w[c * 16 + e] = pack_bf16x2(d.x, d.y);
           }
-        tmem_st32(t_dp, w);
       }
-      tmem_wait_st();
+      // the shared dS tile is free once dQ_{j-1} (its only reader) has completed
+      if (j > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&sm.ds_empty, (j - 1) & 1, kStatusTimeoutMma, abort_flag, p.status));
+        if (!ok) break;
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c)  // one 128-byte row of the swizzled [128 x 64] half tile
+        *reinterpret_cast<uint4*>(ds_row + ((c ^ (row & 7)) << 4)) =
+            make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+      fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&sm.ds_full);
     }
@@ -775,7 +772,7 @@ flash_bwd_dq_tq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_co
     if (ok) {
       tc_fence_after();
       __nv_bfloat16* dq_row = q_row < p.Lq ? p.out + batch * p.sb + (int64_t)q_row * p.sl + head * p.sh : nullptr;
-      store_row_bf16(dq_row, tmem + lb + 256, 1.f, c0, 2);
+      store_row_bf16(dq_row, tmem + lb + 384, 1.f, c0, 2);
     }
   }
   tc_fence_before();
@@ -1157,20 +1154,22 @@ void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, co
     p.sh = dq.stride(2);
     p.out2 = nullptr;
     dim3 grid((Lq + 127) / 128, H, B);
-    // DMAD_FLASH_BWD_DQ=tq: Q and dO held in TMEM (S and dP take A from TMEM); default: both from shared memory
-    static const bool dq_tq = [] {
+    // default: dS staged in shared memory (dP_{j+1} overlaps dS_j); DMAD_FLASH_BWD_DQ=tmem selects the
+    // variant that writes dS back over dP in TMEM
+    static const bool dq_in_tmem = [] {
       const char* e = std::getenv("DMAD_FLASH_BWD_DQ");
-      return e != nullptr && std::string(e) == "tq";
+      return e != nullptr && std::string(e) == "tmem";
     }();
-    if (dq_tq) {
-      const size_t smem = sizeof(DqSmemT) + 1024;
-      C10_CUDA_CHECK(
-          cudaFuncSetAttribute(flash_bwd_dq_tq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-      flash_bwd_dq_tq_kernel<<<grid, 384, smem, stream>>>(tq, tk, tv, tg, p);
-    } else {
+    if (dq_in_tmem) {
       const size_t smem = sizeof(DqSmem) + 1024;
       C10_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
       flash_bwd_dq_kernel<<<grid, 384, smem, stream>>>(tq, tk, tv, tg, p);
+    } else {
+      const size_t smem = sizeof(DqSmem2) + 1024;
+      static_assert(sizeof(DqSmem2) + 1024 <= 232448, "dQ kernel shared memory exceeds the per-CTA limit");
+      C10_CUDA_CHECK(
+          cudaFuncSetAttribute(flash_bwd_dq_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      flash_bwd_dq_smem_kernel<<<grid, 384, smem, stream>>>(tq, tk, tv, tg, p);
     }
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
