@@ -18,8 +18,6 @@
 // tile by columns: group g handles columns [64g, 64g + 64) and writes its bf16 P / dS packed over
 // the first half of its own columns; the TMEM-A MMAs take the halves from [0, 32) and [64, 96).
 #include <cuda_runtime.h>
-#include <cstdlib>
-#include <string>
 #include <cuda_bf16.h>
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -545,244 +543,6 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   }
 }
 
-// ------------------------------------------------------------------ kernel B': dQ with dS staged in shared memory
-// Same work as kernel B, but dS goes from the softmax warps into a shared-memory tile (128-byte-swizzled,
-// K-major: query rows, key columns) instead of back over dP in TMEM, and dQ += dS K reads it from there.
-// That frees dP's TMEM columns as soon as the softmax warps have loaded dP_j, so the MMA thread issues
-// dP_{j+1} (and S_{j+1}) while tile j's dS is still being formed: the tensor pipe no longer waits for the
-// elementwise work of every tile.  TMEM: S double-buffered 0..255, dP 256..383, dQ 384..511.
-struct DqSmem2 {
-  uint8_t q[kTileBytes];
-  uint8_t g[kTileBytes];
-  uint8_t k[2][kTileBytes];
-  uint8_t v[2][kTileBytes];
-  uint8_t ds[kTileBytes];
-  uint64_t q_full;
-  uint64_t kv_full[2], kv_empty[2];
-  uint64_t s_full[2], s_free[2];
-  uint64_t dp_full, dp_free, ds_full, ds_empty, done;
-  uint32_t tmem_base;
-  int abort_flag;
-};
-
-__global__ void __launch_bounds__(384, 1)
-flash_bwd_dq_smem_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                         const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_g,
-                         BwdParams p) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  DqSmem2& sm = *reinterpret_cast<DqSmem2*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  volatile int* abort_flag = &sm.abort_flag;
-  const int warp = warp_id(), lane = lane_id();
-  const int head = blockIdx.y, batch = blockIdx.z;
-  const int q0 = blockIdx.x * 128;
-  const int nkv = (p.Lk + 127) / 128;
-
-  if (threadIdx.x == 0) {
-    mbar_init(&sm.q_full, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&sm.kv_full[s], 1);
-      mbar_init(&sm.kv_empty[s], 1);
-      mbar_init(&sm.s_full[s], 1);
-      mbar_init(&sm.s_free[s], 256);
-    }
-    mbar_init(&sm.dp_full, 1);
-    mbar_init(&sm.dp_free, 256);
-    mbar_init(&sm.ds_full, 256);
-    mbar_init(&sm.ds_empty, 1);
-    mbar_init(&sm.done, 1);
-    sm.abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(&sm.tmem_base, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = sm.tmem_base;
-
-  if (warp == 0) {
-    if (elect_one()) {
-      mbar_arrive_expect_tx(&sm.q_full, 2 * kTileBytes);
-      for (int h = 0; h < 2; ++h) {
-        tma_load_4d(sm.q + h * kHalfBytes, &tm_q, &sm.q_full, h * 64, head, q0, batch);
-        tma_load_4d(sm.g + h * kHalfBytes, &tm_g, &sm.q_full, h * 64, head, q0, batch);
-      }
-      int last_s = -1;
-      uint32_t last_ph = 0;
-      for (int j = 0; j < nkv; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&sm.kv_empty[s], ph ^ 1, kStatusTimeoutEmpty, abort_flag, p.status)) break;
-        mbar_arrive_expect_tx(&sm.kv_full[s], 2 * kTileBytes);
-        for (int h = 0; h < 2; ++h) {
-          tma_load_4d(sm.k[s] + h * kHalfBytes, &tm_k, &sm.kv_full[s], h * 64, head, j * 128, batch);
-          tma_load_4d(sm.v[s] + h * kHalfBytes, &tm_v, &sm.kv_full[s], h * 64, head, j * 128, batch);
-        }
-        last_s = s;
-        last_ph = ph;
-      }
-      mbar_wait(&sm.q_full, 0, kStatusTimeoutTmaFull, nullptr, p.status);
-      if (last_s >= 0) mbar_wait(&sm.kv_full[last_s], last_ph, kStatusTimeoutTmaFull, nullptr, p.status);
-    }
-  } else if (warp == 1) {
-    if (elect_one()) {
-      constexpr uint32_t idesc_kk = idesc_bf16_f32(128, 128, false, false);
-      constexpr uint32_t idesc_mn = idesc_bf16_f32(128, 128, false, true);
-      const uint32_t qa = smem_u32(sm.q), ga = smem_u32(sm.g), dsa = smem_u32(sm.ds);
-      const uint32_t t_dp = tmem + 256, t_dq = tmem + 384;
-      auto gemm_kk = [&](uint32_t d, uint32_t a, uint32_t b) {
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          mma_bf16_ss(d, smem_desc_sw128(a + off, 16, 1024), smem_desc_sw128(b + off, 16, 1024), idesc_kk, kk > 0);
-        }
-      };
-      bool ok = mbar_wait(&sm.q_full, 0, kStatusTimeoutTmaFull, abort_flag, p.status);
-      if (ok) ok = mbar_wait(&sm.kv_full[0], 0, kStatusTimeoutTmaFull, abort_flag, p.status);
-      if (ok) {
-        tc_fence_after();
-        gemm_kk(tmem, qa, smem_u32(sm.k[0]));
-        mma_commit(&sm.s_full[0]);
-        gemm_kk(t_dp, ga, smem_u32(sm.v[0]));
-        mma_commit(&sm.dp_full);
-      }
-      for (int j = 0; ok && j < nkv; ++j) {
-        const int s = j & 1;
-        const bool has_next = j + 1 < nkv;
-        const int s1 = (j + 1) & 1;
-        const uint32_t ph1 = ((j + 1) >> 1) & 1;
-        if (has_next) {
-          if (!(ok = mbar_wait(&sm.kv_full[s1], ph1, kStatusTimeoutTmaFull, abort_flag, p.status))) break;
-          if (j >= 1 && !(ok = mbar_wait(&sm.s_free[s1], ((j - 1) >> 1) & 1, kStatusTimeoutSoftmax, abort_flag, p.status)))
-            break;
-          tc_fence_after();
-          gemm_kk(tmem + s1 * 128, qa, smem_u32(sm.k[s1]));
-          mma_commit(&sm.s_full[s1]);
-          // dP_{j+1} as soon as the softmax warps have loaded dP_j (not after dS_j is formed)
-          if (!(ok = mbar_wait(&sm.dp_free, j & 1, kStatusTimeoutSoftmax, abort_flag, p.status))) break;
-          tc_fence_after();
-          gemm_kk(t_dp, ga, smem_u32(sm.v[s1]));
-          mma_commit(&sm.dp_full);
-        }
-        if (!(ok = mbar_wait(&sm.ds_full, j & 1, kStatusTimeoutSoftmax, abort_flag, p.status))) break;
-        tc_fence_after();
-        const uint32_t kb = smem_u32(sm.k[s]);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {  // dQ += dS K (dS K-major in shared memory, K MN-major)
-          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          mma_bf16_ss(t_dq, smem_desc_sw128(dsa + off, 16, 1024), smem_desc_sw128(kb + kk * 2048, kHalfBytes, 1024),
-                      idesc_mn, (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        mma_commit(&sm.ds_empty);
-        mma_commit(&sm.kv_empty[s]);
-      }
-      mma_commit(&sm.done);
-      mbar_wait(&sm.done, 0, kStatusTimeoutMma, nullptr, p.status);
-    }
-  } else if (warp >= 4) {
-    const int g = (warp - 4) >> 2;  // column group: key columns [64g, 64g + 64)
-    const int c0 = 64 * g;
-    const int wq = warp & 3;
-    const int row = wq * 32 + lane;
-    const int q_row = q0 + row;
-    const uint32_t lb = (uint32_t)(wq * 32) << 16;
-    const uint32_t t_dp = tmem + lb + 256 + c0;
-    const float scale_log2 = p.scale_log2, scale = p.scale;
-    const int64_t bh_off = ((int64_t)batch * p.H + head) * p.Lpad;
-    const float lse2 = p.lse2[bh_off + q_row];
-    const float dval = p.dd[bh_off + q_row];
-    uint8_t* ds_row = sm.ds + g * kHalfBytes + row * 128;
-    bool ok = true;
-    for (int j = 0; j < nkv; ++j) {
-      const int s = j & 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(&sm.s_full[s], (j >> 1) & 1, kStatusTimeoutMma, abort_flag, p.status));
-      if (!ok) break;
-      tc_fence_after();
-      float pv[64];
-      const int kv_valid = p.Lk - j * 128 - c0;
-      {
-        uint32_t r[2][32];
-        tmem_ld32(tmem + lb + s * 128 + c0, r[0]);
-        tmem_ld32(tmem + lb + s * 128 + c0 + 32, r[1]);
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&sm.s_free[s]);
-        if (kv_valid >= 64) {
-          const uint64_t sc2 = f2(scale_log2, scale_log2), nl2 = f2(-lse2, -lse2);
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int e = 0; e < 32; e += 4) {
-              const float2 xa = f2_split(f2_fma(f2(__uint_as_float(r[c][e]), __uint_as_float(r[c][e + 1])), sc2, nl2));
-              const float2 xb =
-                  f2_split(f2_fma(f2(__uint_as_float(r[c][e + 2]), __uint_as_float(r[c][e + 3])), sc2, nl2));
-              const float2 pp = ex2_poly2(xa.y, xb.y);
-              pv[c * 32 + e] = ex2_approx(xa.x);
-              pv[c * 32 + e + 1] = pp.x;
-              pv[c * 32 + e + 2] = ex2_approx(xb.x);
-              pv[c * 32 + e + 3] = pp.y;
-            }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-              pv[c * 32 + e] =
-                  (c * 32 + e < kv_valid) ? ex2_approx(fmaf(__uint_as_float(r[c][e]), scale_log2, -lse2)) : 0.f;
-        }
-      }
-      ok = __all_sync(0xffffffffu, mbar_wait(&sm.dp_full, j & 1, kStatusTimeoutMma, abort_flag, p.status));
-      if (!ok) break;
-      tc_fence_after();
-      uint32_t w[32];
-      {
-        uint32_t r[2][32];
-        tmem_ld32(t_dp, r[0]);
-        tmem_ld32(t_dp + 32, r[1]);
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&sm.dp_free);
-        const uint64_t nd2 = f2(-dval, -dval), sc2 = f2(scale, scale);
-#pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {  // dS = P (dP - D) scale, two columns per packed op
-            const int kv = c * 32 + 2 * e;
-            const uint64_t dp2 = f2(__uint_as_float(r[c][2 * e]), __uint_as_float(r[c][2 * e + 1]));
-            const float2 d = f2_split(f2_mul(f2_mul(f2_add(dp2, nd2), f2(pv[kv], pv[kv + 1])), sc2));
-            w[c * 16 + e] = pack_bf16x2(d.x, d.y);
-          }
-      }
-      // the shared dS tile is free once dQ_{j-1} (its only reader) has completed
-      if (j > 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&sm.ds_empty, (j - 1) & 1, kStatusTimeoutMma, abort_flag, p.status));
-        if (!ok) break;
-      }
-#pragma unroll
-      for (int c = 0; c < 8; ++c)  // one 128-byte row of the swizzled [128 x 64] half tile
-        *reinterpret_cast<uint4*>(ds_row + ((c ^ (row & 7)) << 4)) =
-            make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(&sm.ds_full);
-    }
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.done, 0, kStatusTimeoutMma, abort_flag, p.status));
-    if (ok) {
-      tc_fence_after();
-      __nv_bfloat16* dq_row = q_row < p.Lq ? p.out + batch * p.sb + (int64_t)q_row * p.sl + head * p.sh : nullptr;
-      store_row_bf16(dq_row, tmem + lb + 384, 1.f, c0, 2);
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
 // ------------------------------------------------------------------ fused kernel: dK, dV and dQ
 // One CTA per 128-key tile, as kernel A, that also forms dQ_i = dS_i K for every query tile i and adds
 // it into an fp32 accumulator [B, H, Lpad, 128] with vector reductions (red.global.add.v4.f32): five
@@ -1153,24 +913,10 @@ void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, co
     p.sl = dq.stride(1);
     p.sh = dq.stride(2);
     p.out2 = nullptr;
+    const size_t smem = sizeof(DqSmem) + 1024;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid((Lq + 127) / 128, H, B);
-    // default: dS staged in shared memory (dP_{j+1} overlaps dS_j); DMAD_FLASH_BWD_DQ=tmem selects the
-    // variant that writes dS back over dP in TMEM
-    static const bool dq_in_tmem = [] {
-      const char* e = std::getenv("DMAD_FLASH_BWD_DQ");
-      return e != nullptr && std::string(e) == "tmem";
-    }();
-    if (dq_in_tmem) {
-      const size_t smem = sizeof(DqSmem) + 1024;
-      C10_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-      flash_bwd_dq_kernel<<<grid, 384, smem, stream>>>(tq, tk, tv, tg, p);
-    } else {
-      const size_t smem = sizeof(DqSmem2) + 1024;
-      static_assert(sizeof(DqSmem2) + 1024 <= 232448, "dQ kernel shared memory exceeds the per-CTA limit");
-      C10_CUDA_CHECK(
-          cudaFuncSetAttribute(flash_bwd_dq_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-      flash_bwd_dq_smem_kernel<<<grid, 384, smem, stream>>>(tq, tk, tv, tg, p);
-    }
+    flash_bwd_dq_kernel<<<grid, 384, smem, stream>>>(tq, tk, tv, tg, p);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }
