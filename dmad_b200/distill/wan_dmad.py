@@ -99,6 +99,9 @@ class WanDMADConfig:
     # student): bf16 shards gathered one block ahead, gradients reduce-scattered per block in backward,
     # AdamW on the shards; the blocks are then activation-checkpointed
     fsdp_trainable: bool = False
+    # hybrid sharding (HSDP): shard the block weights over groups of this many consecutive ranks and
+    # replicate across the groups (None: shard over all ranks)
+    fsdp_shard_size: int | None = None
     dp_optimizer: str = "sharded"
     dp_multicast: bool = True
     dp_sync_timeout_s: float = 120.0
@@ -166,11 +169,16 @@ class WanDMAD(nn.Module):
                 self.sharded.append(ShardedFrozenBlocks(self.net_teacher.blocks))
         self.fsdp = {}
         if cfg.fsdp_trainable:
-            from ..parallel.fsdp import ShardedTrainableBlocks
+            from ..parallel.dist import get_world_size
+            from ..parallel.fsdp import ShardedTrainableBlocks, hsdp_groups
             if cfg.dp_optimizer != "sharded":
                 raise ValueError("fsdp_trainable runs with dp_optimizer='sharded'")
+            shard_group = rep_group = None
+            if cfg.fsdp_shard_size and cfg.fsdp_shard_size < get_world_size():
+                shard_group, rep_group = hsdp_groups(cfg.fsdp_shard_size)
             kw_b = dict(betas=cfg.betas, eps=cfg.eps, weight_decay=cfg.weight_decay,
-                        sync_timeout_s=cfg.dp_sync_timeout_s, force_finite=cfg.grad_force_finite)
+                        sync_timeout_s=cfg.dp_sync_timeout_s, force_finite=cfg.grad_force_finite,
+                        group=shard_group, replicate_group=rep_group)
             nl = cfg.net.num_layers
             cfg.checkpoint_critic_blocks = cfg.checkpoint_critic_blocks_student_phase = nl
             self.net_fake_score.checkpoint_blocks = nl

@@ -175,9 +175,15 @@ class ShardedTrainableBlocks(ShardedFrozenBlocks):
     """
 
     def __init__(self, blocks, lr=1e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0, ema: bool = False,
-                 group=None, slots: int = 3, sync_timeout_s: float = 120.0, force_finite: bool = False):
+                 group=None, slots: int = 3, sync_timeout_s: float = 120.0, force_finite: bool = False,
+                 replicate_group=None):
+        """``group``: the ranks the weights are sharded over; ``replicate_group`` (hybrid sharding, HSDP):
+        the ranks holding the same shard in other sharding groups, whose shard gradients are summed before
+        the update (the data-parallel average runs over both)."""
         self._select_trainable = True
         super().__init__(blocks, group=group, slots=slots)
+        self.replicate_group = replicate_group
+        self.replicas = get_world_size(replicate_group) if replicate_group is not None else 1
         self.lr, self.betas, self.eps, self.weight_decay = lr, tuple(betas), eps, weight_decay
         self.force_finite = force_finite
         self.step_count = 0
@@ -261,14 +267,16 @@ class ShardedTrainableBlocks(ShardedFrozenBlocks):
         self.step_count += 1
         total = self.master.numel()
         shard = self.arena.tensor[:total]
-        g = self.grad_acc / self.world
+        if self.replicas > 1:  # HSDP: the same shard's gradient from every replica
+            dist.all_reduce(self.grad_acc, group=self.replicate_group)
+        g = self.grad_acc / (self.world * self.replicas)
         if self.force_finite:
             g = torch.nan_to_num(g, nan=0.0, posinf=0.0, neginf=0.0)
         scale = None
         if max_grad_norm is not None and math.isfinite(max_grad_norm) and max_grad_norm < 1e11:
             ss = (g * g).sum().reshape(1)
             if is_distributed() and self.world > 1:
-                dist.all_reduce(ss, group=self.group)
+                dist.all_reduce(ss, group=self.group)  # replicas hold the same shards: the shard group covers all
             norm = ss.sqrt()
             scale = torch.clamp(max_grad_norm / (norm + 1e-6), max=1.0)
             scale = torch.where(torch.isfinite(norm), scale, torch.zeros_like(scale))
@@ -468,3 +476,25 @@ class FSDPOptimizer:
         self.blocks.load_state_dict(sd["blocks"])
         if self.rest is not None and sd.get("rest") is not None:
             self.rest.load_state_dict(sd["rest"])
+
+
+def hsdp_groups(shard_size: int):
+    """(shard group, replicate group) of this rank for hybrid sharding over the world: consecutive blocks
+    of ``shard_size`` ranks shard the weights, and ranks at the same position of every block replicate
+    them (the reference's (replicate, shard) device mesh, train/wan/rcm/utils/fsdp_helper.py:96-149).
+    Collective: every rank creates every group in the same order."""
+    world, rank = get_world_size(), get_rank()
+    if shard_size <= 0 or world % shard_size:
+        raise ValueError(f"world size {world} is not divisible by the sharding group size {shard_size}")
+    shard = rep = None
+    for b in range(world // shard_size):
+        ranks = list(range(b * shard_size, (b + 1) * shard_size))
+        g = dist.new_group(ranks)
+        if rank in ranks:
+            shard = g
+    for i in range(shard_size):
+        ranks = list(range(i, world, shard_size))
+        g = dist.new_group(ranks)
+        if rank in ranks:
+            rep = g
+    return shard, rep

@@ -184,3 +184,65 @@ def test_wan_dmad_fsdp_trainable_matches_sharded_optimizer():
         assert l0 == l1, (l0, l1)
         assert same
         assert resume[0] == resume[1], resume
+
+
+def _hsdp_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    try:
+        import copy
+
+        import torch.distributed as dist
+        from dmad_b200.distill.wan_dmad import WanDMAD, WanDMADConfig
+        from dmad_b200.models.wan import WanConfig
+        from dmad_b200.parallel.dist import init_distributed
+
+        init_distributed(backend="gloo", timeout_s=120)
+        net = WanConfig(dim=128, ffn_dim=256, num_heads=1, num_layers=2, text_dim=32, freq_dim=64)
+        g = torch.Generator().manual_seed(60 + rank)
+        shp = (1, 16, 2, 4, 8)
+        batch = {"latents": torch.randn(shp, generator=g), "real_latents": torch.randn(shp, generator=g),
+                 "context": torch.randn(1, 5, 32, generator=g)}
+        out = {}
+        for mode in ("replicated", "hsdp"):
+            cfg = WanDMADConfig(net=net, sn_power_iters=2, fsdp_trainable=mode == "hsdp", fsdp_shard_size=2,
+                                checkpoint_student_blocks=2, checkpoint_critic_blocks=2,
+                                checkpoint_critic_blocks_student_phase=2)
+            m = WanDMAD(cfg, device="cpu", dtype=torch.float32, seed=0)
+            with torch.no_grad():
+                for n_ in (m.net, m.net_fake_score):
+                    torch.nn.init.normal_(n_.head.head.weight, std=0.05, generator=torch.Generator().manual_seed(9))
+            torch.manual_seed(5 + rank)
+            losses = [float(m.training_step(batch, it).get("dmad_g_loss", 0.0)) for it in range(4)]
+            out[mode] = (losses, copy.deepcopy(m.state_dicts()[0]))
+            if mode == "hsdp":
+                sh = m.fsdp["critic"]
+                out["sizes"] = (sh.world, sh.replicas)
+        err = max(float((out["replicated"][1][k][n].float() - out["hsdp"][1][k][n].float()).abs().max())
+                  for k in ("net", "net_fake_score") for n in out["replicated"][1][k])
+        q.put((rank, out["replicated"][0], out["hsdp"][0], err, out["sizes"], None))
+        dist.destroy_process_group()
+    except Exception:  # pragma: no cover
+        import traceback
+        q.put((rank, None, None, None, None, traceback.format_exc()))
+
+
+def test_wan_dmad_hsdp_matches_replicated():
+    """Hybrid sharding on 4 gloo ranks: block weights sharded over pairs of ranks and replicated across
+    the pairs train as plain data parallelism does (each rank its own sample)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_hsdp_worker, args=(r, 4, port, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=900) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, l0, l1, err, sizes, e in res:
+        assert e is None, e
+        assert sizes == (2, 2)
+        # four gradients are summed pairwise, then across the pairs, instead of in one all-reduce
+        for a, b in zip(l0, l1):
+            assert abs(a - b) <= 1e-5 * max(1.0, abs(a)), (l0, l1)
+        assert err < 1e-5, err
