@@ -59,6 +59,8 @@ def parse():
                          "GPUs, NVLS above, as measured by benchmarks/bench_collectives.py)")
     ap.add_argument("--fsdp", action="store_true",
                     help="FSDP-style sharding of the trainable block weights (critic, and the student unless LoRA)")
+    ap.add_argument("--fsdp-shard-size", type=int, default=None,
+                    help="with --fsdp: shard within groups of this many ranks, replicate across them (HSDP)")
     ap.add_argument("--dp-optimizer", default="sharded", choices=["sharded", "replicated"],
                     help="sharded: fused reduce-scatter/AdamW/all-gather kernel; replicated: NCCL all-reduce baseline")
     return ap.parse_args()
@@ -209,7 +211,7 @@ def main():
         over = {"num_layers": args.layers} if args.layers else {}
         multicast = {"nvls": True, "p2p": False, "auto": world > 2}[args.dp_path]
         cfg = WanDMADConfig(net=wan_config(args.model, **over), dp_optimizer=args.dp_optimizer, dp_multicast=multicast,
-                            fsdp_trainable=args.fsdp)
+                            fsdp_trainable=args.fsdp, fsdp_shard_size=args.fsdp_shard_size)
         cfg.checkpoint_critic_blocks_student_phase = cfg.net.num_layers
         big = "14b" in args.model.lower()
         cfg.loss_scale = args.cm_loss_scale if args.cm_loss_scale is not None else (100.0 if big else 0.0)
