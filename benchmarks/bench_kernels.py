@@ -28,6 +28,14 @@ def peak_tflops():
         return 1590.0, "fallback"
 
 
+def _peak_hbm():
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    try:
+        return float(json.load(open(p))["hbm_gbs"])
+    except Exception:
+        return 6650.0
+
+
 def _reference_jvp():
     """The reference's Triton JVP attention (`_attention.apply`) from baseline/_ref, or None."""
     import sys
@@ -80,7 +88,8 @@ def main():
     ap.add_argument("--H", type=int, default=12)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--only", default="all", choices=["all", "fwd", "bwd", "bwd_fused", "sdpa", "jvp", "ref_jvp", "gemm"])
+    ap.add_argument("--only", default="all", choices=["all", "fwd", "bwd", "bwd_fused", "sdpa", "jvp", "ref_jvp", "gemm",
+                                                      "rows"])
     ap.add_argument("--gemm", default="32760,8960,1536", help="M,N,K of the GEMM benchmark")
     ap.add_argument("--rank", type=int, default=128, help="LoRA rank of the GEMM benchmark")
     a = ap.parse_args()
@@ -167,6 +176,34 @@ def main():
         fl_lora = fl + 2.0 * M * r * (K + N)
         res.append(("lora_linear_sm100", timeit(ours_lora, a.iters, a.warmup), fl_lora))
         res.append(("cublas_linear_plus_lora", timeit(peft_lora, a.iters, a.warmup), fl_lora))
+    if a.only == "rows":
+        # the memory-bound row kernels of a Wan-1.3B block at 32,760 tokens: bytes moved per call against
+        # the measured copy bandwidth
+        import torch.nn.functional as F
+        from dmad_b200 import ops as O
+        R, D, F_ = 32760, 1536, 8960
+        hbm = _peak_hbm()
+        x = torch.randn(R, D, device="cuda", dtype=torch.bfloat16)
+        amod = torch.randn(21, D, device="cuda") * 0.1
+        cmod = torch.randn(21, D, device="cuda") * 0.1
+        qkv = torch.randn(R, 3 * D, device="cuda", dtype=torch.bfloat16)
+        wq, wk = torch.ones(D, device="cuda"), torch.ones(D, device="cuda")
+        ang = torch.rand(R, 64, device="cuda")
+        cos, sin = ang.cos(), ang.sin()
+        h = torch.randn(R, F_, device="cuda", dtype=torch.bfloat16)
+        gate = torch.randn(21, D, device="cuda") * 0.1
+        y = torch.randn_like(x)
+        rows = [
+            ("ln_mod_fwd", lambda: O.ln_mod(x, amod, cmod, 1.0, 1560, eps=1e-6), 2 * R * D * 2),
+            ("gate_residual_fwd", lambda: O.gate_residual(x, y, gate, 1560), 3 * R * D * 2),
+            ("qk_norm_rope_fwd", lambda: O.qk_norm_rope(qkv, wq, wk, cos, sin, D, 128), (3 + 2) * R * D * 2),
+            ("gelu_tanh_fwd", lambda: O.gelu_tanh(h), 2 * R * F_ * 2),
+        ]
+        for name, fn, nbytes in rows:
+            ms = timeit(fn, a.iters, a.warmup)
+            print(json.dumps({"op": name, "rows": R, "ms": round(ms, 4), "GB/s": round(nbytes / ms / 1e6, 1),
+                              "frac_of_measured_hbm": round(nbytes / ms / 1e6 / hbm, 3)}))
+        return
     for name, ms, fl in res:
         tf = fl / (ms * 1e-3) / 1e12
         print(json.dumps({"op": name, "B": B, "L": L, "Lk": Lk, "H": H, "ms": round(ms, 4), "tflops": round(tf, 1),

@@ -14,6 +14,7 @@
 //     (rcm/utils/rope.py:36-70) from cos/sin tables.
 //   * gelu_tanh_fwd / _bwd.
 #include <torch/extension.h>
+#include <type_traits>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include "common.cuh"
@@ -95,6 +96,90 @@ ln_mod_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx, __nv_bfloat16
   if (threadIdx.x == 0) {
     if (mean_out != nullptr) mean_out[r] = mu;
     rstd_out[r] = rstd;
+  }
+}
+
+// Forward for rows of up to 1536 columns: one warp per row, every lane holding kV 8-column vectors of
+// the row (all loads issued up front), shuffle reductions only (no shared memory, no block barriers).
+// Each warp walks kRows consecutive rows; the modulation rows A / C (fp32, shared by the rows of a
+// group) are re-read per row from L1 rather than held in registers, which keeps two CTAs per SM.
+template <int kV, int kRows>
+__global__ void __launch_bounds__(256, 2)
+ln_mod_fwd_warp_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx, __nv_bfloat16* __restrict__ y, int64_t sy,
+                       float* __restrict__ mean_out, float* __restrict__ rstd_out, ModSpec m, int64_t R, int D,
+                       float eps, bool rms) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r0 = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * kRows;
+  const int nvec = D >> 3;
+#pragma unroll 1
+  for (int rr = 0; rr < kRows; ++rr) {
+    const int64_t r = r0 + rr;
+    if (r >= R) return;
+    const bf16x8* xr = reinterpret_cast<const bf16x8*>(x + r * sx);
+    float v[kV][8];
+    {
+      bf16x8 raw[kV];
+#pragma unroll
+      for (int i = 0; i < kV; ++i) {
+        const int c = lane + 32 * i;
+        if (c < nvec) raw[i] = xr[c];
+      }
+#pragma unroll
+      for (int i = 0; i < kV; ++i) {
+        const int c = lane + 32 * i;
+        if (c < nvec) bf16x8_to_float(raw[i], v[i]);
+      }
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < kV; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nvec) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s += v[i][e];
+      }
+    }
+    const float mu = rms ? 0.f : warp_sum(s) / D;
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kV; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nvec) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float d = v[i][e] - mu;
+          ss += d * d;
+        }
+      }
+    }
+    const float rstd = rsqrtf(warp_sum(ss) / D + eps);
+    const int g = row_group(m, r);
+    const float* ar = m.a != nullptr ? m.a + (int64_t)g * m.a_sg : nullptr;
+    const float* cr = m.c != nullptr ? m.c + (int64_t)g * m.c_sg : nullptr;
+    bf16x8* yr = reinterpret_cast<bf16x8*>(y + r * sy);
+#pragma unroll
+    for (int i = 0; i < kV; ++i) {
+      const int c = lane + 32 * i;
+      if (c < nvec) {
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 8; e += 4) {
+          const float4 av = ar != nullptr ? __ldg(reinterpret_cast<const float4*>(ar + c * 8 + e))
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float4 cv = cr != nullptr ? __ldg(reinterpret_cast<const float4*>(cr + c * 8 + e))
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+          o[e] = (v[i][e] - mu) * rstd * (m.a_add + av.x) + cv.x;
+          o[e + 1] = (v[i][e + 1] - mu) * rstd * (m.a_add + av.y) + cv.y;
+          o[e + 2] = (v[i][e + 2] - mu) * rstd * (m.a_add + av.z) + cv.z;
+          o[e + 3] = (v[i][e + 3] - mu) * rstd * (m.a_add + av.w) + cv.w;
+        }
+        yr[c] = float_to_bf16x8(o);
+      }
+    }
+    if (lane == 0) {
+      if (mean_out != nullptr) mean_out[r] = mu;
+      rstd_out[r] = rstd;
+    }
   }
 }
 
@@ -523,12 +608,31 @@ void ln_mod_fwd(const at::Tensor& x, at::Tensor& y, c10::optional<at::Tensor> me
   float* mp = (mean.has_value() && mean->defined()) ? mean->data_ptr<float>() : nullptr;
   TORCH_CHECK(rms || mp != nullptr, "LayerNorm needs a mean buffer");
   if (R == 0) return;
-  DMAD_ROW_DISPATCH(D / 8, [&] {
-    ln_mod_fwd_kernel<VEC, TH><<<(unsigned)R, TH, 0, at::cuda::getCurrentCUDAStream()>>>(
-        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
-        reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), y.stride(0), mp, rstd.data_ptr<float>(), m, R, (int)D,
-        (float)eps, rms);
-  });
+  const auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  const auto yp = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  // the modulation rows are read as float4: the warp kernel needs them 16-byte aligned
+  const bool mod_aligned = (m.a == nullptr || (reinterpret_cast<uintptr_t>(m.a) % 16 == 0 && m.a_sg % 4 == 0)) &&
+                           (m.c == nullptr || (reinterpret_cast<uintptr_t>(m.c) % 16 == 0 && m.c_sg % 4 == 0));
+  if (D <= 1536 && mod_aligned) {
+    constexpr int kRows = 4;
+    const int64_t warps = (R + kRows - 1) / kRows;
+    const unsigned blocks = (unsigned)((warps + 7) / 8);
+    auto launch = [&](auto kv) {
+      constexpr int V = decltype(kv)::value;
+      ln_mod_fwd_warp_kernel<V, kRows><<<blocks, 256, 0, stream>>>(xp, x.stride(0), yp, y.stride(0), mp,
+                                                                   rstd.data_ptr<float>(), m, R, (int)D, (float)eps, rms);
+    };
+    const int nv = (int)((D / 8 + 31) / 32);
+    if (nv <= 2) launch(std::integral_constant<int, 2>{});
+    else if (nv <= 4) launch(std::integral_constant<int, 4>{});
+    else launch(std::integral_constant<int, 6>{});
+  } else {
+    DMAD_ROW_DISPATCH(D / 8, [&] {
+      ln_mod_fwd_kernel<VEC, TH><<<(unsigned)R, TH, 0, stream>>>(xp, x.stride(0), yp, y.stride(0), mp,
+                                                                  rstd.data_ptr<float>(), m, R, (int)D, (float)eps, rms);
+    });
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
