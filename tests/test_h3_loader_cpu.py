@@ -121,3 +121,33 @@ def test_h3_dmad_trainer_starts_from_model_dir(tmp_path):
             torch.testing.assert_close(got[k], want[k], rtol=0, atol=0)
     out = m.train_iteration()
     assert all(torch.isfinite(torch.tensor(v)) for v in out["student"].values())
+
+
+def test_diffusers_pipeline_runner_matches_euler_inference(tmp_path):
+    """The Diffusers-runner CLI (the reference's run_diffusers_pipeline.py flags) samples with the LoRA
+    attached and the Euler step rule: the same latents as ``h3_inference --euler`` with the same settings,
+    and one output per prompt."""
+    import os
+
+    from dmad_b200.cli.diffusers_pipeline import main as runner
+    from dmad_b200.cli.h3_inference import main as h3
+    from dmad_b200.lora import save_lora_file
+
+    _tiny_folder(tmp_path)
+    (tmp_path / "vae").mkdir()
+    json.dump({"spatial_downsample_factors": [2, 2, 2, 2]}, open(tmp_path / "vae" / "config.json", "w"))
+    g = torch.Generator().manual_seed(4)
+    pairs = {f"transformer_blocks.{i}.attn.{n}": {"A": torch.randn(4, 64, generator=g) * 0.05,
+                                                   "B": torch.randn(64, 4, generator=g) * 0.05}
+             for i in range(2) for n in ("to_q", "to_v")}
+    lora = str(tmp_path / "student.safetensors")
+    save_lora_file(lora, pairs, 4, 4.0)
+    common = ["--model-dir", str(tmp_path), "--lora", lora, "--prompt", "a fox", "--prompt", "a cat", "--steps", "2",
+              "--height", "64", "--width", "64", "--num-frames", "22", "--text-tokens", "4", "--seed", "7"]
+    out = runner(common + ["--output-dir", str(tmp_path / "runner")])
+    ref = h3(common + ["--output-dir", str(tmp_path / "ref"), "--euler"])
+    assert len(out) == 2
+    for (v, a), (rv, ra) in zip(out, ref):
+        assert torch.equal(v, rv) and torch.equal(a, ra)
+    files = sorted(os.listdir(tmp_path / "runner"))
+    assert "settings.json" in files and "0000.txt" in files and "0001.txt" in files
