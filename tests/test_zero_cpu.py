@@ -61,8 +61,9 @@ def _worker(rank, world, port, steps, clip, q):
             for p, g in zip(params, _grads(rank, s, params)):
                 p.grad.add_(g)  # accumulate into the flat-buffer view, as autograd does
             opt.step(ema_beta=0.9, max_grad_norm=clip)
-        ema = opt.full_ema()
-        q.put((rank, [p.detach().clone() for p in params], ema, None))
+        # numpy arrays: tensors sent through the queue would need the worker alive to be received
+        ema = [e.numpy() for e in opt.full_ema()]
+        q.put((rank, [p.detach().numpy().copy() for p in params], ema, None))
         dist.destroy_process_group()
     except Exception as e:  # pragma: no cover
         q.put((rank, None, None, repr(e)))
@@ -84,9 +85,9 @@ def test_sharded_adamw_matches_replicated(clip):
     for rank, w, ema, err in res:
         assert err is None, err
         for a, b in zip(w, ref_w):
-            torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6)
+            torch.testing.assert_close(torch.from_numpy(a), b, rtol=1e-5, atol=1e-6)
         for a, b in zip(ema, ref_ema):
-            torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6)
+            torch.testing.assert_close(torch.from_numpy(a), b, rtol=1e-5, atol=1e-6)
 
 
 def test_flat_views_single_process():
