@@ -110,7 +110,8 @@ struct DkvSmem {
   float dd[2][128];
   uint64_t kv_full;
   uint64_t q_full[2], q_empty[2];
-  uint64_t s_full, dp_full, p_full, ds_full, done;
+  uint64_t s_full, dp_full, done;
+  uint64_t p_part[4], ds_part[4];  // part 2g + c: query columns [64g + 32c, +32) of P^T / dS^T
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -136,8 +137,10 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
     }
     mbar_init(&sm.s_full, 1);
     mbar_init(&sm.dp_full, 1);
-    mbar_init(&sm.p_full, 256);
-    mbar_init(&sm.ds_full, 256);
+    for (int q = 0; q < 4; ++q) {
+      mbar_init(&sm.p_part[q], 128);
+      mbar_init(&sm.ds_part[q], 128);
+    }
     mbar_init(&sm.done, 1);
     sm.abort_flag = 0;
     fence_barrier_init();
@@ -190,11 +193,21 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
           mma_bf16_ss(d, smem_desc_sw128(a + off, 16, 1024), smem_desc_sw128(b + off, 16, 1024), idesc_kk, kk > 0);
         }
       };
-      auto gemm_ts = [&](uint32_t d, uint32_t a_tmem, uint32_t b, bool acc) {
+      // D (+)= A B with A in TMEM (P^T or dS^T), handed over in four parts of 32 columns (K steps 2q and
+      // 2q + 1 for part q), issued as each part lands: parts 0 and 2 (the first halves of the two
+      // column groups, written at the same time) before 1 and 3.
+      auto ts_parts = [&](uint64_t* parts, uint32_t parity, uint32_t d, uint32_t a_tmem, uint32_t b, bool acc) {
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_bf16_ts(d, a_tmem + split_a_col(kk), smem_desc_sw128(b + kk * 2048, kHalfBytes, 1024), idesc_mn,
-                      (acc || kk > 0) ? 1u : 0u);
+        for (int n = 0; n < 4; ++n) {
+          const int q = (n & 1) * 2 + (n >> 1);
+          if (!mbar_wait(&parts[q], parity, kStatusTimeoutSoftmax, abort_flag, p.status)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 2 * q; kk < 2 * q + 2; ++kk)
+            mma_bf16_ts(d, a_tmem + split_a_col(kk), smem_desc_sw128(b + kk * 2048, kHalfBytes, 1024), idesc_mn,
+                        (acc || kk > 0) ? 1u : 0u);
+        }
+        return true;
       };
       bool ok = mbar_wait(&sm.kv_full, 0, kStatusTimeoutTmaFull, abort_flag, p.status);
       if (ok) ok = mbar_wait(&sm.q_full[0], 0, kStatusTimeoutTmaFull, abort_flag, p.status);
@@ -210,18 +223,14 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         const bool has_next = i + 1 < nq;
         const int s1 = (i + 1) & 1;
         const uint32_t ph1 = ((i + 1) >> 1) & 1;
-        if (!(ok = mbar_wait(&sm.p_full, i & 1, kStatusTimeoutSoftmax, abort_flag, p.status))) break;
-        tc_fence_after();
-        gemm_ts(t_dv, t_s, smem_u32(sm.g[s]), i > 0);
+        if (!(ok = ts_parts(sm.p_part, i & 1, t_dv, t_s, smem_u32(sm.g[s]), i > 0))) break;
         if (has_next) {
           if (!(ok = mbar_wait(&sm.q_full[s1], ph1, kStatusTimeoutTmaFull, abort_flag, p.status))) break;
           tc_fence_after();
           gemm_kk(t_s, ka, smem_u32(sm.q[s1]));
           mma_commit(&sm.s_full);
         }
-        if (!(ok = mbar_wait(&sm.ds_full, i & 1, kStatusTimeoutSoftmax, abort_flag, p.status))) break;
-        tc_fence_after();
-        gemm_ts(t_dk, t_dp, smem_u32(sm.q[s]), i > 0);
+        if (!(ok = ts_parts(sm.ds_part, i & 1, t_dk, t_dp, smem_u32(sm.q[s]), i > 0))) break;
         mma_commit(&sm.q_empty[s]);
         if (has_next) {
           gemm_kk(t_dp, va, smem_u32(sm.g[s1]));
@@ -271,15 +280,16 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
             pv[c * 32 + e + 3] = pp.y;
           }
       }
-      {
-        uint32_t w[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) w[e] = pack_bf16x2(pv[2 * e], pv[2 * e + 1]);
-        tmem_st32(t_s, w);
+      for (int c = 0; c < 2; ++c) {  // P^T to the MMA thread in two parts of 32 query columns
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) w[e] = pack_bf16x2(pv[c * 32 + 2 * e], pv[c * 32 + 2 * e + 1]);
+        tmem_st16(t_s + 16 * c, w);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&sm.p_part[2 * g + c]);
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&sm.p_full);
 
       ok = __all_sync(0xffffffffu, mbar_wait(&sm.dp_full, i & 1, kStatusTimeoutMma, abort_flag, p.status));
       if (!ok) break;
@@ -293,7 +303,7 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         const uint64_t sc2 = f2(scale, scale);
         uint32_t w[32];
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+        for (int c = 0; c < 2; ++c) {
 #pragma unroll
           for (int e = 0; e < 16; ++e) {  // dS = P (dP - D) scale, two columns per packed op
             const int q = c * 32 + 2 * e;
@@ -302,11 +312,13 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
             const float2 d = f2_split(ds2);
             w[c * 16 + e] = pack_bf16x2(d.x, d.y);
           }
-        tmem_st32(t_dp, w);
+          // hand this part of dS^T to the MMA thread
+          tmem_st16(t_dp + 16 * c, *reinterpret_cast<const uint32_t(*)[16]>(w + 16 * c));
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&sm.ds_part[2 * g + c]);
+        }
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&sm.ds_full);
     }
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.done, 0, kStatusTimeoutMma, abort_flag, p.status));
     if (ok) {
@@ -336,7 +348,8 @@ struct DqSmem {
   uint64_t q_full;
   uint64_t kv_full[2], kv_empty[2];
   uint64_t s_full[2], s_free[2];
-  uint64_t dp_full, ds_full, done;
+  uint64_t dp_full, done;
+  uint64_t ds_part[4];  // part 2g + c: key columns [64g + 32c, +32) of dS
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -362,7 +375,7 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
       mbar_init(&sm.s_free[s], 256);
     }
     mbar_init(&sm.dp_full, 1);
-    mbar_init(&sm.ds_full, 256);
+    for (int q = 0; q < 4; ++q) mbar_init(&sm.ds_part[q], 128);
     mbar_init(&sm.done, 1);
     sm.abort_flag = 0;
     fence_barrier_init();
@@ -413,6 +426,19 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           mma_bf16_ss(d, smem_desc_sw128(a + off, 16, 1024), smem_desc_sw128(b + off, 16, 1024), idesc_kk, kk > 0);
         }
       };
+      auto ts_parts = [&](uint64_t* parts, uint32_t parity, uint32_t d, uint32_t a_tmem, uint32_t b, bool acc) {
+#pragma unroll
+        for (int n = 0; n < 4; ++n) {  // parts 0 and 2 first, as in the dK / dV kernel
+          const int q = (n & 1) * 2 + (n >> 1);
+          if (!mbar_wait(&parts[q], parity, kStatusTimeoutSoftmax, abort_flag, p.status)) return false;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 2 * q; kk < 2 * q + 2; ++kk)
+            mma_bf16_ts(d, a_tmem + split_a_col(kk), smem_desc_sw128(b + kk * 2048, kHalfBytes, 1024), idesc_mn,
+                        (acc || kk > 0) ? 1u : 0u);
+        }
+        return true;
+      };
       bool ok = mbar_wait(&sm.q_full, 0, kStatusTimeoutTmaFull, abort_flag, p.status);
       if (ok) ok = mbar_wait(&sm.kv_full[0], 0, kStatusTimeoutTmaFull, abort_flag, p.status);
       if (ok) {
@@ -435,13 +461,8 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
           gemm_kk(tmem + s1 * 128, qa, smem_u32(sm.k[s1]));
           mma_commit(&sm.s_full[s1]);
         }
-        if (!(ok = mbar_wait(&sm.ds_full, j & 1, kStatusTimeoutSoftmax, abort_flag, p.status))) break;
-        tc_fence_after();
         const uint32_t kb = smem_u32(sm.k[s]);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_bf16_ts(t_dq, t_dp + split_a_col(kk), smem_desc_sw128(kb + kk * 2048, kHalfBytes, 1024), idesc_mn,
-                      (j > 0 || kk > 0) ? 1u : 0u);
+        if (!(ok = ts_parts(sm.ds_part, j & 1, t_dq, t_dp, kb, j > 0))) break;
         mma_commit(&sm.kv_empty[s]);
         if (has_next) {
           gemm_kk(t_dp, ga, smem_u32(sm.v[s1]));
@@ -514,7 +535,7 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         const uint64_t nd2 = f2(-dval, -dval), sc2 = f2(scale, scale);
         uint32_t w[32];
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+        for (int c = 0; c < 2; ++c) {
 #pragma unroll
           for (int e = 0; e < 16; ++e) {  // dS = P (dP - D) scale, two columns per packed op
             const int kv = c * 32 + 2 * e;
@@ -522,11 +543,13 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
             const float2 d = f2_split(f2_mul(f2_mul(f2_add(dp2, nd2), f2(pv[kv], pv[kv + 1])), sc2));
             w[c * 16 + e] = pack_bf16x2(d.x, d.y);
           }
-        tmem_st32(t_dp, w);
+          // hand this part of dS to the MMA thread
+          tmem_st16(t_dp + 16 * c, *reinterpret_cast<const uint32_t(*)[16]>(w + 16 * c));
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&sm.ds_part[2 * g + c]);
+        }
       }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&sm.ds_full);
     }
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.done, 0, kStatusTimeoutMma, abort_flag, p.status));
     if (ok) {
