@@ -95,14 +95,14 @@ def attach_spectral_norm(layer: nn.Module, power_iters: int = 30, update: str = 
     if not isinstance(w, nn.Parameter) or w.dim() < 2 or (not w.requires_grad and not allow_frozen):
         return False
     mat = w.detach().flatten(1).float()
-    if float(torch.linalg.matrix_norm(mat, ord=2)) < 1e-8:
-        return False
     assert update in ("train", "always"), update
     gen = torch.Generator(device="cpu")
     gen.manual_seed(seed if seed is not None else 0x5EC7)
     u0 = _unit(torch.randn(mat.shape[0], generator=gen).to(mat.device))
     u, v = power_iterate(mat, u0, max(1, int(power_iters)))
     sigma0 = torch.dot(u, mat @ v)
+    if float(sigma0) < 1e-8:  # the power-iteration estimate of the spectral norm (no SVD)
+        return False
     layer.register_buffer("sn_u", u.to(w.dtype if w.dtype.is_floating_point else torch.float32))
     layer.register_buffer("sn_v", v.to(layer.sn_u.dtype))
     layer.register_buffer("sn_gain", sigma0.reshape(()).to(torch.float32))

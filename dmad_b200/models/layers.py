@@ -79,14 +79,20 @@ class SegLinear(nn.Module):
         g = torch.Generator(device="cpu").manual_seed(0)
         for name, sl in self.seg_slices():
             w = self.weight[sl].float()
-            on = (segments is None or name in segments) and float(torch.linalg.matrix_norm(w, ord=2)) >= 1e-8
             u = _l2n(torch.randn(w.shape[0], generator=g).to(dev))
             v = _l2n(torch.randn(w.shape[1], generator=g).to(dev))
-            if on:
+            on = False
+            if segments is None or name in segments:
+                # the power iteration's sigma decides (no SVD: a zero segment gives sigma = 0)
+                ui, vi = u, v
                 for _ in range(power_iters):
-                    v = _l2n(w.t() @ u)
-                    u = _l2n(w @ v)
-                sigma = torch.dot(u, w @ v)
+                    vi = _l2n(w.t() @ ui)
+                    ui = _l2n(w @ vi)
+                sigma = torch.dot(ui, w @ vi)
+                on = float(sigma) >= 1e-8
+                if on:
+                    u, v = ui, vi
+            if on:
                 wn = w / sigma
                 gain = (w.flatten() @ wn.flatten()) / (wn.flatten() @ wn.flatten())
                 n += 1
