@@ -258,6 +258,8 @@ def wan_forward_jvp(model, x, tx, timesteps, t_timesteps, crossattn_emb, attn_me
     e, e0, te, te0 = time_embed_jvp(model, timesteps.reshape(-1).float(), t_timesteps.reshape(-1).float())
     context = model.text_embed(crossattn_emb)
     for blk in model.blocks:
+        for hook in blk._forward_pre_hooks.values():  # as blk(...) would: binds sharded block weights
+            hook(blk, ())
         h, th = block_jvp(blk, h, th, e0, te0, context, cos, sin, B, Ll, rpg, cp, attn_meta)
     m = model.head.modulation.float()[0]
     ho, tho = ln_mod_jvp(h, th, m[1][None] + e, te, m[0][None] + e, te, rpg, cfg.eps)

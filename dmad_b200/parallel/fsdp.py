@@ -78,8 +78,12 @@ class ShardedFrozenBlocks:
             barrier()  # every shard is in place before any peer reads it
 
     def _owned(self, b):
-        """The parameters of block ``b`` this sharding owns: its frozen bf16 weights."""
-        return [p for p in b.parameters() if not p.requires_grad and p.dtype == torch.bfloat16 and p.numel() > 0]
+        """The parameters of block ``b`` this sharding owns: its frozen weights of the blocks' weight dtype
+        (the dtype of the first block's largest frozen tensor: bf16 for a bf16 model on the GPU)."""
+        if not hasattr(self, "_frozen_dtype"):
+            frozen = [p for p in self.blocks[0].parameters() if not p.requires_grad and p.dtype.is_floating_point]
+            self._frozen_dtype = max(frozen, key=lambda p: p.numel()).dtype if frozen else torch.bfloat16
+        return [p for p in b.parameters() if not p.requires_grad and p.dtype == self._frozen_dtype and p.numel() > 0]
 
     # ------------------------------------------------------------------ gather
     def _gather(self, i: int, slot: int):
