@@ -51,8 +51,11 @@ def _worker(rank, world, port, q):
         o1 = m.training_step(batch, 0)
         o2 = m.training_step(batch, 1)
         lora_after = torch.cat([p.detach().reshape(-1) for n_, p in m.net.named_parameters() if p.requires_grad])
+        # the 4-step generation bench.py times, through the sharded student under CP
+        gen = m.generate(batch["context"], shp, num_steps=4, generator=torch.Generator().manual_seed(5))
         vals = torch.tensor([float(o1["dmad_g_loss"]), float(o1.get("scm_loss", o1.get("loss_scm", 0.0))),
-                             float(o2["dmad_d_loss"]), float((lora_after - lora_before).abs().sum())])
+                             float(o2["dmad_d_loss"]), float((lora_after - lora_before).abs().sum()),
+                             float(gen.float().abs().mean())])
         q.put((rank, vals.tolist(), lora_after.sum().item(), sorted(o1.keys())))
         dist.destroy_process_group()
     except Exception as e:  # pragma: no cover - reported to the parent
