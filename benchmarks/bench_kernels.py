@@ -86,6 +86,7 @@ def main():
     ap.add_argument("--L", type=int, default=32760)
     ap.add_argument("--Lk", type=int, default=None)
     ap.add_argument("--H", type=int, default=12)
+    ap.add_argument("--D", type=int, default=128, choices=[64, 128], help="head dim of the attention benchmarks")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--only", default="all", choices=["all", "fwd", "bwd", "bwd_fused", "sdpa", "jvp", "ref_jvp", "gemm",
@@ -99,14 +100,15 @@ def main():
     B, L, H = a.B, a.L, a.H
     Lk = a.Lk or L
     torch.manual_seed(0)
-    q = torch.randn(B, L, H, 128, device="cuda", dtype=torch.bfloat16)
-    k = torch.randn(B, Lk, H, 128, device="cuda", dtype=torch.bfloat16)
-    v = torch.randn(B, Lk, H, 128, device="cuda", dtype=torch.bfloat16)
+    D = a.D
+    q = torch.randn(B, L, H, D, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(B, Lk, H, D, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(B, Lk, H, D, device="cuda", dtype=torch.bfloat16)
     do = torch.randn_like(q)
     o = torch.empty_like(q)
     lse = torch.empty(B, H, e.flash_lse_pad(L), device="cuda")
-    scale = 1 / math.sqrt(128)
-    fl_fwd = 4.0 * B * H * L * Lk * 128
+    scale = 1 / math.sqrt(D)
+    fl_fwd = 4.0 * B * H * L * Lk * D
     peak, src = peak_tflops()
     res = []
     if a.only in ("all", "fwd"):
@@ -117,7 +119,7 @@ def main():
         dq, dk, dv, dd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(lse)
         ms = timeit(lambda: e.flash_bwd(q, k, v, o, do, lse, dq, dk, dv, dd, scale), a.iters, a.warmup)
         res.append(("flash_bwd_sm100", ms, 2.5 * fl_fwd))
-    if a.only in ("all", "bwd", "bwd_fused"):
+    if a.only in ("all", "bwd", "bwd_fused") and D == 128:
         e.flash_fwd(q, k, v, o, lse, scale)
         dq, dk, dv, dd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(lse)
         acc = torch.empty(B * H * lse.shape[-1] * 128, device="cuda")
@@ -135,7 +137,7 @@ def main():
             gt = do.transpose(1, 2)
             ms = timeit(lambda: torch.autograd.grad(out, (qg, kg, vg), gt, retain_graph=True), a.iters, a.warmup)
             res.append(("cudnn_sdpa_bwd", ms, 2.5 * fl_fwd))
-    if a.only in ("all", "jvp", "ref_jvp"):
+    if a.only in ("all", "jvp", "ref_jvp") and D == 128:
         tq, tk, tv = (torch.randn_like(t) * 0.5 for t in (q, k, v))
         to = torch.empty_like(q)
         fl_jvp = 3.0 * fl_fwd  # S, tq k^T, q tk^T, P V, P tV, (P * tS) V
@@ -206,7 +208,7 @@ def main():
         return
     for name, ms, fl in res:
         tf = fl / (ms * 1e-3) / 1e12
-        print(json.dumps({"op": name, "B": B, "L": L, "Lk": Lk, "H": H, "ms": round(ms, 4), "tflops": round(tf, 1),
+        print(json.dumps({"op": name, "B": B, "L": L, "Lk": Lk, "H": H, "D": a.D, "ms": round(ms, 4), "tflops": round(tf, 1),
                           f"frac_of_{src}_bf16_peak": round(tf / peak, 3)}))
 
 

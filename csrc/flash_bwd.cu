@@ -1,4 +1,4 @@
-// Flash-attention backward for sm_100a (bf16, head dim 128), two tcgen05 kernels.
+// Flash-attention backward for sm_100a (bf16, head dim 64 or 128), two tcgen05 kernels.
 //
 // Functional parity target: the backward the reference pairs with its attention
 // forward (flash-attn 2 `_flash_attn_backward`, called from
@@ -9,7 +9,7 @@
 //   S^T = K Q^T and dP^T = V dO^T go to TMEM; the row owner (thread = key)
 //   forms P^T (written back as bf16 over S^T) and dS^T = P^T (dP^T - D) s
 //   (written back as bf16 over dP^T); dV += P^T dO and dK += dS^T Q are
-//   TMEM-A MMAs.  TMEM: S^T 0..127, dP^T 128..255, dV 256..383, dK 384..511.
+//   TMEM-A MMAs.  TMEM: S^T 0..127, dP^T 128..255, dV 256.., dK 384.. (d columns each).
 // Kernel B (dQ): one CTA per 128-query tile, looping over 128-key tiles with
 //   a double-buffered S, dP, and dQ += dS K as a TMEM-A MMA.
 // Splitting dQ from dK/dV costs two extra GEMMs per tile pair but needs no
@@ -27,7 +27,7 @@
 
 namespace dmad {
 
-void check_bhld(const at::Tensor& x, const char* name);
+void check_bhld(const at::Tensor& x, const char* name, int64_t d = 128);
 int* device_status_ptr(int device);
 int64_t flash_lse_pad(int64_t L);
 
@@ -78,6 +78,7 @@ __device__ __forceinline__ void store_row_bf16(__nv_bfloat16* row, uint32_t tmem
 __device__ __forceinline__ uint32_t split_a_col(int kk) { return kk < 4 ? kk * 8 : 64 + (kk - 4) * 8; }
 
 // ------------------------------------------------------------------ D = rowsum(dO * O)
+template <int kD>
 __global__ void bwd_dot_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout,
                                float* __restrict__ dd, int64_t osb, int64_t osl, int64_t osh, int64_t gsb,
                                int64_t gsl, int64_t gsh, int B, int H, int Lq, int Lpad) {
@@ -89,11 +90,18 @@ __global__ void bwd_dot_kernel(const __nv_bfloat16* __restrict__ o, const __nv_b
   const int b = row / ((int64_t)Lpad * H);
   float acc = 0.f;
   if (q < Lq) {
-    const uint2 ov = *reinterpret_cast<const uint2*>(o + b * osb + q * osl + h * osh + lane * 4);
-    const uint2 gv = *reinterpret_cast<const uint2*>(dout + b * gsb + q * gsl + h * gsh + lane * 4);
-    const float2 o0 = unpack_bf16x2(ov.x), o1 = unpack_bf16x2(ov.y);
-    const float2 g0 = unpack_bf16x2(gv.x), g1 = unpack_bf16x2(gv.y);
-    acc = o0.x * g0.x + o0.y * g0.y + o1.x * g1.x + o1.y * g1.y;
+    if constexpr (kD == 128) {  // four elements a lane
+      const uint2 ov = *reinterpret_cast<const uint2*>(o + b * osb + q * osl + h * osh + lane * 4);
+      const uint2 gv = *reinterpret_cast<const uint2*>(dout + b * gsb + q * gsl + h * gsh + lane * 4);
+      const float2 o0 = unpack_bf16x2(ov.x), o1 = unpack_bf16x2(ov.y);
+      const float2 g0 = unpack_bf16x2(gv.x), g1 = unpack_bf16x2(gv.y);
+      acc = o0.x * g0.x + o0.y * g0.y + o1.x * g1.x + o1.y * g1.y;
+    } else {  // two
+      const float2 o0 = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(o + b * osb + q * osl + h * osh + lane * 2));
+      const float2 g0 =
+          unpack_bf16x2(*reinterpret_cast<const uint32_t*>(dout + b * gsb + q * gsl + h * gsh + lane * 2));
+      acc = o0.x * g0.x + o0.y * g0.y;
+    }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
   }
@@ -101,11 +109,13 @@ __global__ void bwd_dot_kernel(const __nv_bfloat16* __restrict__ o, const __nv_b
 }
 
 // ------------------------------------------------------------------ kernel A: dK, dV
+template <int kD>
 struct DkvSmem {
-  uint8_t k[kTileBytes];
-  uint8_t v[kTileBytes];
-  uint8_t q[2][kTileBytes];
-  uint8_t g[2][kTileBytes];  // dO
+  static constexpr int kT = kD / 64 * kHalfBytes;  // 128 rows x kD bf16 as 64-column panels
+  uint8_t k[kT];
+  uint8_t v[kT];
+  uint8_t q[2][kT];
+  uint8_t g[2][kT];  // dO
   float lse[2][128];
   float dd[2][128];
   uint64_t kv_full;
@@ -116,12 +126,15 @@ struct DkvSmem {
   int abort_flag;
 };
 
+template <int kD>
 __global__ void __launch_bounds__(384, 1)
 flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                       const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_g,
                       BwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  DkvSmem& sm = *reinterpret_cast<DkvSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  using Smem = DkvSmem<kD>;
+  constexpr int kPanels = kD / 64, kT = Smem::kT;
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   volatile int* abort_flag = &sm.abort_flag;
   const int warp = warp_id(), lane = lane_id();
   const int head = blockIdx.y, batch = blockIdx.z;
@@ -156,8 +169,8 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
 
   if (warp == 0) {
     if (elect_one()) {
-      mbar_arrive_expect_tx(&sm.kv_full, 2 * kTileBytes);
-      for (int h = 0; h < 2; ++h) {
+      mbar_arrive_expect_tx(&sm.kv_full, 2 * kT);
+      for (int h = 0; h < kPanels; ++h) {
         tma_load_4d(sm.k + h * kHalfBytes, &tm_k, &sm.kv_full, h * 64, head, k0, batch);
         tma_load_4d(sm.v + h * kHalfBytes, &tm_v, &sm.kv_full, h * 64, head, k0, batch);
       }
@@ -167,8 +180,8 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
         const int s = i & 1;
         const uint32_t ph = (i >> 1) & 1;
         if (!mbar_wait(&sm.q_empty[s], ph ^ 1, kStatusTimeoutEmpty, abort_flag, p.status)) break;
-        mbar_arrive_expect_tx(&sm.q_full[s], 2 * kTileBytes + 2 * 512);
-        for (int h = 0; h < 2; ++h) {
+        mbar_arrive_expect_tx(&sm.q_full[s], 2 * kT + 2 * 512);
+        for (int h = 0; h < kPanels; ++h) {
           tma_load_4d(sm.q[s] + h * kHalfBytes, &tm_q, &sm.q_full[s], h * 64, head, i * 128, batch);
           tma_load_4d(sm.g[s] + h * kHalfBytes, &tm_g, &sm.q_full[s], h * 64, head, i * 128, batch);
         }
@@ -183,12 +196,12 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
   } else if (warp == 1) {
     if (elect_one()) {
       constexpr uint32_t idesc_kk = idesc_bf16_f32(128, 128, false, false);
-      constexpr uint32_t idesc_mn = idesc_bf16_f32(128, 128, false, true);
+      constexpr uint32_t idesc_mn = idesc_bf16_f32(128, kD, false, true);
       const uint32_t ka = smem_u32(sm.k), va = smem_u32(sm.v);
       const uint32_t t_s = tmem, t_dp = tmem + 128, t_dv = tmem + 256, t_dk = tmem + 384;
       auto gemm_kk = [&](uint32_t d, uint32_t a, uint32_t b) {
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
+        for (int kk = 0; kk < kD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
           mma_bf16_ss(d, smem_desc_sw128(a + off, 16, 1024), smem_desc_sw128(b + off, 16, 1024), idesc_kk, kk > 0);
         }
@@ -327,8 +340,9 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
       const bool valid = kr < p.Lk;
       __nv_bfloat16* dv_row = valid ? p.out2 + batch * p.sb2 + (int64_t)kr * p.sl2 + head * p.sh2 : nullptr;
       __nv_bfloat16* dk_row = valid ? p.out + batch * p.sb + (int64_t)kr * p.sl + head * p.sh : nullptr;
-      store_row_bf16(dv_row, tmem + lb + 256, 1.f, c0, 2);
-      store_row_bf16(dk_row, tmem + lb + 384, 1.f, c0, 2);
+      // group g stores output columns [g d / 2, (g + 1) d / 2)
+      store_row_bf16(dv_row, tmem + lb + 256, 1.f, g * (kD / 2), kD / 64);
+      store_row_bf16(dk_row, tmem + lb + 384, 1.f, g * (kD / 2), kD / 64);
     }
   }
   tc_fence_before();
@@ -340,11 +354,13 @@ flash_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_con
 }
 
 // ------------------------------------------------------------------ kernel B: dQ
+template <int kD>
 struct DqSmem {
-  uint8_t q[kTileBytes];
-  uint8_t g[kTileBytes];
-  uint8_t k[2][kTileBytes];
-  uint8_t v[2][kTileBytes];
+  static constexpr int kT = kD / 64 * kHalfBytes;
+  uint8_t q[kT];
+  uint8_t g[kT];
+  uint8_t k[2][kT];
+  uint8_t v[2][kT];
   uint64_t q_full;
   uint64_t kv_full[2], kv_empty[2];
   uint64_t s_full[2], s_free[2];
@@ -354,12 +370,15 @@ struct DqSmem {
   int abort_flag;
 };
 
+template <int kD>
 __global__ void __launch_bounds__(384, 1)
 flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_g,
                     BwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  DqSmem& sm = *reinterpret_cast<DqSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  using Smem = DqSmem<kD>;
+  constexpr int kPanels = kD / 64, kT = Smem::kT;
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   volatile int* abort_flag = &sm.abort_flag;
   const int warp = warp_id(), lane = lane_id();
   const int head = blockIdx.y, batch = blockIdx.z;
@@ -391,8 +410,8 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
 
   if (warp == 0) {
     if (elect_one()) {
-      mbar_arrive_expect_tx(&sm.q_full, 2 * kTileBytes);
-      for (int h = 0; h < 2; ++h) {
+      mbar_arrive_expect_tx(&sm.q_full, 2 * kT);
+      for (int h = 0; h < kPanels; ++h) {
         tma_load_4d(sm.q + h * kHalfBytes, &tm_q, &sm.q_full, h * 64, head, q0, batch);
         tma_load_4d(sm.g + h * kHalfBytes, &tm_g, &sm.q_full, h * 64, head, q0, batch);
       }
@@ -402,8 +421,8 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
         const int s = j & 1;
         const uint32_t ph = (j >> 1) & 1;
         if (!mbar_wait(&sm.kv_empty[s], ph ^ 1, kStatusTimeoutEmpty, abort_flag, p.status)) break;
-        mbar_arrive_expect_tx(&sm.kv_full[s], 2 * kTileBytes);
-        for (int h = 0; h < 2; ++h) {
+        mbar_arrive_expect_tx(&sm.kv_full[s], 2 * kT);
+        for (int h = 0; h < kPanels; ++h) {
           tma_load_4d(sm.k[s] + h * kHalfBytes, &tm_k, &sm.kv_full[s], h * 64, head, j * 128, batch);
           tma_load_4d(sm.v[s] + h * kHalfBytes, &tm_v, &sm.kv_full[s], h * 64, head, j * 128, batch);
         }
@@ -416,12 +435,12 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
   } else if (warp == 1) {
     if (elect_one()) {
       constexpr uint32_t idesc_kk = idesc_bf16_f32(128, 128, false, false);
-      constexpr uint32_t idesc_mn = idesc_bf16_f32(128, 128, false, true);
+      constexpr uint32_t idesc_mn = idesc_bf16_f32(128, kD, false, true);
       const uint32_t qa = smem_u32(sm.q), ga = smem_u32(sm.g);
       const uint32_t t_dp = tmem + 256, t_dq = tmem + 384;
       auto gemm_kk = [&](uint32_t d, uint32_t a, uint32_t b) {
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
+        for (int kk = 0; kk < kD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
           mma_bf16_ss(d, smem_desc_sw128(a + off, 16, 1024), smem_desc_sw128(b + off, 16, 1024), idesc_kk, kk > 0);
         }
@@ -555,7 +574,7 @@ flash_bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_const
     if (ok) {
       tc_fence_after();
       __nv_bfloat16* dq_row = q_row < p.Lq ? p.out + batch * p.sb + (int64_t)q_row * p.sl + head * p.sh : nullptr;
-      store_row_bf16(dq_row, tmem + lb + 384, 1.f, c0, 2);
+      store_row_bf16(dq_row, tmem + lb + 384, 1.f, g * (kD / 2), kD / 64);
     }
   }
   tc_fence_before();
@@ -863,7 +882,7 @@ __global__ void dq_from_acc_kernel(const float* __restrict__ acc, __nv_bfloat16*
 }
 
 CUtensorMap make_map(const at::Tensor& x) {
-  const uint64_t dims[4] = {128, (uint64_t)x.size(2), (uint64_t)x.size(1), (uint64_t)x.size(0)};
+  const uint64_t dims[4] = {(uint64_t)x.size(3), (uint64_t)x.size(2), (uint64_t)x.size(1), (uint64_t)x.size(0)};
   const uint64_t strides[3] = {(uint64_t)x.stride(2) * 2, (uint64_t)x.stride(1) * 2, (uint64_t)x.stride(0) * 2};
   const uint32_t box[4] = {64, 1, 128, 1};
   return make_tmap_bf16(x.data_ptr(), 4, dims, strides, box);
@@ -871,20 +890,23 @@ CUtensorMap make_map(const at::Tensor& x) {
 
 }  // namespace
 
-// dq, dk, dv may be strided views (e.g. slices of one fused [B, L, 3, H, 128] buffer).
+// [B, L, H, d] tensors, d = 64 or 128; dq, dk, dv may be strided views (e.g. slices of one fused
+// [B, L, 3, H, d] buffer).
 // lse2: [B, H, Lpad] log2-domain LSE from flash_fwd; dd_scratch: [B, H, Lpad] fp32 work
 // buffer that receives rowsum(dO * O).
 void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
                const at::Tensor& dout, const at::Tensor& lse2, at::Tensor& dq, at::Tensor& dk, at::Tensor& dv,
                at::Tensor& dd_scratch, double scale) {
-  check_bhld(q, "q");
-  check_bhld(k, "k");
-  check_bhld(v, "v");
-  check_bhld(o, "o");
-  check_bhld(dout, "dout");
-  check_bhld(dq, "dq");
-  check_bhld(dk, "dk");
-  check_bhld(dv, "dv");
+  TORCH_CHECK(q.dim() == 4 && (q.size(3) == 64 || q.size(3) == 128), "q must be [B, L, H, 64 or 128]");
+  const int d = (int)q.size(3);
+  check_bhld(q, "q", d);
+  check_bhld(k, "k", d);
+  check_bhld(v, "v", d);
+  check_bhld(o, "o", d);
+  check_bhld(dout, "dout", d);
+  check_bhld(dq, "dq", d);
+  check_bhld(dk, "dk", d);
+  check_bhld(dv, "dv", d);
   const int B = q.size(0), Lq = q.size(1), H = q.size(2), Lk = k.size(1);
   const int64_t Lpad = flash_lse_pad(Lq);
   TORCH_CHECK(lse2.is_contiguous() && lse2.scalar_type() == at::kFloat && lse2.dim() == 3 && lse2.size(2) == Lpad,
@@ -897,7 +919,8 @@ void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, co
   {
     const int64_t rows = (int64_t)B * H * Lpad;
     const int warps = 8;
-    bwd_dot_kernel<<<(unsigned)((rows + warps - 1) / warps), warps * 32, 0, stream>>>(
+    auto dot = d == 64 ? bwd_dot_kernel<64> : bwd_dot_kernel<128>;
+    dot<<<(unsigned)((rows + warps - 1) / warps), warps * 32, 0, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
         dd_scratch.data_ptr<float>(), o.stride(0), o.stride(1), o.stride(2), dout.stride(0), dout.stride(1),
         dout.stride(2), B, H, Lq, (int)Lpad);
@@ -923,11 +946,11 @@ void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, co
     p.sb2 = dv.stride(0);
     p.sl2 = dv.stride(1);
     p.sh2 = dv.stride(2);
-    const size_t smem = sizeof(DkvSmem) + 1024;
-    C10_CUDA_CHECK(
-        cudaFuncSetAttribute(flash_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const size_t smem = (d == 64 ? sizeof(DkvSmem<64>) : sizeof(DkvSmem<128>)) + 1024;
+    auto kern = d == 64 ? flash_bwd_dkdv_kernel<64> : flash_bwd_dkdv_kernel<128>;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid((Lk + 127) / 128, H, B);
-    flash_bwd_dkdv_kernel<<<grid, 384, smem, stream>>>(tq, tk, tv, tg, p);
+    kern<<<grid, 384, smem, stream>>>(tq, tk, tv, tg, p);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
   {
@@ -936,10 +959,11 @@ void flash_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, co
     p.sl = dq.stride(1);
     p.sh = dq.stride(2);
     p.out2 = nullptr;
-    const size_t smem = sizeof(DqSmem) + 1024;
-    C10_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const size_t smem = (d == 64 ? sizeof(DqSmem<64>) : sizeof(DqSmem<128>)) + 1024;
+    auto kern = d == 64 ? flash_bwd_dq_kernel<64> : flash_bwd_dq_kernel<128>;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     dim3 grid((Lq + 127) / 128, H, B);
-    flash_bwd_dq_kernel<<<grid, 384, smem, stream>>>(tq, tk, tv, tg, p);
+    kern<<<grid, 384, smem, stream>>>(tq, tk, tv, tg, p);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }
@@ -974,7 +998,7 @@ void flash_bwd_fused(const at::Tensor& q, const at::Tensor& k, const at::Tensor&
   const int64_t rows = (int64_t)B * H * Lpad;
   {
     const int warps = 8;
-    bwd_dot_kernel<<<(unsigned)((rows + warps - 1) / warps), warps * 32, 0, stream>>>(
+    bwd_dot_kernel<128><<<(unsigned)((rows + warps - 1) / warps), warps * 32, 0, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
         dd_scratch.data_ptr<float>(), o.stride(0), o.stride(1), o.stride(2), dout.stride(0), dout.stride(1),
         dout.stride(2), B, H, Lq, (int)Lpad);
@@ -1140,7 +1164,7 @@ extern "C" int dmad_flash_attn_bwd_noalloc(const void* q, const void* k, const v
   if (cudaMemsetAsync(sym.status, 0, sizeof(int), s) != cudaSuccess) return DMAD_NOALLOC_ERR_CUDA;
   {
     const int warps = 8;
-    bwd_dot_kernel<<<(unsigned)((rows + warps - 1) / warps), warps * 32, 0, s>>>(
+    bwd_dot_kernel<128><<<(unsigned)((rows + warps - 1) / warps), warps * 32, 0, s>>>(
         static_cast<const __nv_bfloat16*>(o), static_cast<const __nv_bfloat16*>(dout), sym.rows, so[0], so[1], so[2],
         sg[0], sg[1], sg[2], B, H, Lq, (int)Lpad);
   }
@@ -1162,21 +1186,21 @@ extern "C" int dmad_flash_attn_bwd_noalloc(const void* q, const void* k, const v
   p.sb2 = sdv[0];
   p.sl2 = sdv[1];
   p.sh2 = sdv[2];
-  const size_t smem_a = sizeof(DkvSmem) + 1024;
-  if (cudaFuncSetAttribute(flash_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_a) !=
+  const size_t smem_a = sizeof(DkvSmem<128>) + 1024;
+  if (cudaFuncSetAttribute(flash_bwd_dkdv_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_a) !=
       cudaSuccess)
     return DMAD_NOALLOC_ERR_CUDA;
-  flash_bwd_dkdv_kernel<<<dim3((Lk + 127) / 128, H, B), 384, smem_a, s>>>(tq, tk, tv, tg, p);
+  flash_bwd_dkdv_kernel<128><<<dim3((Lk + 127) / 128, H, B), 384, smem_a, s>>>(tq, tk, tv, tg, p);
   p.out = static_cast<__nv_bfloat16*>(dq);
   p.sb = sdq[0];
   p.sl = sdq[1];
   p.sh = sdq[2];
   p.out2 = nullptr;
-  const size_t smem_b = sizeof(DqSmem) + 1024;
-  if (cudaFuncSetAttribute(flash_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_b) !=
+  const size_t smem_b = sizeof(DqSmem<128>) + 1024;
+  if (cudaFuncSetAttribute(flash_bwd_dq_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_b) !=
       cudaSuccess)
     return DMAD_NOALLOC_ERR_CUDA;
-  flash_bwd_dq_kernel<<<dim3((Lq + 127) / 128, H, B), 384, smem_b, s>>>(tq, tk, tv, tg, p);
+  flash_bwd_dq_kernel<128><<<dim3((Lq + 127) / 128, H, B), 384, smem_b, s>>>(tq, tk, tv, tg, p);
   if (cudaGetLastError() != cudaSuccess) return DMAD_NOALLOC_ERR_CUDA;
   return DMAD_NOALLOC_OK;
 }

@@ -1,4 +1,4 @@
-// Flash-attention forward for sm_100a (bf16 in/out, fp32 accumulate, head dim 128).
+// Flash-attention forward for sm_100a (bf16 in/out, fp32 accumulate, head dim 64 or 128).
 //
 // Functional parity target: the reference's attention entry point
 // (train/wan/rcm/utils/attention.py:120-167, cuDNN SDPA on cc 100) and the
@@ -10,7 +10,7 @@
 //   warp 1      : TMEM owner and the single MMA-issuing thread
 //   warps 4..7  : softmax for query tile 0   (thread i owns TMEM lane / query row i)
 //   warps 8..11 : softmax for query tile 1
-// TMEM (512 columns): per tile, S at [t*256, +128) and O at [t*256+128, +128).
+// TMEM (512 columns): per tile, S at [t*256, +128) and O at [t*256+128, +d).
 // P is written back as bf16 over the first 64 columns of S and consumed by a
 // TMEM-A (".kind::f16 [d], [a], b") MMA, so it never touches shared memory.
 // Each tile alternates S = Q K_j^T -> softmax -> O += P V_j; the MMA thread
@@ -34,15 +34,15 @@ int* device_status_ptr(int device);
 
 namespace {
 
-constexpr int kHeadDim = 128;
 constexpr int kTileM = 128;   // query rows per tile
 constexpr int kTileN = 128;   // keys per KV tile
 constexpr int kStages = 2;
 constexpr int kHalfBytes = 128 * 128;            // one 128-row x 64-col bf16 swizzle panel
-constexpr int kTileBytes = 2 * kHalfBytes;       // 128 x 128 bf16
 constexpr float kRescaleThreshold = 8.0f;        // log2 units
 
+template <int kD>
 struct FwdSmem {
+  static constexpr int kTileBytes = kD / 64 * kHalfBytes;  // 128 rows x kD bf16 as 64-column panels
   // 1024-byte aligned panels (required by the 128B swizzle atoms)
   uint8_t q[2][kTileBytes];
   uint8_t k[kStages][kTileBytes];
@@ -57,7 +57,7 @@ struct FwdSmem {
 };
 
 struct FwdParams {
-  __nv_bfloat16* o;  // [B, Lq, H, 128] with strides below
+  __nv_bfloat16* o;  // [B, Lq, H, d] with strides below
   float* lse;        // [B, H, Lpad] log2-domain LSE (+inf on padding rows)
   int64_t o_sb, o_sl, o_sh;
   int Lq, Lk, H, Lpad;
@@ -65,24 +65,26 @@ struct FwdParams {
   int* status;       // device status word (bounded-wait failures)
   // optional second copy of every output row, scattered to the rank that owns the row
   // (context-parallel head->sequence exchange): row g of sample b goes to
-  // scat[g / scat_ll] + (b * scat_ll + g % scat_ll) * scat_ld + scat_col + head * 128
+  // scat[g / scat_ll] + (b * scat_ll + g % scat_ll) * scat_ld + scat_col + head * d
   int64_t scat[16];
   int scat_n, scat_ll, scat_col;
   int64_t scat_ld;
   // optional running merge over successive key blocks (ring context parallelism):
-  // acc_o fp32 [B, Lq, H, 128] and acc_lse (log2) [B, H, Lpad] hold the softmax-weighted output
+  // acc_o fp32 [B, Lq, H, d] and acc_lse (log2) [B, H, Lpad] hold the softmax-weighted output
   // of the blocks seen so far; acc_read merges into them, acc_final also writes the bf16 o
   float* acc_o;
   float* acc_lse;
   int acc_read, acc_final;
 };
 
-template <int kPolyPer8, int kPSplit>
+template <int kD, int kPolyPer8, int kPSplit>
 __global__ void __launch_bounds__(384, 1)
 flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                  const __grid_constant__ CUtensorMap tm_v, FwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  FwdSmem& sm = *reinterpret_cast<FwdSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  using Smem = FwdSmem<kD>;
+  constexpr int kPanels = kD / 64, kTileBytes = Smem::kTileBytes;
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   volatile int* abort_flag = &sm.abort_flag;
 
   const int warp = warp_id();
@@ -127,7 +129,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     if (elect_one()) {
       mbar_arrive_expect_tx(&sm.q_full, 2 * kTileBytes);
       for (int t = 0; t < 2; ++t)
-        for (int h = 0; h < 2; ++h)
+        for (int h = 0; h < kPanels; ++h)
           tma_load_4d(sm.q[t] + h * kHalfBytes, &tm_q, &sm.q_full, h * 64, head, q0 + t * kTileM, batch);
       int last_s = -1, last_ph = 0;
       for (int j = 0; j < nkv; ++j) {
@@ -135,7 +137,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         const uint32_t ph = (j / kStages) & 1;
         if (!mbar_wait(&sm.k_empty[s], ph ^ 1, kStatusTimeoutEmpty, abort_flag, p.status)) break;
         mbar_arrive_expect_tx(&sm.k_full[s], kTileBytes);
-        for (int h = 0; h < 2; ++h)
+        for (int h = 0; h < kPanels; ++h)
           tma_load_4d(sm.k[s] + h * kHalfBytes, &tm_k, &sm.k_full[s], h * 64, head, j * kTileN, batch);
         if (!mbar_wait(&sm.v_empty[s], ph ^ 1, kStatusTimeoutEmpty, abort_flag, p.status)) {
           // K load of this stage is in flight: wait for it before leaving
@@ -143,7 +145,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
           break;
         }
         mbar_arrive_expect_tx(&sm.v_full[s], kTileBytes);
-        for (int h = 0; h < 2; ++h)
+        for (int h = 0; h < kPanels; ++h)
           tma_load_4d(sm.v[s] + h * kHalfBytes, &tm_v, &sm.v_full[s], h * 64, head, j * kTileN, batch);
         last_s = s;
         last_ph = ph;
@@ -159,7 +161,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
       constexpr uint32_t idesc_qk = idesc_bf16_f32(128, 128, false, false);
-      constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 128, false, true);
+      constexpr uint32_t idesc_pv = idesc_bf16_f32(128, kD, false, true);
       const uint32_t q_addr0 = smem_u32(sm.q[0]);
       const uint32_t q_addr1 = smem_u32(sm.q[1]);
       bool ok = mbar_wait(&sm.q_full, 0, kStatusTimeoutTmaFull, abort_flag, p.status);
@@ -169,7 +171,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         const uint32_t ka = smem_u32(sm.k[s]);
         const uint32_t d_tmem = tmem + t * 256;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
+        for (int kk = 0; kk < kD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
           mma_bf16_ss(d_tmem, smem_desc_sw128(qa + off, 16, 1024), smem_desc_sw128(ka + off, 16, 1024), idesc_qk,
                       kk > 0);
@@ -290,7 +292,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
         // O holds the sum over tiles < j (PV(j-1) finished before S(j) completed).
         if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < kD / 32; ++c) {
             uint32_t r[32];
             tmem_ld32(o_tmem + c * 32, r);
             tmem_wait_ld();
@@ -399,10 +401,10 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       const float nl = mx + __log2f(exp2f(lp - mx) + exp2f(lse_j - mx));
       const float wa = p.acc_read ? exp2f(lp - nl) : 0.f;
       const float wb = exp2f(m_used - nl);
-      float* arow = p.acc_o + (((int64_t)batch * p.Lq + q_row) * p.H + head) * 128;
+      float* arow = p.acc_o + (((int64_t)batch * p.Lq + q_row) * p.H + head) * kD;
       __nv_bfloat16* orow = p.o + batch * p.o_sb + (int64_t)q_row * p.o_sl + head * p.o_sh;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < kD / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(o_tmem + c * 32, r);
         tmem_wait_ld();
@@ -436,7 +438,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
       const bool valid = q_row < p.Lq;
       __nv_bfloat16* orow = p.o + batch * p.o_sb + (int64_t)q_row * p.o_sl + head * p.o_sh;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < kD / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(o_tmem + c * 32, r);
         tmem_wait_ld();
@@ -453,7 +455,7 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
             if (p.scat_n > 0) {
               const int peer = q_row / p.scat_ll, lr = q_row - peer * p.scat_ll;
               __nv_bfloat16* srow = reinterpret_cast<__nv_bfloat16*>(p.scat[peer]) +
-                                    ((int64_t)batch * p.scat_ll + lr) * p.scat_ld + p.scat_col + head * 128;
+                                    ((int64_t)batch * p.scat_ll + lr) * p.scat_ld + p.scat_col + head * kD;
               reinterpret_cast<uint4*>(srow + c * 32)[v] = w;
             }
           }
@@ -471,10 +473,10 @@ flash_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant
   }
 }
 
-// q/k/v: [B, L, H, 128] bf16 views (last dim contiguous, any row / head / batch stride
-// that is a multiple of 8 elements).
+// q/k/v: [B, L, H, d] bf16 views, d = 64 or 128 (last dim contiguous, any row / head / batch
+// stride that is a multiple of 8 elements); boxes of 128 rows x 64 columns.
 CUtensorMap make_qkv_map(const at::Tensor& x) {
-  const uint64_t dims[4] = {128, (uint64_t)x.size(2), (uint64_t)x.size(1), (uint64_t)x.size(0)};
+  const uint64_t dims[4] = {(uint64_t)x.size(3), (uint64_t)x.size(2), (uint64_t)x.size(1), (uint64_t)x.size(0)};
   const uint64_t strides[3] = {(uint64_t)x.stride(2) * 2, (uint64_t)x.stride(1) * 2, (uint64_t)x.stride(0) * 2};
   const uint32_t box[4] = {64, 1, 128, 1};
   return make_tmap_bf16(x.data_ptr(), 4, dims, strides, box);
@@ -482,16 +484,17 @@ CUtensorMap make_qkv_map(const at::Tensor& x) {
 
 }  // namespace
 
-void check_bhld(const at::Tensor& x, const char* name) {
+// d: the head dim the kernel was written for (64 or 128)
+void check_bhld(const at::Tensor& x, const char* name, int64_t d) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16, name, " must be a CUDA bf16 tensor");
-  TORCH_CHECK(x.dim() == 4 && x.size(3) == kHeadDim, name, " must be [B, L, H, 128]");
+  TORCH_CHECK(x.dim() == 4 && x.size(3) == d, name, " must be [B, L, H, ", d, "]");
   TORCH_CHECK(x.stride(3) == 1, name, " last dim must be contiguous");
   TORCH_CHECK(x.stride(2) % 8 == 0 && x.stride(1) % 8 == 0 && x.stride(0) % 8 == 0, name,
               " strides must be multiples of 8 elements");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0, name, " must be 16-byte aligned");
 }
 
-size_t flash_fwd_smem_bytes() { return sizeof(FwdSmem) + 1024; }
+size_t flash_fwd_smem_bytes(int d) { return (d == 64 ? sizeof(FwdSmem<64>) : sizeof(FwdSmem<128>)) + 1024; }
 
 int64_t flash_lse_pad(int64_t L) { return (L + 255) / 256 * 256; }
 
@@ -500,10 +503,12 @@ static void flash_fwd_launch(const at::Tensor& q, const at::Tensor& k, const at:
                              at::Tensor& lse, double scale, const std::vector<int64_t>& scat, int64_t scat_ld,
                              int64_t scat_col, float* acc_o = nullptr, float* acc_lse = nullptr, int acc_read = 0,
                              int acc_final = 0) {
-  check_bhld(q, "q");
-  check_bhld(k, "k");
-  check_bhld(v, "v");
-  check_bhld(o, "o");
+  TORCH_CHECK(q.dim() == 4 && (q.size(3) == 64 || q.size(3) == 128), "q must be [B, L, H, 64 or 128]");
+  const int d = (int)q.size(3);
+  check_bhld(q, "q", d);
+  check_bhld(k, "k", d);
+  check_bhld(v, "v", d);
+  check_bhld(o, "o", d);
   TORCH_CHECK(k.sizes() == v.sizes(), "k and v shapes differ");
   TORCH_CHECK(q.size(0) == k.size(0) && q.size(2) == k.size(2), "q/k batch or head mismatch");
   TORCH_CHECK(o.sizes() == q.sizes(), "o shape mismatch");
@@ -544,10 +549,10 @@ static void flash_fwd_launch(const at::Tensor& q, const at::Tensor& k, const at:
     TORCH_CHECK(scat_ld % 8 == 0 && scat_col % 8 == 0, "scatter row stride / column must be multiples of 8");
     for (int i = 0; i < p.scat_n; ++i) TORCH_CHECK(scat[i] % 16 == 0, "scatter targets must be 16-byte aligned");
   }
-  const size_t smem = flash_fwd_smem_bytes();
+  const size_t smem = flash_fwd_smem_bytes(d);
   // four P parts per tile (measured at L = 32760, H = 12: 5.65-5.75 ms against 5.85-5.91 ms with
   // P handed over whole); half of the exponentials on the FMA pipe (2 of 8: same time, none: +6 %)
-  auto kern = flash_fwd_kernel<4, 4>;
+  auto kern = d == 64 ? flash_fwd_kernel<64, 4, 4> : flash_fwd_kernel<128, 4, 4>;
   C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid((Lq + 2 * kTileM - 1) / (2 * kTileM), H, B);
   kern<<<grid, 384, smem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, p);
@@ -562,15 +567,15 @@ void flash_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at
 }
 
 // One key block of ring attention: merges softmax(q k^T) v over this block into the fp32 running
-// output acc_o [B, Lq, H, 128] (contiguous) and its log2 LSE acc_lse [B, H, round_up(Lq, 256)];
+// output acc_o [B, Lq, H, d] (contiguous) and its log2 LSE acc_lse [B, H, round_up(Lq, 256)];
 // read = merge with the previous blocks, final = also write the bf16 result to o (and lse if given).
 void flash_fwd_accumulate(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o,
                           at::Tensor& lse, at::Tensor& acc_o, at::Tensor& acc_lse, bool read, bool final_,
                           double scale) {
   TORCH_CHECK(acc_o.is_cuda() && acc_o.scalar_type() == at::kFloat && acc_o.is_contiguous() && acc_o.dim() == 4 &&
                   acc_o.size(0) == q.size(0) && acc_o.size(1) == q.size(1) && acc_o.size(2) == q.size(2) &&
-                  acc_o.size(3) == 128,
-              "acc_o must be contiguous fp32 [B, Lq, H, 128]");
+                  acc_o.size(3) == q.size(3),
+              "acc_o must be contiguous fp32 [B, Lq, H, d]");
   TORCH_CHECK(acc_lse.is_cuda() && acc_lse.scalar_type() == at::kFloat && acc_lse.is_contiguous() &&
                   acc_lse.dim() == 3 && acc_lse.size(2) == flash_lse_pad(q.size(1)),
               "acc_lse must be fp32 [B, H, round_up(Lq, 256)]");
@@ -580,7 +585,7 @@ void flash_fwd_accumulate(const at::Tensor& q, const at::Tensor& k, const at::Te
 
 // flash_fwd that also stores every output row into the [B*Ll, ld] row buffer of the rank that
 // owns the row (scatter[r] = that rank's buffer address, Ll = Lq / #ranks), at columns
-// col + head * 128 -- the reverse all-to-all of context parallelism fused into the epilogue.
+// col + head * d -- the reverse all-to-all of context parallelism fused into the epilogue.
 void flash_fwd_scatter(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
                        double scale, std::vector<int64_t> scatter, int64_t ld, int64_t col) {
   TORCH_CHECK(!scatter.empty(), "scatter targets required");

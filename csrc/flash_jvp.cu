@@ -42,7 +42,7 @@
 namespace dmad {
 
 int* device_status_ptr(int device);
-void check_bhld(const at::Tensor& x, const char* name);
+void check_bhld(const at::Tensor& x, const char* name, int64_t d = 128);
 int64_t flash_lse_pad(int64_t L);
 
 namespace {

@@ -8,7 +8,8 @@ sd_unified_model.py), written from its published structure:
   downsample), (1280, 2 ResNets, 2 transformers of depth 10); mid: ResNet, transformer of depth 10,
   ResNet; up: mirrored with 3 ResNets per level; GroupNorm(32) + SiLU + ``conv_out`` 320 -> 4;
 * transformers: GroupNorm -> Linear in -> [LN, self-attn; LN, cross-attn to the 77 x 2048 text;
-  LN, GEGLU feed-forward x4] x depth -> Linear out, residual; heads of 64 channels.
+  LN, GEGLU feed-forward x4] x depth -> Linear out, residual; heads of 64 channels (on CUDA the
+  tcgen05 flash kernels, forward and backward; on the CPU PyTorch's SDPA).
 ``classify_forward`` (train/image/main/sd_unet_forward.py) = encoder + mid block only, returning the
 bottleneck (``return_bottleneck=True``).  Random-init weights; ~2.6 B parameters.
 """
@@ -59,11 +60,15 @@ class Attention(nn.Module):
     def forward(self, x, ctx=None):
         ctx = x if ctx is None else ctx
         B, N, C = x.shape
-        q = self.to_q(x).view(B, N, self.heads, -1).transpose(1, 2)
-        k = self.to_k(ctx).view(B, ctx.shape[1], self.heads, -1).transpose(1, 2)
-        v = self.to_v(ctx).view(B, ctx.shape[1], self.heads, -1).transpose(1, 2)
-        o = F.scaled_dot_product_attention(q, k, v)
-        return self.to_out[0](o.transpose(1, 2).reshape(B, N, C))
+        q = self.to_q(x).view(B, N, self.heads, -1)
+        k = self.to_k(ctx).view(B, ctx.shape[1], self.heads, -1)
+        v = self.to_v(ctx).view(B, ctx.shape[1], self.heads, -1)
+        if x.is_cuda:  # the tcgen05 flash kernels (head dim 64), forward and backward
+            from .. import ops
+            o = ops.flash_attention(q, k, v)
+        else:
+            o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)).transpose(1, 2)
+        return self.to_out[0](o.reshape(B, N, C))
 
 
 class GEGLU(nn.Module):

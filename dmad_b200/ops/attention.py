@@ -21,11 +21,11 @@ _FUSED_MIN_CTAS = 296  # two waves of the 148 SMs
 
 
 def flash_bwd_into(q, k, v, o, do, lse, dq, dk, dv, dd, scale):
-    """dq, dk, dv of softmax(q k^T scale) v given o, do and the forward's log2 LSE ([B, L, H, 128] bf16,
-    strided outputs allowed; ``dd`` an fp32 [B, H, Lpad] work buffer)."""
+    """dq, dk, dv of softmax(q k^T scale) v given o, do and the forward's log2 LSE ([B, L, H, D] bf16 with
+    D = 64 or 128, strided outputs allowed; ``dd`` an fp32 [B, H, Lpad] work buffer)."""
     e = ext()
-    B, Lq, H, _ = q.shape
-    if BWD_IMPL == "fused" and -(-k.shape[1] // 128) * H * B >= _FUSED_MIN_CTAS:
+    B, Lq, H, D = q.shape
+    if BWD_IMPL == "fused" and D == 128 and -(-k.shape[1] // 128) * H * B >= _FUSED_MIN_CTAS:
         acc = torch.empty(B * H * lse.shape[-1] * 128, dtype=torch.float32, device=q.device)
         e.flash_bwd_fused(q, k, v, o, do, lse, dq, dk, dv, dd, acc, float(scale))
     else:
@@ -47,7 +47,7 @@ def _lse_pad(L: int) -> int:
 
 @torch.library.custom_op("dmad::flash_attn_fwd", mutates_args=(), device_types="cuda")
 def flash_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float) -> tuple[torch.Tensor, torch.Tensor]:
-    """(o [B, Lq, H, 128] bf16, log2 LSE [B, H, round_up(Lq, 256)] fp32) of one tcgen05 forward.  A
+    """(o [B, Lq, H, D] bf16, log2 LSE [B, H, round_up(Lq, 256)] fp32) of one tcgen05 forward.  A
     dispatcher op, so that selective activation checkpointing can keep its outputs."""
     B, Lq, H, D = q.shape
     o = torch.empty((B, Lq, H, D), dtype=q.dtype, device=q.device)
@@ -82,12 +82,13 @@ class _FlashAttn(torch.autograd.Function):
         return dq, dk, dv, None
 
 
-def _supported(q, k, v) -> bool:
-    return q.is_cuda and q.shape[-1] == 128 and q.dtype == torch.bfloat16 and k.dtype == q.dtype and v.dtype == q.dtype
+def _supported(q, k, v, dims=(64, 128)) -> bool:
+    return (q.is_cuda and q.shape[-1] in dims and q.dtype == torch.bfloat16 and k.dtype == q.dtype
+            and v.dtype == q.dtype and k.shape[-1] == q.shape[-1] and v.shape[-1] == q.shape[-1])
 
 
 def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float | None = None) -> torch.Tensor:
-    """softmax(q k^T * scale) v for [B, L, H, 128] bf16 tensors (strided views allowed).
+    """softmax(q k^T * scale) v for [B, L, H, D] bf16 tensors, D = 64 or 128 (strided views allowed).
 
     CUDA: sm_100a tcgen05 forward/backward kernels.  CPU: fp32 PyTorch math.
     """
@@ -95,7 +96,7 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: fl
     if not q.is_cuda:
         return attention_reference(q, k, v, scale)
     if not _supported(q, k, v):
-        raise ValueError(f"flash_attention: need CUDA bf16 [B, L, H, 128], got {tuple(q.shape)} {q.dtype}")
+        raise ValueError(f"flash_attention: need CUDA bf16 [B, L, H, 64 or 128], got {tuple(q.shape)} {q.dtype}")
     return _FlashAttn.apply(q, k, v, scale)
 
 
@@ -162,6 +163,6 @@ def flash_attention_jvp(q, k, v, tq, tk=None, tv=None, scale: float | None = Non
     scale = float(scale) if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     if not q.is_cuda:
         return attention_jvp_reference(q, k, v, tq, tk, tv, scale)
-    if not _supported(q, k, v) or tq.dtype != q.dtype:
+    if not _supported(q, k, v, dims=(128,)) or tq.dtype != q.dtype:
         raise ValueError(f"flash_attention_jvp: need CUDA bf16 [B, L, H, 128], got {tuple(q.shape)} {q.dtype}")
     return _FlashAttnJvp.apply(q, k, v, tq, tk, tv, scale)

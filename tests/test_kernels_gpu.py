@@ -78,6 +78,51 @@ def test_flash_bwd(B, Lq, Lk, H):
         assert rel < 2e-2, (name, rel.item())
 
 
+@pytest.mark.parametrize("B,Lq,Lk,H", [(1, 128, 128, 1), (2, 999, 999, 3), (1, 4096, 4096, 2), (2, 1024, 77, 4),
+                                       (1, 300, 700, 2)])
+def test_flash_head_dim_64(B, Lq, Lk, H):
+    """Head dim 64 (the SDXL U-Net's): forward O and LSE, and dQ / dK / dV, against fp32 autograd;
+    Lk = 77 is the text cross-attention."""
+    from dmad_b200 import ops
+    e = ops.ext()
+    torch.manual_seed(4)
+    q = torch.randn(B, Lq, H, 64, device=dev, dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(B, Lk, H, 64, device=dev, dtype=torch.bfloat16, requires_grad=True)
+    v = torch.randn(B, Lk, H, 64, device=dev, dtype=torch.bfloat16, requires_grad=True)
+    g = torch.randn(B, Lq, H, 64, device=dev, dtype=torch.bfloat16)
+    scale = 1 / math.sqrt(64)
+    o_, lse = torch.empty_like(q), torch.empty(B, H, e.flash_lse_pad(Lq), device=dev)
+    e.flash_fwd(q.detach(), k.detach(), v.detach(), o_, lse, scale)
+    o = ops.flash_attention(q, k, v)
+    o.backward(g)
+    torch.cuda.synchronize()
+    ops.check_device_status()
+    qr, kr, vr = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+    ref, ref_lse = _attn_ref(qr, kr, vr, scale)
+    ref.backward(g.float())
+    assert (o.float() - ref).abs().max().item() < 2e-2
+    assert torch.equal(o, o_)
+    assert ((lse[:, :, :Lq] * math.log(2)) - ref_lse).abs().max().item() < 1e-2
+    for a, b, name in ((q.grad, qr.grad, "dq"), (k.grad, kr.grad, "dk"), (v.grad, vr.grad, "dv")):
+        rel = (a.float() - b).norm() / b.norm()
+        assert rel < 2e-2, (name, rel.item())
+
+
+def test_sdxl_attention_module_on_flash_kernels():
+    """The SDXL Attention block (10 heads of 64) on CUDA against its CPU SDPA path, self and cross."""
+    from dmad_b200.models.sdxl import Attention
+    torch.manual_seed(5)
+    for ctx_dim in (None, 2048):
+        m = Attention(640, ctx_dim)
+        x = torch.randn(2, 1024, 640)
+        ctx = torch.randn(2, 77, 2048) if ctx_dim else None
+        ref = m(x, ctx)
+        mc = m.to(dev, torch.bfloat16)
+        out = mc(x.to(dev, torch.bfloat16), ctx.to(dev, torch.bfloat16) if ctx is not None else None)
+        rel = (out.float().cpu() - ref).norm() / ref.norm()
+        assert rel < 2e-2, (ctx_dim, rel.item())
+
+
 @pytest.mark.parametrize("B,Lq,Lk,H", [(1, 128, 128, 1), (1, 384, 256, 2), (1, 999, 999, 1), (2, 300, 512, 2),
                                         (1, 1000, 1300, 3)])
 def test_flash_bwd_fused(B, Lq, Lk, H):
