@@ -106,16 +106,25 @@ class SegLinear(nn.Module):
         self.register_buffer("sn_v", torch.stack(vs), persistent=True)
         self.register_buffer("sn_gain", torch.cat(gains).float(), persistent=True)
         self.register_buffer("sn_mask", torch.tensor(mask, dtype=torch.bool, device=dev), persistent=True)
+        self._sn_on = list(mask)  # host copy of sn_mask: reading the device tensor would wait for the GPU
         self.sn_enabled = n > 0
         return n
+
+    def _sn_segments_on(self):
+        """Which segments carry the spectral norm, from the host copy of ``sn_mask`` (refreshed when a
+        state dict is loaded), so that the forward never reads a device tensor back."""
+        if getattr(self, "_sn_on", None) is None:
+            self._sn_on = [bool(b) for b in self.sn_mask.tolist()]
+        return self._sn_on
 
     def _sn_row_scale(self):
         """Per-output-row scale gain/sigma (differentiable in W through sigma = u^T W v)."""
         w = self.weight
         scales = []
+        on = self._sn_segments_on()
         for i, (name, sl) in enumerate(self.seg_slices()):
             o = sl.stop - sl.start
-            if not bool(self.sn_mask[i]):
+            if not on[i]:
                 scales.append(torch.ones(o, device=w.device, dtype=torch.float32))
                 continue
             ws = w[sl].float()
@@ -144,8 +153,9 @@ class SegLinear(nn.Module):
         if not self.sn_enabled:
             return self.weight.detach().clone()
         w = self.weight.detach().float().clone()
+        on = self._sn_segments_on()
         for i, (name, sl) in enumerate(self.seg_slices()):
-            if not bool(self.sn_mask[i]):
+            if not on[i]:
                 continue
             ws = w[sl]
             v = _l2n(ws.t() @ self.sn_u[sl].float())
@@ -263,6 +273,7 @@ class SegLinear(nn.Module):
                     self.sn_gain[i:i + 1].copy_(state_dict[key + "sn_gain"].reshape(1))
                     # a stored power-iteration state means the layer is spectrally normed
                     self.sn_mask[i:i + 1].copy_(state_dict.get(key + "sn_mask", torch.ones(1, dtype=torch.bool)))
+                    self._sn_on = None  # re-read from the loaded mask on the next forward
                     consumed.update(key + n for n in ("sn_u", "sn_v", "sn_gain", "sn_mask"))
                 if self.lora_rank and name in self.lora_segments:
                     r = self.lora_rank
