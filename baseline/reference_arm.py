@@ -16,8 +16,9 @@ with the critic heads, frozen-gain spectral norm and master-weight AdamW written
 torch APIs exactly as the reference registers them.  None of dmad_b200's models, kernels or
 engine is used on this path.
 
-Install (done once on the build machine; the reference ships no packaging metadata):
-    copy train/wan/{rcm,imaginaire} to /tmp, add a pyproject.toml, then
+Install (the reference ships no packaging metadata; ``provision`` does this when baseline/_ref is missing and
+the reference checkout is on the machine): copy train/wan/{rcm,imaginaire} to a scratch directory, add a
+pyproject.toml, then
     python -m pip install --no-index --no-build-isolation --no-deps --target baseline/_ref <copy>
 """
 from __future__ import annotations
@@ -292,9 +293,62 @@ class ReferenceWanDMAD:
         return torch.nan_to_num(x.float())
 
 
+_PYPROJECT = """[build-system]
+requires = ["setuptools"]
+build-backend = "setuptools.build_meta"
+
+[project]
+name = "dmad-reference-wan"
+version = "0.0.0"
+
+[tool.setuptools.packages.find]
+include = ["rcm*", "imaginaire*"]
+"""
+
+
+def _reference_checkout():
+    try:
+        with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+            path = json.load(f).get("reference_path")
+    except (OSError, ValueError):
+        return None
+    return path if path and os.path.isdir(os.path.join(path, "train", "wan", "rcm")) else None
+
+
+def provision(log=sys.stderr) -> bool:
+    """Installs the unmodified reference into baseline/_ref when it is missing and the reference checkout
+    (BASELINE.json's ``reference_path``) is on this machine: ``train/wan/{rcm,imaginaire}`` copied to a
+    scratch directory with packaging metadata added, ``pip install --no-index --no-deps --target``, and
+    ``train/image/{main,third_party}`` copied beside them.  Returns whether baseline/_ref is in place."""
+    if os.path.isdir(os.path.join(REF, "rcm", "networks")):
+        return True
+    src = _reference_checkout()
+    if src is None:
+        return False
+    import shutil
+    import subprocess
+    import tempfile
+
+    with tempfile.TemporaryDirectory() as tmp:
+        for name in ("rcm", "imaginaire"):
+            shutil.copytree(os.path.join(src, "train", "wan", name), os.path.join(tmp, name))
+        with open(os.path.join(tmp, "pyproject.toml"), "w") as f:
+            f.write(_PYPROJECT)
+        print(f"# installing the reference from {src} into {REF}", file=log, flush=True)
+        rc = subprocess.call([sys.executable, "-m", "pip", "install", "--no-index", "--no-build-isolation", "--no-deps",
+                              "--target", REF, tmp], stdout=log, stderr=log)
+    if rc != 0:
+        return False
+    for name in ("main", "third_party"):
+        dst = os.path.join(REF, "image", name)
+        if not os.path.isdir(dst):
+            shutil.copytree(os.path.join(src, "train", "image", name), dst)
+    return os.path.isdir(os.path.join(REF, "rcm", "networks"))
+
+
 def build_reference_trainer(args, device):
-    if not os.path.isdir(os.path.join(REF, "rcm", "networks")):
-        _unavailable("baseline/_ref missing: the reference has no setup.py/pyproject.toml, so it must be installed "
-                     "from a copy with packaging metadata added (see baseline/reference_arm.py)")
+    if not provision():
+        _unavailable("baseline/_ref missing and no reference checkout to install it from: the reference has no "
+                     "setup.py/pyproject.toml, so it is installed from a copy with packaging metadata added")
         return None
     return ReferenceWanDMAD(device, layers=args.layers)
