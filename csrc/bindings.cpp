@@ -37,6 +37,12 @@ void qk_norm_rope_bwd(const at::Tensor& gq, const at::Tensor& gk, const at::Tens
 void rope_apply(const at::Tensor& x, at::Tensor& y, const at::Tensor& cosT, const at::Tensor& sinT, int64_t hd,
                 bool inverse);
 void gelu_fwd(const at::Tensor& x, at::Tensor& y);
+at::Tensor sn_weight_fwd(const at::Tensor& w, at::Tensor& u, at::Tensor& v, const at::Tensor& gain,
+                         at::Tensor& scale, at::Tensor& sigma, std::vector<int64_t> offsets, std::vector<int64_t> on,
+                         bool train);
+at::Tensor sn_weight_bwd(const at::Tensor& g, const at::Tensor& w, const at::Tensor& u, const at::Tensor& v,
+                         const at::Tensor& gain, const at::Tensor& scale, const at::Tensor& sigma,
+                         std::vector<int64_t> offsets, std::vector<int64_t> on);
 void gelu_bwd(const at::Tensor& g, const at::Tensor& x, at::Tensor& dx);
 void fused_adamw(std::vector<at::Tensor> master, std::vector<at::Tensor> grads, std::vector<at::Tensor> exp_avg,
                  std::vector<at::Tensor> exp_avg_sq, std::vector<at::Tensor> lowp, std::vector<at::Tensor> ema,
@@ -99,6 +105,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_norm_rope_bwd", &dmad::qk_norm_rope_bwd);
   m.def("rope_apply", &dmad::rope_apply);
   m.def("gelu_fwd", &dmad::gelu_fwd);
+  m.def("sn_weight_fwd", &dmad::sn_weight_fwd);
+  m.def("sn_weight_bwd", &dmad::sn_weight_bwd);
   m.def("gelu_bwd", &dmad::gelu_bwd);
   m.def("fused_adamw", &dmad::fused_adamw);
   m.def("multi_sumsq", &dmad::multi_sumsq);

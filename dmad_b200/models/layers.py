@@ -38,6 +38,30 @@ def _l2n(x, eps=1e-12):
     return x / x.norm().clamp_min(eps)
 
 
+class _SNWeight(torch.autograd.Function):
+    """W -> bf16(W * gain_s / sigma_s) on the fused CUDA kernels; ``u`` [O] and ``v`` [nseg, I] (fp32) are
+    the power-iteration state, updated in place when ``train``."""
+
+    @staticmethod
+    def forward(ctx, w, u, v, gain, offsets, on, train):
+        from ..ops import ext
+        scale = torch.empty(w.shape[0], dtype=torch.float32, device=w.device)
+        sigma = torch.empty(len(on), dtype=torch.float32, device=w.device)
+        out = ext().sn_weight_fwd(w, u, v, gain, scale, sigma, offsets, on, bool(train))
+        ctx.save_for_backward(w, u.clone(), v.clone(), gain, scale, sigma)
+        ctx.meta = (offsets, on)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        from ..ops import ext
+        w, u, v, gain, scale, sigma = ctx.saved_tensors
+        if g.stride(-1) != 1 or g.stride(0) % 8 or g.data_ptr() % 16:
+            g = g.contiguous()
+        dw = ext().sn_weight_bwd(g, w, u, v, gain, scale, sigma, *ctx.meta)
+        return dw, None, None, None, None, None, None
+
+
 class SegLinear(nn.Module):
     def __init__(self, in_features: int, segments: Sequence[tuple[str, int]], bias: bool = True, flat_name: str = ""):
         super().__init__()
@@ -143,7 +167,30 @@ class SegLinear(nn.Module):
     def effective_weight(self):
         if not self.sn_enabled:
             return self.weight
+        if self.weight.is_cuda:  # fused kernels: power iteration, scaled weight and its gradient
+            return self._sn_weight_fused()
         return (self.weight.float() * self._sn_row_scale()[:, None]).to(self.weight.dtype)
+
+    def _sn_weight_fused(self):
+        """``effective_weight`` through the fused spectral-norm kernels (the math of ``_sn_row_scale``:
+        one power iteration per training forward, sigma differentiable in W with u, v held constant)."""
+        on = [int(b) for b in self._sn_segments_on()]
+        offs = [0]
+        for _, sl in self.seg_slices():
+            offs.append(sl.stop)
+        u32 = self.sn_u if self.sn_u.dtype == torch.float32 else self.sn_u.float()
+        v32 = self.sn_v if self.sn_v.dtype == torch.float32 else self.sn_v.float()
+        if getattr(self, "_sn_gain32", None) is None:
+            self._sn_gain32 = self.sn_gain.float().contiguous().clone()
+        w = self.weight
+        if w.stride(-1) != 1 or w.stride(0) % 8 or w.data_ptr() % 16:
+            w = w.contiguous()
+        w_eff = _SNWeight.apply(w, u32, v32, self._sn_gain32, offs, on, self.training)
+        if self.training and u32 is not self.sn_u:
+            with torch.no_grad():
+                self.sn_u.copy_(u32)
+                self.sn_v.copy_(v32)
+        return w_eff
 
     @torch.no_grad()
     def folded_weight(self):
@@ -274,6 +321,7 @@ class SegLinear(nn.Module):
                     # a stored power-iteration state means the layer is spectrally normed
                     self.sn_mask[i:i + 1].copy_(state_dict.get(key + "sn_mask", torch.ones(1, dtype=torch.bool)))
                     self._sn_on = None  # re-read from the loaded mask on the next forward
+                    self._sn_gain32 = None
                     consumed.update(key + n for n in ("sn_u", "sn_v", "sn_gain", "sn_mask"))
                 if self.lora_rank and name in self.lora_segments:
                     r = self.lora_rank
