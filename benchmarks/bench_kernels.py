@@ -201,6 +201,22 @@ def main():
             ("qk_norm_rope_fwd", lambda: O.qk_norm_rope(qkv, wq, wk, cos, sin, D, 128), (3 + 2) * R * D * 2),
             ("gelu_tanh_fwd", lambda: O.gelu_tanh(h), 2 * R * F_ * 2),
         ]
+        e = O.ext()
+        dy, dxb = torch.randn_like(x), torch.empty_like(x)
+        xf = x.float()
+        mean, rstd = xf.mean(1), torch.rsqrt(xf.var(1, unbiased=False) + 1e-6)
+        da, dc, dg = torch.zeros_like(amod), torch.zeros_like(cmod), torch.zeros_like(gate)
+        gqk = torch.randn(R, 2 * D, device="cuda", dtype=torch.bfloat16)
+        dqk = torch.empty(R, 2 * D, device="cuda", dtype=torch.bfloat16)
+        rq, rk = torch.rand(R, device="cuda") + 0.5, torch.rand(R, device="cuda") + 0.5
+        dwq, dwk = torch.zeros(D, device="cuda"), torch.zeros(D, device="cuda")
+        rows += [  # backward kernels: algorithmic bytes (each input read once, each output written once)
+            ("ln_mod_bwd", lambda: e.ln_mod_bwd(dy, x, mean, rstd, amod, 1.0, 1560, None, False, dxb, None, da, dc,
+                                                None, None, None, None), 3 * R * D * 2),
+            ("gate_residual_bwd", lambda: e.gate_res_bwd(dy, y, dxb, gate, dg, 1560, None), 3 * R * D * 2),
+            ("qk_norm_rope_bwd", lambda: e.qk_norm_rope_bwd(gqk[:, :D], gqk[:, D:], qkv, dqk, wq, wk, cos, sin, rq, rk,
+                                                            dwq, dwk, D, 128), 6 * R * D * 2),
+        ]
         for name, fn, nbytes in rows:
             ms = timeit(fn, a.iters, a.warmup)
             print(json.dumps({"op": name, "rows": R, "ms": round(ms, 4), "GB/s": round(nbytes / ms / 1e6, 1),

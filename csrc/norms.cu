@@ -183,10 +183,7 @@ ln_mod_fwd_warp_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx, __nv_bfl
   }
 }
 
-// Backward.  Each block walks `rows_per_block` consecutive rows, keeps the
-// per-column partial sums of dy*n (-> da) and dy (-> dc) in registers and
-// flushes them with atomics whenever the group changes.
-// Optional fusions:
+// Backward arguments (the kernels follow).  Optional fusions:
 //   dres   : dx_total = LN_bwd(dy) + dres
 //   gate/yg: the input of the norm was out = xg + yg * gate[g]; additionally
 //            write dyg = dx_total * gate and accumulate dgate += dx_total * yg.
@@ -217,103 +214,137 @@ struct LnBwdArgs {
   int rows_per_block;
 };
 
-template <int kMaxVec, int kTh>
-__global__ void __launch_bounds__(kTh)
-ln_mod_bwd_kernel(LnBwdArgs p, ModSpec m) {
-  __shared__ float red[32];
+// Two-pass backward.  Pass 1, one warp per row: the row statistics mean(dn) and mean(dn * n) of
+// dn = dy * A (no block barriers, two CTAs of 8 rows per SM).  Pass 2, one thread per 8-column vector
+// (column tiles of 256 vectors) over a tile of consecutive rows per block: dx (plus the optional
+// residual-gradient and gated-residual fusions) from those statistics, with the column sums dA, dC
+// (and dgate) accumulated in registers over the tile and flushed once per tile and group.  A one-pass
+// kernel with two block reductions per row was latency-bound; this reads x and dy twice but keeps
+// four rows of loads in flight per thread.
+__global__ void __launch_bounds__(256, 2)
+ln_bwd_stats_kernel(LnBwdArgs p, ModSpec m, float2* __restrict__ stats) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= p.R) return;
   const int nvec = p.D >> 3;
-  const int64_t r0 = (int64_t)blockIdx.x * p.rows_per_block;
-  const int64_t r1 = min(p.R, r0 + p.rows_per_block);
-  float acc_a[kMaxVec][8], acc_c[kMaxVec][8], acc_g[kMaxVec][8];
+  const float mu = p.rms ? 0.f : p.mean[r];
+  const float rstd = p.rstd[r];
+  const int g = row_group(m, r);
+  const float* ar = m.a != nullptr ? m.a + (int64_t)g * m.a_sg : nullptr;
+  const bf16x8* xr = reinterpret_cast<const bf16x8*>(p.x + r * p.sx);
+  const bf16x8* dyr = reinterpret_cast<const bf16x8*>(p.dy + r * p.sdy);
+  float s1 = 0.f, s2 = 0.f;
+#pragma unroll 4
+  for (int c = lane; c < nvec; c += 32) {
+    float xv[8], gv[8];
+    bf16x8_to_float(xr[c], xv);
+    bf16x8_to_float(dyr[c], gv);
 #pragma unroll
-  for (int i = 0; i < kMaxVec; ++i)
+    for (int e = 0; e < 8; e += 4) {
+      const float4 av = ar != nullptr ? __ldg(reinterpret_cast<const float4*>(ar + c * 8 + e))
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float aa[4] = {av.x, av.y, av.z, av.w};
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc_a[i][e] = acc_c[i][e] = acc_g[i][e] = 0.f;
-  int cur_g = -1;
-  auto flush = [&](int g) {
-    if (g < 0) return;
-#pragma unroll
-    for (int i = 0; i < kMaxVec; ++i) {
-      const int c = threadIdx.x + i * kTh;
-      if (c < nvec) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int col = c * 8 + e;
-          if (p.da != nullptr) atomicAdd(p.da + (int64_t)g * p.D + col, acc_a[i][e]);
-          if (p.dc != nullptr) atomicAdd(p.dc + (int64_t)g * p.D + col, acc_c[i][e]);
-          if (p.dgate != nullptr) atomicAdd(p.dgate + (int64_t)g * p.D + col, acc_g[i][e]);
-          acc_a[i][e] = acc_c[i][e] = acc_g[i][e] = 0.f;
-        }
-      }
-    }
-  };
-  for (int64_t r = r0; r < r1; ++r) {
-    const int g = row_group(m, r);
-    if (g != cur_g) {
-      flush(cur_g);
-      cur_g = g;
-    }
-    const float mu = p.rms ? 0.f : p.mean[r];
-    const float rstd = p.rstd[r];
-    const float* ar = m.a != nullptr ? m.a + (int64_t)g * m.a_sg : nullptr;
-    const bf16x8* xr = reinterpret_cast<const bf16x8*>(p.x + r * p.sx);
-    const bf16x8* dyr = reinterpret_cast<const bf16x8*>(p.dy + r * p.sdy);
-    float n[kMaxVec][8], dn[kMaxVec][8];
-    float s1 = 0.f, s2 = 0.f;
-#pragma unroll
-    for (int i = 0; i < kMaxVec; ++i) {
-      const int c = threadIdx.x + i * kTh;
-      if (c < nvec) {
-        float xv[8], gv[8];
-        bf16x8_to_float(xr[c], xv);
-        bf16x8_to_float(dyr[c], gv);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int col = c * 8 + e;
-          n[i][e] = (xv[e] - mu) * rstd;
-          const float A = m.a_add + (ar != nullptr ? ar[col] : 0.f);
-          dn[i][e] = gv[e] * A;
-          acc_a[i][e] += gv[e] * n[i][e];
-          acc_c[i][e] += gv[e];
-          s1 += dn[i][e];
-          s2 += dn[i][e] * n[i][e];
-        }
-      }
-    }
-    const float mdn = p.rms ? 0.f : block_sum(s1, red) / p.D;
-    const float mdnn = block_sum(s2, red) / p.D;
-    bf16x8* dxr = reinterpret_cast<bf16x8*>(p.dx + r * p.sdx);
-    const bf16x8* dresr = p.dres != nullptr ? reinterpret_cast<const bf16x8*>(p.dres + r * p.sdres) : nullptr;
-    const float* gr = p.gate != nullptr ? p.gate + (int64_t)g * p.gate_sg : nullptr;
-    const bf16x8* ygr = p.yg != nullptr ? reinterpret_cast<const bf16x8*>(p.yg + r * p.syg) : nullptr;
-    bf16x8* dygr = p.dyg != nullptr ? reinterpret_cast<bf16x8*>(p.dyg + r * p.sdyg) : nullptr;
-#pragma unroll
-    for (int i = 0; i < kMaxVec; ++i) {
-      const int c = threadIdx.x + i * kTh;
-      if (c < nvec) {
-        float o[8];
-        float rv[8];
-        if (dresr != nullptr) bf16x8_to_float(dresr[c], rv);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          o[e] = rstd * (dn[i][e] - mdn - n[i][e] * mdnn) + (dresr != nullptr ? rv[e] : 0.f);
-        }
-        dxr[c] = float_to_bf16x8(o);
-        if (gr != nullptr) {
-          float yv[8], d[8];
-          bf16x8_to_float(ygr[c], yv);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int col = c * 8 + e;
-            d[e] = o[e] * gr[col];
-            acc_g[i][e] += o[e] * yv[e];
-          }
-          dygr[c] = float_to_bf16x8(d);
-        }
+      for (int k = 0; k < 4; ++k) {
+        const float n = (xv[e + k] - mu) * rstd;
+        const float dn = gv[e + k] * (m.a_add + aa[k]);
+        s1 += dn;
+        s2 = fmaf(dn, n, s2);
       }
     }
   }
-  flush(cur_g);
+  s1 = warp_sum(s1);
+  s2 = warp_sum(s2);
+  if (lane == 0) stats[r] = make_float2(p.rms ? 0.f : s1 / p.D, s2 / p.D);
+}
+
+template <int kChunk>
+__global__ void __launch_bounds__(256)
+ln_bwd_apply_kernel(LnBwdArgs p, ModSpec m, const float2* __restrict__ stats) {
+  const int nvec = p.D >> 3;
+  const int c = blockIdx.y * 256 + threadIdx.x;  // column tiles of 256 vectors (2048 columns)
+  if (c >= nvec) return;
+  const int64_t r0 = (int64_t)blockIdx.x * p.rows_per_block;
+  const int64_t r1 = min(p.R, r0 + p.rows_per_block);
+  const bool has_gate = p.gate != nullptr;
+  float acc_a[8], acc_c[8], acc_g[8], A[8], Gt[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc_a[e] = acc_c[e] = acc_g[e] = A[e] = Gt[e] = 0.f;
+  int cur = -1;
+  auto flush = [&]() {
+    if (cur < 0) return;
+    const int64_t base = (int64_t)cur * p.D + c * 8;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (p.da != nullptr) atomicAdd(p.da + base + e, acc_a[e]);
+      if (p.dc != nullptr) atomicAdd(p.dc + base + e, acc_c[e]);
+      if (has_gate && p.dgate != nullptr) atomicAdd(p.dgate + base + e, acc_g[e]);
+      acc_a[e] = acc_c[e] = acc_g[e] = 0.f;
+    }
+  };
+  for (int64_t rb = r0; rb < r1; rb += kChunk) {
+    // loads of the chunk's rows first, then the arithmetic row by row
+    bf16x8 xraw[kChunk], dyraw[kChunk], rraw[kChunk], yraw[kChunk];
+#pragma unroll
+    for (int k = 0; k < kChunk; ++k) {
+      const int64_t r = rb + k;
+      if (r < r1) {
+        xraw[k] = reinterpret_cast<const bf16x8*>(p.x + r * p.sx)[c];
+        dyraw[k] = reinterpret_cast<const bf16x8*>(p.dy + r * p.sdy)[c];
+        if (p.dres != nullptr) rraw[k] = reinterpret_cast<const bf16x8*>(p.dres + r * p.sdres)[c];
+        if (has_gate) yraw[k] = reinterpret_cast<const bf16x8*>(p.yg + r * p.syg)[c];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kChunk; ++k) {
+      const int64_t r = rb + k;
+      if (r >= r1) break;
+      const int g = row_group(m, r);
+      if (g != cur) {
+        flush();
+        cur = g;
+        const float* ar = m.a != nullptr ? m.a + (int64_t)g * m.a_sg + c * 8 : nullptr;
+        const float* gr = has_gate ? p.gate + (int64_t)g * p.gate_sg + c * 8 : nullptr;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          A[e] = m.a_add + (ar != nullptr ? ar[e] : 0.f);
+          Gt[e] = gr != nullptr ? gr[e] : 0.f;
+        }
+      }
+      const float mu = p.rms ? 0.f : p.mean[r];
+      const float rstd = p.rstd[r];
+      const float2 st = stats[r];
+      float xv[8], gv[8], o[8];
+      bf16x8_to_float(xraw[k], xv);
+      bf16x8_to_float(dyraw[k], gv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float n = (xv[e] - mu) * rstd;
+        const float dn = gv[e] * A[e];
+        acc_a[e] = fmaf(gv[e], n, acc_a[e]);
+        acc_c[e] += gv[e];
+        o[e] = rstd * (dn - st.x - n * st.y);
+      }
+      if (p.dres != nullptr) {
+        float rv[8];
+        bf16x8_to_float(rraw[k], rv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] += rv[e];
+      }
+      reinterpret_cast<bf16x8*>(p.dx + r * p.sdx)[c] = float_to_bf16x8(o);
+      if (has_gate) {
+        float yv[8], d[8];
+        bf16x8_to_float(yraw[k], yv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          d[e] = o[e] * Gt[e];
+          acc_g[e] = fmaf(o[e], yv[e], acc_g[e]);
+        }
+        reinterpret_cast<bf16x8*>(p.dyg + r * p.sdyg)[c] = float_to_bf16x8(d);
+      }
+    }
+  }
+  flush();
 }
 
 __global__ void gate_res_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t sx, const __nv_bfloat16* __restrict__ y,
@@ -334,57 +365,63 @@ __global__ void gate_res_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t
   reinterpret_cast<bf16x8*>(out + r * so)[c] = float_to_bf16x8(o);
 }
 
-// Gated-residual backward: dy = dout * gate[g], dgate[g] += sum_rows dout * y.
-template <int kMaxVec, int kTh>
-__global__ void __launch_bounds__(kTh)
+// Gated-residual backward: dy = dout * gate[g], dgate[g] += sum_rows dout * y.  One thread per 8-column
+// vector (column tiles of 256 vectors) over a tile of consecutive rows, the loads of four rows issued
+// before their arithmetic; the column sums stay in registers and are flushed once per tile and group.
+template <int kChunk>
+__global__ void __launch_bounds__(256)
 gate_res_bwd_kernel(const __nv_bfloat16* __restrict__ dout, int64_t sdo, const __nv_bfloat16* __restrict__ y, int64_t sy,
                     __nv_bfloat16* __restrict__ dy, int64_t sdy, float* __restrict__ dgate, ModSpec m, int64_t R, int D,
                     int rows_per_block) {
   const int nvec = D >> 3;
+  const int c = blockIdx.y * 256 + threadIdx.x;
+  if (c >= nvec) return;
   const int64_t r0 = (int64_t)blockIdx.x * rows_per_block, r1 = min(R, r0 + rows_per_block);
-  float acc[kMaxVec][8];
+  float acc[8], Gt[8];
 #pragma unroll
-  for (int i = 0; i < kMaxVec; ++i)
+  for (int e = 0; e < 8; ++e) acc[e] = Gt[e] = 0.f;
+  int cur = -1;
+  auto flush = [&]() {
+    if (cur < 0 || dgate == nullptr) return;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
-  int cur_g = -1;
-  auto flush = [&](int g) {
-    if (g < 0 || dgate == nullptr) return;
-#pragma unroll
-    for (int i = 0; i < kMaxVec; ++i) {
-      const int c = threadIdx.x + i * kTh;
-      if (c < nvec)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          atomicAdd(dgate + (int64_t)g * D + c * 8 + e, acc[i][e]);
-          acc[i][e] = 0.f;
-        }
+    for (int e = 0; e < 8; ++e) {
+      atomicAdd(dgate + (int64_t)cur * D + c * 8 + e, acc[e]);
+      acc[e] = 0.f;
     }
   };
-  for (int64_t r = r0; r < r1; ++r) {
-    const int g = row_group(m, r);
-    if (g != cur_g) {
-      flush(cur_g);
-      cur_g = g;
-    }
-    const float* ar = m.a + (int64_t)g * m.a_sg;
+  for (int64_t rb = r0; rb < r1; rb += kChunk) {
+    bf16x8 graw[kChunk], yraw[kChunk];
 #pragma unroll
-    for (int i = 0; i < kMaxVec; ++i) {
-      const int c = threadIdx.x + i * kTh;
-      if (c < nvec) {
-        float gv[8], yv[8], o[8];
-        bf16x8_to_float(reinterpret_cast<const bf16x8*>(dout + r * sdo)[c], gv);
-        bf16x8_to_float(reinterpret_cast<const bf16x8*>(y + r * sy)[c], yv);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          o[e] = gv[e] * ar[c * 8 + e];
-          acc[i][e] += gv[e] * yv[e];
-        }
-        reinterpret_cast<bf16x8*>(dy + r * sdy)[c] = float_to_bf16x8(o);
+    for (int k = 0; k < kChunk; ++k) {
+      if (rb + k < r1) {
+        graw[k] = reinterpret_cast<const bf16x8*>(dout + (rb + k) * sdo)[c];
+        yraw[k] = reinterpret_cast<const bf16x8*>(y + (rb + k) * sy)[c];
       }
     }
+#pragma unroll
+    for (int k = 0; k < kChunk; ++k) {
+      const int64_t r = rb + k;
+      if (r >= r1) break;
+      const int g = row_group(m, r);
+      if (g != cur) {
+        flush();
+        cur = g;
+        const float* ar = m.a + (int64_t)g * m.a_sg + c * 8;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) Gt[e] = ar[e];
+      }
+      float gv[8], yv[8], o[8];
+      bf16x8_to_float(graw[k], gv);
+      bf16x8_to_float(yraw[k], yv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        o[e] = gv[e] * Gt[e];
+        acc[e] = fmaf(gv[e], yv[e], acc[e]);
+      }
+      reinterpret_cast<bf16x8*>(dy + r * sdy)[c] = float_to_bf16x8(o);
+    }
   }
-  flush(cur_g);
+  flush();
 }
 
 // ------------------------------------------------------------------ q/k RMSNorm + RoPE
@@ -440,79 +477,106 @@ qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ src, int64_t ss, __nv_
 
 // Backward: g (grad of the rotated output, q at col 0 / k at col D, row stride sg)
 // -> dx (grad of the pre-norm input, row stride sdx); dw accumulates (fp32 [D]).
-template <int kMaxVec, int kTh>
-__global__ void __launch_bounds__(kTh)
-qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ gq, int64_t sgq, const __nv_bfloat16* __restrict__ gk,
-                        int64_t sgk, const __nv_bfloat16* __restrict__ src, int64_t ss, __nv_bfloat16* __restrict__ dx,
-                        int64_t sdx, const float* __restrict__ wq, const float* __restrict__ wk,
-                        const float* __restrict__ cosT, const float* __restrict__ sinT, const float* __restrict__ rstd_q,
-                        const float* __restrict__ rstd_k, float* __restrict__ dwq, float* __restrict__ dwk, int64_t R,
-                        int D, int hd, int Lrope, int rows_per_block) {
-  __shared__ float red[32];
-  const int which = blockIdx.y;
-  const int nvec = D >> 3;
-  const float* w = which == 0 ? wq : wk;
-  float* dw = which == 0 ? dwq : dwk;
-  const __nv_bfloat16* g = which == 0 ? gq : gk;
-  const int64_t sg = which == 0 ? sgq : sgk;
-  float accw[kMaxVec][8];
+struct QkBwd {
+  const __nv_bfloat16* g[2];  // gq, gk
+  int64_t sg[2];
+  const __nv_bfloat16* src;
+  int64_t ss;
+  __nv_bfloat16* dx;
+  int64_t sdx;
+  const float* w[2];
+  const float* cosT;
+  const float* sinT;
+  const float* rstd[2];
+  float* dw[2];
+  int64_t R;
+  int D, hd, Lrope, rows_per_block;
+};
+
+// Pass 1, one warp per row and per q / k (blockIdx.y): mean(dn * n) of dn = rot^-1(g) * w, n = x * rstd.
+__global__ void __launch_bounds__(256, 2) qk_bwd_stats_kernel(QkBwd p, float* __restrict__ stats) {
+  const int which = blockIdx.y, lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= p.R) return;
+  const int nvec = p.D >> 3;
+  const float rstd = p.rstd[which][r];
+  const int64_t tr = (r % p.Lrope) * (p.hd >> 1);
+  const bf16x8* xr = reinterpret_cast<const bf16x8*>(p.src + r * p.ss + which * p.D);
+  const bf16x8* gr = reinterpret_cast<const bf16x8*>(p.g[which] + r * p.sg[which]);
+  const float* w = p.w[which];
+  float s2 = 0.f;
+#pragma unroll 4
+  for (int c = lane; c < nvec; c += 32) {
+    float xv[8], gv[8];
+    bf16x8_to_float(xr[c], xv);
+    bf16x8_to_float(gr[c], gv);
 #pragma unroll
-  for (int i = 0; i < kMaxVec; ++i)
+    for (int e = 0; e < 8; e += 2) {
+      const int col = c * 8 + e;
+      const int pi = (col % p.hd) >> 1;
+      const float cs = p.cosT[tr + pi], sn = p.sinT[tr + pi];
+      const float da0 = gv[e] * cs + gv[e + 1] * sn;  // inverse rotation of the output gradient
+      const float da1 = -gv[e] * sn + gv[e + 1] * cs;
+      s2 = fmaf(da0 * w[col], xv[e] * rstd, s2);
+      s2 = fmaf(da1 * w[col + 1], xv[e + 1] * rstd, s2);
+    }
+  }
+  s2 = warp_sum(s2);
+  if (lane == 0) stats[which * p.R + r] = s2 / p.D;
+}
+
+// Pass 2: dx = rstd (dn - n mean(dn n)) and dw += sum_rows rot^-1(g) * n, one thread per 8-column vector
+// (column tiles of 256 vectors, blockIdx.z = q / k) over a tile of rows, four rows of loads at a time.
+template <int kChunk>
+__global__ void __launch_bounds__(256) qk_bwd_apply_kernel(QkBwd p, const float* __restrict__ stats) {
+  const int which = blockIdx.z;
+  const int nvec = p.D >> 3;
+  const int c = blockIdx.y * 256 + threadIdx.x;
+  if (c >= nvec) return;
+  const int64_t r0 = (int64_t)blockIdx.x * p.rows_per_block, r1 = min(p.R, r0 + p.rows_per_block);
+  const float* w = p.w[which];
+  float W[8], acc[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) accw[i][e] = 0.f;
-  const int64_t r0 = (int64_t)blockIdx.x * rows_per_block, r1 = min(R, r0 + rows_per_block);
-  for (int64_t r = r0; r < r1; ++r) {
-    const float rstd = (which == 0 ? rstd_q : rstd_k)[r];
-    const int64_t tr = (r % Lrope) * (hd >> 1);
-    const bf16x8* xr = reinterpret_cast<const bf16x8*>(src + r * ss + which * D);
-    const bf16x8* gr = reinterpret_cast<const bf16x8*>(g + r * sg);
-    float n[kMaxVec][8], dn[kMaxVec][8];
-    float s2 = 0.f;
+  for (int e = 0; e < 8; ++e) {
+    W[e] = w[c * 8 + e];
+    acc[e] = 0.f;
+  }
+  const int pi0 = ((c * 8) % p.hd) >> 1;  // a vector never straddles a head (hd is a multiple of 8)
+  for (int64_t rb = r0; rb < r1; rb += kChunk) {
+    bf16x8 xraw[kChunk], graw[kChunk];
 #pragma unroll
-    for (int i = 0; i < kMaxVec; ++i) {
-      const int c = threadIdx.x + i * kTh;
-      if (c < nvec) {
-        float xv[8], gv[8];
-        bf16x8_to_float(xr[c], xv);
-        bf16x8_to_float(gr[c], gv);
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          const int col = c * 8 + e;
-          const int pi = (col % hd) >> 1;
-          const float cs = cosT[tr + pi], sn = sinT[tr + pi];
-          // inverse rotation of the output gradient
-          const float da0 = gv[e] * cs + gv[e + 1] * sn;
-          const float da1 = -gv[e] * sn + gv[e + 1] * cs;
-          n[i][e] = xv[e] * rstd;
-          n[i][e + 1] = xv[e + 1] * rstd;
-          accw[i][e] += da0 * n[i][e];
-          accw[i][e + 1] += da1 * n[i][e + 1];
-          dn[i][e] = da0 * w[col];
-          dn[i][e + 1] = da1 * w[col + 1];
-          s2 += dn[i][e] * n[i][e] + dn[i][e + 1] * n[i][e + 1];
-        }
+    for (int k = 0; k < kChunk; ++k) {
+      if (rb + k < r1) {
+        xraw[k] = reinterpret_cast<const bf16x8*>(p.src + (rb + k) * p.ss + which * p.D)[c];
+        graw[k] = reinterpret_cast<const bf16x8*>(p.g[which] + (rb + k) * p.sg[which])[c];
       }
     }
-    const float mdnn = block_sum(s2, red) / D;
-    bf16x8* dxr = reinterpret_cast<bf16x8*>(dx + r * sdx + which * D);
 #pragma unroll
-    for (int i = 0; i < kMaxVec; ++i) {
-      const int c = threadIdx.x + i * kTh;
-      if (c < nvec) {
-        float o[8];
+    for (int k = 0; k < kChunk; ++k) {
+      const int64_t r = rb + k;
+      if (r >= r1) break;
+      const float rstd = p.rstd[which][r];
+      const float mdnn = stats[which * p.R + r];
+      const int64_t tr = (r % p.Lrope) * (p.hd >> 1) + pi0;
+      float xv[8], gv[8], o[8];
+      bf16x8_to_float(xraw[k], xv);
+      bf16x8_to_float(graw[k], gv);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = rstd * (dn[i][e] - n[i][e] * mdnn);
-        dxr[c] = float_to_bf16x8(o);
+      for (int e = 0; e < 8; e += 2) {
+        const float cs = p.cosT[tr + (e >> 1)], sn = p.sinT[tr + (e >> 1)];
+        const float da0 = gv[e] * cs + gv[e + 1] * sn;
+        const float da1 = -gv[e] * sn + gv[e + 1] * cs;
+        const float n0 = xv[e] * rstd, n1 = xv[e + 1] * rstd;
+        acc[e] = fmaf(da0, n0, acc[e]);
+        acc[e + 1] = fmaf(da1, n1, acc[e + 1]);
+        o[e] = rstd * (da0 * W[e] - n0 * mdnn);
+        o[e + 1] = rstd * (da1 * W[e + 1] - n1 * mdnn);
       }
+      reinterpret_cast<bf16x8*>(p.dx + r * p.sdx + which * p.D)[c] = float_to_bf16x8(o);
     }
   }
 #pragma unroll
-  for (int i = 0; i < kMaxVec; ++i) {
-    const int c = threadIdx.x + i * kTh;
-    if (c < nvec)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) atomicAdd(dw + c * 8 + e, accw[i][e]);
-  }
+  for (int e = 0; e < 8; ++e) atomicAdd(p.dw[which] + c * 8 + e, acc[e]);
 }
 
 // Standalone interleaved RoPE on [R, H, hd] rows (forward sign +1, backward -1).
@@ -636,6 +700,15 @@ void ln_mod_fwd(const at::Tensor& x, at::Tensor& y, c10::optional<at::Tensor> me
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Rows per block of the tiled backward kernels: about two blocks per SM (one wave) over row tiles x
+// column tiles, a multiple of their four-row load chunk.
+static int row_tile(int64_t R, int64_t ctiles, int device) {
+  static int sms = 0;
+  if (sms == 0) C10_CUDA_CHECK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+  const int64_t want = std::max<int64_t>(1, 2 * sms / ctiles);
+  return (int)std::max<int64_t>(4, ((R + want - 1) / want + 3) / 4 * 4);
+}
+
 void ln_mod_bwd(const at::Tensor& dy, const at::Tensor& x, c10::optional<at::Tensor> mean, const at::Tensor& rstd,
                 c10::optional<at::Tensor> a, double a_add, int64_t rows_per_group, c10::optional<at::Tensor> gidx,
                 bool rms, at::Tensor& dx, c10::optional<at::Tensor> dres, c10::optional<at::Tensor> da,
@@ -684,10 +757,18 @@ void ln_mod_bwd(const at::Tensor& dy, const at::Tensor& x, c10::optional<at::Ten
   p.R = R;
   p.D = (int)D;
   p.rms = rms;
-  p.rows_per_block = 32;
   if (R == 0) return;
-  const unsigned blocks = (unsigned)((R + p.rows_per_block - 1) / p.rows_per_block);
-  DMAD_ROW_DISPATCH(D / 8, [&] { ln_mod_bwd_kernel<VEC, TH><<<blocks, TH, 0, at::cuda::getCurrentCUDAStream()>>>(p, m); });
+  auto stream = at::cuda::getCurrentCUDAStream();
+  // two passes: row statistics, then dx and the column sums by row tiles
+  at::Tensor stats = at::empty({R, 2}, x.options().dtype(at::kFloat));
+  float2* sp = reinterpret_cast<float2*>(stats.data_ptr<float>());
+  ln_bwd_stats_kernel<<<(unsigned)((R + 7) / 8), 256, 0, stream>>>(p, m, sp);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const int64_t nvec = D / 8, ctiles = (nvec + 255) / 256;
+  p.rows_per_block = row_tile(R, ctiles, x.get_device());
+  const dim3 grid((unsigned)((R + p.rows_per_block - 1) / p.rows_per_block), (unsigned)ctiles);
+  const int th = (int)std::min<int64_t>(256, (nvec + 31) / 32 * 32);
+  ln_bwd_apply_kernel<4><<<grid, th, 0, stream>>>(p, m, sp);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -719,14 +800,14 @@ void gate_res_bwd(const at::Tensor& dout, const at::Tensor& y, at::Tensor& dy, c
   c10::cuda::CUDAGuard guard(y.device());
   ModSpec m = make_mod(gate, c10::nullopt, 0.0, rows_per_group, gidx, D);
   if (R == 0) return;
-  const int rpb = 32;
-  const unsigned blocks = (unsigned)((R + rpb - 1) / rpb);
-  DMAD_ROW_DISPATCH(D / 8, [&] {
-    gate_res_bwd_kernel<VEC, TH><<<blocks, TH, 0, at::cuda::getCurrentCUDAStream()>>>(
-        reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0),
-        reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), y.stride(0),
-        reinterpret_cast<__nv_bfloat16*>(dy.data_ptr()), dy.stride(0), dgate.data_ptr<float>(), m, R, (int)D, rpb);
-  });
+  const int64_t nvec = D / 8, ctiles = (nvec + 255) / 256;
+  const int rpb = row_tile(R, ctiles, y.get_device());
+  const dim3 grid((unsigned)((R + rpb - 1) / rpb), (unsigned)ctiles);
+  const int th = (int)std::min<int64_t>(256, (nvec + 31) / 32 * 32);
+  gate_res_bwd_kernel<4><<<grid, th, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0),
+      reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), y.stride(0),
+      reinterpret_cast<__nv_bfloat16*>(dy.data_ptr()), dy.stride(0), dgate.data_ptr<float>(), m, R, (int)D, rpb);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -760,17 +841,37 @@ void qk_norm_rope_bwd(const at::Tensor& gq, const at::Tensor& gk, const at::Tens
   const int64_t R = src.size(0);
   if (R == 0) return;
   c10::cuda::CUDAGuard guard(src.device());
-  const int rpb = 32;
-  dim3 grid((unsigned)((R + rpb - 1) / rpb), 2);
-  DMAD_ROW_DISPATCH(D / 8, [&] {
-    qk_norm_rope_bwd_kernel<VEC, TH><<<grid, TH, 0, at::cuda::getCurrentCUDAStream()>>>(
-        reinterpret_cast<const __nv_bfloat16*>(gq.data_ptr()), gq.stride(0),
-        reinterpret_cast<const __nv_bfloat16*>(gk.data_ptr()), gk.stride(0),
-        reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), src.stride(0),
-        reinterpret_cast<__nv_bfloat16*>(dx.data_ptr()), dx.stride(0), wq.data_ptr<float>(), wk.data_ptr<float>(),
-        cosT.data_ptr<float>(), sinT.data_ptr<float>(), rstd_q.data_ptr<float>(), rstd_k.data_ptr<float>(),
-        dwq.data_ptr<float>(), dwk.data_ptr<float>(), R, (int)D, (int)hd, (int)cosT.size(0), rpb);
-  });
+  TORCH_CHECK(hd % 8 == 0 && D % hd == 0, "head dim must be a multiple of 8 dividing D");
+  QkBwd p{};
+  p.g[0] = reinterpret_cast<const __nv_bfloat16*>(gq.data_ptr());
+  p.g[1] = reinterpret_cast<const __nv_bfloat16*>(gk.data_ptr());
+  p.sg[0] = gq.stride(0);
+  p.sg[1] = gk.stride(0);
+  p.src = reinterpret_cast<const __nv_bfloat16*>(src.data_ptr());
+  p.ss = src.stride(0);
+  p.dx = reinterpret_cast<__nv_bfloat16*>(dx.data_ptr());
+  p.sdx = dx.stride(0);
+  p.w[0] = wq.data_ptr<float>();
+  p.w[1] = wk.data_ptr<float>();
+  p.cosT = cosT.data_ptr<float>();
+  p.sinT = sinT.data_ptr<float>();
+  p.rstd[0] = rstd_q.data_ptr<float>();
+  p.rstd[1] = rstd_k.data_ptr<float>();
+  p.dw[0] = dwq.data_ptr<float>();
+  p.dw[1] = dwk.data_ptr<float>();
+  p.R = R;
+  p.D = (int)D;
+  p.hd = (int)hd;
+  p.Lrope = (int)cosT.size(0);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  at::Tensor stats = at::empty({2, R}, src.options().dtype(at::kFloat));
+  qk_bwd_stats_kernel<<<dim3((unsigned)((R + 7) / 8), 2), 256, 0, stream>>>(p, stats.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const int64_t nvec = D / 8, ctiles = (nvec + 255) / 256;
+  p.rows_per_block = row_tile(R, 2 * ctiles, src.get_device());
+  const dim3 grid((unsigned)((R + p.rows_per_block - 1) / p.rows_per_block), (unsigned)ctiles, 2);
+  const int th = (int)std::min<int64_t>(256, (nvec + 31) / 32 * 32);
+  qk_bwd_apply_kernel<4><<<grid, th, 0, stream>>>(p, stats.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

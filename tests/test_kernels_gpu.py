@@ -174,6 +174,50 @@ def test_ln_mod(D, R, G, rms):
     assert ((c.grad - cr.grad).norm() / cr.grad.norm()).item() < 1e-2
 
 
+@pytest.mark.parametrize("D,R,G", [(1536, 999, 3), (5120, 130, 2), (128, 77, 5)])
+@pytest.mark.parametrize("rms", [False, True])
+def test_ln_mod_bwd_fusions_and_row_groups(D, R, G, rms):
+    """The backward kernels with an explicit per-row group index (groups interleaved, so the column sums
+    change group many times inside a row tile), the residual-gradient addend and the gated-residual
+    fusion, against fp32 PyTorch."""
+    from dmad_b200 import ops
+    e = ops.ext()
+    torch.manual_seed(7)
+    x = torch.randn(R, D, device=dev, dtype=torch.bfloat16)
+    dy = torch.randn(R, D, device=dev, dtype=torch.bfloat16)
+    dres = torch.randn(R, D, device=dev, dtype=torch.bfloat16)
+    yg = torch.randn(R, D, device=dev, dtype=torch.bfloat16)
+    a = 0.1 * torch.randn(G, D, device=dev)
+    gate = torch.randn(G, D, device=dev)
+    gidx = (torch.arange(R, device=dev) * 7 // 5 % G).int()
+    xf = x.float()
+    mean = None if rms else xf.mean(1)
+    var = (xf * xf).mean(1) if rms else xf.var(1, unbiased=False)
+    rstd = torch.rsqrt(var + 1e-6)
+    dx = torch.empty_like(x)
+    dyg = torch.empty_like(x)
+    da = torch.zeros(G, D, device=dev)
+    dc = torch.zeros(G, D, device=dev)
+    dgate = torch.zeros(G, D, device=dev)
+    e.ln_mod_bwd(dy, x, mean, rstd, a, 1.0, R, gidx, rms, dx, dres, da, dc, gate, yg, dyg, dgate)
+    torch.cuda.synchronize()
+    ops.check_device_status()
+    g = gidx.long()
+    n = (xf - (0.0 if rms else mean[:, None])) * rstd[:, None]
+    A = 1.0 + a[g]
+    dn = dy.float() * A
+    mdn = 0.0 if rms else dn.mean(1, keepdim=True)
+    ref_dx = rstd[:, None] * (dn - mdn - n * (dn * n).mean(1, keepdim=True)) + dres.float()
+    ref_da = torch.zeros(G, D, device=dev).index_add_(0, g, dy.float() * n)
+    ref_dc = torch.zeros(G, D, device=dev).index_add_(0, g, dy.float())
+    ref_dyg = ref_dx * gate[g]
+    ref_dgate = torch.zeros(G, D, device=dev).index_add_(0, g, ref_dx * yg.float())
+    for got, ref, name in ((dx, ref_dx, "dx"), (dyg, ref_dyg, "dyg"), (da, ref_da, "da"), (dc, ref_dc, "dc"),
+                           (dgate, ref_dgate, "dgate")):
+        rel = (got.float() - ref).norm() / ref.norm()
+        assert rel < 1e-2, (name, rel.item())
+
+
 def test_gate_residual():
     from dmad_b200.ops import gate_residual
     R, D, G = 600, 1536, 3
