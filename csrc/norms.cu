@@ -491,6 +491,7 @@ struct QkBwd {
   float* dw[2];
   int64_t R;
   int D, hd, Lrope, rows_per_block;
+  bool hd_pow2;
 };
 
 // Pass 1, one warp per row and per q / k (blockIdx.y): mean(dn * n) of dn = rot^-1(g) * w, n = x * rstd.
@@ -500,7 +501,8 @@ __global__ void __launch_bounds__(256, 2) qk_bwd_stats_kernel(QkBwd p, float* __
   if (r >= p.R) return;
   const int nvec = p.D >> 3;
   const float rstd = p.rstd[which][r];
-  const int64_t tr = (r % p.Lrope) * (p.hd >> 1);
+  const float* cr = p.cosT + (int64_t)((int)r % p.Lrope) * (p.hd >> 1);
+  const float* sr = p.sinT + (cr - p.cosT);
   const bf16x8* xr = reinterpret_cast<const bf16x8*>(p.src + r * p.ss + which * p.D);
   const bf16x8* gr = reinterpret_cast<const bf16x8*>(p.g[which] + r * p.sg[which]);
   const float* w = p.w[which];
@@ -510,15 +512,18 @@ __global__ void __launch_bounds__(256, 2) qk_bwd_stats_kernel(QkBwd p, float* __
     float xv[8], gv[8];
     bf16x8_to_float(xr[c], xv);
     bf16x8_to_float(gr[c], gv);
+    // the vector's four rotation angles: table entries [pi, pi + 4) of the row (hd a multiple of 8)
+    const int pi = (p.hd_pow2 ? ((c * 8) & (p.hd - 1)) : ((c * 8) % p.hd)) >> 1;
+    const float4 cs4 = *reinterpret_cast<const float4*>(cr + pi), sn4 = *reinterpret_cast<const float4*>(sr + pi);
+    const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + c * 8)), w1 = __ldg(reinterpret_cast<const float4*>(w + c * 8 + 4));
+    const float cs[4] = {cs4.x, cs4.y, cs4.z, cs4.w}, sn[4] = {sn4.x, sn4.y, sn4.z, sn4.w};
+    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
     for (int e = 0; e < 8; e += 2) {
-      const int col = c * 8 + e;
-      const int pi = (col % p.hd) >> 1;
-      const float cs = p.cosT[tr + pi], sn = p.sinT[tr + pi];
-      const float da0 = gv[e] * cs + gv[e + 1] * sn;  // inverse rotation of the output gradient
-      const float da1 = -gv[e] * sn + gv[e + 1] * cs;
-      s2 = fmaf(da0 * w[col], xv[e] * rstd, s2);
-      s2 = fmaf(da1 * w[col + 1], xv[e + 1] * rstd, s2);
+      const float da0 = gv[e] * cs[e >> 1] + gv[e + 1] * sn[e >> 1];  // inverse rotation of the output gradient
+      const float da1 = -gv[e] * sn[e >> 1] + gv[e + 1] * cs[e >> 1];
+      s2 = fmaf(da0 * wv[e], xv[e] * rstd, s2);
+      s2 = fmaf(da1 * wv[e + 1], xv[e + 1] * rstd, s2);
     }
   }
   s2 = warp_sum(s2);
@@ -542,6 +547,7 @@ __global__ void __launch_bounds__(256) qk_bwd_apply_kernel(QkBwd p, const float*
     acc[e] = 0.f;
   }
   const int pi0 = ((c * 8) % p.hd) >> 1;  // a vector never straddles a head (hd is a multiple of 8)
+  int rot = (int)(r0 % p.Lrope);           // rotation-table row of the current row, advanced row by row
   for (int64_t rb = r0; rb < r1; rb += kChunk) {
     bf16x8 xraw[kChunk], graw[kChunk];
 #pragma unroll
@@ -557,13 +563,17 @@ __global__ void __launch_bounds__(256) qk_bwd_apply_kernel(QkBwd p, const float*
       if (r >= r1) break;
       const float rstd = p.rstd[which][r];
       const float mdnn = stats[which * p.R + r];
-      const int64_t tr = (r % p.Lrope) * (p.hd >> 1) + pi0;
+      const int64_t tr = (int64_t)rot * (p.hd >> 1) + pi0;
+      if (++rot == p.Lrope) rot = 0;
+      const float4 cs4 = *reinterpret_cast<const float4*>(p.cosT + tr);
+      const float4 sn4 = *reinterpret_cast<const float4*>(p.sinT + tr);
+      const float csv[4] = {cs4.x, cs4.y, cs4.z, cs4.w}, snv[4] = {sn4.x, sn4.y, sn4.z, sn4.w};
       float xv[8], gv[8], o[8];
       bf16x8_to_float(xraw[k], xv);
       bf16x8_to_float(graw[k], gv);
 #pragma unroll
       for (int e = 0; e < 8; e += 2) {
-        const float cs = p.cosT[tr + (e >> 1)], sn = p.sinT[tr + (e >> 1)];
+        const float cs = csv[e >> 1], sn = snv[e >> 1];
         const float da0 = gv[e] * cs + gv[e + 1] * sn;
         const float da1 = -gv[e] * sn + gv[e + 1] * cs;
         const float n0 = xv[e] * rstd, n1 = xv[e + 1] * rstd;
@@ -862,7 +872,15 @@ void qk_norm_rope_bwd(const at::Tensor& gq, const at::Tensor& gk, const at::Tens
   p.R = R;
   p.D = (int)D;
   p.hd = (int)hd;
+  p.hd_pow2 = (hd & (hd - 1)) == 0;
   p.Lrope = (int)cosT.size(0);
+  TORCH_CHECK(cosT.is_contiguous() && sinT.is_contiguous() && cosT.size(1) == hd / 2 &&
+                  (reinterpret_cast<uintptr_t>(cosT.data_ptr()) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(sinT.data_ptr()) & 15) == 0,
+              "rotation tables must be contiguous 16-byte aligned fp32 [L, hd / 2]");
+  TORCH_CHECK(wq.is_contiguous() && wk.is_contiguous() && (reinterpret_cast<uintptr_t>(wq.data_ptr()) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(wk.data_ptr()) & 15) == 0,
+              "norm weights must be contiguous and 16-byte aligned");
   auto stream = at::cuda::getCurrentCUDAStream();
   at::Tensor stats = at::empty({2, R}, src.options().dtype(at::kFloat));
   qk_bwd_stats_kernel<<<dim3((unsigned)((R + 7) / 8), 2), 256, 0, stream>>>(p, stats.data_ptr<float>());
