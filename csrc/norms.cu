@@ -475,6 +475,67 @@ qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ src, int64_t ss, __nv_
   if (threadIdx.x == 0) (which == 0 ? rstd_q : rstd_k)[r] = rstd;
 }
 
+// Forward for rows of up to 2048 columns: one warp per row and per q / k (blockIdx.y), every lane holding
+// kV 8-column vectors (all loads issued up front), a shuffle reduction for the RMS, the rotation angles
+// and norm weights read as vectors.  Needs contiguous 16-byte aligned tables [L, hd / 2] and weights.
+template <int kV>
+__global__ void __launch_bounds__(256, 2)
+qk_norm_rope_fwd_warp_kernel(const __nv_bfloat16* __restrict__ src, int64_t ss, __nv_bfloat16* __restrict__ dst,
+                             int64_t sd, const float* __restrict__ wq, const float* __restrict__ wk,
+                             const float* __restrict__ cosT, const float* __restrict__ sinT, float* __restrict__ rstd_q,
+                             float* __restrict__ rstd_k, int64_t R, int D, int hd, int Lrope, float eps, bool hd_pow2) {
+  const int lane = threadIdx.x & 31;
+  const int which = blockIdx.y;
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= R) return;
+  const int nvec = D >> 3;
+  const bf16x8* xr = reinterpret_cast<const bf16x8*>(src + r * ss + which * D);
+  const float* w = which == 0 ? wq : wk;
+  float v[kV][8];
+  {
+    bf16x8 raw[kV];
+#pragma unroll
+    for (int i = 0; i < kV; ++i)
+      if (lane + 32 * i < nvec) raw[i] = xr[lane + 32 * i];
+#pragma unroll
+    for (int i = 0; i < kV; ++i)
+      if (lane + 32 * i < nvec) bf16x8_to_float(raw[i], v[i]);
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kV; ++i)
+    if (lane + 32 * i < nvec) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s = fmaf(v[i][e], v[i][e], s);
+    }
+  const float rstd = rsqrtf(warp_sum(s) / D + eps);
+  const float* cr = cosT + (int64_t)((int)r % Lrope) * (hd >> 1);
+  const float* sr = sinT + (cr - cosT);
+  bf16x8* yr = reinterpret_cast<bf16x8*>(dst + r * sd + which * D);
+#pragma unroll
+  for (int i = 0; i < kV; ++i) {
+    const int c = lane + 32 * i;
+    if (c < nvec) {
+      const int pi = (hd_pow2 ? ((c * 8) & (hd - 1)) : ((c * 8) % hd)) >> 1;
+      const float4 cs4 = *reinterpret_cast<const float4*>(cr + pi), sn4 = *reinterpret_cast<const float4*>(sr + pi);
+      const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + c * 8));
+      const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + c * 8 + 4));
+      const float cs[4] = {cs4.x, cs4.y, cs4.z, cs4.w}, sn[4] = {sn4.x, sn4.y, sn4.z, sn4.w};
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        const float a0 = v[i][e] * rstd * wv[e];
+        const float a1 = v[i][e + 1] * rstd * wv[e + 1];
+        o[e] = a0 * cs[e >> 1] - a1 * sn[e >> 1];
+        o[e + 1] = a1 * cs[e >> 1] + a0 * sn[e >> 1];
+      }
+      yr[c] = float_to_bf16x8(o);
+    }
+  }
+  if (lane == 0) (which == 0 ? rstd_q : rstd_k)[r] = rstd;
+}
+
 // Backward: g (grad of the rotated output, q at col 0 / k at col D, row stride sg)
 // -> dx (grad of the pre-norm input, row stride sdx); dw accumulates (fp32 [D]).
 struct QkBwd {
@@ -832,6 +893,32 @@ void qk_norm_rope_fwd(const at::Tensor& src, at::Tensor& dst, const at::Tensor& 
   const int64_t R = src.size(0);
   if (R == 0) return;
   c10::cuda::CUDAGuard guard(src.device());
+  const bool vec_ok = D <= 2048 && hd % 8 == 0 && D % hd == 0 && cosT.is_contiguous() && sinT.is_contiguous() &&
+                      cosT.size(1) == hd / 2 && (reinterpret_cast<uintptr_t>(cosT.data_ptr()) & 15) == 0 &&
+                      (reinterpret_cast<uintptr_t>(sinT.data_ptr()) & 15) == 0 && wq.is_contiguous() &&
+                      wk.is_contiguous() && (reinterpret_cast<uintptr_t>(wq.data_ptr()) & 15) == 0 &&
+                      (reinterpret_cast<uintptr_t>(wk.data_ptr()) & 15) == 0;
+  if (vec_ok) {
+    const int nvec = (int)(D / 8);
+    const dim3 wgrid((unsigned)((R + 7) / 8), 2);
+    auto launch = [&](auto kv) {
+      qk_norm_rope_fwd_warp_kernel<decltype(kv)::value><<<wgrid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+          reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), src.stride(0),
+          reinterpret_cast<__nv_bfloat16*>(dst.data_ptr()), dst.stride(0), wq.data_ptr<float>(), wk.data_ptr<float>(),
+          cosT.data_ptr<float>(), sinT.data_ptr<float>(), rstd_q.data_ptr<float>(), rstd_k.data_ptr<float>(), R,
+          (int)D, (int)hd, (int)cosT.size(0), (float)eps, (hd & (hd - 1)) == 0);
+    };
+    if (nvec <= 64)
+      launch(std::integral_constant<int, 2>{});
+    else if (nvec <= 128)
+      launch(std::integral_constant<int, 4>{});
+    else if (nvec <= 192)
+      launch(std::integral_constant<int, 6>{});
+    else
+      launch(std::integral_constant<int, 8>{});
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   dim3 grid((unsigned)R, 2);
   DMAD_ROW_DISPATCH(D / 8, [&] {
     qk_norm_rope_fwd_kernel<VEC, TH><<<grid, TH, 0, at::cuda::getCurrentCUDAStream()>>>(

@@ -49,6 +49,36 @@ __global__ void sn_wtu_kernel(const __nv_bfloat16* __restrict__ w, int64_t ldw, 
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0.f;
   int s = seg_of(m, r0);
+  if (r1 <= m.off[s + 1]) {  // the whole chunk in one segment (the usual case): four rows of loads at a time
+    if (!m.on[s]) return;
+    int r = r0;
+    for (; r + 4 <= r1; r += 4) {
+      bf16x8 raw[4];
+      float ur[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        raw[k] = reinterpret_cast<const bf16x8*>(w + (int64_t)(r + k) * ldw)[c8];
+        ur[k] = u[r + k];
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float wv[8];
+        bf16x8_to_float(raw[k], wv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = fmaf(wv[e], ur[k], acc[e]);
+      }
+    }
+    for (; r < r1; ++r) {
+      float wv[8];
+      bf16x8_to_float(reinterpret_cast<const bf16x8*>(w + (int64_t)r * ldw)[c8], wv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = fmaf(wv[e], u[r], acc[e]);
+    }
+    float* dst = t + (int64_t)s * I + c8 * 8;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) atomicAdd(dst + e, acc[e]);
+    return;
+  }
   auto flush = [&](int seg) {
     if (!m.on[seg]) return;
     float* dst = t + (int64_t)seg * I + c8 * 8;
@@ -287,7 +317,7 @@ at::Tensor sn_weight_fwd(const at::Tensor& w, at::Tensor& u, at::Tensor& v, cons
   const __nv_bfloat16* wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
   if (train) {
     at::Tensor t = at::zeros({m.n, I}, f32);
-    const int threads = 128, rows = 32;
+    const int threads = 64, rows = 32;  // 8-column vectors per block x rows per chunk
     dim3 grid((unsigned)((I / 8 + threads - 1) / threads), (unsigned)((O + rows - 1) / rows));
     sn_wtu_kernel<<<grid, threads, 0, stream>>>(wp, w.stride(0), (int)O, (int)I, u.data_ptr<float>(),
                                                 t.data_ptr<float>(), m, rows);
