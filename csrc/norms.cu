@@ -790,6 +790,12 @@ void ln_mod_bwd(const at::Tensor& dy, const at::Tensor& x, c10::optional<at::Ten
   check_rows(x, "x", D);
   check_rows(dx, "dx", D);
   c10::cuda::CUDAGuard guard(x.device());
+  // the statistics pass reads the modulation rows as float4: an unaligned view is copied first
+  if (a.has_value() && a->defined() && a->dim() == 2 && a->size(0) > 1 &&
+      ((reinterpret_cast<uintptr_t>(a->data_ptr()) & 15) != 0 || a->stride(0) % 4 != 0))
+    a = a->contiguous().clone(at::MemoryFormat::Contiguous);
+  else if (a.has_value() && a->defined() && (reinterpret_cast<uintptr_t>(a->data_ptr()) & 15) != 0)
+    a = a->clone(at::MemoryFormat::Contiguous);
   ModSpec m = make_mod(a, c10::nullopt, a_add, rows_per_group, gidx, D);
   LnBwdArgs p{};
   p.dy = reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr());
