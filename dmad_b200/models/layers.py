@@ -167,7 +167,8 @@ class SegLinear(nn.Module):
     def effective_weight(self):
         if not self.sn_enabled:
             return self.weight
-        if self.weight.is_cuda and self.weight.dtype == torch.bfloat16 and self.in_features % 8 == 0:
+        if (self.weight.is_cuda and self.weight.dtype == torch.bfloat16 and self.in_features % 8 == 0
+                and len(self.segments) <= 8):
             return self._sn_weight_fused()  # fused kernels: power iteration, scaled weight and its gradient
         return (self.weight.float() * self._sn_row_scale()[:, None]).to(self.weight.dtype)
 
