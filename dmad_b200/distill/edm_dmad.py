@@ -259,6 +259,29 @@ class EDMDMAD:
         self.step_count = 0
         self.eye = torch.eye(cfg.label_dim, device=self.device)
 
+    def ema_files(self) -> dict:
+        """{file name: EMA generator} in the reference's checkpoint naming (train_edm.py:106-124): the
+        first of ``ema_kimg`` is the primary ``pytorch_model_ema.bin``, every other one
+        ``pytorch_model_ema_<int(kimg)>.bin``."""
+        out = {}
+        for i, (kimg, ema) in enumerate(self.emas.items()):
+            out["pytorch_model_ema.bin" if i == 0 else f"pytorch_model_ema_{int(kimg)}.bin"] = ema
+        return out
+
+    def export_emas(self, out_dir: str):
+        """Writes the generator EMAs of a checkpoint as plain EDMPrecond state dicts (spectral norm, if
+        any, folded into the weights), loadable by the reference's networks and by ``tools.edm_eval_folder``."""
+        import os
+
+        from ..algorithms.spectral import fold_spectral_norm
+
+        os.makedirs(out_dir, exist_ok=True)
+        for name, ema in self.ema_files().items():
+            net = copy.deepcopy(ema).cpu().eval()
+            with torch.no_grad():
+                fold_spectral_norm(net)
+            torch.save(net.state_dict(), os.path.join(out_dir, name))
+
     def synthetic_batch(self, gen: torch.Generator | None = None):
         """Config-1 inputs: images U[-1, 1], labels U{0..999}; teacher samples drawn the same way."""
         c, B, r = self.cfg, self.cfg.batch_size, self.cfg.resolution

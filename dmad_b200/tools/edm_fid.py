@@ -90,14 +90,11 @@ def load_detector(path: str, device, trust_pickle: bool = False):
 
 
 @torch.no_grad()
-def inception_stats(source: ImageSource, detector, indices=None, batch: int = 64, device="cpu"):
-    """(mu, sigma) in float64 of the detector's features over the selected images."""
-    idx = np.arange(len(source)) if indices is None else np.asarray(indices)
-    if len(idx) < 2:
-        raise ValueError(f"need at least 2 images to compute statistics, found {len(idx)}")
+def batch_stats(batches, detector, device="cpu"):
+    """(mu, sigma) in float64 of the detector's features over uint8 NCHW image batches."""
     mu = sigma = None
-    for s in range(0, len(idx), batch):
-        imgs = torch.from_numpy(np.stack([source.load(int(i)) for i in idx[s:s + batch]]))
+    n = 0
+    for imgs in batches:
         if imgs.shape[1] == 1:
             imgs = imgs.repeat(1, 3, 1, 1)
         try:
@@ -110,11 +107,23 @@ def inception_stats(source: ImageSource, detector, indices=None, batch: int = 64
             sigma = torch.zeros(f.shape[1], f.shape[1], dtype=torch.float64, device=f.device)
         mu += f.sum(0)
         sigma += f.T @ f
-    n = len(idx)
+        n += f.shape[0]
+    if n < 2:
+        raise ValueError(f"need at least 2 images to compute statistics, found {n}")
     mu /= n
     sigma -= torch.outer(mu, mu) * n
     sigma /= n - 1
     return mu.cpu().numpy(), sigma.cpu().numpy()
+
+
+def inception_stats(source: ImageSource, detector, indices=None, batch: int = 64, device="cpu"):
+    """(mu, sigma) in float64 of the detector's features over the selected images."""
+    idx = np.arange(len(source)) if indices is None else np.asarray(indices)
+    if len(idx) < 2:
+        raise ValueError(f"need at least 2 images to compute statistics, found {len(idx)}")
+    batches = (torch.from_numpy(np.stack([source.load(int(i)) for i in idx[s:s + batch]]))
+               for s in range(0, len(idx), batch))
+    return batch_stats(batches, detector, device)
 
 
 def main(argv=None):

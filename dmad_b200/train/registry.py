@@ -98,14 +98,17 @@ class _IterationAdapter:
         return shared, (per_rank or None)
 
     def export_artifacts(self, ckpt_dir: str):
-        """Extra files of a published checkpoint (rank 0), e.g. the H3 LoRA exports."""
-        fn = getattr(self.model, "export_loras", None)
+        """Extra files of a published checkpoint (rank 0): the H3 LoRA exports, the EDM generator EMAs."""
+        fn = getattr(self.model, "export_loras", None) or getattr(self.model, "export_emas", None)
         if fn is not None:
             fn(ckpt_dir)
 
     def load_state_dicts(self, shared, per_rank):
         for k, m in self.modules.items():
-            m.load_state_dict(shared[f"module/{k}"])
+            key = f"module/{k}"
+            if key not in shared and k.startswith("ema_") and "module/generator" in shared:
+                key = "module/generator"  # a checkpoint written before the EMAs were saved: restart them
+            m.load_state_dict(shared[key])
         for k, o in self.optims.items():
             if self._per_rank(o):
                 if not per_rank or f"optim/{k}" not in per_rank:
@@ -158,8 +161,9 @@ def _build_edm(cfg: dict, device, seed: int):
 
     def step(batch, it):
         return model.train_step(batch if batch is not None else model.synthetic_batch(gen))
-    return _IterationAdapter(model, step, {"generator": model.generator, "critic": model.critic},
-                             {"generator": model.opt_g, "critic": model.opt_c})
+    modules = {"generator": model.generator, "critic": model.critic}
+    modules.update({f"ema_{kimg:g}": ema for kimg, ema in model.emas.items()})  # saved, so a resume keeps them
+    return _IterationAdapter(model, step, modules, {"generator": model.opt_g, "critic": model.opt_c})
 
 
 @register_model("sdxl_dmad")
