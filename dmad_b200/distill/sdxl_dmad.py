@@ -61,6 +61,13 @@ class SDXLDMADConfig:
     gradient_checkpointing: bool = True
     unet_kwargs: dict | None = None
     batch_size: int = 4  # per GPU (config 4)
+    # the reference trainer's optimiser settings (train_sd.py:130-137, :246, :249-257): AdamW weight decay,
+    # gradient clipping of both nets, and a generator EMA with a half-life of ema_kimg thousand images
+    # (ramped up to ema_rampup x the images seen), exported as pytorch_model_ema.bin
+    weight_decay: float = 0.01
+    max_grad_norm: float = 10.0
+    ema_kimg: float = 1000.0
+    ema_rampup: float = 0.05
     # data-parallel optimiser: "sharded" = fp32 state sharded over the ranks, one fused reduce-scatter /
     # AdamW / all-gather kernel per step; "nccl" = NCCL all-reduce of the gradients, then torch's AdamW
     # on every rank (the library path, as the reference's accelerate DDP + AdamW)
@@ -103,18 +110,25 @@ class SDXLDMAD:
         from ..parallel.dist import broadcast_module
         for m in (self.generator, self.critic, self.head_real, self.head_teacher):
             broadcast_module(m)
+        self.gen_params, self.critic_params_all = gp, cp
+        self.gen_ema = None  # fp32 EMA of the generator (the nccl path; the sharded optimiser holds its own)
         if cfg.dp_optimizer == "sharded":
             from ..parallel.zero import ShardedAdamW
-            self.opt_g = ShardedAdamW(gp, lr=cfg.generator_lr, betas=cfg.betas)
-            self.opt_c = ShardedAdamW(cp, lr=cfg.guidance_lr, betas=cfg.betas)
+            self.opt_g = ShardedAdamW(gp, lr=cfg.generator_lr, betas=cfg.betas, weight_decay=cfg.weight_decay,
+                                      ema=True)
+            self.opt_c = ShardedAdamW(cp, lr=cfg.guidance_lr, betas=cfg.betas, weight_decay=cfg.weight_decay)
             self.sync_g = self.sync_c = None
         elif cfg.dp_optimizer == "nccl":
             from ..parallel.dp import GradSync
-            self.opt_g = torch.optim.AdamW(gp, lr=cfg.generator_lr, betas=cfg.betas, foreach=True)
-            self.opt_c = torch.optim.AdamW(cp, lr=cfg.guidance_lr, betas=cfg.betas, foreach=True)
+            self.opt_g = torch.optim.AdamW(gp, lr=cfg.generator_lr, betas=cfg.betas, weight_decay=cfg.weight_decay,
+                                           foreach=True)
+            self.opt_c = torch.optim.AdamW(cp, lr=cfg.guidance_lr, betas=cfg.betas, weight_decay=cfg.weight_decay,
+                                           foreach=True)
             self.sync_g, self.sync_c = GradSync(gp), GradSync(cp)
+            self.gen_ema = [p.detach().float().clone() for p in gp]
         else:
             raise ValueError(f"unknown dp_optimizer {cfg.dp_optimizer!r}")
+        self.step_count = 0
         self.time_ids = torch.tensor([[cfg.resolution, cfg.resolution, 0, 0, cfg.resolution, cfg.resolution]],
                                      device=self.device, dtype=torch.float32)
 
@@ -209,9 +223,15 @@ class SDXLDMAD:
         tl = (-dt).mean() if w is None else (-dt * w).sum() / w.sum().clamp(min=1.0) + (-dt).sum() * 0.0
         loss_g = cfg.teacher_loss_weight * tl + cfg.real_loss_weight * (-dr).mean()
         loss_g.backward()
+        decay = self.ema_decay(B)
         if self.sync_g is not None:
             self.sync_g.sync()
-        self.opt_g.step()
+            torch.nn.utils.clip_grad_norm_(self.gen_params, cfg.max_grad_norm)
+            self.opt_g.step()
+            with torch.no_grad():
+                torch._foreach_lerp_(self.gen_ema, [p.detach().float() for p in self.gen_params], 1.0 - decay)
+        else:
+            self.opt_g.step(ema_beta=decay, max_grad_norm=cfg.max_grad_norm)
         self.opt_g.zero_grad(set_to_none=True)
         for p in self._critic_params():
             p.requires_grad_(True)
@@ -224,6 +244,53 @@ class SDXLDMAD:
         loss_c.backward()
         if self.sync_c is not None:
             self.sync_c.sync()
-        self.opt_c.step()
+            torch.nn.utils.clip_grad_norm_(self.critic_params_all, cfg.max_grad_norm)
+            self.opt_c.step()
+        else:
+            self.opt_c.step(max_grad_norm=cfg.max_grad_norm)
         self.opt_c.zero_grad(set_to_none=True)
+        self.step_count += 1
         return {"generator_loss": loss_g.detach(), "critic_loss": loss_c.detach()}
+
+    # ------------------------------------------------------------------ generator EMA
+    def ema_decay(self, batch: int) -> float:
+        """Per-step EMA decay: half-life ema_kimg thousand images, at most ema_rampup x the images seen."""
+        from ..parallel.dist import get_world_size
+        total = batch * get_world_size()
+        done = getattr(self.opt_g, "step_count", self.step_count)  # the sharded optimiser checkpoints its count
+        nimg = (done + 1) * total
+        half = self.cfg.ema_kimg * 1000
+        if self.cfg.ema_rampup > 0:
+            half = min(half, nimg * self.cfg.ema_rampup)
+        return 0.5 ** (total / max(half, 1e-8))
+
+    def ema_params(self) -> list:
+        """The generator EMA, one full tensor per trainable generator parameter."""
+        return self.opt_g.full_ema() if self.gen_ema is None else self.gen_ema
+
+    def ema_state_dict(self) -> dict:
+        """The generator's state dict with the EMA in place of its trainable weights."""
+        sd = {k: v.detach().clone() for k, v in self.generator.state_dict().items()}
+        names = {id(p): n for n, p in self.generator.named_parameters()}
+        for p, e in zip(self.gen_params, self.ema_params()):
+            sd[names[id(p)]] = e.detach().to("cpu", torch.float32).reshape(p.shape).clone()
+        return sd
+
+    def export_emas(self, out_dir: str):
+        """``pytorch_model_ema.bin`` of a checkpoint, as the reference's trainer writes it (train_sd.py:209)."""
+        import os
+
+        os.makedirs(out_dir, exist_ok=True)
+        torch.save({k: v.cpu() for k, v in self.ema_state_dict().items()}, os.path.join(out_dir, "pytorch_model_ema.bin"))
+
+    def ema_state(self):
+        """Checkpoint state of the EMA kept outside the optimiser (the nccl path)."""
+        return None if self.gen_ema is None else {"gen_ema": [e.cpu() for e in self.gen_ema],
+                                                  "step_count": self.step_count}
+
+    def load_ema_state(self, st):
+        if st is not None and self.gen_ema is not None:
+            for d, v in zip(self.gen_ema, st["gen_ema"]):
+                d.copy_(v.to(d.device))
+        if st is not None:
+            self.step_count = int(st.get("step_count", self.step_count))

@@ -95,6 +95,9 @@ class _IterationAdapter:
         extra = getattr(self.model, "critic_state", None)
         if extra is not None:
             shared["critic_state"] = extra()
+        ema = getattr(self.model, "ema_state", None)
+        if ema is not None and ema() is not None:
+            shared["ema_state"] = ema()
         return shared, (per_rank or None)
 
     def export_artifacts(self, ckpt_dir: str):
@@ -118,6 +121,8 @@ class _IterationAdapter:
                 o.load_state_dict(shared[f"optim/{k}"])
         if "critic_state" in shared and hasattr(self.model, "load_critic_state"):
             self.model.load_critic_state(shared["critic_state"])
+        if "ema_state" in shared and hasattr(self.model, "load_ema_state"):
+            self.model.load_ema_state(shared["ema_state"])
 
 
 def _dtype(device):

@@ -89,3 +89,39 @@ def test_frozen_gain_spectral_norm_properties():
     net.train()
     net[0](x).sum().backward()
     assert net[0].weight.grad is not None and torch.isfinite(net[0].weight.grad).all()
+
+
+def test_sdxl_generator_ema_weight_decay_and_clip():
+    """The SDXL trainer's optimiser settings of the reference (AdamW weight decay, clipping at
+    max_grad_norm) and its generator EMA: the exported EMA follows the half-life recursion of the weights
+    after every step, on both data-parallel optimiser paths."""
+    import copy
+    import os
+    import tempfile
+
+    from dmad_b200.distill.sdxl_dmad import SDXLDMAD, SDXLDMADConfig
+    for dp in ("sharded", "nccl"):
+        cfg = SDXLDMADConfig(latent=32, sn_iters=3, dp_optimizer=dp, generator_lr=1e-3, ema_kimg=0.001,
+                             max_grad_norm=1.0,
+                             unet_kwargs=dict(channels=(32, 64, 64), depths=(0, 1, 1), ctx_dim=32, pooled_dim=16,
+                                              addition_time_embed_dim=8))
+        d = SDXLDMAD(cfg, device="cpu", dtype=torch.float32)
+        ema = [p.detach().clone() for p in d.gen_params]
+        B = 2
+        g = torch.Generator().manual_seed(1)
+        for _ in range(3):
+            b = {"noise": torch.randn(B, 4, 32, 32, generator=g), "real": torch.randn(B, 4, 32, 32, generator=g),
+                 "teacher": torch.randn(B, 4, 32, 32, generator=g), "ctx": torch.randn(B, 7, 32, generator=g),
+                 "pooled": torch.randn(B, 16, generator=g)}
+            decay = d.ema_decay(B)
+            d.train_step(b)
+            ema = [e * decay + p.detach() * (1 - decay) for e, p in zip(ema, d.gen_params)]
+        for a, b_ in zip(d.ema_params(), ema):
+            torch.testing.assert_close(a.reshape(b_.shape).float(), b_, rtol=1e-4, atol=1e-6)
+        assert any(not torch.equal(a.reshape(p.shape), p.detach()) for a, p in zip(d.ema_params(), d.gen_params))
+        with tempfile.TemporaryDirectory() as tmp:
+            d.export_emas(tmp)
+            sd = torch.load(os.path.join(tmp, "pytorch_model_ema.bin"))
+        assert sd.keys() == d.generator.state_dict().keys()
+        net = copy.deepcopy(d.generator)
+        net.load_state_dict(sd)
