@@ -49,14 +49,21 @@ class SDXLDMADConfig:
     denoising_timestep: int = 1000
     critic_max_timestep: int = 1000
     teacher_gap_route: bool = True
-    gap_tau: float = 2.0
+    gap_tau: float = 0.5
     critic_spectral_norm: bool = True
     sn_iters: int = 200
     generator_lr: float = 5e-7
     guidance_lr: float = 5e-7
-    betas: tuple = (0.0, 0.999)
-    teacher_loss_weight: float = 1.0
-    real_loss_weight: float = 1.0
+    # defaults of the reference's SDXL launcher (experiments/sdxl/train_common.sh)
+    betas: tuple = (0.0, 0.99)
+    teacher_loss_weight: float = 5e-3
+    real_loss_weight: float = 5e-3
+    critic_loss_weight: float = 1e-2
+    generator_spectral_norm: bool = True  # frozen-gain SN on the generator's encoder + mid-block convs
+    warmup_steps: int = 500  # learning rate ramps linearly from 0 over these steps (constant afterwards)
+    # one-step generator (the reference's 1-step runs): pure noise in at this timestep, no backward
+    # simulation; None = the multi-step generator of num_denoising_step steps
+    conditioning_timestep: int | None = None
     backward_simulation: bool = True
     gradient_checkpointing: bool = True
     unet_kwargs: dict | None = None
@@ -92,6 +99,9 @@ class SDXLDMAD:
                 nn.init.zeros_(m.bias)
         if cfg.critic_spectral_norm:
             for mod in (self.critic.down_blocks, self.critic.mid_block, self.head_real, self.head_teacher):
+                apply_scaled_spectral_norm(mod, cfg.sn_iters)
+        if cfg.generator_spectral_norm:  # sd_unified_model.py:53-60
+            for mod in (self.generator.down_blocks, self.generator.mid_block):
                 apply_scaled_spectral_norm(mod, cfg.sn_iters)
         for m in (self.generator, self.critic):
             m.gradient_checkpointing = cfg.gradient_checkpointing
@@ -203,15 +213,20 @@ class SDXLDMAD:
         cfg = self.cfg
         noise, ctx, pooled = batch["noise"], batch["ctx"], batch["pooled"]
         B = noise.shape[0]
+        self._apply_warmup()
         with torch.no_grad():
-            if cfg.backward_simulation:
-                clean, t = self.sample_backward(torch.randn_like(noise), ctx, pooled)
+            if cfg.conditioning_timestep is not None:  # one-step generator: pure noise at a fixed timestep
+                t = torch.full((B,), cfg.conditioning_timestep, device=self.device, dtype=torch.long)
+                noisy = noise.clone()
             else:
-                t = self.step_list[torch.randint(0, cfg.num_denoising_step, (B,), device=self.device)]
-                clean = batch["teacher"]
-            noisy = self.add_noise(clean, noise, t)
-            pure = t == cfg.denoising_timestep - 1
-            noisy[pure] = noise[pure]
+                if cfg.backward_simulation:
+                    clean, t = self.sample_backward(torch.randn_like(noise), ctx, pooled)
+                else:
+                    t = self.step_list[torch.randint(0, cfg.num_denoising_step, (B,), device=self.device)]
+                    clean = batch["teacher"]
+                noisy = self.add_noise(clean, noise, t)
+                pure = t == cfg.denoising_timestep - 1
+                noisy[pure] = noise[pure]
         self.generator.train()
         eps = self.unet(self.generator, noisy, t, ctx, pooled).float()
         G = self.x0_from_eps(noisy, eps, t)
@@ -241,7 +256,7 @@ class SDXLDMAD:
         dR_Q, dQ_Q = self.critic_logits(batch["teacher"], tc, ctx, pooled)
         loss_c = F.softplus(-dR_T).mean() + F.softplus(dR_G).mean() + F.softplus(-dQ_Q).mean() + F.softplus(dQ_G).mean()
         self.update_gap(dR_T.detach(), dR_Q.detach(), tc)
-        loss_c.backward()
+        (cfg.critic_loss_weight * loss_c).backward()
         if self.sync_c is not None:
             self.sync_c.sync()
             torch.nn.utils.clip_grad_norm_(self.critic_params_all, cfg.max_grad_norm)
@@ -251,6 +266,19 @@ class SDXLDMAD:
         self.opt_c.zero_grad(set_to_none=True)
         self.step_count += 1
         return {"generator_loss": loss_g.detach(), "critic_loss": loss_c.detach()}
+
+    def _apply_warmup(self):
+        """Learning rates of this step: linear from 0 over warmup_steps, then constant (the reference's
+        constant_with_warmup schedule, stepped after every optimiser step)."""
+        w = self.cfg.warmup_steps
+        done = getattr(self.opt_g, "step_count", self.step_count)
+        f = 1.0 if w <= 0 else min(1.0, done / w)
+        for opt, base in ((self.opt_g, self.cfg.generator_lr), (self.opt_c, self.cfg.guidance_lr)):
+            if isinstance(opt, torch.optim.Optimizer):
+                for g in opt.param_groups:
+                    g["lr"] = base * f
+            else:  # the sharded optimiser keeps one learning rate
+                opt.lr = base * f
 
     # ------------------------------------------------------------------ generator EMA
     def ema_decay(self, batch: int) -> float:

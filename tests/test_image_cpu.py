@@ -125,3 +125,23 @@ def test_sdxl_generator_ema_weight_decay_and_clip():
         assert sd.keys() == d.generator.state_dict().keys()
         net = copy.deepcopy(d.generator)
         net.load_state_dict(sd)
+
+
+def test_sdxl_one_step_mode_and_warmup():
+    """The one-step variant (pure noise in at the conditioning timestep) trains, and the learning rate
+    ramps from 0 over the warm-up steps (the first update leaves the generator unchanged)."""
+    from dmad_b200.distill.sdxl_dmad import SDXLDMAD, SDXLDMADConfig
+    cfg = SDXLDMADConfig(latent=32, sn_iters=3, conditioning_timestep=399, warmup_steps=2, generator_lr=1e-3,
+                         unet_kwargs=dict(channels=(32, 64, 64), depths=(0, 1, 1), ctx_dim=32, pooled_dim=16,
+                                          addition_time_embed_dim=8))
+    d = SDXLDMAD(cfg, device="cpu", dtype=torch.float32)
+    before = [p.detach().clone() for p in d.gen_params]
+    B = 2
+    b = {"noise": torch.randn(B, 4, 32, 32), "real": torch.randn(B, 4, 32, 32), "teacher": torch.randn(B, 4, 32, 32),
+         "ctx": torch.randn(B, 7, 32), "pooled": torch.randn(B, 16)}
+    out = d.train_step(b)
+    assert all(torch.isfinite(v) for v in out.values())
+    assert all(torch.equal(a, p.detach()) for a, p in zip(before, d.gen_params))
+    d.train_step(b)
+    assert abs(d.opt_g.lr - 0.5 * cfg.generator_lr) < 1e-12
+    assert any(not torch.equal(a, p.detach()) for a, p in zip(before, d.gen_params))
