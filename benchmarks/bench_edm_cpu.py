@@ -79,7 +79,11 @@ def run_ours(steps, warmup):
     from dmad_b200.distill.edm_dmad import EDMDMAD, EDMDMADConfig
 
     torch.manual_seed(0)
-    m = EDMDMAD(EDMDMADConfig(batch_size=B, critic_sigma="karras"), device="cpu")
+    # the settings the reference arm below is built with (its train_edm.py argument defaults where the
+    # harness passes none): no generator spectral norm, uncapped critic noise, one EMA
+    m = EDMDMAD(EDMDMADConfig(batch_size=B, critic_sigma="karras", generator_spectral_norm=False,
+                              critic_max_timestep=None, gap_tau=2.0, r1_batch_size=2, ema_kimg=(0.5,), warmup_steps=0,
+                              teacher_loss_weight=1.0, real_loss_weight=1.0), device="cpu")
     batch = _inputs()
     return _time(lambda: m.train_step(batch), steps, warmup)
 

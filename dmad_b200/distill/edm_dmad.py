@@ -55,6 +55,10 @@ def make_binary_head(channels, spatial):
 
 @dataclass
 class EDMDMADConfig:
+    """Defaults: the reference's gap-routing ImageNet-64 recipe (experiments/imagenet/train_common.sh with
+    dmad_imagenet_gaproute.sh: generator spectral norm, critic spectral norm and gap routing, critic noise
+    capped at index 500, loss weights 3e-3, learning rates 2e-6 with a 500-step warm-up, generator EMAs of
+    1000, 8000 and 16000 kimg)."""
     resolution: int = 64
     label_dim: int = 1000
     batch_size: int = 4
@@ -65,27 +69,28 @@ class EDMDMADConfig:
     num_train_timesteps: int = 1000
     min_step_percent: float = 0.02
     max_step_percent: float = 0.98
-    critic_max_timestep: int | None = None
+    critic_max_timestep: int | None = 500
     critic_sigma: str = "karras"        # "karras" | "lognormal" (config 1: P_mean -1.2, P_std 1.2)
     p_mean: float = -1.2
     p_std: float = 1.2
     critic_clean: bool = False
     critic_spectral_norm: bool = True
-    generator_spectral_norm: bool = False
+    generator_spectral_norm: bool = True
     teacher_gap_route: bool = True
-    gap_tau: float = 2.0
+    gap_tau: float = 0.5
     r1_gamma: float = 0.0
-    r1_batch_size: int = 2
+    r1_batch_size: int = 16
     pretrained_critic: str = ""          # e.g. "vgg16_bn,tf_efficientnet_lite0": Projected-GAN feature critic
     model_id: str = ""                   # pretrained EDM teacher (.pkl release pickle, .pt / .safetensors)
-    teacher_loss_weight: float = 1.0
-    real_loss_weight: float = 1.0
+    teacher_loss_weight: float = 3e-3
+    real_loss_weight: float = 3e-3
     generator_lr: float = 2e-6
     guidance_lr: float = 2e-6
     betas: tuple = (0.0, 0.99)
     max_grad_norm: float = 10.0
-    ema_kimg: tuple = (0.5,)
+    ema_kimg: tuple = (1000.0, 8000.0, 16000.0)  # the first is the primary EMA
     ema_rampup: float = 0.05
+    warmup_steps: int = 500  # learning rates ramp linearly from 0 over these steps (constant afterwards)
 
 
 class EDMCritic(nn.Module):
@@ -259,6 +264,13 @@ class EDMDMAD:
         self.step_count = 0
         self.eye = torch.eye(cfg.label_dim, device=self.device)
 
+    def ema_state(self) -> dict:
+        """Trainer state outside the modules and optimisers: the step count (learning-rate warm-up, EMA ramp-up)."""
+        return {"step_count": self.step_count}
+
+    def load_ema_state(self, st):
+        self.step_count = int(st.get("step_count", self.step_count))
+
     def ema_files(self) -> dict:
         """{file name: EMA generator} in the reference's checkpoint naming (train_edm.py:106-124): the
         first of ``ema_kimg`` is the primary ``pytorch_model_ema.bin``, every other one
@@ -297,6 +309,10 @@ class EDMDMAD:
 
     def train_step(self, batch):
         c = self.cfg
+        f = 1.0 if c.warmup_steps <= 0 else min(1.0, self.step_count / c.warmup_steps)
+        for opt, base in ((self.opt_g, c.generator_lr), (self.opt_c, c.guidance_lr)):
+            for g in opt.param_groups:  # constant_with_warmup, stepped after every optimiser step
+                g["lr"] = base * f
         B = batch["noise"].shape[0]
         sigma = torch.full((B,), c.conditioning_sigma, device=self.device)
         self.generator.train()

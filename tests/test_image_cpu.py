@@ -5,7 +5,7 @@ import torch
 def test_edm_config1_step():
     from dmad_b200.distill.edm_dmad import EDMDMAD, EDMDMADConfig
     torch.manual_seed(0)
-    m = EDMDMAD(EDMDMADConfig(critic_sigma="lognormal"))
+    m = EDMDMAD(EDMDMADConfig(critic_sigma="lognormal", warmup_steps=0))
     b = m.synthetic_batch(torch.Generator().manual_seed(0))
     before = [p.detach().clone() for p in m.generator.parameters()]
     out = m.train_step(b)
